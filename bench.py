@@ -1,0 +1,355 @@
+#!/usr/bin/env python
+"""MoE-layer tokens/s on B200: the Qwen3-30B-A3B-shaped layer with INT8 experts.
+
+Workload: hidden 2048, 128 routed experts, top-8 with
+renormalised probabilities, expert intermediate 768, SwiGLU, INT8
+per-projection affine expert weights quantised from seeded N(0, 0.02^2),
+Zipf(1.1)-skewed router logits, activations ~N(0,1), 4096 tokens per GPU per
+step (the prefill batch; --tokens picks 1/16/256 for decode-sized batches).
+Seeded synthetic inputs stand in for real checkpoints and prompts.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--tokens T]
+  python bench.py --impl reference ...    the reference's own CPU path
+
+One JSON line on rank 0.  `value` is device-timed (CUDA events per step,
+inputs resident in HBM, L2 flushed between steps); `e2e` is the same metric
+through hmoe_moe_forward_host with page-locked host buffers, both copies
+inside the timed region.  `roofline` covers the dominant stage, timed live
+with events the library records at stage boundaries.  `cpu_baseline` is the
+reference's own CPU implementation (oracle/_ref, compiled from its sources)
+on a bounded token sample, on this host's cores.
+
+Multi-GPU (torchrun, one process per GPU): every rank holds the whole layer
+and routes its own 4096 tokens -- independent replicas, weak scaling -- until
+expert parallelism replaces it; the time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "hypermoe-engine_b200"))
+
+METRIC = "MoE-layer tokens/s (Qwen3-30B-A3B shape, INT8 experts)"
+UNIT = "tokens/s"
+STAGES = ["route", "group", "gate_up", "down", "combine"]
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--tokens", type=int, default=4096)
+    p.add_argument("--config", default="c3")
+    p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--impl", default="hmoe", choices=["hmoe", "reference"])
+    p.add_argument("--variant", type=int, default=0, help="0 auto, 1 GEMV only, 2 GEMM only")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-seconds", type=float, default=12.0)
+    return p.parse_args()
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained"), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+class Clocks:
+    """nvidia-smi sampler for the timed region (clocks and throttle reasons)."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.index)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def algorithmic(cfg, T, ids_np, offsets_np):
+    """Algorithmic bytes and FLOPs per stage for one layer call."""
+    H, I, E, k, S = cfg.hidden, cfg.intermediate, cfg.experts, cfg.top_k, cfg.shared_experts
+    counts = offsets_np[1:] - offsets_np[:-1]
+    U = int((counts > 0).sum()) + S
+    rows = T * (k + S)
+    return {
+        "route": {"bytes": T * H * 4 + H * E * 4 + T * k * 8, "flops": 2 * T * H * E},
+        "group": {"bytes": T * k * 8 * 2, "flops": 0},
+        "gate_up": {"bytes": U * 2 * H * I + rows * H * 4 + rows * I * 4, "flops": 4 * rows * H * I},
+        "down": {"bytes": U * H * I + rows * I * 4 + rows * H * 4, "flops": 2 * rows * H * I},
+        "combine": {"bytes": rows * H * 4 + T * H * 4, "flops": 0},
+        "layer": {"bytes": U * 3 * H * I + H * E * 4 + 8 * T * H, "flops": T * (2 * H * E + (k + S) * 6 * H * I)},
+        "unique_experts": U,
+    }
+
+
+def cpu_reference_sample(cfg, host_layer, x_all, seconds, threads):
+    """Times the reference's CPU path on growing token samples until one takes
+    about `seconds`; returns (tokens/s, tokens in the sample, seconds)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    if not O.ref_available():
+        O.build(reference=False)
+    rl = O.RefLayer(host_layer)
+    n = 1
+    while True:
+        t0 = time.perf_counter()
+        rl.forward(x_all[:n], threads=threads)
+        dt = time.perf_counter() - t0
+        if dt >= seconds or n >= x_all.shape[0]:
+            return n / dt, n, dt
+        n = min(x_all.shape[0], max(n + 1, int(n * min(8.0, 1.2 * seconds / max(dt, 1e-3)))))
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    import numpy as np
+    import hmoe_api as H
+
+    cfg = H.CONFIGS[args.config]
+    T = args.tokens
+    config = {"workload": f"{args.config}: qwen3-30b-a3b moe layer" if args.config == "c3" else args.config,
+              "hidden": cfg.hidden, "experts": cfg.experts, "top_k": cfg.top_k,
+              "intermediate": cfg.intermediate, "shared_experts": cfg.shared_experts,
+              "tokens_per_gpu": T, "routing": "zipf1.1" if cfg.zipf_alpha else "uniform",
+              "weights": "int8 per-projection affine", "seed": args.seed}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        threads = os.cpu_count() or 1
+        host_layer = H.make_host_layer(cfg, seed=args.seed)
+        x = H.make_tokens(cfg, max(T, 1), seed=args.seed)
+        per_step = max(1.0, min(6.0, 150.0 / max(1, args.steps + args.warmup)))
+        rate, n, dt = cpu_reference_sample(cfg, host_layer, x, per_step, threads)
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        rl = O.RefLayer(host_layer)
+        for _ in range(args.warmup):
+            rl.forward(x[:n], threads=threads)
+        times = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            rl.forward(x[:n], threads=threads)
+            times.append(time.perf_counter() - t0)
+        value = n / statistics.mean(times)
+        sample = (f"{n} of the {T} tokens per step (reference MoERuntime CPU branch: CpuRouterBackend + "
+                  f"CpuTensorBackend INT8 GEMMs, expert groups spread over {threads} host threads)")
+        print(json.dumps({
+            "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.mean(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded)", "config": config,
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }))
+        return
+
+    import torch
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    H.set_variant(args.variant)
+    host_layer = H.make_host_layer(cfg, seed=args.seed)
+    x_np = H.make_tokens(cfg, T, seed=args.seed + 7919 * rank)
+    layer = H.DeviceLayer(host_layer, dev)
+    x = torch.from_numpy(x_np).to(dev)
+    y = torch.empty_like(x)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    import ctypes
+    arr = (ctypes.c_void_p * 6)(*[e.cuda_event for e in ev])
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # routing facts for the algorithmic byte/FLOP counts
+    ids, scores, offsets, _, _ = layer.route(x)
+    torch.cuda.synchronize()
+    alg = algorithmic(cfg, T, ids.cpu().numpy(), offsets.cpu().numpy())
+
+    for _ in range(args.warmup):
+        layer.forward(x, y)
+    barrier()
+
+    # device-timed region: K steps, L2 flushed between steps (outside the events)
+    H.check("stage events", H.lib().hmoe_set_stage_events(arr, 6))
+    launches0 = H.lib().hmoe_launch_count()
+    clocks = Clocks(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local])
+                    if os.environ.get("CUDA_VISIBLE_DEVICES") else local)
+    clocks.start()
+    stage_ms = {s: [] for s in STAGES}
+    step_ms = []
+    barrier()
+    for _ in range(args.steps):
+        flush.zero_()
+        layer.forward(x, y)
+        ev[5].synchronize()
+        step_ms.append(ev[0].elapsed_time(ev[5]))
+        for i, s in enumerate(STAGES):
+            stage_ms[s].append(ev[i].elapsed_time(ev[i + 1]))
+    barrier()
+    clk = clocks.stop()
+    launches = H.lib().hmoe_launch_count() - launches0
+    H.check("stage events", H.lib().hmoe_set_stage_events(None, 0))
+    ms = statistics.mean(step_ms)
+    if dist is not None:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = world * T / (ms * 1e-3)
+
+    # e2e: host buffers through hmoe_moe_forward_host, copies inside the region
+    xh = torch.from_numpy(x_np).pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    for _ in range(max(1, args.warmup // 2)):
+        layer.forward_host(xh, yh)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_ms = []
+    for _ in range(args.steps):
+        flush.zero_()
+        e0.record(stream)
+        layer.forward_host(xh, yh)
+        e1.record(stream)
+        e1.synchronize()
+        e2e_ms.append(e0.elapsed_time(e1))
+    em = statistics.mean(e2e_ms)
+    if dist is not None:
+        t = torch.tensor([em], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        em = float(t.item())
+    e2e = {"value": world * T / (em * 1e-3), "unit": UNIT, "h2d_bytes_per_step": int(x_np.nbytes),
+           "d2h_bytes_per_step": int(x_np.nbytes)}
+
+    status = layer.read_status()
+    if rank != 0:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    peaks = load_peaks()
+    avg = {s: statistics.mean(v) for s, v in stage_ms.items()}
+    top = max(STAGES, key=lambda s: avg[s])
+    a = alg[top]
+    ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
+    tensor = a["flops"] > 0 and a["flops"] / max(a["bytes"], 1) > ridge
+    dt_s = avg[top] * 1e-3
+    if tensor:
+        roof = {"bound": "tensor", "achieved": a["flops"] / dt_s / 1e12, "peak": peaks["bf16_tflops"],
+                "unit": "TFLOP/s"}
+    else:
+        roof = {"bound": "hbm", "achieved": a["bytes"] / dt_s / 1e9, "peak": peaks["hbm_gbs"], "unit": "GB/s"}
+    roof["frac"] = roof["achieved"] / roof["peak"]
+    roof["kernel"] = top
+    roof["peak_source"] = peaks["source"] + (" burst" if tensor else "")
+    roof["traffic"] = None
+    tr_path = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tr_path):
+        with open(tr_path) as f:
+            tr = json.load(f)
+        key = f"{args.config}:T{T}:{top}"
+        if key in tr:
+            roof["traffic"] = tr[key]["bytes_per_launch"]
+    layer_roof_ms = 1e3 * max(alg["layer"]["bytes"] / (peaks["hbm_gbs"] * 1e9),
+                              alg["layer"]["flops"] / (peaks["bf16_tflops"] * 1e12))
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        rate, n, dt = cpu_reference_sample(cfg, host_layer, x_np, args.cpu_seconds, threads)
+        cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "reference",
+               "sample": f"{n} tokens of this workload through the reference CPU path "
+                         f"(oracle/_ref), {dt:.1f} s, expert groups over {threads} threads"}
+
+    # tensor-core GEMM present (hmoe_set_variant(2) is refused without it)?
+    has_gemm = H.lib().hmoe_set_variant(2) == 0
+    H.lib().hmoe_set_variant(args.variant)
+    used_gemm = has_gemm and args.variant != 1 and T * cfg.top_k / cfg.experts > 16
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32" if not used_gemm else "bf16",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights quantised to INT8)",
+        "config": dict(config, parallelism=("replicas" if world > 1 else "single"),
+                       l2="inputs larger than L2 (604 MB INT8 arena) and a 256 MiB flush between steps"),
+        "e2e": e2e, "gpu_launches": launches,
+        "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
+        "stages_ms": avg, "layer_roofline_ms": layer_roof_ms,
+        "layer_roofline_frac": layer_roof_ms / ms, "unique_experts": alg["unique_experts"],
+        "device_status": {"status": status[0], "near_ties": status[1], "sequential_logits": status[2]},
+    }
+    print(json.dumps(line))
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

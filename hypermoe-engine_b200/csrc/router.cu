@@ -1,0 +1,492 @@
+// router.cu -- router logits, softmax, top-k, renormalisation and the
+// device-built expert grouping (histogram, prefix offsets, permutation).
+//
+// Contract: the selected ids (and therefore the permutation) equal those of
+// the reference CPU router, CpuRouterBackend::routeToken
+// (src/router/CpuRouterBackend.cpp:35-91), on the same inputs:
+//
+//  * logits.  The reference computes float(sum_i double(h_i)*double(W_ie))
+//    sequentially in i order.  A product of two floats is exact in double,
+//    so only the summation order can differ.  Here the sum is formed in P
+//    parallel chunks (fixed order), and a rigorous bound on the difference
+//    between any two orderings, (H + L + P + 2) * 2^-53 * sum|h_i W_ie|, is
+//    checked against the distance to the nearest float rounding boundary.
+//    When the bound does not certify that both orders round to the same
+//    float, that logit is recomputed in the reference's sequential order.
+//    Every logit is therefore bit-identical to the reference's.
+//
+//  * softmax.  exp(l - max) is evaluated in double and rounded to float
+//    (a correctly rounded expf).  The reference calls glibc expf, which is
+//    not correctly rounded for ~1e-4 of inputs (always within 1 ulp).  exp
+//    is monotone, so the selection can only differ from the reference where
+//    two candidate probabilities adjacent in rank are within 2 ulp of each
+//    other while their logits differ.  Such near-ties are counted in the
+//    workspace status word (hmoe_read_status) so callers and tests can see
+//    that the certificate covered every token.
+//
+//  * the denominator is a double sum in expert order, the probabilities
+//    float(double(e)/D), selection (score desc, id asc), renormalisation by
+//    a double sum in rank order -- all as in the reference.
+#include "common.cuh"
+
+#include <cfloat>
+#include <climits>
+
+namespace hmoe {
+
+constexpr int kRouteTokens = 4;  // tokens per CTA in the fused router
+constexpr int kMaxExperts = 256; // E_pad <= 256 (8 candidates per lane)
+constexpr int kMaxTopK = 32;
+
+struct RouteArgs {
+    const float* x;     // [T, H]
+    const float* w;     // [H, E]
+    const float* bias;  // [E] or null
+    int T, H, E, k, softmax, renorm;
+    uint32_t* ids;      // [T, k]
+    float* scores;      // [T, k]
+    int32_t* counts;    // [E] (zeroed by the caller), may be null
+    DeviceStatus* st;
+};
+
+__device__ __forceinline__ bool better(float pa, int ia, float pb, int ib) {
+    return pa > pb || (pa == pb && ia < ib);
+}
+
+// Distance check of a double sum against float rounding boundaries.
+__device__ __forceinline__ bool rounding_certified(double s, double beta) {
+    const float f = static_cast<float>(s);
+    const double fd = static_cast<double>(f);
+    const double lo = 0.5 * (fd + static_cast<double>(nextafterf(f, -FLT_MAX * 2.0f)));
+    const double hi = 0.5 * (fd + static_cast<double>(nextafterf(f, FLT_MAX * 2.0f)));
+    return (s - beta > lo) && (s + beta < hi);
+}
+
+// Selection, renormalisation and near-tie accounting for one token held by
+// one warp: lanes own candidates j = lane + 32*c.  `lv` are exact logits.
+template <int C>
+__device__ void select_token(const float (&lv)[C], int E, int k, int softmax,
+                             int renorm, float* ev_smem, uint32_t* ids_out,
+                             float* scores_out, int32_t* counts,
+                             DeviceStatus* st, bool write_probs,
+                             float* probs_out) {
+    const int lane = threadIdx.x & 31;
+    float p[C];
+    float m = -FLT_MAX * 2.0f;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        const int j = lane + 32 * c;
+        if (j < E) m = fmaxf(m, lv[c]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    bool ok = true;
+    if (softmax) {
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            const int j = lane + 32 * c;
+            const float d = lv[c] - m; // float subtraction, as the reference
+            const float e = static_cast<float>(exp(static_cast<double>(d)));
+            p[c] = e;
+            if (j < E) ev_smem[j] = e;
+        }
+        __syncwarp();
+        double den = 0.0;
+        if (lane == 0)
+            for (int j = 0; j < E; ++j) den += static_cast<double>(ev_smem[j]);
+        den = __shfl_sync(0xffffffffu, den, 0);
+        __syncwarp();
+        if (!(isfinite(den) && den > 0.0)) ok = false;
+#pragma unroll
+        for (int c = 0; c < C; ++c) p[c] = static_cast<float>(static_cast<double>(p[c]) / den);
+    } else {
+#pragma unroll
+        for (int c = 0; c < C; ++c) p[c] = lv[c];
+    }
+    if (write_probs) {
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            const int j = lane + 32 * c;
+            if (j < E) probs_out[j] = p[c];
+        }
+    }
+    unsigned selected = 0; // bit c: candidate c of this lane taken
+    double rsum = 0.0;
+    float prev_p = 0.0f, prev_l = 0.0f;
+    float chosen[kMaxTopK];
+    bool tie = false;
+    const int rounds = k < E ? k + 1 : k; // one extra to see rank k
+    for (int r = 0; r < rounds; ++r) {
+        float bp = -FLT_MAX * 2.0f, bl = 0.0f;
+        int bi = INT_MAX;
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            const int j = lane + 32 * c;
+            if (j < E && !((selected >> c) & 1u) && better(p[c], j, bp, bi)) {
+                bp = p[c];
+                bi = j;
+                bl = lv[c];
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float op = __shfl_xor_sync(0xffffffffu, bp, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            const float ol = __shfl_xor_sync(0xffffffffu, bl, o);
+            if (better(op, oi, bp, bi)) {
+                bp = op;
+                bi = oi;
+                bl = ol;
+            }
+        }
+        if (r > 0 && softmax && bl != prev_l) {
+            const int d = abs(__float_as_int(prev_p) - __float_as_int(bp));
+            if (d <= 2) tie = true;
+        }
+        prev_p = bp;
+        prev_l = bl;
+        if (r == k) break;
+        if ((bi & 31) == lane) selected |= 1u << (bi >> 5);
+        chosen[r] = bp;
+        rsum += static_cast<double>(bp);
+        if (lane == 0) {
+            ids_out[r] = static_cast<uint32_t>(bi);
+            if (counts) atomicAdd(counts + bi, 1);
+        }
+    }
+    if (lane == 0) {
+        if (renorm) {
+            if (!(isfinite(rsum) && rsum != 0.0)) ok = false;
+            if (ok) {
+                for (int r = 0; r < k; ++r)
+                    scores_out[r] = static_cast<float>(static_cast<double>(chosen[r]) / rsum);
+            } else {
+                for (int r = 0; r < k; ++r) scores_out[r] = chosen[r];
+                scores_out[0] = __int_as_float(0x7fc00000); // NaN, CudaKernels.cu:201-202
+            }
+        } else {
+            for (int r = 0; r < k; ++r) scores_out[r] = chosen[r];
+            if (!ok) scores_out[0] = __int_as_float(0x7fc00000);
+        }
+        if (!ok) device_fail(st, HMOE_NON_FINITE_ROUTER);
+        if (tie && st) atomicAdd(&st->near_ties, 1);
+    }
+}
+
+// Fused router.  Block = E_pad * P threads: thread (e = tid % E_pad,
+// q = tid / E_pad) sums chunk q of the hidden dimension for expert e over
+// kRouteTokens tokens.  Dynamic smem: x tile, double partials, |.| partials,
+// logits, per-warp exp scratch.
+template <int C>
+__global__ void __launch_bounds__(1024) route_kernel(RouteArgs a, int E_pad, int P) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int H = a.H, E = a.E;
+    float* xs = reinterpret_cast<float*>(smem);                                   // [TB][H]
+    double* part = reinterpret_cast<double*>(xs + kRouteTokens * H);              // [TB][P][E_pad]
+    float* absb = reinterpret_cast<float*>(part + kRouteTokens * P * E_pad);      // [TB][P][E_pad]
+    float* logit = absb + kRouteTokens * P * E_pad;                               // [TB][E_pad]
+    float* evs = logit + kRouteTokens * E_pad;                                    // [TB][E_pad]
+
+    const int tid = threadIdx.x;
+    const int e = tid % E_pad, q = tid / E_pad;
+    const int t0 = blockIdx.x * kRouteTokens;
+    const int nt = min(kRouteTokens, a.T - t0);
+    for (int i = tid; i < nt * H; i += blockDim.x) xs[i] = a.x[static_cast<size_t>(t0) * H + i];
+    __syncthreads();
+
+    const int L = (H + P - 1) / P;
+    const int i0 = min(H, q * L), i1 = min(H, i0 + L);
+    double acc[kRouteTokens];
+    float aab[kRouteTokens];
+#pragma unroll
+    for (int t = 0; t < kRouteTokens; ++t) {
+        acc[t] = 0.0;
+        aab[t] = 0.0f;
+    }
+    if (e < E) {
+        for (int i = i0; i < i1; ++i) {
+            const float wf = a.w[static_cast<size_t>(i) * E + e];
+            const double wd = static_cast<double>(wf);
+            const float wa = fabsf(wf);
+#pragma unroll
+            for (int t = 0; t < kRouteTokens; ++t) {
+                const float xv = xs[t * H + i];
+                acc[t] = fma(static_cast<double>(xv), wd, acc[t]);
+                aab[t] = fmaf(fabsf(xv), wa, aab[t]);
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < kRouteTokens; ++t) {
+        part[(t * P + q) * E_pad + e] = acc[t];
+        absb[(t * P + q) * E_pad + e] = aab[t];
+    }
+    __syncthreads();
+
+    for (int t = q; t < nt && e < E; t += P) {
+        double s = 0.0;
+        float A = 0.0f;
+        for (int r = 0; r < P; ++r) {
+            s += part[(t * P + r) * E_pad + e];
+            A += absb[(t * P + r) * E_pad + e];
+        }
+        if (a.bias) {
+            s += static_cast<double>(a.bias[e]);
+            A += fabsf(a.bias[e]);
+        }
+        // A (FP32, positive terms) is within (H+2)*2^-23 of the true sum.
+        const double Aup = static_cast<double>(A) * (1.0 + (H + 2) * 0x1.0p-22) + 0x1.0p-140;
+        const double beta = static_cast<double>(H + L + P + 4) * 0x1.0p-53 * Aup * 1.01;
+        if (!rounding_certified(s, beta)) {
+            const float* xr = xs + t * H;
+            double seq = 0.0;
+            for (int i = 0; i < H; ++i)
+                seq = fma(static_cast<double>(xr[i]), static_cast<double>(a.w[static_cast<size_t>(i) * E + e]), seq);
+            if (a.bias) seq = fma(1.0, static_cast<double>(a.bias[e]), seq);
+            s = seq;
+            if (a.st) atomicAdd(&a.st->sequential_logits, 1);
+        }
+        if (!isfinite(s)) device_fail(a.st, HMOE_NON_FINITE_ROUTER);
+        logit[t * E_pad + e] = static_cast<float>(s);
+    }
+    __syncthreads();
+
+    const int warp = tid >> 5, lane = tid & 31;
+    const int nwarps = blockDim.x >> 5;
+    for (int t = warp; t < nt; t += nwarps) {
+        float lv[C];
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            const int j = lane + 32 * c;
+            lv[c] = j < E ? logit[t * E_pad + j] : 0.0f;
+        }
+        const size_t tok = static_cast<size_t>(t0 + t);
+        select_token<C>(lv, E, a.k, a.softmax, a.renorm, evs + t * E_pad,
+                        a.ids + tok * a.k, a.scores + tok * a.k, a.counts,
+                        a.st, false, nullptr);
+    }
+}
+
+// kernels::routerTopK drop-in (CudaKernels.cu:152-204): one warp per token,
+// logits given, probabilities written back in place when softmax != 0.
+template <int C>
+__global__ void router_topk_kernel(float* logits, int T, int E, int k,
+                                   int softmax, int renorm, uint32_t* ids,
+                                   float* scores) {
+    __shared__ float evs[8][kMaxExperts];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 8 + warp;
+    if (t >= T) return;
+    float* row = logits + static_cast<size_t>(t) * E;
+    float lv[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        const int j = lane + 32 * c;
+        lv[c] = j < E ? row[j] : 0.0f;
+    }
+    select_token<C>(lv, E, k, softmax, renorm, evs[warp], ids + static_cast<size_t>(t) * k,
+                    scores + static_cast<size_t>(t) * k, nullptr, nullptr, softmax != 0, row);
+}
+
+// ------------------------------------------------------------ grouping
+
+struct GroupArgs {
+    const uint32_t* ids;   // [T, k]
+    const float* scores;   // [T, k]
+    const int32_t* counts; // [E] routed counts
+    int T, k, E, S;        // S shared experts
+    int small_max;         // experts with count <= small_max use the GEMV
+    int32_t* offsets;      // [E+S+1]
+    uint32_t* perm_token;  // [T*(k+S)] token of each permuted row
+    float* perm_weight;    // [T*(k+S)] routing weight of each row
+    int32_t* inv;          // [T*(k+S)] row of (token, slot); slots k.. = shared
+    int32_t* small_list;   // [E+S] experts for the GEMV, ascending id
+    int32_t* large_list;   // [E+S] experts for the tensor-core GEMM
+    int32_t* list_sizes;   // [2]
+};
+
+__device__ __forceinline__ int group_count(const GroupArgs& g, int e) {
+    return e < g.E ? g.counts[e] : g.T;
+}
+
+// One CTA per expert (routed then shared).  Tokens are placed in ascending
+// order inside the expert's group, exactly as routeBatch appends them.
+__global__ void __launch_bounds__(256) group_kernel(GroupArgs g) {
+    __shared__ int red[3][8];
+    __shared__ int warp_hits[8];
+    __shared__ int base_s;
+    const int e = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // Offset and list positions of expert e from the counts of e' < e.
+    int off = 0, small_before = 0, large_before = 0;
+    const int total = g.E + g.S;
+    const bool last = e == total - 1;
+    for (int j = tid; j < (last ? total : e); j += blockDim.x) {
+        const int c = group_count(g, j);
+        if (j < e) off += c;
+        const bool sm = c > 0 && c <= g.small_max;
+        const bool lg = c > g.small_max;
+        if (j < e) {
+            small_before += sm;
+            large_before += lg;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        off += __shfl_xor_sync(0xffffffffu, off, o);
+        small_before += __shfl_xor_sync(0xffffffffu, small_before, o);
+        large_before += __shfl_xor_sync(0xffffffffu, large_before, o);
+    }
+    if (lane == 0) {
+        red[0][warp] = off;
+        red[1][warp] = small_before;
+        red[2][warp] = large_before;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int o = 0, s = 0, l = 0;
+        for (int w = 0; w < 8; ++w) {
+            o += red[0][w];
+            s += red[1][w];
+            l += red[2][w];
+        }
+        const int c = group_count(g, e);
+        g.offsets[e] = o;
+        if (c > 0 && c <= g.small_max) g.small_list[s] = e;
+        if (c > g.small_max) g.large_list[l] = e;
+        if (last) {
+            g.offsets[total] = o + c;
+            g.list_sizes[0] = s + (c > 0 && c <= g.small_max);
+            g.list_sizes[1] = l + (c > g.small_max);
+        }
+        base_s = o;
+    }
+    __syncthreads();
+    int base = base_s;
+    const int slots = g.k + g.S;
+    if (e >= g.E) {
+        const int s = e - g.E;
+        for (int t = tid; t < g.T; t += blockDim.x) {
+            const int row = base + t;
+            g.perm_token[row] = static_cast<uint32_t>(t);
+            g.perm_weight[row] = 1.0f;
+            g.inv[static_cast<size_t>(t) * slots + g.k + s] = row;
+        }
+        return;
+    }
+    for (int t0 = 0; t0 < g.T; t0 += blockDim.x) {
+        const int t = t0 + tid;
+        int slot = -1;
+        if (t < g.T) {
+            const uint32_t* r = g.ids + static_cast<size_t>(t) * g.k;
+            for (int j = 0; j < g.k; ++j)
+                if (r[j] == static_cast<uint32_t>(e)) slot = j;
+        }
+        const unsigned mask = __ballot_sync(0xffffffffu, slot >= 0);
+        if (lane == 0) warp_hits[warp] = __popc(mask);
+        __syncthreads();
+        int before = 0, chunk = 0;
+        for (int w = 0; w < 8; ++w) {
+            before += w < warp ? warp_hits[w] : 0;
+            chunk += warp_hits[w];
+        }
+        if (slot >= 0) {
+            const int row = base + before + __popc(mask & ((1u << lane) - 1u));
+            g.perm_token[row] = static_cast<uint32_t>(t);
+            g.perm_weight[row] = g.scores[static_cast<size_t>(t) * g.k + slot];
+            g.inv[static_cast<size_t>(t) * slots + slot] = row;
+        }
+        base += chunk;
+        __syncthreads();
+    }
+}
+
+// ------------------------------------------------------------ launchers
+
+int route_smem_bytes(int H, int E_pad, int P) {
+    return kRouteTokens * H * 4 + kRouteTokens * P * E_pad * (8 + 4) + 2 * kRouteTokens * E_pad * 4;
+}
+
+hmoe_status launch_route(const float* x, const float* w, const float* bias,
+                         int T, int H, int E, int k, int softmax, int renorm,
+                         uint32_t* ids, float* scores, int32_t* counts,
+                         DeviceStatus* st, cudaStream_t stream) {
+    if (T <= 0) return HMOE_OK;
+    if (E <= 0 || E > kMaxExperts || k <= 0 || k > E || k > kMaxTopK || H <= 0)
+        return HMOE_INVALID_ARGUMENT;
+    const int E_pad = (E + 31) / 32 * 32;
+    int P = 1024 / E_pad;
+    while (P > 1 && P * 8 > H) P >>= 1; // keep chunks >= 8 long
+    const int smem = route_smem_bytes(H, E_pad, P);
+    if (smem > 227 * 1024) return HMOE_UNSUPPORTED;
+    RouteArgs a{x, w, bias, T, H, E, k, softmax, renorm, ids, scores, counts, st};
+    const unsigned grid = static_cast<unsigned>((T + kRouteTokens - 1) / kRouteTokens);
+    const int C = E_pad / 32;
+#define HMOE_ROUTE_CASE(CC)                                                                       \
+    case CC:                                                                                      \
+        cudaFuncSetAttribute(route_kernel<CC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
+        route_kernel<CC><<<grid, E_pad * P, smem, stream>>>(a, E_pad, P);                          \
+        break;
+    switch (C) {
+        HMOE_ROUTE_CASE(1)
+        HMOE_ROUTE_CASE(2)
+        HMOE_ROUTE_CASE(3)
+        HMOE_ROUTE_CASE(4)
+        HMOE_ROUTE_CASE(5)
+        HMOE_ROUTE_CASE(6)
+        HMOE_ROUTE_CASE(7)
+        HMOE_ROUTE_CASE(8)
+    default: return HMOE_UNSUPPORTED;
+    }
+#undef HMOE_ROUTE_CASE
+    return check_launch("hmoe route kernel");
+}
+
+hmoe_status launch_group(const uint32_t* ids, const float* scores,
+                         const int32_t* counts, int T, int k, int E, int S,
+                         int small_max, int32_t* offsets, uint32_t* perm_token,
+                         float* perm_weight, int32_t* inv, int32_t* small_list,
+                         int32_t* large_list, int32_t* list_sizes,
+                         cudaStream_t stream) {
+    GroupArgs g{ids, scores, counts, T, k, E, S, small_max, offsets, perm_token,
+                perm_weight, inv, small_list, large_list, list_sizes};
+    group_kernel<<<E + S, 256, 0, stream>>>(g);
+    return check_launch("hmoe group kernel");
+}
+
+} // namespace hmoe
+
+extern "C" hmoe_status hmoe_router_topk(float* logits, size_t tokens,
+                                        size_t experts, size_t top_k,
+                                        int softmax, int renormalize,
+                                        uint32_t* selected_ids,
+                                        float* selected_scores, void* stream) {
+    using namespace hmoe;
+    if (tokens == 0) return HMOE_OK;
+    if (!logits || !selected_ids || !selected_scores || experts == 0 ||
+        top_k == 0 || top_k > experts || experts > kMaxExperts || top_k > kMaxTopK ||
+        tokens > static_cast<size_t>(INT_MAX))
+        return HMOE_INVALID_ARGUMENT;
+    const int C = static_cast<int>((experts + 31) / 32);
+    const unsigned grid = static_cast<unsigned>((tokens + 7) / 8);
+    const int T = static_cast<int>(tokens), E = static_cast<int>(experts), K = static_cast<int>(top_k);
+    cudaStream_t s = as_stream(stream);
+#define HMOE_TOPK_CASE(CC)                                                                         \
+    case CC:                                                                                       \
+        router_topk_kernel<CC><<<grid, 256, 0, s>>>(logits, T, E, K, softmax, renormalize,          \
+                                                   selected_ids, selected_scores);                 \
+        break;
+    switch (C) {
+        HMOE_TOPK_CASE(1)
+        HMOE_TOPK_CASE(2)
+        HMOE_TOPK_CASE(3)
+        HMOE_TOPK_CASE(4)
+        HMOE_TOPK_CASE(5)
+        HMOE_TOPK_CASE(6)
+        HMOE_TOPK_CASE(7)
+        HMOE_TOPK_CASE(8)
+    default: return HMOE_UNSUPPORTED;
+    }
+#undef HMOE_TOPK_CASE
+    return check_launch("CUDA router top-k kernel");
+}

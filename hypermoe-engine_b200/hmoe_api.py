@@ -1,0 +1,319 @@
+"""ctypes binding of include/hmoe.h (lib/libhmoe.so) plus layer helpers.
+
+Host glue for tests and the benchmark: PyTorch provides device memory and
+streams; every computation happens inside libhmoe.so.  Loading fails loudly
+when the library has not been built -- there is no fallback path.
+
+The layer helper mirrors how the reference's runtime holds an all-resident
+MoE layer: one INT8 expert arena in the ExpertPacker layout
+(tools/model_convert/ExpertPacker.cpp:150-247), the router matrix
+[H, E] (CpuRouterBackend.cpp:44-45 indexing) and per-projection
+QuantizationParameters (Quantization.hpp:19-25).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass
+from typing import Optional
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "lib", "libhmoe.so")
+
+OK = 0
+STATUS_NAMES = {
+    0: "HMOE_OK", 1: "HMOE_INVALID_ARGUMENT", 2: "HMOE_NON_FINITE_ROUTER",
+    3: "HMOE_CUDA_ERROR", 4: "HMOE_NCCL_ERROR", 5: "HMOE_TIMEOUT",
+    6: "HMOE_WORKSPACE_TOO_SMALL", 7: "HMOE_UNSUPPORTED",
+}
+
+# Every symbol include/hmoe.h declares (checked by tests/test_capi.py).
+EXPORTS = [
+    "hmoe_last_error", "hmoe_activation", "hmoe_int8_weight_matmul",
+    "hmoe_int8_weight_matmul_cooperative", "hmoe_int8_gemm_plan",
+    "hmoe_router_topk", "hmoe_gather_rows", "hmoe_scatter_add_rows",
+    "hmoe_zero", "hmoe_workspace_size", "hmoe_route", "hmoe_moe_forward",
+    "hmoe_set_variant", "hmoe_read_status", "hmoe_synth_normal",
+    "hmoe_synth_zipf_bias", "hmoe_quantize_int8", "hmoe_synth_arena",
+    "hmoe_set_stage_events", "hmoe_launch_count", "hmoe_moe_forward_host",
+]
+HOST_IO = 1 << 62
+
+
+class HmoeError(RuntimeError):
+    def __init__(self, fn: str, code: int, detail: str = ""):
+        super().__init__(f"{fn} -> {STATUS_NAMES.get(code, code)} {detail}".strip())
+        self.code = code
+
+
+class ExpertQuant(ctypes.Structure):
+    _fields_ = [("scale", ctypes.c_float * 3), ("zero_point", ctypes.c_int32 * 3)]
+
+
+class LayerDesc(ctypes.Structure):
+    _fields_ = [
+        ("hidden", ctypes.c_uint32), ("intermediate", ctypes.c_uint32),
+        ("experts", ctypes.c_uint32), ("top_k", ctypes.c_uint32),
+        ("softmax", ctypes.c_int32), ("renormalize", ctypes.c_int32),
+        ("shared_experts", ctypes.c_uint32), ("reserved0", ctypes.c_uint32),
+        ("router_weight", ctypes.c_void_p), ("router_bias", ctypes.c_void_p),
+        ("arena", ctypes.c_void_p), ("expert_stride", ctypes.c_uint64),
+        ("gate_offset", ctypes.c_uint64), ("up_offset", ctypes.c_uint64),
+        ("down_offset", ctypes.c_uint64), ("quant", ctypes.c_void_p),
+        ("ep_rank", ctypes.c_int32), ("ep_size", ctypes.c_int32),
+    ]
+
+
+class GemmPlan(ctypes.Structure):
+    _fields_ = [("implementation", ctypes.c_int32), ("partitions", ctypes.c_size_t),
+                ("blocks", ctypes.c_size_t), ("scratch_elements", ctypes.c_size_t)]
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Loads libhmoe.so (raises if it is missing)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(
+                f"{LIB_PATH} is not built; run `python -c 'import __graft_entry__ as g; g.build()'`")
+        L = ctypes.CDLL(LIB_PATH)
+        vp, sz, i32, u64, f32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int32, ctypes.c_uint64, ctypes.c_float
+        L.hmoe_last_error.restype = ctypes.c_char_p
+        sigs = {
+            "hmoe_activation": [ctypes.c_int, vp, vp, sz, vp],
+            "hmoe_int8_weight_matmul": [vp, vp, vp, sz, sz, sz, f32, i32, vp],
+            "hmoe_int8_weight_matmul_cooperative": [vp, vp, vp, vp, sz, sz, sz, sz, f32, i32, vp],
+            "hmoe_int8_gemm_plan": [sz, sz, sz, i32, ctypes.POINTER(GemmPlan)],
+            "hmoe_router_topk": [vp, sz, sz, sz, ctypes.c_int, ctypes.c_int, vp, vp, vp],
+            "hmoe_gather_rows": [vp, vp, vp, sz, sz, vp],
+            "hmoe_scatter_add_rows": [vp, vp, vp, vp, sz, sz, vp],
+            "hmoe_zero": [vp, sz, vp],
+            "hmoe_workspace_size": [ctypes.POINTER(LayerDesc), sz, ctypes.POINTER(sz)],
+            "hmoe_route": [ctypes.POINTER(LayerDesc), vp, sz, vp, vp, vp, vp, vp, vp, sz, vp],
+            "hmoe_moe_forward": [ctypes.POINTER(LayerDesc), vp, vp, sz, vp, sz, vp],
+            "hmoe_moe_forward_host": [ctypes.POINTER(LayerDesc), vp, vp, sz, vp, sz, vp],
+            "hmoe_set_variant": [i32],
+            "hmoe_read_status": [vp, ctypes.POINTER(i32), ctypes.POINTER(i32), ctypes.POINTER(i32), vp],
+            "hmoe_quantize_int8": [vp, sz, vp, vp, vp, vp],
+        }
+        for name, args in sigs.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = ctypes.c_int
+        L.hmoe_set_stage_events.argtypes = [ctypes.POINTER(ctypes.c_void_p), i32]
+        L.hmoe_set_stage_events.restype = ctypes.c_int
+        L.hmoe_launch_count.argtypes = []
+        L.hmoe_launch_count.restype = ctypes.c_int64
+        L.hmoe_synth_normal.argtypes = [u64, u64, f32, vp, sz, ctypes.c_int]
+        L.hmoe_synth_normal.restype = None
+        L.hmoe_synth_zipf_bias.argtypes = [u64, f32, vp, sz]
+        L.hmoe_synth_zipf_bias.restype = None
+        L.hmoe_synth_arena.argtypes = [u64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                       ctypes.c_uint32, ctypes.c_uint32, f32, vp, u64, u64, u64, u64,
+                                       vp, ctypes.c_int]
+        L.hmoe_synth_arena.restype = None
+        _lib = L
+    return _lib
+
+
+def check(fn: str, code: int) -> None:
+    if code != OK:
+        detail = lib().hmoe_last_error().decode(errors="replace") if code == 3 else ""
+        raise HmoeError(fn, code, detail)
+
+
+def _ptr(a) -> int:
+    """Data pointer of a numpy array or torch tensor (0 for None)."""
+    if a is None:
+        return 0
+    if isinstance(a, np.ndarray):
+        return a.ctypes.data
+    return a.data_ptr()
+
+
+def _stream(stream) -> int:
+    if stream is None:
+        import torch
+        return torch.cuda.current_stream().cuda_stream
+    return stream if isinstance(stream, int) else stream.cuda_stream
+
+
+# ---------------------------------------------------------------- synth
+
+def synth_normal(seed: int, stream: int, sigma: float, shape, threads: int = 0) -> np.ndarray:
+    n = int(np.prod(shape))
+    out = np.empty(n, dtype=np.float32)
+    lib().hmoe_synth_normal(seed, stream, sigma, out.ctypes.data, n, threads or os.cpu_count() or 1)
+    return out.reshape(shape)
+
+
+def synth_zipf_bias(seed: int, alpha: float, E: int) -> np.ndarray:
+    out = np.empty(E, dtype=np.float32)
+    lib().hmoe_synth_zipf_bias(seed, alpha, out.ctypes.data, E)
+    return out
+
+
+def quantize_int8(w: np.ndarray):
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    q = np.empty(w.shape, dtype=np.int8)
+    scale = ctypes.c_float()
+    zp = ctypes.c_int32()
+    err = ctypes.c_float()
+    check("hmoe_quantize_int8", lib().hmoe_quantize_int8(
+        w.ctypes.data, w.size, q.ctypes.data, ctypes.byref(scale), ctypes.byref(zp), ctypes.byref(err)))
+    return q, scale.value, zp.value, err.value
+
+
+# ---------------------------------------------------------------- layers
+
+@dataclass
+class LayerConfig:
+    hidden: int
+    intermediate: int
+    experts: int
+    top_k: int
+    softmax: bool = True
+    renormalize: bool = True
+    shared_experts: int = 0
+    zipf_alpha: Optional[float] = None  # None: no router bias
+    sigma: float = 0.02
+
+    @property
+    def proj_bytes(self) -> int:
+        return self.hidden * self.intermediate
+
+    @property
+    def expert_stride(self) -> int:
+        # ExpertPacker: blob = gate|up|down, blob start aligned to 4096.
+        return (3 * self.proj_bytes + 4095) // 4096 * 4096
+
+
+# BASELINE.json configurations (the MoE layer of each).
+CONFIGS = {
+    "c1": LayerConfig(256, 512, 8, 2, True, True, 0, None),
+    "c2": LayerConfig(2048, 1408, 60, 4, True, False, 4, None),
+    "c3": LayerConfig(2048, 768, 128, 8, True, True, 0, 1.1),
+    "c5": LayerConfig(4096, 1536, 128, 8, True, True, 0, 1.1),
+}
+
+
+@dataclass
+class HostLayer:
+    """Seeded synthetic layer in host memory (numpy)."""
+    cfg: LayerConfig
+    router_w: np.ndarray        # [H, E] f32
+    router_bias: Optional[np.ndarray]
+    arena: np.ndarray           # int8 [(E+S) * stride]
+    quant: np.ndarray           # ExpertQuant-compatible structured bytes
+    scales: np.ndarray          # [(E+S), 3] f32
+    zps: np.ndarray             # [(E+S), 3] i32
+
+
+def make_host_layer(cfg: LayerConfig, seed: int = 0, layer: int = 0, threads: int = 0) -> HostLayer:
+    threads = threads or os.cpu_count() or 1
+    H, I, E, S = cfg.hidden, cfg.intermediate, cfg.experts, cfg.shared_experts
+    router_w = synth_normal(seed, 2 + (layer << 8), cfg.sigma, (H, E), threads)
+    bias = synth_zipf_bias(seed + layer, cfg.zipf_alpha, E) if cfg.zipf_alpha else None
+    total = E + S
+    stride = cfg.expert_stride
+    arena = np.zeros(total * stride, dtype=np.int8)
+    quant = (ExpertQuant * total)()
+    lib().hmoe_synth_arena(seed, layer, 0, total, H, I, cfg.sigma, arena.ctypes.data, stride,
+                           0, cfg.proj_bytes, 2 * cfg.proj_bytes, ctypes.addressof(quant), threads)
+    qbytes = np.frombuffer(bytes(quant), dtype=np.uint8).copy()
+    scales = np.array([[quant[e].scale[p] for p in range(3)] for e in range(total)], dtype=np.float32)
+    zps = np.array([[quant[e].zero_point[p] for p in range(3)] for e in range(total)], dtype=np.int32)
+    return HostLayer(cfg, router_w, bias, arena, qbytes, scales, zps)
+
+
+def make_tokens(cfg: LayerConfig, T: int, seed: int = 0, threads: int = 0) -> np.ndarray:
+    return synth_normal(seed, 1, 1.0, (T, cfg.hidden), threads)
+
+
+class DeviceLayer:
+    """A HostLayer resident on the current CUDA device, plus its descriptor."""
+
+    def __init__(self, host: HostLayer, device="cuda"):
+        import torch
+        cfg = host.cfg
+        self.host = host
+        self.cfg = cfg
+        self.router_w = torch.from_numpy(host.router_w).to(device)
+        self.router_bias = torch.from_numpy(host.router_bias).to(device) if host.router_bias is not None else None
+        self.arena = torch.from_numpy(host.arena).to(device)
+        self.quant = torch.from_numpy(host.quant).to(device)
+        d = LayerDesc()
+        d.hidden, d.intermediate, d.experts, d.top_k = cfg.hidden, cfg.intermediate, cfg.experts, cfg.top_k
+        d.softmax, d.renormalize = int(cfg.softmax), int(cfg.renormalize)
+        d.shared_experts = cfg.shared_experts
+        d.router_weight = self.router_w.data_ptr()
+        d.router_bias = self.router_bias.data_ptr() if self.router_bias is not None else None
+        d.arena = self.arena.data_ptr()
+        d.expert_stride = cfg.expert_stride
+        d.gate_offset, d.up_offset, d.down_offset = 0, cfg.proj_bytes, 2 * cfg.proj_bytes
+        d.quant = self.quant.data_ptr()
+        d.ep_rank, d.ep_size = 0, 1
+        self.desc = d
+        self._ws = None
+
+    def workspace_bytes(self, T: int, host_io: bool = False) -> int:
+        n = ctypes.c_size_t()
+        check("hmoe_workspace_size", lib().hmoe_workspace_size(
+            ctypes.byref(self.desc), T | (HOST_IO if host_io else 0), ctypes.byref(n)))
+        return n.value
+
+    def workspace(self, T: int, host_io: bool = False):
+        import torch
+        need = self.workspace_bytes(T, host_io)
+        if self._ws is None or self._ws.numel() < need:
+            self._ws = torch.empty(need, dtype=torch.uint8, device=self.arena.device)
+        return self._ws
+
+    def forward(self, x, y=None, stream=None):
+        import torch
+        T = x.shape[0]
+        if y is None:
+            y = torch.empty((T, self.cfg.hidden), dtype=torch.float32, device=x.device)
+        ws = self.workspace(T)
+        check("hmoe_moe_forward", lib().hmoe_moe_forward(
+            ctypes.byref(self.desc), x.data_ptr(), y.data_ptr(), T, ws.data_ptr(), ws.numel(), _stream(stream)))
+        return y
+
+    def forward_host(self, x_host, y_host, stream=None):
+        """x_host/y_host: page-locked CPU tensors [T, H] FP32."""
+        T = x_host.shape[0]
+        ws = self.workspace(T, host_io=True)
+        check("hmoe_moe_forward_host", lib().hmoe_moe_forward_host(
+            ctypes.byref(self.desc), x_host.data_ptr(), y_host.data_ptr(), T, ws.data_ptr(), ws.numel(),
+            _stream(stream)))
+        return y_host
+
+    def route(self, x, stream=None):
+        import torch
+        T, k, E = x.shape[0], self.cfg.top_k, self.cfg.experts
+        dev = x.device
+        ids = torch.empty((T, k), dtype=torch.int32, device=dev)
+        scores = torch.empty((T, k), dtype=torch.float32, device=dev)
+        offsets = torch.empty(E + 1, dtype=torch.int32, device=dev)
+        gtok = torch.empty(T * k, dtype=torch.int32, device=dev)
+        gsc = torch.empty(T * k, dtype=torch.float32, device=dev)
+        ws = self.workspace(T)
+        check("hmoe_route", lib().hmoe_route(
+            ctypes.byref(self.desc), x.data_ptr(), T, ids.data_ptr(), scores.data_ptr(), offsets.data_ptr(),
+            gtok.data_ptr(), gsc.data_ptr(), ws.data_ptr(), ws.numel(), _stream(stream)))
+        return ids, scores, offsets, gtok, gsc
+
+    def read_status(self, stream=None):
+        st, ties, seq = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        check("hmoe_read_status", lib().hmoe_read_status(
+            self._ws.data_ptr(), ctypes.byref(st), ctypes.byref(ties), ctypes.byref(seq), _stream(stream)))
+        return st.value, ties.value, seq.value
+
+
+def set_variant(v: int) -> None:
+    check("hmoe_set_variant", lib().hmoe_set_variant(v))

@@ -1,0 +1,264 @@
+/*
+ * hmoe.h -- C ABI of the B200 (sm_100a) HyperMoE sparse-expert hot path.
+ *
+ * Library: hypermoe-engine_b200/lib/libhmoe.so.  Plain pointers and sizes
+ * only; every device pointer is CUDA global memory on the current device and
+ * every `stream` is a cudaStream_t passed as void* (the reference's
+ * StreamHandle, src/backend/Backend.hpp:12).  All launches are
+ * stream-ordered and return before completion; no entry point allocates,
+ * frees or synchronises unless its comment says so.  Errors are returned as
+ * hmoe_status; nothing throws across this boundary.
+ *
+ * Two groups of entry points:
+ *
+ *  1. Per-operator drop-ins for the reference's CUDA kernel launchers
+ *     hypermoe::backend::cuda::kernels::* (src/backend/cuda/CudaKernels.hpp:
+ *     10-46) and planInt8Gemm (src/backend/cuda/Int8GemmPlan.hpp:19-20).
+ *     Same arguments, same meaning, FP32 results within the reference's own
+ *     CUDA-vs-CPU tolerance (1e-5 + 1e-5*|ref|).  The C++ shim in
+ *     hypermoe-engine_b200/host/CudaKernelsShim.cpp defines the reference's
+ *     C++ symbols over these.
+ *
+ *  2. The fused layer path that replaces the per-expert host loop of
+ *     MoERuntime::executeBatch (src/core/runtime/MoERuntime.cpp:58-349) when
+ *     every expert of the layer is resident: route -> permute -> grouped
+ *     INT8 expert MLP (dequantised to BF16 for tensor cores, FP32
+ *     accumulation, SwiGLU fused) -> deterministic weighted combine.
+ */
+#ifndef HMOE_H
+#define HMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+    HMOE_OK = 0,
+    HMOE_INVALID_ARGUMENT = 1,  /* std::invalid_argument in the reference */
+    HMOE_NON_FINITE_ROUTER = 2, /* "router produced a non-finite score" */
+    HMOE_CUDA_ERROR = 3,        /* launch/runtime error (checkLaunch) */
+    HMOE_NCCL_ERROR = 4,
+    HMOE_TIMEOUT = 5,
+    HMOE_WORKSPACE_TOO_SMALL = 6,
+    HMOE_UNSUPPORTED = 7
+} hmoe_status;
+
+/* Last CUDA error string seen by this thread (checkLaunch's message). */
+const char *hmoe_last_error(void);
+
+/* ------------------------------------------------ 1. per-operator drop-ins */
+
+/* kernels::activation (CudaKernels.hpp:10-11): type 0 = SiLU, 1 = GELU(erf). */
+hmoe_status hmoe_activation(int type, const float *input, float *output,
+                            size_t elements, void *stream);
+
+/* kernels::int8WeightMatmul (CudaKernels.hpp:12-15):
+ * output[r,c] = sum_k left[r,k] * (float(right[k,c] - zero_point) * scale),
+ * left [rows,inner] FP32, right [inner,columns] INT8 row-major. */
+hmoe_status hmoe_int8_weight_matmul(const float *left, const int8_t *right,
+                                    float *output, size_t rows, size_t inner,
+                                    size_t columns, float scale,
+                                    int32_t zero_point, void *stream);
+
+/* kernels::int8WeightMatmulCooperative (CudaKernels.hpp:16-21).  Validates
+ * `partitions` against hmoe_int8_gemm_plan(..., COOPERATIVE) exactly as the
+ * reference does (CudaKernels.cu:330-333) and returns
+ * HMOE_INVALID_ARGUMENT on a mismatch or a missing `partials` buffer. */
+hmoe_status hmoe_int8_weight_matmul_cooperative(
+    const float *left, const int8_t *right, float *output, float *partials,
+    size_t rows, size_t inner, size_t columns, size_t partitions, float scale,
+    int32_t zero_point, void *stream);
+
+/* planInt8Gemm (Int8GemmPlan.hpp:8-20, Int8GemmPlan.cpp:29-53). */
+typedef enum {
+    HMOE_INT8_GEMM_AUTO = 0,
+    HMOE_INT8_GEMM_REFERENCE = 1,
+    HMOE_INT8_GEMM_COOPERATIVE = 2
+} hmoe_int8_gemm_mode;
+
+typedef struct {
+    int32_t implementation; /* hmoe_int8_gemm_mode, never AUTO */
+    size_t partitions;
+    size_t blocks;
+    size_t scratch_elements;
+} hmoe_int8_gemm_plan_t;
+
+hmoe_status hmoe_int8_gemm_plan(size_t rows, size_t inner, size_t columns,
+                                int32_t mode, hmoe_int8_gemm_plan_t *plan);
+
+/* kernels::routerTopK (CudaKernels.hpp:28-31).  `logits` [tokens,experts]
+ * is overwritten with probabilities when softmax != 0, as the reference
+ * kernel does.  Selection is (score desc, id asc); renormalisation uses a
+ * double sum; a non-finite or zero selected sum writes NaN to the token's
+ * first score (CudaKernels.cu:195-203). */
+hmoe_status hmoe_router_topk(float *logits, size_t tokens, size_t experts,
+                             size_t top_k, int softmax, int renormalize,
+                             uint32_t *selected_ids, float *selected_scores,
+                             void *stream);
+
+/* kernels::gatherRows (CudaKernels.hpp:40-41): output[r,:] = input[rows[r],:]. */
+hmoe_status hmoe_gather_rows(const float *input, float *output,
+                             const uint32_t *rows, size_t row_count,
+                             size_t width, void *stream);
+
+/* kernels::scatterAddRows (CudaKernels.hpp:42-45):
+ * output[rows[r],:] += input[r,:] * weights[r] (atomic, like the reference). */
+hmoe_status hmoe_scatter_add_rows(const float *input, float *output,
+                                  const uint32_t *rows, const float *weights,
+                                  size_t row_count, size_t width,
+                                  void *stream);
+
+/* kernels::zero (CudaKernels.hpp:46). */
+hmoe_status hmoe_zero(float *output, size_t elements, void *stream);
+
+/* ------------------------------------------------------- 2. fused layer */
+
+/* Quantisation parameters of one expert: gate, up, down
+ * (ExpertMlpWeights, src/experts/ExpertExecutor.hpp:18-43; each
+ * QuantizationParameters{scale, zeroPoint}, Quantization.hpp:19-25). */
+typedef struct {
+    float scale[3];
+    int32_t zero_point[3];
+} hmoe_expert_quant;
+
+/* One MoE layer, all experts resident on this device.
+ *
+ * Expert weights: one INT8 arena in the ExpertPacker layout
+ * (tools/model_convert/ExpertPacker.cpp:150-247): expert e's blob starts at
+ * arena + e*expert_stride and holds gate [H,I], up [H,I], down [I,H], each
+ * row-major [in,out] (INPUT_OUTPUT), at gate_offset/up_offset/down_offset
+ * inside the blob.  ExpertWeightMap::createViews (ExpertWeightMap.cpp:
+ * 65-108) slices exactly these views.  expert_stride and the offsets must
+ * be multiples of 16 bytes and H, I multiples of 64.
+ *
+ * Routed experts are ids [0, experts); `shared_experts` always-on experts
+ * follow them in the arena (ids experts..experts+shared-1), see every token
+ * with weight 1.0, and are combined after the routed ones.
+ *
+ * `router_bias` (NULL for none) is added to each logit as the last term of
+ * the double accumulation (what the reference computes for a hidden row
+ * extended by 1 and a router matrix extended by the bias row).
+ *
+ * ep_rank/ep_size: expert parallelism (1 process per GPU).  With
+ * ep_size > 1 this rank owns routed experts
+ * [ep_rank*experts/ep_size, (ep_rank+1)*experts/ep_size) and `arena`,
+ * `quant` cover only those (plus the shared experts); see
+ * hmoe_ep_moe_forward. */
+typedef struct {
+    uint32_t hidden;          /* H */
+    uint32_t intermediate;    /* I */
+    uint32_t experts;         /* E, routed */
+    uint32_t top_k;           /* k */
+    int32_t softmax;          /* RoutingNormalization::Softmax */
+    int32_t renormalize;      /* RouterConfig::renormalizeSelected */
+    uint32_t shared_experts;  /* always-on experts after the routed ones */
+    uint32_t reserved0;
+    const float *router_weight; /* device [H, E] FP32 row-major */
+    const float *router_bias;   /* device [E] FP32 or NULL */
+    const int8_t *arena;        /* device, see above */
+    uint64_t expert_stride;
+    uint64_t gate_offset, up_offset, down_offset;
+    const hmoe_expert_quant *quant; /* device [experts + shared_experts] */
+    int32_t ep_rank, ep_size;
+} hmoe_layer_desc;
+
+/* Scratch bytes hmoe_route / hmoe_moe_forward need for up to max_tokens
+ * (OR max_tokens with HMOE_WORKSPACE_HOST_IO to include the staging area of
+ * hmoe_moe_forward_host). */
+#define HMOE_WORKSPACE_HOST_IO ((size_t)1 << 62)
+hmoe_status hmoe_workspace_size(const hmoe_layer_desc *desc,
+                                size_t max_tokens, size_t *bytes);
+
+/* Router + device-built expert grouping (CudaTensorBackend::routeTopK,
+ * CudaTensorBackend.cpp:601-652, plus the grouping of
+ * CpuRouterBackend::routeBatch, CpuRouterBackend.cpp:140-158), in one
+ * stream-ordered call with no host readback.
+ *   ids/scores [T,k]  rank order (score desc, id asc), bit-exact selection
+ *                     against the CPU router on the same inputs;
+ *   offsets [E+1]     exclusive prefix of tokens per routed expert;
+ *   group_tokens [T*k], group_scores [T*k]: expert groups, ascending expert,
+ *                     tokens ascending inside a group.
+ * Any output pointer may be NULL. */
+hmoe_status hmoe_route(const hmoe_layer_desc *desc, const float *x,
+                       size_t tokens, uint32_t *ids, float *scores,
+                       int32_t *offsets, uint32_t *group_tokens,
+                       float *group_scores, void *workspace,
+                       size_t workspace_bytes, void *stream);
+
+/* One MoE layer forward: y[T,H] FP32 = sum over the token's experts, in
+ * ascending expert id, of routing_weight * expert_mlp(x).  x [T,H] FP32. */
+hmoe_status hmoe_moe_forward(const hmoe_layer_desc *desc, const float *x,
+                             float *y, size_t tokens, void *workspace,
+                             size_t workspace_bytes, void *stream);
+
+/* hmoe_moe_forward for callers holding HOST buffers (the reference's CPU
+ * backend callers): copies x_host [T,H] into the workspace, runs the layer
+ * and copies y back to y_host, all on `stream` (page-locked host memory
+ * makes the copies asynchronous).  Returns after enqueueing; y_host is
+ * valid once the stream has completed.  Needs hmoe_workspace_size(...,
+ * HMOE_WORKSPACE_HOST_IO) bytes. */
+hmoe_status hmoe_moe_forward_host(const hmoe_layer_desc *desc,
+                                  const float *x_host, float *y_host,
+                                  size_t tokens, void *workspace,
+                                  size_t workspace_bytes, void *stream);
+
+/* Forces the expert-MLP variant for measurement: 0 = automatic (GEMV for
+ * experts with few tokens, tensor-core GEMM otherwise), 1 = GEMV only,
+ * 2 = tensor-core GEMM only.  Process-wide. */
+hmoe_status hmoe_set_variant(int32_t variant);
+
+/* Measurement hooks.  hmoe_set_stage_events registers `count` (= 6)
+ * cudaEvent_t handles (passed as void*) that every later hmoe_moe_forward
+ * records on its stream at the stage boundaries: [0] start, [1] after the
+ * router, [2] after the grouping, [3] after gate/up, [4] after down,
+ * [5] after the combine.  count = 0 unregisters them.  Process-wide, for
+ * benchmarks; the events are the caller's. */
+hmoe_status hmoe_set_stage_events(void *const *events, int32_t count);
+
+/* Number of kernels this library has launched in the process so far. */
+int64_t hmoe_launch_count(void);
+
+/* Synchronises `stream` and reads the device status word the last call on
+ * `workspace` left: status (hmoe_status), the number of router near-ties the
+ * device could not certify against the CPU's expf rounding, and the number
+ * of logits it recomputed in sequential order.  Resets the word. */
+hmoe_status hmoe_read_status(void *workspace, int32_t *status,
+                             int32_t *near_ties, int32_t *sequential_logits,
+                             void *stream);
+
+/* ----------------------------------------- host-side synthetic inputs */
+
+/* Seeded counter-based normal generator (SplitMix64 + Box-Muller in double),
+ * identical on every host: out[i] = sigma * N(0,1) for stream `stream`. */
+void hmoe_synth_normal(uint64_t seed, uint64_t stream, float sigma, float *out,
+                       size_t n, int threads);
+
+/* Zipf(alpha) per-expert logit bias: bias[e] = -alpha*ln(pi(e)+1) for a
+ * seeded permutation pi of [0, E). */
+void hmoe_synth_zipf_bias(uint64_t seed, float alpha, float *bias, size_t E);
+
+/* Symmetric per-tensor INT8 quantiser (quantizeInt8,
+ * src/tensor/quantization/Quantization.cpp:45-79). */
+hmoe_status hmoe_quantize_int8(const float *w, size_t n, int8_t *q,
+                               float *scale, int32_t *zero_point,
+                               float *max_abs_error);
+
+/* Fills a host INT8 arena (layout as in hmoe_layer_desc) for `count`
+ * experts starting at expert id `first`: gate/up/down ~ N(0, sigma^2) from
+ * streams derived from (layer, expert, projection), each quantised per
+ * projection.  quant[count] receives the parameters. */
+void hmoe_synth_arena(uint64_t seed, uint32_t layer, uint32_t first,
+                      uint32_t count, uint32_t H, uint32_t I, float sigma,
+                      int8_t *arena, uint64_t expert_stride,
+                      uint64_t gate_offset, uint64_t up_offset,
+                      uint64_t down_offset, hmoe_expert_quant *quant,
+                      int threads);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* HMOE_H */

@@ -1,0 +1,214 @@
+"""ctypes access to the two CPU checkers (TEST INFRASTRUCTURE ONLY).
+
+  port()  -> oracle/_build/libhmoe_oracle.so, the C restatement
+             (oracle/hmoe_oracle.c) of the reference CPU hot path;
+  ref()   -> oracle/_ref/libhmoe_ref.so, the reference's own CPU classes
+             compiled from its sources (oracle/Makefile, oracle/ref_harness.cpp).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg use
+this module; the product path never imports it.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+PORT_PATH = os.path.join(HERE, "_build", "libhmoe_oracle.so")
+REF_PATH = os.path.join(HERE, "_ref", "libhmoe_ref.so")
+
+_port = None
+_ref = None
+
+vp, sz, i32, f32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int32, ctypes.c_float
+
+
+def build(reference: bool = True) -> None:
+    """Builds the port (always) and the reference library (when its sources exist)."""
+    targets = ["oracle"]
+    if reference and os.path.isdir(os.environ.get("HMOE_REFERENCE", "/root/reference")):
+        targets.append("ref")
+    env = dict(os.environ)
+    if "HMOE_REFERENCE" in os.environ:
+        env["REF"] = os.environ["HMOE_REFERENCE"]
+    subprocess.run(["make", "-C", HERE, "-j8", *targets], check=True, env=env,
+                   stdout=subprocess.DEVNULL)
+
+
+def _p(a):
+    return 0 if a is None else a.ctypes.data
+
+
+def port() -> ctypes.CDLL:
+    global _port
+    if _port is None:
+        if not os.path.exists(PORT_PATH):
+            build(reference=False)
+        L = ctypes.CDLL(PORT_PATH)
+        L.hmo_route_batch.argtypes = [vp, vp, vp, sz, sz, sz, sz, ctypes.c_int, ctypes.c_int,
+                                      vp, vp, vp, vp, vp, vp]
+        L.hmo_int8_matmul.argtypes = [vp, vp, vp, sz, sz, sz, f32, i32]
+        L.hmo_int8_matmul.restype = None
+        L.hmo_expert_mlp.argtypes = [vp, sz, sz, sz, vp, vp, vp, vp, vp, vp]
+        L.hmo_expert_mlp.restype = None
+        L.hmo_moe_layer.argtypes = [vp, sz, sz, sz, sz, sz, ctypes.c_int, ctypes.c_int, vp, vp, sz,
+                                    vp, sz, sz, sz, sz, vp, vp, vp, vp, vp, vp]
+        L.hmo_quantize_int8.argtypes = [vp, sz, vp, vp, vp, vp]
+        L.hmo_silu.argtypes = [f32]
+        L.hmo_silu.restype = f32
+        _port = L
+    return _port
+
+
+def ref() -> ctypes.CDLL:
+    global _ref
+    if _ref is None:
+        if not os.path.exists(REF_PATH):
+            raise FileNotFoundError(f"{REF_PATH} is not built (needs the reference sources)")
+        L = ctypes.CDLL(REF_PATH)
+        L.hmr_route_batch.argtypes = [vp, vp, vp, sz, sz, sz, sz, ctypes.c_int, ctypes.c_int,
+                                      vp, vp, vp, vp, vp]
+        L.hmr_int8_matmul.argtypes = [vp, vp, vp, sz, sz, sz, f32, i32]
+        L.hmr_expert_mlp.argtypes = [vp, sz, sz, sz, vp, vp, vp, vp, vp, vp]
+        L.hmr_quantize_int8.argtypes = [vp, sz, vp, vp, vp, vp]
+        L.hmr_layer_create.argtypes = [sz, sz, sz, sz, ctypes.c_int, ctypes.c_int, vp, vp, sz, vp, sz,
+                                       sz, sz, sz, vp, vp]
+        L.hmr_layer_create.restype = vp
+        L.hmr_layer_destroy.argtypes = [vp]
+        L.hmr_layer_destroy.restype = None
+        L.hmr_layer_forward.argtypes = [vp, vp, sz, vp, vp, vp, vp, ctypes.c_int]
+        _ref = L
+    return _ref
+
+
+def ref_available() -> bool:
+    return os.path.exists(REF_PATH)
+
+
+class OracleError(RuntimeError):
+    pass
+
+
+# ------------------------------------------------------------- wrappers
+
+def route(lib, x, w, bias, k, softmax=True, renorm=True):
+    """(ids [T,k] u32, scores [T,k] f32, offsets [E+1], group_tokens, group_scores)."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    T, H = x.shape
+    E = w.shape[1]
+    ids = np.zeros((T, k), np.uint32)
+    sc = np.zeros((T, k), np.float32)
+    off = np.zeros(E + 1, np.int32)
+    gt = np.zeros(T * k, np.uint32)
+    gs = np.zeros(T * k, np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, np.float32)
+    if lib is port():
+        st = lib.hmo_route_batch(_p(x), _p(w), _p(b), T, H, E, k, int(softmax), int(renorm),
+                                 _p(ids), _p(sc), _p(off), _p(gt), _p(gs), None)
+    else:
+        st = lib.hmr_route_batch(_p(x), _p(w), _p(b), T, H, E, k, int(softmax), int(renorm),
+                                 _p(ids), _p(sc), _p(off), _p(gt), _p(gs))
+    if st != 0:
+        raise OracleError(f"route failed with status {st}")
+    return ids, sc, off, gt, gs
+
+
+def int8_matmul(lib, left, q, scale, zp):
+    left = np.ascontiguousarray(left, np.float32)
+    q = np.ascontiguousarray(q, np.int8)
+    rows, K = left.shape
+    N = q.shape[1]
+    out = np.zeros((rows, N), np.float32)
+    if lib is port():
+        lib.hmo_int8_matmul(_p(left), _p(q), _p(out), rows, K, N, scale, zp)
+    else:
+        st = lib.hmr_int8_matmul(_p(left), _p(q), _p(out), rows, K, N, scale, zp)
+        if st != 0:
+            raise OracleError(f"int8 matmul failed with status {st}")
+    return out
+
+
+def expert_mlp(lib, x, gate, up, down, scales, zps):
+    x = np.ascontiguousarray(x, np.float32)
+    rows, H = x.shape
+    I = gate.shape[1]
+    y = np.zeros((rows, H), np.float32)
+    s = np.ascontiguousarray(scales, np.float32)
+    z = np.ascontiguousarray(zps, np.int32)
+    args = (_p(x), rows, H, I, _p(np.ascontiguousarray(gate)), _p(np.ascontiguousarray(up)),
+            _p(np.ascontiguousarray(down)), _p(s), _p(z), _p(y))
+    if lib is port():
+        lib.hmo_expert_mlp(*args)
+    else:
+        st = lib.hmr_expert_mlp(*args)
+        if st != 0:
+            raise OracleError(f"expert mlp failed with status {st}")
+    return y
+
+
+def quantize(lib, w):
+    w = np.ascontiguousarray(w, np.float32)
+    q = np.zeros(w.shape, np.int8)
+    s, z, e = ctypes.c_float(), ctypes.c_int32(), ctypes.c_float()
+    fn = lib.hmo_quantize_int8 if lib is port() else lib.hmr_quantize_int8
+    st = fn(_p(w), w.size, _p(q), ctypes.byref(s), ctypes.byref(z), ctypes.byref(e))
+    if st != 0:
+        raise OracleError(f"quantize failed with status {st}")
+    return q, s.value, z.value, e.value
+
+
+def moe_layer_port(host_layer, x):
+    """Full layer through the C port: (out [T,H], ids, scores, offsets)."""
+    L = port()
+    c = host_layer.cfg
+    x = np.ascontiguousarray(x, np.float32)
+    T = x.shape[0]
+    out = np.zeros((T, c.hidden), np.float32)
+    ids = np.zeros((T, c.top_k), np.uint32)
+    sc = np.zeros((T, c.top_k), np.float32)
+    off = np.zeros(c.experts + 1, np.int32)
+    st = L.hmo_moe_layer(_p(x), T, c.hidden, c.intermediate, c.experts, c.top_k, int(c.softmax),
+                         int(c.renormalize), _p(host_layer.router_w), _p(host_layer.router_bias),
+                         c.shared_experts, _p(host_layer.arena), c.expert_stride, 0, c.proj_bytes,
+                         2 * c.proj_bytes, _p(host_layer.scales), _p(host_layer.zps), _p(out), _p(ids),
+                         _p(sc), _p(off))
+    if st != 0:
+        raise OracleError(f"moe layer failed with status {st}")
+    return out, ids, sc, off
+
+
+class RefLayer:
+    """A resident layer inside the reference's own CPU classes."""
+
+    def __init__(self, host_layer):
+        c = host_layer.cfg
+        self.cfg = c
+        self._keep = host_layer
+        self.handle = ref().hmr_layer_create(
+            c.hidden, c.intermediate, c.experts, c.top_k, int(c.softmax), int(c.renormalize),
+            _p(host_layer.router_w), _p(host_layer.router_bias), c.shared_experts, _p(host_layer.arena),
+            c.expert_stride, 0, c.proj_bytes, 2 * c.proj_bytes, _p(host_layer.scales), _p(host_layer.zps))
+        if not self.handle:
+            raise OracleError("hmr_layer_create failed")
+
+    def forward(self, x, threads=1, want_routing=False):
+        c = self.cfg
+        x = np.ascontiguousarray(x, np.float32)
+        T = x.shape[0]
+        out = np.zeros((T, c.hidden), np.float32)
+        ids = np.zeros((T, c.top_k), np.uint32) if want_routing else None
+        sc = np.zeros((T, c.top_k), np.float32) if want_routing else None
+        off = np.zeros(c.experts + 1, np.int32) if want_routing else None
+        st = ref().hmr_layer_forward(self.handle, _p(x), T, _p(out), _p(ids), _p(sc), _p(off), threads)
+        if st != 0:
+            raise OracleError(f"hmr_layer_forward failed with status {st}")
+        return (out, ids, sc, off) if want_routing else out
+
+    def __del__(self):
+        if getattr(self, "handle", None):
+            ref().hmr_layer_destroy(self.handle)
+            self.handle = None
