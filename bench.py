@@ -220,6 +220,9 @@ def main():
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    for e in ev:  # torch creates the CUDA event on first record
+        e.record(stream)
+    torch.cuda.synchronize()
     import ctypes
     arr = (ctypes.c_void_p * 6)(*[e.cuda_event for e in ev])
 

@@ -84,7 +84,9 @@ hmoe_status validate_desc(const hmoe_layer_desc* d) {
     if (d->hidden % 64 || d->intermediate % 64) return HMOE_UNSUPPORTED;
     if (d->expert_stride % 16 || d->gate_offset % 16 || d->up_offset % 16 || d->down_offset % 16)
         return HMOE_INVALID_ARGUMENT;
-    if (d->experts > 256 || d->top_k > 32 || d->shared_experts > 64) return HMOE_UNSUPPORTED;
+    if (d->experts > 256 || d->top_k > 32 || d->shared_experts > 64 ||
+        d->top_k + d->shared_experts > static_cast<uint32_t>(kMaxSlots))
+        return HMOE_UNSUPPORTED;
     if (d->ep_size != 1 || d->ep_rank != 0) return HMOE_UNSUPPORTED; // see hmoe_ep_*
     return HMOE_OK;
 }
@@ -97,7 +99,7 @@ hmoe_status validate_desc(const hmoe_layer_desc* d) {
 __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ yrows,
                                                       const int32_t* __restrict__ inv, int slots,
                                                       int H, float* __restrict__ out) {
-    __shared__ int rows_s[64];
+    __shared__ int rows_s[kMaxSlots];
     const int t = blockIdx.x;
     if (threadIdx.x == 0) {
         int n = 0;

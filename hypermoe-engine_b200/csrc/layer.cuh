@@ -18,6 +18,9 @@ Workspace plan_workspace(const hmoe_layer_desc& d, size_t T, int local_experts);
 // GEMV; larger groups use the tcgen05 grouped GEMM.
 constexpr int kDefaultSmallMax = 16;
 
+// Upper bound of a token's rows (top_k routed + shared experts).
+constexpr int kMaxSlots = 96;
+
 struct GemvArgs {
     const int32_t* list;        // experts to process
     const int32_t* list_size;   // device count

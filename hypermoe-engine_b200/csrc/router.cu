@@ -110,6 +110,15 @@ __device__ void select_token(const float (&lv)[C], int E, int k, int softmax,
             if (j < E) probs_out[j] = p[c];
         }
     }
+    // Selection key: a NaN probability (only possible for a token whose
+    // logits or denominator are not finite, which is flagged above and by
+    // the logit pass) ranks lowest, so every round still picks a valid id.
+#pragma unroll
+    for (int c = 0; c < C; ++c)
+        if (p[c] != p[c]) {
+            p[c] = -FLT_MAX * 2.0f;
+            ok = false;
+        }
     unsigned selected = 0; // bit c: candidate c of this lane taken
     double rsum = 0.0;
     float prev_p = 0.0f, prev_l = 0.0f;
@@ -146,6 +155,10 @@ __device__ void select_token(const float (&lv)[C], int E, int k, int softmax,
         prev_p = bp;
         prev_l = bl;
         if (r == k) break;
+        if (bi >= E) { // unreachable: E - r > 0 candidates remain
+            bi = 0;
+            ok = false;
+        }
         if ((bi & 31) == lane) selected |= 1u << (bi >> 5);
         chosen[r] = bp;
         rsum += static_cast<double>(bp);
