@@ -71,6 +71,9 @@ Workspace plan_workspace(const hmoe_layer_desc& d, size_t T, int local_experts) 
     w.hmid = take(R * static_cast<size_t>(d.intermediate) * 4);
     w.yrows = take(R * static_cast<size_t>(d.hidden) * 4);
     w.xperm = take(R * static_cast<size_t>(d.hidden) * 2);
+    w.hmid16 = take(R * static_cast<size_t>(d.intermediate) * 2);
+    w.tile_count = take(16);
+    w.tiles = take((R / 128 + E + S + 2) * 16);
     w.total = off;
     (void)local_experts;
     return w;

@@ -9,6 +9,7 @@ namespace hmoe {
 struct Workspace {
     size_t status, counts, zero_bytes, offsets, list_sizes, small_list, large_list;
     size_t ids, scores, perm_token, perm_weight, inv, hmid, yrows, xperm;
+    size_t hmid16, tiles, tile_count;
     size_t total;
 };
 

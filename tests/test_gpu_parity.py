@@ -237,8 +237,8 @@ def test_layer_matches_reference_fixture(cuda, golden, name, cfg, T, seed):
     assert dl.read_status()[0] == 0
 
 
-@pytest.mark.parametrize("variant", [0, 1])
-@pytest.mark.parametrize("T", [1, 33, 256])
+@pytest.mark.parametrize("variant", [0, 1, 2])
+@pytest.mark.parametrize("T", [1, 33, 256, 4096])
 def test_layer_c3_against_port(cuda, T, variant):
     cfg = H.CONFIGS["c3"]
     hl = H.make_host_layer(cfg, seed=5)
@@ -253,6 +253,22 @@ def test_layer_c3_against_port(cuda, T, variant):
         H.set_variant(0)
     # a token's output depends only on its own routing: compare a subset
     assert_layer_close(y[sub], out_p)
+
+
+@pytest.mark.parametrize("cfg,T", [("c1", 64), ("c2", 40), ("c2", 1)])
+def test_layer_configs_gemm_and_gemv_agree_with_port(cuda, cfg, T):
+    c = H.CONFIGS[cfg]
+    hl = H.make_host_layer(c, seed=9)
+    x = H.make_tokens(c, T, seed=9)
+    out_p, ids_p, _, _ = O.moe_layer_port(hl, x)
+    dl = H.DeviceLayer(hl, cuda)
+    for v in (1, 2, 0):
+        H.set_variant(v)
+        try:
+            y = host(dl.forward(t(x, cuda)))
+        finally:
+            H.set_variant(0)
+        assert_layer_close(y, out_p)
 
 
 def test_layer_is_deterministic(cuda):
