@@ -1,71 +1,91 @@
 // expert_gemm_sm100.cu -- grouped INT8-weight expert GEMM on the 5th-
-// generation tensor cores (tcgen05 + TMEM), for expert groups with many
-// tokens (prefill).
+// generation tensor cores (tcgen05 + TMEM).
 //
-// Replaces, for those groups, the three per-expert INT8 projections of
-// ExpertMlpExecutor::execute (src/experts/ExpertExecutor.cpp:118-131),
-// out[r,c] = sum_k x[r,k] * (float(q[k,c] - zp) * scale)
-// (CpuTensorBackend.cpp:173-186 / CudaKernels.cu:30-107), together with
-// the SiLU, the multiply and the routing weight.
+// Replaces the three per-expert INT8 projections of ExpertMlpExecutor::
+// execute (src/experts/ExpertExecutor.cpp:118-131),
+//     out[r,c] = sum_k x[r,k] * (float(q[k,c] - zp) * scale)
+// (CpuTensorBackend.cpp:173-186; the reference's CUDA kernels
+// CudaKernels.cu:30-107), together with the SiLU, the elementwise multiply
+// and the routing weight, for every expert of the layer in one launch per
+// projection pair.
 //
 // Formulation ("weights as M"): for expert e, output features n and tokens
 // t, D[n, t] = sum_k W[k, n] * X[t, k].  The INT8 weight tile W[k0:k0+64,
-// n0:n0+128] ([in,out] row-major, i.e. the packed layout as stored) is the
-// MN-major A operand; the token tile (BF16 rows, K contiguous) is the
-// K-major B operand; M = 128 features, N = up to 128 tokens, so one tile
-// serves 1..128 tokens of an expert and decode-sized and prefill-sized
-// groups use the same code.
+// n0:n0+128] -- the packed [in,out] layout exactly as stored -- becomes the
+// MN-major BF16 A operand after an exact in-shared-memory dequantisation
+// (q - zp is an integer in [-255, 255]); the expert's token rows (BF16, K
+// contiguous, TMA with 128-byte swizzle) are the K-major B operand.
+// M = 128 features, N = 16..256 tokens, FP32 accumulation in TMEM.
 //
-// Per CTA (192 threads, one output tile):
-//   warp 0     TMA producer: INT8 weight tile(s) (3-D map over the expert
-//              arena) and the BF16 token tile (128-byte swizzle) per
-//              64-deep K block, into a 3/4-stage ring.
-//   warp 1     MMA issuer: one thread issues tcgen05.mma (BF16 x BF16 ->
-//              FP32 in TMEM) and tcgen05.commit to release each stage.
-//   warps 2-5  dequantise: INT8 -> exact BF16 (q - zp, |q - zp| <= 255) into
-//              the swizzled MN-major A layout, fence to the async proxy,
-//              signal the MMA thread; then the epilogue: tcgen05.ld the
-//              accumulators, apply the projection scale, SwiGLU (gate/up,
-//              BF16 out) or the routing weight (down, FP32 out).
-// Every mbarrier wait is bounded in time; on expiry the CTA records
-// HMOE_TIMEOUT in the workspace status word, drains its own TMA loads and
-// MMAs (again bounded), frees its TMEM and exits.
+// Persistent kernel over CTA pairs (thread-block clusters of 2), one CTA per
+// SM.  The pair runs the 2-SM MMA (tcgen05 .cta_group::2, M = 256): each CTA
+// holds half of the A rows and half of the token tile, which halves the
+// shared-memory traffic per MMA FLOP compared with one CTA.  For gate/up a
+// CTA's 128 A rows are 64 gate features and the same 64 up features, so
+// both projections come out of one MMA and SwiGLU stays inside the CTA.
+// Warp roles (15 warps per CTA):
+//   warp 0      TMA producer of INT8 weight tiles (two [64 k][64 n] boxes per
+//               stage, 4-deep staging ring)
+//   warp 1      TMA producer of this CTA's half of the BF16 token tile
+//               (4-deep ring; bytes counted on the leader's barrier)
+//   warp 2      TMEM owner; in the leader CTA one thread issues the pair MMA
+//               and multicasts tcgen05.commit to both CTAs' barriers
+//   warps 3-10  dequantise INT8 -> BF16 into the swizzled A layout and
+//               signal the leader
+//   warps 11-14 epilogue: tcgen05.ld from double-buffered accumulators,
+//               projection scale, SwiGLU (gate/up -> BF16 rows) or routing
+//               weight (down -> FP32 rows), overlapping the next main loop.
+// Work items are (token tile of <= 256 rows of one expert, feature block),
+// longest tiles first, dealt round-robin to the pairs.
+//
 #include "common.cuh"
 #include "layer.cuh"
 #include "sm100.cuh"
 
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <mutex>
 
 namespace hmoe {
 
 namespace {
 
-constexpr int kTileM = 128;   // output features per CTA (MMA M)
-constexpr int kTileT = 128;   // tokens per tile (MMA N <= 128)
+constexpr int kTileT = 256;   // tokens per work item (pair MMA N <= 256)
+constexpr int kHalfT = 128;   // token rows per CTA (B box height)
 constexpr int kBK = 64;       // K per stage (128 bytes of BF16)
-constexpr int kThreadsGemm = 192;
+constexpr int kWStages = 4;   // INT8 staging ring
+constexpr int kAStages = 3;   // BF16 A ring (dequantised weights)
+constexpr int kBStages = 4;   // BF16 token-tile ring
+constexpr int kDequantWarps = 8;
+constexpr int kEpiWarps = 8;                // two groups of 4 (one per column half)
+constexpr int kThreadsGemm = 32 * (3 + kDequantWarps + kEpiWarps);
 constexpr uint64_t kWaitNs = 2000000000ull; // 2 s per wait
+constexpr uint32_t kTmemCols = 512;         // 2 accumulator buffers x 256 columns
 
-constexpr int kABytes = kTileM * kBK * 2;   // 16 KB BF16 A tile
-constexpr int kBBytes = kTileT * kBK * 2;   // 16 KB BF16 B tile
-constexpr int kSBytes = kTileM * kBK;       // 8 KB INT8 staging tile
+constexpr int kABytes = 128 * kBK * 2;     // 16 KB: 128 A rows (two 64-row atoms)
+constexpr int kBBytes = kHalfT * kBK * 2;  // 16 KB: 128 token rows
+constexpr int kSBytes = 64 * kBK;          // 4 KB: one [64 k][64 n] INT8 box
+// Epilogue scratch per column-half group: gate/up exchange (2 x 64 x 16
+// FP32) and an output staging tile (32 tokens x 128 FP32 for down, 32 x 64
+// BF16 for gate/up).
+constexpr int kXchBytes = 2 * 64 * 16 * 4;  // 8 KB
+constexpr int kStgBytes = 32 * 128 * 4;     // 16 KB
+constexpr int kXBytes = 2 * (kXchBytes + kStgBytes);
 
-template <bool GATE_UP>
-struct Cfg {
-    static constexpr int NP = GATE_UP ? 2 : 1;                  // projections
-    static constexpr int kStages = GATE_UP ? 3 : 4;
-    static constexpr int kStageBytes = NP * (kABytes + kSBytes) + kBBytes;
-    static constexpr int kTmemCols = GATE_UP ? 256 : 128;
-    static constexpr int kSmem = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
-};
+constexpr int kSOff = 0;
+constexpr int kAOff = kSOff + kWStages * 2 * kSBytes;
+constexpr int kBOff = kAOff + kAStages * kABytes;
+constexpr int kXOff = kBOff + kBStages * kBBytes;
+constexpr int kBarOff = kXOff + kXBytes;
+constexpr int kSmem = kBarOff + 512 + 1024 /*alignment slack*/;
+static_assert(kSmem <= 232448, "shared memory budget");
 
 struct GemmArgs {
-    const int4* tiles;          // (expert, first row, rows, 0)
+    const int4* tiles;          // (expert, first row, rows, 0), longest first
     const int32_t* tile_count;
+    int nblocks;                // feature blocks per pair
     const hmoe_expert_quant* quant;
-    int proj0;                  // quant index of the first projection
     const float* perm_weight;   // down: routing weight per row
     void* out;                  // gate/up: BF16 hmid [R,N]; down: FP32 rows [R,N]
     int K, N;
@@ -77,8 +97,9 @@ __device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-// 16 INT8 weights (one 16-byte chunk of a staging row) -> 16 BF16 values
-// q - zp, exact.  (u + 2^23) - (2^23 + 128 + zp) with u = q + 128.
+// 16 INT8 weights -> 16 BF16 values q - zp, exact:
+// float(2^23 + u) - (2^23 + 128 + zp) with u = q + 128; BF16 keeps the
+// integer exactly (|q - zp| <= 255 needs 8 significant bits).
 __device__ __forceinline__ void dequant16(const uint4 q, float off, uint32_t (&o)[8]) {
     const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
@@ -93,213 +114,388 @@ __device__ __forceinline__ void dequant16(const uint4 q, float off, uint32_t (&o
     }
 }
 
-// Staging [64 k][128 n] INT8 -> A [2 atoms of 64 n][64 k][128 B], 128-byte
-// swizzle (16-byte chunk index XOR (k mod 8)).  128 threads, 4 chunks each.
-__device__ __forceinline__ void dequant_tile(const uint8_t* stage, uint8_t* a, float off, int dt) {
+// Two staging boxes [64 k][64 n] INT8 (atom 0 and atom 1) -> A [2 atoms of
+// 64 MN][64 k][128 B] with the 128-byte swizzle (16-byte chunk index XOR
+// (k mod 8)).  256 threads, two 16-byte input chunks each.  Eight
+// consecutive threads cover rows k, k+1 (k even) of one box: their loads
+// read two 64-byte rows that fall in different bank halves, and their
+// 16-byte stores land in 8 distinct chunk positions (row k gets even
+// chunks, row k+1 odd ones), so neither side has bank conflicts.
+__device__ __forceinline__ void dequant_stage(const uint8_t* s0, const uint8_t* s1, uint8_t* a, float off0,
+                                              float off1, int dt) {
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const int c = dt + 128 * i;  // 16-byte chunk of the staging tile
-        const int k = c >> 3, j = c & 7;
-        const uint4 q = *reinterpret_cast<const uint4*>(stage + k * 128 + j * 16);
+    for (int i = 0; i < 2; ++i) {
+        const int u = dt + 256 * i;
+        const int q = u & 3, r = (u >> 2) & 1, atom = (u >> 3) & 1, kp = u >> 4;
+        const int k = 2 * kp + r;
+        const uint4 v = *reinterpret_cast<const uint4*>((atom ? s1 : s0) + k * 64 + q * 16);
         uint32_t o[8];
-        dequant16(q, off, o);
-        const int atom = j >> 2, cc = (j & 3) * 2;
+        dequant16(v, atom ? off1 : off0, o);
         uint8_t* row = a + atom * 8192 + k * 128;
+        const int cc = 2 * q;
         *reinterpret_cast<uint4*>(row + ((cc ^ (k & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
         *reinterpret_cast<uint4*>(row + (((cc + 1) ^ (k & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
     }
 }
 
+// Named barrier of one epilogue group (4 warps; ids 1, 2; 0 = __syncthreads).
+__device__ __forceinline__ void epi_barrier(int group) {
+    asm volatile("bar.sync %0, 128;" ::"r"(group + 1) : "memory");
+}
+
+__device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
+
 template <bool GATE_UP>
 __global__ void __launch_bounds__(kThreadsGemm, 1)
     expert_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                        const __grid_constant__ CUtensorMap tm_b, GemmArgs a) {
-    using C = Cfg<GATE_UP>;
-    constexpr int S = C::kStages;
-    const int tile = blockIdx.y;
-    if (tile >= *a.tile_count) return; // whole CTA, before any barrier or TMEM use
+    const int n_items = *a.tile_count * a.nblocks;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+    if (pair >= n_items) return; // both CTAs of the pair, before any barrier/TMEM use
+    const uint32_t rank = sm100::cluster_rank();
+    const bool leader = rank == 0;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    // stage s: [A0 | A1 | B | S0 | S1]
-    auto A = [&](int s, int p) { return smem + s * C::kStageBytes + p * kABytes; };
-    auto B = [&](int s) { return smem + s * C::kStageBytes + C::NP * kABytes; };
-    auto Sg = [&](int s, int p) { return smem + s * C::kStageBytes + C::NP * kABytes + kBBytes + p * kSBytes; };
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * C::kStageBytes);
-    uint64_t* full = bars;
-    uint64_t* aready = bars + S;
-    uint64_t* empty = bars + 2 * S;
-    uint64_t* accfull = bars + 3 * S;
-    uint32_t* tmem_s = reinterpret_cast<uint32_t*>(bars + 3 * S + 1);
+    auto S = [&](int s, int p) { return smem + kSOff + (s * 2 + p) * kSBytes; };
+    auto A = [&](int s) { return smem + kAOff + s * kABytes; };
+    auto B = [&](int s) { return smem + kBOff + s * kBBytes; };
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
+    uint64_t* full_w = bars;                  // [kWStages] local: weights landed
+    uint64_t* empty_w = full_w + kWStages;    // [kWStages] local: staging consumed
+    uint64_t* full_b = empty_w + kWStages;    // [kBStages] leader: both token halves landed
+    uint64_t* empty_b = full_b + kBStages;    // [kBStages] both: MMA done with the slot
+    uint64_t* aready = empty_b + kBStages;    // [kAStages] leader: A written in both CTAs
+    uint64_t* empty_a = aready + kAStages;    // [kAStages] both: MMA done with A
+    uint64_t* accfull = empty_a + kAStages;   // [2] both: accumulator ready
+    uint64_t* accempty = accfull + 2;         // [2] leader: both epilogues drained it
+    uint64_t* drain = accempty + 2;           // [1] both: every MMA done
+    uint32_t* tmem_s = reinterpret_cast<uint32_t*>(drain + 1);
     volatile int* abort_s = reinterpret_cast<volatile int*>(tmem_s + 1);
 
-    const int4 td = a.tiles[tile];
-    const int e = td.x, row0 = td.y, rows = td.z;
-    const int n0 = blockIdx.x * kTileM;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nkb = a.K / kBK;
 
-    if (warp == 0) {
-        sm100::tmem_alloc(tmem_s, C::kTmemCols);
-        sm100::tmem_relinquish();
+    if (warp == 2) {
+        sm100::tmem_alloc_pair(tmem_s, kTmemCols);
+        sm100::tmem_relinquish_pair();
     }
-    if (threadIdx.x == 32) {
-        for (int s = 0; s < S; ++s) {
-            sm100::mbar_init(&full[s], 1);
-            sm100::mbar_init(&aready[s], 4);
-            sm100::mbar_init(&empty[s], 1);
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kWStages; ++s) {
+            sm100::mbar_init(&full_w[s], 1);
+            sm100::mbar_init(&empty_w[s], kDequantWarps);
         }
-        sm100::mbar_init(accfull, 1);
+        for (int s = 0; s < kBStages; ++s) {
+            sm100::mbar_init(&full_b[s], 1);
+            sm100::mbar_init(&empty_b[s], 1);
+        }
+        for (int s = 0; s < kAStages; ++s) {
+            sm100::mbar_init(&aready[s], 2 * kDequantWarps);
+            sm100::mbar_init(&empty_a[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            sm100::mbar_init(&accfull[b], 1);
+            sm100::mbar_init(&accempty[b], 2 * kEpiWarps);
+        }
+        sm100::mbar_init(drain, 1);
         *abort_s = 0;
         sm100::fence_mbarrier_init();
     }
     sm100::tc_fence_before();
-    __syncthreads();
+    sm100::cluster_sync_all(); // barriers of both CTAs initialised, TMEM allocated
     sm100::tc_fence_after();
     const uint32_t tmem = *tmem_s;
-    const uint32_t nmma = static_cast<uint32_t>((rows + 15) & ~15);
 
     auto fail = [&]() {
         *abort_s = 1;
         device_fail(a.st, HMOE_TIMEOUT);
     };
 
-    if (warp == 0 && lane == 0) {
-        // ------------------------------------------------ TMA producer
-        sm100::prefetch_tmap(&tm_w0);
-        if (GATE_UP) sm100::prefetch_tmap(&tm_w1);
-        sm100::prefetch_tmap(&tm_b);
-        constexpr uint32_t bytes = C::NP * kSBytes + kBBytes;
-        int issued = 0;
-        for (int kb = 0; kb < nkb; ++kb) {
-            const int s = kb % S;
-            if (kb >= S && !sm100::mbar_wait(&empty[s], ((kb / S) - 1) & 1, abort_s, kWaitNs)) {
-                fail();
-                break;
-            }
-            sm100::mbar_arrive_expect_tx(&full[s], bytes);
-            sm100::tma_load_3d(Sg(s, 0), &tm_w0, n0, kb * kBK, e, &full[s]);
-            if (GATE_UP) sm100::tma_load_3d(Sg(s, 1), &tm_w1, n0, kb * kBK, e, &full[s]);
-            sm100::tma_load_2d(B(s), &tm_b, kb * kBK, row0, &full[s]);
-            issued = kb + 1;
-        }
-        if (*abort_s) {
-            // drain this CTA's own loads still in flight before exit
-            for (int kb = (issued > S ? issued - S : 0); kb < issued; ++kb)
-                sm100::mbar_wait_for(&full[kb % S], (kb / S) & 1, kWaitNs);
-        }
-    } else if (warp == 1 && lane == 0) {
-        // ------------------------------------------------ MMA issuer
-        const uint32_t idesc = sm100::make_idesc_bf16(kTileM, nmma, true, false);
-        for (int kb = 0; kb < nkb; ++kb) {
-            const int s = kb % S;
-            if (!sm100::mbar_wait(&full[s], (kb / S) & 1, abort_s, kWaitNs) ||
-                !sm100::mbar_wait(&aready[s], (kb / S) & 1, abort_s, kWaitNs)) {
-                fail();
-                break;
-            }
-            sm100::tc_fence_after();
-            const uint32_t b0 = sm100::smem_u32(B(s));
-#pragma unroll
-            for (int ks = 0; ks < kBK / 16; ++ks) {
-                const uint64_t bd = sm100::make_smem_desc(b0 + ks * 32, 16, 1024, 2);
-#pragma unroll
-                for (int p = 0; p < C::NP; ++p) {
-                    const uint64_t ad = sm100::make_smem_desc(sm100::smem_u32(A(s, p)) + ks * 2048, 8192, 1024, 2);
-                    sm100::mma_bf16(tmem + p * 128, ad, bd, idesc, (kb | ks) != 0);
+    if (warp == 0) {
+        // ------------------------------------------------ INT8 weight producer
+        if (lane == 0) {
+            sm100::prefetch_tmap(&tm_w0);
+            sm100::prefetch_tmap(&tm_w1);
+            uint32_t it = 0;
+            for (int item = pair; item < n_items && !*abort_s; item += npairs) {
+                const int4 td = a.tiles[item / a.nblocks];
+                const int nb = item % a.nblocks;
+                // gate/up: both boxes at the CTA's 64 features; down: two
+                // adjacent 64-feature boxes of the CTA's 128 features
+                const int x0 = GATE_UP ? nb * 128 + 64 * static_cast<int>(rank) : nb * 256 + 128 * static_cast<int>(rank);
+                const int x1 = GATE_UP ? x0 : x0 + 64;
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % kWStages;
+                    if (it >= kWStages &&
+                        !sm100::mbar_wait(&empty_w[s], ((it / kWStages) - 1) & 1, abort_s, kWaitNs)) {
+                        fail();
+                        break;
+                    }
+                    sm100::mbar_arrive_expect_tx(&full_w[s], 2 * kSBytes);
+                    sm100::tma_load_3d(S(s, 0), &tm_w0, x0, kb * kBK, td.x, &full_w[s]);
+                    sm100::tma_load_3d(S(s, 1), &tm_w1, x1, kb * kBK, td.x, &full_w[s]);
                 }
             }
-            sm100::mma_commit(&empty[s]);
+            if (*abort_s) // drain this CTA's own loads before it exits
+                for (uint32_t i = (it > kWStages ? it - kWStages : 0); i < it; ++i)
+                    sm100::mbar_wait_for(&full_w[i % kWStages], (i / kWStages) & 1, kWaitNs);
         }
-        sm100::mma_commit(accfull); // also on abort: completes once issued MMAs finish
-    } else if (warp >= 2) {
-        // ------------------------------------------------ dequant + epilogue
-        const int dt = threadIdx.x - 64;
-        const hmoe_expert_quant qp = a.quant[e];
-        const float off0 = 8388608.0f + 128.0f + static_cast<float>(qp.zero_point[a.proj0]);
-        const float off1 = GATE_UP ? 8388608.0f + 128.0f + static_cast<float>(qp.zero_point[a.proj0 + 1]) : 0.0f;
-        bool ok = true;
-        for (int kb = 0; kb < nkb; ++kb) {
-            const int s = kb % S;
-            if (!sm100::mbar_wait(&full[s], (kb / S) & 1, abort_s, kWaitNs)) {
+    } else if (warp == 1) {
+        // ------------------------------------------------ BF16 token-tile producer
+        if (lane == 0) {
+            sm100::prefetch_tmap(&tm_b);
+            uint32_t it = 0;
+            for (int item = pair; item < n_items && !*abort_s; item += npairs) {
+                const int4 td = a.tiles[item / a.nblocks];
+                const int half = ((td.z + 15) & ~15) >> 1;
+                const int y = td.y + static_cast<int>(rank) * half;
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int s = it % kBStages;
+                    if (it >= kBStages &&
+                        !sm100::mbar_wait(&empty_b[s], ((it / kBStages) - 1) & 1, abort_s, kWaitNs)) {
+                        fail();
+                        break;
+                    }
+                    if (leader) sm100::mbar_arrive_expect_tx(&full_b[s], 2 * kBBytes);
+                    sm100::tma_load_2d_pair(B(s), &tm_b, kb * kBK, y,
+                                            sm100::map_shared(sm100::smem_u32(&full_b[s]), 0));
+                }
+            }
+            // Loads in flight complete on the leader's barriers; the teardown
+            // cluster barrier below keeps both CTAs alive until then.
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------ MMA issuer (leader)
+        if (leader && lane == 0) {
+            uint32_t it = 0;
+            int j = 0;
+            for (int item = pair; item < n_items && !*abort_s; item += npairs, ++j) {
+                const int4 td = a.tiles[item / a.nblocks];
+                const uint32_t nmma = static_cast<uint32_t>((td.z + 15) & ~15);
+                const uint32_t idesc = sm100::make_idesc_bf16(256, nmma, true, false);
+                const int buf = j & 1;
+                if (j >= 2 && !sm100::mbar_wait_cluster(&accempty[buf], ((j >> 1) - 1) & 1, abort_s, kWaitNs)) {
+                    fail();
+                    break;
+                }
+                sm100::tc_fence_after();
+                const uint32_t d0 = tmem + static_cast<uint32_t>(buf * kTileT);
+                bool ok = true;
+                for (int kb = 0; kb < nkb; ++kb, ++it) {
+                    const int as = it % kAStages, bs = it % kBStages;
+                    if (!sm100::mbar_wait_cluster(&full_b[bs], (it / kBStages) & 1, abort_s, kWaitNs) ||
+                        !sm100::mbar_wait_cluster(&aready[as], (it / kAStages) & 1, abort_s, kWaitNs)) {
+                        fail();
+                        ok = false;
+                        break;
+                    }
+                    sm100::tc_fence_after();
+                    const uint32_t a0 = sm100::smem_u32(A(as)), b0 = sm100::smem_u32(B(bs));
+#pragma unroll
+                    for (int ks = 0; ks < kBK / 16; ++ks) {
+                        const uint64_t ad = sm100::make_smem_desc(a0 + ks * 2048, 8192, 1024, 2);
+                        const uint64_t bd = sm100::make_smem_desc(b0 + ks * 32, 16, 1024, 2);
+                        sm100::mma_bf16_pair(d0, ad, bd, idesc, (kb | ks) != 0);
+                    }
+                    sm100::mma_commit_pair(&empty_a[as], 0x3);
+                    sm100::mma_commit_pair(&empty_b[bs], 0x3);
+                }
+                if (!ok) break;
+                sm100::mma_commit_pair(&accfull[buf], 0x3);
+            }
+            sm100::mma_commit_pair(drain, 0x3); // completes once every MMA has finished
+        }
+    } else if (warp < 3 + kDequantWarps) {
+        // ------------------------------------------------ dequantise
+        const int dt = threadIdx.x - 96;
+        uint32_t wi = 0, ai = 0;
+        for (int item = pair; item < n_items && !*abort_s; item += npairs) {
+            const int4 td = a.tiles[item / a.nblocks];
+            const hmoe_expert_quant qp = a.quant[td.x];
+            const float off0 = 8388608.0f + 128.0f + static_cast<float>(qp.zero_point[GATE_UP ? 0 : 2]);
+            const float off1 = 8388608.0f + 128.0f + static_cast<float>(qp.zero_point[GATE_UP ? 1 : 2]);
+            bool ok = true;
+            for (int kb = 0; kb < nkb; ++kb, ++wi, ++ai) {
+                const int ws = wi % kWStages, as = ai % kAStages;
+                if (!sm100::mbar_wait(&full_w[ws], (wi / kWStages) & 1, abort_s, kWaitNs) ||
+                    (ai >= kAStages &&
+                     !sm100::mbar_wait_cluster(&empty_a[as], ((ai / kAStages) - 1) & 1, abort_s, kWaitNs))) {
+                    fail();
+                    ok = false;
+                    break;
+                }
+                dequant_stage(S(ws, 0), S(ws, 1), A(as), off0, off1, dt);
+                sm100::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    sm100::mbar_arrive(&empty_w[ws]);
+                    sm100::mbar_arrive_remote(sm100::map_shared(sm100::smem_u32(&aready[as]), 0));
+                }
+            }
+            if (!ok) break;
+        }
+    } else {
+        // ------------------------------------------------ epilogue
+        // Two groups of 4 warps; group h handles the 32-column chunks with
+        // index = h (mod 2).  Each warp reads its TMEM lane quarter q.
+        const int e = warp - (3 + kDequantWarps);
+        const int grp = e >> 2;
+        const int q = warp & 3;                 // TMEM lane quarter of this warp
+        const int m = q * 32 + lane;            // accumulator row (TMEM lane)
+        const int gt = (q & 3) * 32 + lane;     // thread index inside the group
+        const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
+        uint8_t* xbase = smem + kXOff + grp * (kXchBytes + kStgBytes);
+        float* xg = reinterpret_cast<float*>(xbase);            // [16 t][64 f] gate, tokens 16..31
+        float* xu = xg + 64 * 16;                               // [16 t][64 f] up, tokens 0..15
+        uint8_t* stg = xbase + kXchBytes;                       // output staging
+        int j = 0;
+        for (int item = pair; item < n_items && !*abort_s; item += npairs, ++j) {
+            const int4 td = a.tiles[item / a.nblocks];
+            const int row0 = td.y, rows = td.z;
+            const int nb = item % a.nblocks;
+            const uint32_t nmma = static_cast<uint32_t>((rows + 15) & ~15);
+            const int buf = j & 1;
+            if (!sm100::mbar_wait_cluster(&accfull[buf], (j >> 1) & 1, abort_s, kWaitNs)) {
                 fail();
-                ok = false;
                 break;
             }
-            dequant_tile(Sg(s, 0), A(s, 0), off0, dt);
-            if (GATE_UP) dequant_tile(Sg(s, 1), A(s, 1), off1, dt);
-            sm100::fence_proxy_async_smem();
-            __syncwarp();
-            if (lane == 0) sm100::mbar_arrive(&aready[s]);
-        }
-        if (ok && sm100::mbar_wait(accfull, 0, abort_s, kWaitNs)) {
             sm100::tc_fence_after();
-            const int q = warp & 3;            // TMEM lane quarter of this warp
-            const int m = q * 32 + lane;       // output feature within the tile
-            const int n = n0 + m;
-            const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
-            if (GATE_UP) {
-                const float sg = qp.scale[a.proj0], su = qp.scale[a.proj0 + 1];
-                __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
-                for (uint32_t c0 = 0; c0 < nmma; c0 += 32) {
-                    uint32_t g[32], u[32];
-                    sm100::tmem_ld32(lane_addr + c0, g);
-                    sm100::tmem_ld32(lane_addr + 128 + c0, u);
-                    sm100::tmem_wait_ld();
+            const hmoe_expert_quant qp = a.quant[td.x];
+            const uint32_t col = static_cast<uint32_t>(buf * kTileT);
+            for (uint32_t c0 = 32u * grp; c0 < nmma; c0 += 64) {
+                uint32_t v[32];
+                sm100::tmem_ld32(lane_addr + col + c0, v);
+                sm100::tmem_wait_ld();
+                const int nt = min(32, rows - static_cast<int>(c0)); // valid tokens in the chunk
+                if (GATE_UP) {
+                    // rows 0-63: gate of features f, rows 64-127: up of the same
+                    // f.  Warps q<2 finish tokens 0..15, warps q>=2 tokens 16..31.
+                    const float sg = qp.scale[0], su = qp.scale[1];
+                    if (q < 2) {
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int t = static_cast<int>(c0) + j;
-                        if (t < rows && n < a.N) {
-                            const float gv = sg * __uint_as_float(g[j]);
-                            const float uv = su * __uint_as_float(u[j]);
-                            out[static_cast<size_t>(row0 + t) * a.N + n] = __float2bfloat16_rn(silu(gv) * uv);
+                        for (int i = 0; i < 16; ++i) xg[i * 64 + m] = sg * __uint_as_float(v[16 + i]);
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) xu[i * 64 + (m - 64)] = su * __uint_as_float(v[i]);
+                    }
+                    epi_barrier(grp);
+                    __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(stg); // [32 t][64 f]
+                    const int f = m & 63;
+                    if (q < 2) {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const float gv = sg * __uint_as_float(v[i]);
+                            const float uv = xu[i * 64 + f];
+                            st[i * 64 + f] = __float2bfloat16_rn(silu_fast(gv) * uv);
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 16; ++i) {
+                            const float gv = xg[i * 64 + f];
+                            const float uv = su * __uint_as_float(v[16 + i]);
+                            st[(16 + i) * 64 + f] = __float2bfloat16_rn(silu_fast(gv) * uv);
                         }
                     }
-                }
-            } else {
-                const float sd = qp.scale[a.proj0];
-                float* out = static_cast<float*>(a.out);
-                for (uint32_t c0 = 0; c0 < nmma; c0 += 32) {
-                    uint32_t d[32];
-                    sm100::tmem_ld32(lane_addr + c0, d);
-                    sm100::tmem_wait_ld();
+                    epi_barrier(grp);
+                    // 32 rows x 128 B, 16-byte pieces, coalesced per row
+                    const int f0 = nb * 128 + 64 * static_cast<int>(rank);
+                    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const int t = static_cast<int>(c0) + j;
-                        if (t < rows && n < a.N)
-                            out[static_cast<size_t>(row0 + t) * a.N + n] =
-                                a.perm_weight[row0 + t] * (sd * __uint_as_float(d[j]));
+                    for (int p = 0; p < 2; ++p) {
+                        const int idx = gt + 128 * p;      // 256 pieces
+                        const int t = idx >> 3, c = idx & 7;
+                        if (t < nt && f0 + c * 8 < a.N)
+                            *reinterpret_cast<uint4*>(out + static_cast<size_t>(row0 + c0 + t) * a.N + f0 + c * 8) =
+                                *reinterpret_cast<const uint4*>(st + t * 64 + c * 8);
                     }
+                    epi_barrier(grp);
+                } else {
+                    const float sd = qp.scale[2];
+                    const float wl = lane < nt ? a.perm_weight[row0 + c0 + lane] : 0.0f;
+                    float* st = reinterpret_cast<float*>(stg); // [32 t][128 f]
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) {
+                        const float wt = __shfl_sync(0xffffffffu, wl, i);
+                        st[i * 128 + m] = wt * (sd * __uint_as_float(v[i]));
+                    }
+                    epi_barrier(grp);
+                    const int f0 = nb * 256 + 128 * static_cast<int>(rank);
+                    float* out = static_cast<float*>(a.out);
+#pragma unroll
+                    for (int p = 0; p < 8; ++p) {
+                        const int idx = gt + 128 * p;      // 1024 pieces of 4 floats
+                        const int t = idx >> 5, c = idx & 31;
+                        if (t < nt && f0 + c * 4 < a.N)
+                            *reinterpret_cast<float4*>(out + static_cast<size_t>(row0 + c0 + t) * a.N + f0 + c * 4) =
+                                *reinterpret_cast<const float4*>(st + t * 128 + c * 4);
+                    }
+                    epi_barrier(grp);
                 }
             }
-        } else if (ok) {
-            fail();
+            sm100::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive_remote(sm100::map_shared(sm100::smem_u32(&accempty[buf]), 0));
         }
     }
-    // teardown: every thread arrives here, including after an abort
+    // teardown: every thread of both CTAs arrives here, also after an abort
+    if (warp == 2) {
+        sm100::mbar_wait_for(drain, 0, kWaitNs); // every pair MMA has completed
+    }
     sm100::tc_fence_before();
-    __syncthreads();
-    if (warp == 0) {
-        // after an abort, let the MMAs already issued finish before freeing TMEM
-        if (*abort_s) sm100::mbar_wait_for(accfull, 0, kWaitNs);
+    sm100::cluster_sync_all();
+    if (warp == 2) {
         sm100::tc_fence_after();
-        sm100::tmem_dealloc(tmem, C::kTmemCols);
+        sm100::tmem_dealloc_pair(tmem, kTmemCols);
     }
 }
 
-// Builds the GEMM tile list: every expert on the large list is cut into
-// tiles of at most kTileT consecutive permuted rows.
-__global__ void tile_list_kernel(const int32_t* large_list, const int32_t* list_sizes, const int32_t* offsets,
-                                 int4* tiles, int32_t* tile_count, int capacity) {
-    if (threadIdx.x != 0) return;
-    int n = 0;
-    const int nl = list_sizes[1];
-    for (int i = 0; i < nl; ++i) {
-        const int e = large_list[i];
-        const int r0 = offsets[e], cnt = offsets[e + 1] - r0;
-        for (int j = 0; j < cnt && n < capacity; j += kTileT) tiles[n++] = make_int4(e, r0 + j, min(kTileT, cnt - j), 0);
+// Cuts every expert on the large list into tiles of <= kTileT consecutive
+// permuted rows: all full tiles first, then the remainders in decreasing
+// size (ties by list position), so the persistent CTAs start with the
+// longest work items.  One CTA, one thread per listed expert.
+__global__ void __launch_bounds__(256) tile_list_kernel(const int32_t* large_list, const int32_t* list_sizes,
+                                                        const int32_t* offsets, int4* tiles,
+                                                        int32_t* tile_count, int capacity) {
+    __shared__ int full_s[256], rem_s[256], off_s[256];
+    __shared__ int total_full_s;
+    const int nl = min(list_sizes[1], 256);
+    const int i = threadIdx.x;
+    int e = -1, r0 = 0, cnt = 0;
+    if (i < nl) {
+        e = large_list[i];
+        r0 = offsets[e];
+        cnt = offsets[e + 1] - r0;
     }
-    *tile_count = n;
+    full_s[i] = cnt / kTileT;
+    rem_s[i] = cnt % kTileT;
+    __syncthreads();
+    if (i == 0) {
+        int acc = 0;
+        for (int j = 0; j < nl; ++j) {
+            off_s[j] = acc;
+            acc += full_s[j];
+        }
+        total_full_s = acc;
+    }
+    __syncthreads();
+    if (i < nl) {
+        for (int f = 0; f < full_s[i]; ++f) {
+            const int pos = off_s[i] + f;
+            if (pos < capacity) tiles[pos] = make_int4(e, r0 + f * kTileT, kTileT, 0);
+        }
+        if (rem_s[i] > 0) {
+            int before = 0;
+            for (int j = 0; j < nl; ++j)
+                before += rem_s[j] > rem_s[i] || (rem_s[j] == rem_s[i] && j < i);
+            const int pos = total_full_s + before;
+            if (pos < capacity) tiles[pos] = make_int4(e, r0 + full_s[i] * kTileT, rem_s[i], 0);
+        }
+    }
+    if (i == 0) {
+        int parts = 0;
+        for (int j = 0; j < nl; ++j) parts += rem_s[j] > 0;
+        *tile_count = min(capacity, total_full_s + parts);
+    }
 }
 
 // X_perm[row] = BF16(x[perm_token[row]]) for the rows of every GEMM tile.
@@ -336,40 +532,67 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// INT8 weights of one projection across all experts: dims {N, K, experts}.
+// INT8 weights of one projection across all experts: dims {N, K, experts},
+// box [64 k][64 n].
 bool map_weights(CUtensorMap* m, const int8_t* base, int N, int K, int experts, uint64_t stride) {
     const cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(K),
                                 static_cast<cuuint64_t>(experts)};
     const cuuint64_t strides[2] = {static_cast<cuuint64_t>(N), stride};
-    const cuuint32_t box[3] = {kTileM, kBK, 1};
+    const cuuint32_t box[3] = {64, kBK, 1};
     const cuuint32_t es[3] = {1, 1, 1};
     return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(base), dims, strides, box, es,
                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// BF16 rows [rows, K] (K contiguous), 128-byte swizzle, box 64 x kTileT.
+// BF16 rows [rows, K] (K contiguous), 128-byte swizzle, box 64 x 128 rows.
 bool map_rows(CUtensorMap* m, const void* base, int K, int rows) {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
-    const cuuint32_t box[2] = {kBK, kTileT};
+    const cuuint32_t box[2] = {kBK, kHalfT};
     const cuuint32_t es[2] = {1, 1};
     return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+int sm_count() {
+    static int n = 0;
+    if (n == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
 template <bool GATE_UP>
 hmoe_status launch_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& b, const GemmArgs& args,
-                        int tile_capacity, cudaStream_t s) {
-    using C = Cfg<GATE_UP>;
+                        int item_capacity, cudaStream_t s) {
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(expert_gemm_kernel<GATE_UP>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+        cudaFuncSetAttribute(expert_gemm_kernel<GATE_UP>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
         attr = true;
     }
-    const dim3 grid(static_cast<unsigned>((args.N + kTileM - 1) / kTileM), static_cast<unsigned>(tile_capacity));
-    expert_gemm_kernel<GATE_UP><<<grid, kThreadsGemm, C::kSmem, s>>>(w0, w1, b, args);
+    const int pairs = std::max(1, std::min(sm_count() / 2, item_capacity));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * pairs));
+    cfg.blockDim = dim3(kThreadsGemm);
+    cfg.dynamicSmemBytes = kSmem;
+    cfg.stream = s;
+    cudaLaunchAttribute attrs[1];
+    attrs[0].id = cudaLaunchAttributeClusterDimension;
+    attrs[0].val.clusterDim.x = 2;
+    attrs[0].val.clusterDim.y = 1;
+    attrs[0].val.clusterDim.z = 1;
+    cfg.attrs = attrs;
+    cfg.numAttrs = 1;
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, expert_gemm_kernel<GATE_UP>, w0, w1, b, args);
+    if (err != cudaSuccess) {
+        set_last_error(GATE_UP ? "hmoe expert GEMM gate/up launch" : "hmoe expert GEMM down launch", err);
+        return HMOE_CUDA_ERROR;
+    }
     return check_launch(GATE_UP ? "hmoe expert GEMM gate/up" : "hmoe expert GEMM down");
 }
 
@@ -393,6 +616,8 @@ bool gemm_available() {
     return avail == 1;
 }
 
+size_t gemm_tile_bytes(size_t rows, int experts) { return (rows / kTileT + experts + 2) * sizeof(int4); }
+
 hmoe_status launch_expert_gemm_gate_up(const hmoe_layer_desc& d, const float* x, size_t T, char* ws,
                                        const Workspace& w, int list_capacity, cudaStream_t s) {
     const int H = static_cast<int>(d.hidden), I = static_cast<int>(d.intermediate);
@@ -401,9 +626,9 @@ hmoe_status launch_expert_gemm_gate_up(const hmoe_layer_desc& d, const float* x,
     const int R = static_cast<int>(T * (d.top_k + d.shared_experts));
     auto* tiles = reinterpret_cast<int4*>(ws + w.tiles);
     auto* tcount = reinterpret_cast<int32_t*>(ws + w.tile_count);
-    tile_list_kernel<<<1, 32, 0, s>>>(reinterpret_cast<int32_t*>(ws + w.large_list),
-                                      reinterpret_cast<int32_t*>(ws + w.list_sizes),
-                                      reinterpret_cast<int32_t*>(ws + w.offsets), tiles, tcount, cap);
+    tile_list_kernel<<<1, 256, 0, s>>>(reinterpret_cast<int32_t*>(ws + w.large_list),
+                                       reinterpret_cast<int32_t*>(ws + w.list_sizes),
+                                       reinterpret_cast<int32_t*>(ws + w.offsets), tiles, tcount, cap);
     hmoe_status r = check_launch("hmoe tile list");
     if (r != HMOE_OK) return r;
     auto* xperm = reinterpret_cast<__nv_bfloat16*>(ws + w.xperm);
@@ -416,9 +641,10 @@ hmoe_status launch_expert_gemm_gate_up(const hmoe_layer_desc& d, const float* x,
         set_last_error_text("hmoe: cuTensorMapEncodeTiled failed (gate/up)");
         return HMOE_CUDA_ERROR;
     }
-    GemmArgs a{tiles, tcount, d.quant, 0, nullptr, ws + w.hmid16, H, I,
+    const int nb = (I + 127) / 128; // 128 features (64 per CTA) per pair
+    GemmArgs a{tiles, tcount, nb, d.quant, nullptr, ws + w.hmid16, H, I,
                reinterpret_cast<DeviceStatus*>(ws + w.status)};
-    return launch_gemm<true>(mg, mu, mb, a, cap, s);
+    return launch_gemm<true>(mg, mu, mb, a, cap * nb, s);
 }
 
 hmoe_status launch_expert_gemm_down(const hmoe_layer_desc& d, size_t T, char* ws, const Workspace& w,
@@ -433,10 +659,11 @@ hmoe_status launch_expert_gemm_down(const hmoe_layer_desc& d, size_t T, char* ws
         set_last_error_text("hmoe: cuTensorMapEncodeTiled failed (down)");
         return HMOE_CUDA_ERROR;
     }
-    GemmArgs a{reinterpret_cast<int4*>(ws + w.tiles), reinterpret_cast<int32_t*>(ws + w.tile_count), d.quant, 2,
+    const int nb = (H + 255) / 256; // 256 features (128 per CTA) per pair
+    GemmArgs a{reinterpret_cast<int4*>(ws + w.tiles), reinterpret_cast<int32_t*>(ws + w.tile_count), nb, d.quant,
                reinterpret_cast<float*>(ws + w.perm_weight), ws + w.yrows, I, H,
                reinterpret_cast<DeviceStatus*>(ws + w.status)};
-    return launch_gemm<false>(md, md, mb, a, cap, s);
+    return launch_gemm<false>(md, md, mb, a, cap * nb, s);
 }
 
 } // namespace hmoe

@@ -174,11 +174,15 @@ hmoe_status launch_expert_gemv(bool gate_up, const GemvArgs& args, int list_capa
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t err;
+    static size_t attr_set[2] = {0, 0};
+    if (smem > attr_set[gate_up]) {
+        cudaFuncSetAttribute(gate_up ? expert_gemv_kernel<true> : expert_gemv_kernel<false>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        attr_set[gate_up] = smem;
+    }
     if (gate_up) {
-        cudaFuncSetAttribute(expert_gemv_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         err = cudaLaunchKernelEx(&cfg, expert_gemv_kernel<true>, args);
     } else {
-        cudaFuncSetAttribute(expert_gemv_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
         err = cudaLaunchKernelEx(&cfg, expert_gemv_kernel<false>, args);
     }
     if (err != cudaSuccess) {

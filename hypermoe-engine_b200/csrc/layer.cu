@@ -178,7 +178,7 @@ hmoe_status enqueue_experts(const hmoe_layer_desc& d, const float* x, size_t T, 
     // Worst-case list sizes: experts that can hold >= 1 (GEMV) or > small_max
     // (GEMM) tokens.
     const int shared_small = (static_cast<long>(T) <= small_max) ? S : 0;
-    const int small_cap = static_cast<int>(std::min<long>(E, assignments)) + shared_small;
+    const int small_cap = small_max <= 0 ? 0 : static_cast<int>(std::min<long>(E, assignments)) + shared_small;
     const int large_cap = static_cast<int>(std::min<long>(E, assignments / (small_max + 1))) + (S - shared_small);
     GemvArgs g{};
     g.list = reinterpret_cast<int32_t*>(ws + w.small_list);
@@ -229,10 +229,15 @@ hmoe_status enqueue_experts(const hmoe_layer_desc& d, const float* x, size_t T, 
     return HMOE_OK;
 }
 
-int small_threshold() {
-    if (g_variant == 1) return INT_MAX / 2;
+// Experts with at most this many tokens take the GEMV.  The choice is made
+// per launch from the batch size alone (the host never reads the routing):
+// decode-sized batches stream every touched expert through the GEMV, larger
+// ones run every expert on the tensor-core GEMM.
+int small_threshold(size_t T, const hmoe_layer_desc& d) {
+    if (g_variant == 1 || !gemm_available()) return INT_MAX / 2;
     if (g_variant == 2) return 0;
-    return gemm_available() ? kDefaultSmallMax : INT_MAX / 2;
+    const size_t assignments = T * (d.top_k + d.shared_experts);
+    return assignments <= static_cast<size_t>(kGemvMaxAssignments) ? INT_MAX / 2 : 0;
 }
 
 } // namespace hmoe
@@ -281,7 +286,7 @@ hmoe_status hmoe_route(const hmoe_layer_desc* desc, const float* x, size_t token
     if (workspace_bytes < w.total) return HMOE_WORKSPACE_TOO_SMALL;
     char* ws = static_cast<char*>(workspace);
     cudaStream_t s = as_stream(stream);
-    hmoe_status r = enqueue_route(*desc, x, tokens, ws, w, small_threshold(), s);
+    hmoe_status r = enqueue_route(*desc, x, tokens, ws, w, small_threshold(tokens, *desc), s);
     if (r != HMOE_OK) return r;
     const size_t tk = tokens * desc->top_k;
     auto copy = [&](void* dst, size_t src_off, size_t bytes) {
@@ -311,7 +316,7 @@ hmoe_status hmoe_moe_forward(const hmoe_layer_desc* desc, const float* x, float*
     if (workspace_bytes < w.total) return HMOE_WORKSPACE_TOO_SMALL;
     char* ws = static_cast<char*>(workspace);
     cudaStream_t s = as_stream(stream);
-    const int small_max = small_threshold();
+    const int small_max = small_threshold(tokens, *desc);
     stage(0, s);
     hmoe_status r = enqueue_route(*desc, x, tokens, ws, w, small_max, s);
     if (r != HMOE_OK) return r;

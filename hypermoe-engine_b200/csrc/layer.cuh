@@ -15,9 +15,9 @@ struct Workspace {
 
 Workspace plan_workspace(const hmoe_layer_desc& d, size_t T, int local_experts);
 
-// Expert groups with at most this many tokens use the weight-streaming
-// GEMV; larger groups use the tcgen05 grouped GEMM.
-constexpr int kDefaultSmallMax = 16;
+// Batches with at most this many (token, expert) assignments use the
+// weight-streaming GEMV for every expert; larger ones the tcgen05 GEMM.
+constexpr int kGemvMaxAssignments = 64;
 
 // Upper bound of a token's rows (top_k routed + shared experts).
 constexpr int kMaxSlots = 96;

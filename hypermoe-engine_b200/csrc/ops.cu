@@ -127,7 +127,11 @@ hmoe_status launch_int8_matmul(const float* left, const int8_t* right, float* ou
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    cudaFuncSetAttribute(int8_matmul_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    static size_t attr_set = 0;
+    if (smem > attr_set) {
+        cudaFuncSetAttribute(int8_matmul_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+        attr_set = smem;
+    }
     const cudaError_t err = cudaLaunchKernelEx(&cfg, int8_matmul_kernel, left, right, out,
                                                static_cast<int>(rows), static_cast<int>(K),
                                                static_cast<int>(N), scale, static_cast<int>(zp), KS);

@@ -29,12 +29,19 @@
 //    a double sum in rank order -- all as in the reference.
 #include "common.cuh"
 
+#include <cooperative_groups.h>
+
 #include <cfloat>
+#include <algorithm>
 #include <climits>
+
+namespace cg = cooperative_groups;
 
 namespace hmoe {
 
-constexpr int kRouteTokens = 4;  // tokens per CTA in the fused router
+constexpr int kRouteTokens = 8;  // tokens per CTA in the fused router
+constexpr int kRouteChunk = 1024; // hidden rows staged per pass (as doubles)
+constexpr int kRouteFallbacks = 64; // queued sequential recomputations per CTA
 constexpr int kMaxExperts = 256; // E_pad <= 256 (8 candidates per lane)
 constexpr int kMaxTopK = 32;
 
@@ -186,98 +193,206 @@ __device__ void select_token(const float (&lv)[C], int E, int k, int softmax,
     }
 }
 
-// Fused router.  Block = E_pad * P threads: thread (e = tid % E_pad,
-// q = tid / E_pad) sums chunk q of the hidden dimension for expert e over
-// kRouteTokens tokens.  Dynamic smem: x tile, double partials, |.| partials,
-// logits, per-warp exp scratch.
+// The reference's sequential double accumulation for one (token, expert),
+// by a single thread (used only when the per-CTA queue overflows).
+__device__ double sequential_logit(const RouteArgs& a, int tok, int e) {
+    const float* xr = a.x + static_cast<size_t>(tok) * a.H;
+    double s = 0.0;
+    for (int i = 0; i < a.H; ++i)
+        s = fma(static_cast<double>(xr[i]), static_cast<double>(a.w[static_cast<size_t>(i) * a.E + e]), s);
+    if (a.bias) s = fma(1.0, static_cast<double>(a.bias[e]), s);
+    if (a.st) atomicAdd(&a.st->sequential_logits, 1);
+    return s;
+}
+
+// Fused router.  Grid (KS, ceil(T/kRouteTokens)), clusters of KS CTAs along
+// x: CTA r of a cluster sums hidden rows [r*H/KS, (r+1)*H/KS) for
+// kRouteTokens tokens and every expert.  Thread (quad = tid % EQ,
+// p = tid / EQ) owns experts 4*quad..4*quad+3 and the rows i = p (mod P)
+// of each staged chunk; the token rows are staged as doubles, so one shared
+// load feeds four DFMAs and the router matrix is read with 16-byte loads.
+// Partial sums meet in (distributed) shared memory and are added in a fixed
+// order (rank, p).  The certificate bounds sum_i |x_i W_ie| by
+// ||x|| ||W_e|| (Cauchy-Schwarz).
 template <int C>
-__global__ void __launch_bounds__(1024) route_kernel(RouteArgs a, int E_pad, int P) {
+__global__ void __launch_bounds__(256) route_kernel(RouteArgs a, int EQ, int P, int KS) {
     extern __shared__ __align__(16) unsigned char smem[];
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = static_cast<int>(cluster.block_rank());
     const int H = a.H, E = a.E;
-    float* xs = reinterpret_cast<float*>(smem);                                   // [TB][H]
-    double* part = reinterpret_cast<double*>(xs + kRouteTokens * H);              // [TB][P][E_pad]
-    float* absb = reinterpret_cast<float*>(part + kRouteTokens * P * E_pad);      // [TB][P][E_pad]
-    float* logit = absb + kRouteTokens * P * E_pad;                               // [TB][E_pad]
-    float* evs = logit + kRouteTokens * E_pad;                                    // [TB][E_pad]
+    const int E_pad = 4 * EQ;
+    const int part_bytes = max(kRouteTokens * kRouteChunk * 8, kRouteTokens * P * E_pad * 8);
+    double* xs = reinterpret_cast<double*>(smem);                               // [TB][chunk] (phase 1)
+    double* part = reinterpret_cast<double*>(smem);                             // [TB][P][E_pad] (after)
+    float* wsq = reinterpret_cast<float*>(smem + part_bytes);                   // [P][E_pad]
+    double* xn = reinterpret_cast<double*>(wsq + P * E_pad);                    // [TB]
+    float* logit = reinterpret_cast<float*>(xn + kRouteTokens);                 // [TB][E_pad]
+    float* evs = logit + kRouteTokens * E_pad;                                  // [TB][E_pad]
+    int* fb_count = reinterpret_cast<int*>(evs + kRouteTokens * E_pad);         // [1]
+    int* fb_list = fb_count + 1;                                                // [kRouteFallbacks]
 
     const int tid = threadIdx.x;
-    const int e = tid % E_pad, q = tid / E_pad;
-    const int t0 = blockIdx.x * kRouteTokens;
+    const int quad = tid % EQ, p = tid / EQ;
+    const bool active = p < P;
+    const int t0 = blockIdx.y * kRouteTokens;
     const int nt = min(kRouteTokens, a.T - t0);
-    for (int i = tid; i < nt * H; i += blockDim.x) xs[i] = a.x[static_cast<size_t>(t0) * H + i];
-    __syncthreads();
+    const int h0 = rank * (H / KS), h1 = h0 + H / KS;
+    const bool vec4 = (E % 4) == 0;
+    if (tid == 0) *fb_count = 0;
 
-    const int L = (H + P - 1) / P;
-    const int i0 = min(H, q * L), i1 = min(H, i0 + L);
-    double acc[kRouteTokens];
-    float aab[kRouteTokens];
+    double acc[kRouteTokens][4];
+    float sq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int t = 0; t < kRouteTokens; ++t) {
-        acc[t] = 0.0;
-        aab[t] = 0.0f;
-    }
-    if (e < E) {
-        for (int i = i0; i < i1; ++i) {
-            const float wf = a.w[static_cast<size_t>(i) * E + e];
-            const double wd = static_cast<double>(wf);
-            const float wa = fabsf(wf);
+    for (int t = 0; t < kRouteTokens; ++t)
 #pragma unroll
-            for (int t = 0; t < kRouteTokens; ++t) {
-                const float xv = xs[t * H + i];
-                acc[t] = fma(static_cast<double>(xv), wd, acc[t]);
-                aab[t] = fmaf(fabsf(xv), wa, aab[t]);
+        for (int j = 0; j < 4; ++j) acc[t][j] = 0.0;
+
+    for (int c0 = h0; c0 < h1; c0 += kRouteChunk) {
+        const int cn = min(kRouteChunk, h1 - c0);
+        for (int idx = tid; idx < kRouteTokens * cn; idx += blockDim.x) {
+            const int t = idx / cn, i = idx % cn;
+            xs[t * kRouteChunk + i] = t < nt ? static_cast<double>(a.x[static_cast<size_t>(t0 + t) * H + c0 + i]) : 0.0;
+        }
+        __syncthreads();
+        if (active) {
+            // W rows are loaded two iterations ahead of their use.
+            auto load_w = [&](int i, float (&wv)[4]) {
+                if (i >= cn) return;
+                const float* wr = a.w + static_cast<size_t>(c0 + i) * E + 4 * quad;
+                if (vec4) {
+                    const float4 w4 = __ldg(reinterpret_cast<const float4*>(wr));
+                    wv[0] = w4.x; wv[1] = w4.y; wv[2] = w4.z; wv[3] = w4.w;
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) wv[j] = 4 * quad + j < E ? wr[j] : 0.0f;
+                }
+            };
+            float wn1[4] = {0.f, 0.f, 0.f, 0.f}, wn2[4] = {0.f, 0.f, 0.f, 0.f};
+            load_w(p, wn1);
+            load_w(p + P, wn2);
+            for (int i = p; i < cn; i += P) {
+                float wv[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    wv[j] = wn1[j];
+                    wn1[j] = wn2[j];
+                }
+                load_w(i + 2 * P, wn2);
+                double wd[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    wd[j] = static_cast<double>(wv[j]);
+                    sq[j] = fmaf(wv[j], wv[j], sq[j]);
+                }
+#pragma unroll
+                for (int t = 0; t < kRouteTokens; ++t) {
+                    if (t < nt) {
+                        const double xv = xs[t * kRouteChunk + i];
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) acc[t][j] = fma(xv, wd[j], acc[t][j]);
+                    }
+                }
             }
         }
+        __syncthreads();
     }
+    if (active) {
 #pragma unroll
-    for (int t = 0; t < kRouteTokens; ++t) {
-        part[(t * P + q) * E_pad + e] = acc[t];
-        absb[(t * P + q) * E_pad + e] = aab[t];
-    }
-    __syncthreads();
-
-    for (int t = q; t < nt && e < E; t += P) {
-        double s = 0.0;
-        float A = 0.0f;
-        for (int r = 0; r < P; ++r) {
-            s += part[(t * P + r) * E_pad + e];
-            A += absb[(t * P + r) * E_pad + e];
-        }
-        if (a.bias) {
-            s += static_cast<double>(a.bias[e]);
-            A += fabsf(a.bias[e]);
-        }
-        // A (FP32, positive terms) is within (H+2)*2^-23 of the true sum.
-        const double Aup = static_cast<double>(A) * (1.0 + (H + 2) * 0x1.0p-22) + 0x1.0p-140;
-        const double beta = static_cast<double>(H + L + P + 4) * 0x1.0p-53 * Aup * 1.01;
-        if (!rounding_certified(s, beta)) {
-            const float* xr = xs + t * H;
-            double seq = 0.0;
-            for (int i = 0; i < H; ++i)
-                seq = fma(static_cast<double>(xr[i]), static_cast<double>(a.w[static_cast<size_t>(i) * E + e]), seq);
-            if (a.bias) seq = fma(1.0, static_cast<double>(a.bias[e]), seq);
-            s = seq;
-            if (a.st) atomicAdd(&a.st->sequential_logits, 1);
-        }
-        if (!isfinite(s)) device_fail(a.st, HMOE_NON_FINITE_ROUTER);
-        logit[t * E_pad + e] = static_cast<float>(s);
-    }
-    __syncthreads();
-
-    const int warp = tid >> 5, lane = tid & 31;
-    const int nwarps = blockDim.x >> 5;
-    for (int t = warp; t < nt; t += nwarps) {
-        float lv[C];
+        for (int t = 0; t < kRouteTokens; ++t)
 #pragma unroll
-        for (int c = 0; c < C; ++c) {
-            const int j = lane + 32 * c;
-            lv[c] = j < E ? logit[t * E_pad + j] : 0.0f;
-        }
-        const size_t tok = static_cast<size_t>(t0 + t);
-        select_token<C>(lv, E, a.k, a.softmax, a.renorm, evs + t * E_pad,
-                        a.ids + tok * a.k, a.scores + tok * a.k, a.counts,
-                        a.st, false, nullptr);
+            for (int j = 0; j < 4; ++j) part[(t * P + p) * E_pad + 4 * quad + j] = acc[t][j];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) wsq[p * E_pad + 4 * quad + j] = sq[j];
     }
+    cluster.sync();
+
+    if (rank == 0) {
+        // ||x_t||^2 in double, one warp per token (this CTA covers all of H
+        // through the cluster, so the rows are read from global memory).
+        const int warp = tid >> 5, lane = tid & 31;
+        for (int t = warp; t < kRouteTokens; t += blockDim.x >> 5) {
+            double s = 0.0;
+            if (t < nt)
+                for (int i = lane; i < H; i += 32) {
+                    const double v = a.x[static_cast<size_t>(t0 + t) * H + i];
+                    s = fma(v, v, s);
+                }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            if (lane == 0) xn[t] = s;
+        }
+        __syncthreads();
+        // Phase 2: exact float logits.  Thread (quad, p) finalises token p;
+        // logits the certificate cannot settle are queued and recomputed in
+        // the reference's sequential order by whole warps (phase 2b).
+        for (int t = p; active && t < nt; t += P) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int e = 4 * quad + j;
+                if (e >= E) continue;
+                double s = 0.0;
+                float w2 = 0.0f;
+                for (int r = 0; r < KS; ++r) {
+                    const double* rp = cluster.map_shared_rank(part, r);
+                    const float* rw = cluster.map_shared_rank(wsq, r);
+                    for (int q = 0; q < P; ++q) {
+                        s += rp[(t * P + q) * E_pad + e];
+                        w2 += rw[q * E_pad + e];
+                    }
+                }
+                double A = sqrt(xn[t] * (1.0 + 0x1.0p-40)) *
+                           sqrt(static_cast<double>(w2) * (1.0 + (H + 64) * 0x1.0p-22)) * (1.0 + 0x1.0p-40);
+                if (a.bias) {
+                    s += static_cast<double>(a.bias[e]);
+                    A += fabs(static_cast<double>(a.bias[e]));
+                }
+                const int L = H / (P * KS) + 1;
+                const double beta = static_cast<double>(H + L + P * KS + 4) * 0x1.0p-53 * A * 1.01 + 0x1.0p-1060;
+                if (!rounding_certified(s, beta)) {
+                    const int slot = atomicAdd(fb_count, 1);
+                    if (slot < kRouteFallbacks) fb_list[slot] = t * 256 + e;
+                    else s = sequential_logit(a, t0 + t, e); // queue full: this thread does it
+                }
+                if (!isfinite(s)) device_fail(a.st, HMOE_NON_FINITE_ROUTER);
+                logit[t * E_pad + e] = static_cast<float>(s);
+            }
+        }
+        __syncthreads();
+        // Phase 2b: warp-cooperative sequential recomputation.
+        const int nfb = min(*fb_count, kRouteFallbacks);
+        for (int f = warp; f < nfb; f += blockDim.x >> 5) {
+            const int t = fb_list[f] >> 8, e = fb_list[f] & 255;
+            const float* xr = a.x + static_cast<size_t>(t0 + t) * H;
+            double s = 0.0;
+            for (int i0 = 0; i0 < H; i0 += 32) {
+                const int i = i0 + lane;
+                // products of two floats are exact in double
+                const double prod = i < H ? static_cast<double>(xr[i]) * static_cast<double>(a.w[static_cast<size_t>(i) * E + e]) : 0.0;
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) s += __shfl_sync(0xffffffffu, prod, jj);
+            }
+            if (a.bias) s += static_cast<double>(a.bias[e]);
+            if (lane == 0) {
+                if (!isfinite(s)) device_fail(a.st, HMOE_NON_FINITE_ROUTER);
+                logit[t * E_pad + e] = static_cast<float>(s);
+                if (a.st) atomicAdd(&a.st->sequential_logits, 1);
+            }
+        }
+        __syncthreads();
+        // Phase 3: softmax, selection, renormalisation; one warp per token.
+        for (int t = warp; t < nt; t += blockDim.x >> 5) {
+            float lv[C];
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+                const int j = lane + 32 * c;
+                lv[c] = j < E ? logit[t * E_pad + j] : 0.0f;
+            }
+            const size_t tok = static_cast<size_t>(t0 + t);
+            select_token<C>(lv, E, a.k, a.softmax, a.renorm, evs + t * E_pad, a.ids + tok * a.k,
+                            a.scores + tok * a.k, a.counts, a.st, false, nullptr);
+        }
+    }
+    cluster.sync(); // keep every CTA's shared memory alive until rank 0 is done
 }
 
 // kernels::routerTopK drop-in (CudaKernels.cu:152-204): one warp per token,
@@ -416,8 +531,9 @@ __global__ void __launch_bounds__(256) group_kernel(GroupArgs g) {
 
 // ------------------------------------------------------------ launchers
 
-int route_smem_bytes(int H, int E_pad, int P) {
-    return kRouteTokens * H * 4 + kRouteTokens * P * E_pad * (8 + 4) + 2 * kRouteTokens * E_pad * 4;
+int route_smem_bytes(int E_pad, int P) {
+    const int part = std::max(kRouteTokens * kRouteChunk * 8, kRouteTokens * P * E_pad * 8);
+    return part + P * E_pad * 4 + kRouteTokens * 8 + 2 * kRouteTokens * E_pad * 4 + (1 + kRouteFallbacks) * 4;
 }
 
 hmoe_status launch_route(const float* x, const float* w, const float* bias,
@@ -425,21 +541,41 @@ hmoe_status launch_route(const float* x, const float* w, const float* bias,
                          uint32_t* ids, float* scores, int32_t* counts,
                          DeviceStatus* st, cudaStream_t stream) {
     if (T <= 0) return HMOE_OK;
-    if (E <= 0 || E > kMaxExperts || k <= 0 || k > E || k > kMaxTopK || H <= 0)
+    if (E <= 0 || E > kMaxExperts || k <= 0 || k > E || k > kMaxTopK || H <= 0 || H % 8)
         return HMOE_INVALID_ARGUMENT;
-    const int E_pad = (E + 31) / 32 * 32;
-    int P = 1024 / E_pad;
-    while (P > 1 && P * 8 > H) P >>= 1; // keep chunks >= 8 long
-    const int smem = route_smem_bytes(H, E_pad, P);
-    if (smem > 227 * 1024) return HMOE_UNSUPPORTED;
+    const int EQ = (E + 3) / 4;
+    const int P = std::min(32, 256 / EQ); // row lanes; phase 2 maps token t to lane t mod P
+    if (EQ * P > 256 || P < 1) return HMOE_UNSUPPORTED;
+    const int E_pad = 4 * EQ;
+    const int smem = route_smem_bytes(E_pad, P);
+    const int rows = (T + kRouteTokens - 1) / kRouteTokens;
+    int KS = 1; // split H over a cluster when there are few token blocks
+    while (KS < 8 && rows * KS < 74 && (H / (KS * 2)) % 8 == 0 && H / (KS * 2) >= 64) KS *= 2;
     RouteArgs a{x, w, bias, T, H, E, k, softmax, renorm, ids, scores, counts, st};
-    const unsigned grid = static_cast<unsigned>((T + kRouteTokens - 1) / kRouteTokens);
-    const int C = E_pad / 32;
-#define HMOE_ROUTE_CASE(CC)                                                                       \
-    case CC:                                                                                      \
-        cudaFuncSetAttribute(route_kernel<CC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
-        route_kernel<CC><<<grid, E_pad * P, smem, stream>>>(a, E_pad, P);                          \
-        break;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(KS), static_cast<unsigned>(rows));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(KS);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const int C = (E + 31) / 32;
+    cudaError_t err = cudaErrorInvalidValue;
+#define HMOE_ROUTE_CASE(CC)                                                                          \
+    case CC: {                                                                                       \
+        static int attr_set = 0;                                                                     \
+        if (smem > attr_set) {                                                                       \
+            cudaFuncSetAttribute(route_kernel<CC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
+            attr_set = smem;                                                                         \
+        }                                                                                            \
+        err = cudaLaunchKernelEx(&cfg, route_kernel<CC>, a, EQ, P, KS);                              \
+        break;                                                                                       \
+    }
     switch (C) {
         HMOE_ROUTE_CASE(1)
         HMOE_ROUTE_CASE(2)
@@ -452,6 +588,10 @@ hmoe_status launch_route(const float* x, const float* w, const float* bias,
     default: return HMOE_UNSUPPORTED;
     }
 #undef HMOE_ROUTE_CASE
+    if (err != cudaSuccess) {
+        set_last_error("hmoe route kernel launch", err);
+        return HMOE_CUDA_ERROR;
+    }
     return check_launch("hmoe route kernel");
 }
 
