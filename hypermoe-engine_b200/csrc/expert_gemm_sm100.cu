@@ -211,62 +211,78 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
         device_fail(a.st, HMOE_TIMEOUT);
     };
 
+    // Role loops keep every warp converged: all 32 lanes run the loop and the
+    // waits, lane 0 alone issues TMA / MMA instructions, then __syncwarp.
     if (warp == 0) {
         // ------------------------------------------------ INT8 weight producer
         if (lane == 0) {
             sm100::prefetch_tmap(&tm_w0);
             sm100::prefetch_tmap(&tm_w1);
-            uint32_t it = 0;
-            for (int item = pair; item < n_items && !*abort_s; item += npairs) {
-                const int4 td = a.tiles[item / a.nblocks];
-                const int nb = item % a.nblocks;
-                // gate/up: both boxes at the CTA's 64 features; down: two
-                // adjacent 64-feature boxes of the CTA's 128 features
-                const int x0 = GATE_UP ? nb * 128 + 64 * static_cast<int>(rank) : nb * 256 + 128 * static_cast<int>(rank);
-                const int x1 = GATE_UP ? x0 : x0 + 64;
-                for (int kb = 0; kb < nkb; ++kb, ++it) {
-                    const int s = it % kWStages;
-                    if (it >= kWStages &&
-                        !sm100::mbar_wait(&empty_w[s], ((it / kWStages) - 1) & 1, abort_s, kWaitNs)) {
-                        fail();
-                        break;
-                    }
+        }
+        uint32_t it = 0;
+        for (int item = pair; item < n_items && !*abort_s; item += npairs) {
+            const int4 td = a.tiles[item / a.nblocks];
+            const int nb = item % a.nblocks;
+            // gate/up: both boxes at the CTA's 64 features; down: two
+            // adjacent 64-feature boxes of the CTA's 128 features
+            const int x0 = GATE_UP ? nb * 128 + 64 * static_cast<int>(rank) : nb * 256 + 128 * static_cast<int>(rank);
+            const int x1 = GATE_UP ? x0 : x0 + 64;
+            bool ok = true;
+            for (int kb = 0; kb < nkb; ++kb, ++it) {
+                const int s = it % kWStages;
+                if (it >= kWStages &&
+                    !sm100::mbar_wait(&empty_w[s], ((it / kWStages) - 1) & 1, abort_s, kWaitNs)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
                     sm100::mbar_arrive_expect_tx(&full_w[s], 2 * kSBytes);
                     sm100::tma_load_3d(S(s, 0), &tm_w0, x0, kb * kBK, td.x, &full_w[s]);
                     sm100::tma_load_3d(S(s, 1), &tm_w1, x1, kb * kBK, td.x, &full_w[s]);
                 }
+                __syncwarp();
             }
-            if (*abort_s) // drain this CTA's own loads before it exits
-                for (uint32_t i = (it > kWStages ? it - kWStages : 0); i < it; ++i)
-                    sm100::mbar_wait_for(&full_w[i % kWStages], (i / kWStages) & 1, kWaitNs);
+            if (!ok) {
+                if (lane == 0) fail();
+                break;
+            }
         }
+        if (*abort_s) // drain this CTA's own loads before it exits
+            for (uint32_t i = (it > kWStages ? it - kWStages : 0); i < it; ++i)
+                sm100::mbar_wait_for(&full_w[i % kWStages], (i / kWStages) & 1, kWaitNs);
     } else if (warp == 1) {
         // ------------------------------------------------ BF16 token-tile producer
-        if (lane == 0) {
-            sm100::prefetch_tmap(&tm_b);
-            uint32_t it = 0;
-            for (int item = pair; item < n_items && !*abort_s; item += npairs) {
-                const int4 td = a.tiles[item / a.nblocks];
-                const int half = ((td.z + 15) & ~15) >> 1;
-                const int y = td.y + static_cast<int>(rank) * half;
-                for (int kb = 0; kb < nkb; ++kb, ++it) {
-                    const int s = it % kBStages;
-                    if (it >= kBStages &&
-                        !sm100::mbar_wait(&empty_b[s], ((it / kBStages) - 1) & 1, abort_s, kWaitNs)) {
-                        fail();
-                        break;
-                    }
+        if (lane == 0) sm100::prefetch_tmap(&tm_b);
+        uint32_t it = 0;
+        for (int item = pair; item < n_items && !*abort_s; item += npairs) {
+            const int4 td = a.tiles[item / a.nblocks];
+            const int half = ((td.z + 15) & ~15) >> 1;
+            const int y = td.y + static_cast<int>(rank) * half;
+            bool ok = true;
+            for (int kb = 0; kb < nkb; ++kb, ++it) {
+                const int s = it % kBStages;
+                if (it >= kBStages &&
+                    !sm100::mbar_wait(&empty_b[s], ((it / kBStages) - 1) & 1, abort_s, kWaitNs)) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
                     if (leader) sm100::mbar_arrive_expect_tx(&full_b[s], 2 * kBBytes);
                     sm100::tma_load_2d_pair(B(s), &tm_b, kb * kBK, y,
                                             sm100::map_shared(sm100::smem_u32(&full_b[s]), 0));
                 }
+                __syncwarp();
             }
-            // Loads in flight complete on the leader's barriers; the teardown
-            // cluster barrier below keeps both CTAs alive until then.
+            if (!ok) {
+                if (lane == 0) fail();
+                break;
+            }
         }
+        // Loads in flight complete on the leader's barriers; the teardown
+        // cluster barrier below keeps both CTAs alive until then.
     } else if (warp == 2) {
         // ------------------------------------------------ MMA issuer (leader)
-        if (leader && lane == 0) {
+        if (leader) {
             uint32_t it = 0;
             int j = 0;
             for (int item = pair; item < n_items && !*abort_s; item += npairs, ++j) {
@@ -275,7 +291,7 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
                 const uint32_t idesc = sm100::make_idesc_bf16(256, nmma, true, false);
                 const int buf = j & 1;
                 if (j >= 2 && !sm100::mbar_wait_cluster(&accempty[buf], ((j >> 1) - 1) & 1, abort_s, kWaitNs)) {
-                    fail();
+                    if (lane == 0) fail();
                     break;
                 }
                 sm100::tc_fence_after();
@@ -285,25 +301,32 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
                     const int as = it % kAStages, bs = it % kBStages;
                     if (!sm100::mbar_wait_cluster(&full_b[bs], (it / kBStages) & 1, abort_s, kWaitNs) ||
                         !sm100::mbar_wait_cluster(&aready[as], (it / kAStages) & 1, abort_s, kWaitNs)) {
-                        fail();
                         ok = false;
                         break;
                     }
                     sm100::tc_fence_after();
-                    const uint32_t a0 = sm100::smem_u32(A(as)), b0 = sm100::smem_u32(B(bs));
+                    if (lane == 0) {
+                        const uint32_t a0 = sm100::smem_u32(A(as)), b0 = sm100::smem_u32(B(bs));
 #pragma unroll
-                    for (int ks = 0; ks < kBK / 16; ++ks) {
-                        const uint64_t ad = sm100::make_smem_desc(a0 + ks * 2048, 8192, 1024, 2);
-                        const uint64_t bd = sm100::make_smem_desc(b0 + ks * 32, 16, 1024, 2);
-                        sm100::mma_bf16_pair(d0, ad, bd, idesc, (kb | ks) != 0);
+                        for (int ks = 0; ks < kBK / 16; ++ks) {
+                            const uint64_t ad = sm100::make_smem_desc(a0 + ks * 2048, 8192, 1024, 2);
+                            const uint64_t bd = sm100::make_smem_desc(b0 + ks * 32, 16, 1024, 2);
+                            sm100::mma_bf16_pair(d0, ad, bd, idesc, (kb | ks) != 0);
+                        }
+                        sm100::mma_commit_pair(&empty_a[as], 0x3);
+                        sm100::mma_commit_pair(&empty_b[bs], 0x3);
                     }
-                    sm100::mma_commit_pair(&empty_a[as], 0x3);
-                    sm100::mma_commit_pair(&empty_b[bs], 0x3);
+                    __syncwarp();
                 }
-                if (!ok) break;
-                sm100::mma_commit_pair(&accfull[buf], 0x3);
+                if (!ok) {
+                    if (lane == 0) fail();
+                    break;
+                }
+                if (lane == 0) sm100::mma_commit_pair(&accfull[buf], 0x3);
+                __syncwarp();
             }
-            sm100::mma_commit_pair(drain, 0x3); // completes once every MMA has finished
+            if (lane == 0) sm100::mma_commit_pair(drain, 0x3); // completes once every MMA has finished
+            __syncwarp();
         }
     } else if (warp < 3 + kDequantWarps) {
         // ------------------------------------------------ dequantise

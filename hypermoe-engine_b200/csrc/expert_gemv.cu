@@ -26,13 +26,13 @@ namespace cg = cooperative_groups;
 
 namespace hmoe {
 
-constexpr int kGemvWarps = 4;
+constexpr int kGemvWarps = 8;
 constexpr int kGemvCols = 256; // 32 lanes x 8 columns
-constexpr int kGemvTokens = 4; // tokens per pass
+constexpr int kGemvRows = 8;   // weight rows in flight per lane
 
 
 
-template <bool GATE_UP>
+template <bool GATE_UP, int kGemvTokens>
 __global__ void __launch_bounds__(kGemvWarps * 32) expert_gemv_kernel(GemvArgs a) {
     constexpr int NP = GATE_UP ? 2 : 1;
     extern __shared__ __align__(16) float gsm[];
@@ -83,26 +83,41 @@ __global__ void __launch_bounds__(kGemvWarps * 32) expert_gemv_kernel(GemvArgs a
 #pragma unroll
                 for (int c = 0; c < 8; ++c) acc[t][p][c] = 0.0f;
         if (col_ok) {
-#pragma unroll 4
-            for (int kk = warp; kk < kc; kk += kGemvWarps) {
-                const size_t off = static_cast<size_t>(kb + kk) * N + col;
-                const uint2 q0 = __ldg(reinterpret_cast<const uint2*>(w0 + off));
-                float wv[NP][8];
-                dequant4(q0.x, zp0, &wv[0][0]);
-                dequant4(q0.y, zp0, &wv[0][4]);
-                if constexpr (GATE_UP) {
-                    const uint2 q1 = __ldg(reinterpret_cast<const uint2*>(w1 + off));
-                    dequant4(q1.x, zp1, &wv[1][0]);
-                    dequant4(q1.y, zp1, &wv[1][4]);
+            // kGemvRows weight rows per lane are loaded before any is used,
+            // so every lane keeps kGemvRows x NP 8-byte loads in flight.
+            for (int k0 = warp; k0 < kc; k0 += kGemvWarps * kGemvRows) {
+                uint2 qv[kGemvRows][NP];
+#pragma unroll
+                for (int r = 0; r < kGemvRows; ++r) {
+                    const int kk = k0 + r * kGemvWarps;
+                    if (kk < kc) {
+                        const size_t off = static_cast<size_t>(kb + kk) * N + col;
+                        qv[r][0] = __ldg(reinterpret_cast<const uint2*>(w0 + off));
+                        if constexpr (GATE_UP) qv[r][1] = __ldg(reinterpret_cast<const uint2*>(w1 + off));
+                    } else {
+                        qv[r][0] = make_uint2(0u, 0u);
+                        if constexpr (GATE_UP) qv[r][1] = make_uint2(0u, 0u);
+                    }
                 }
 #pragma unroll
-                for (int t = 0; t < kGemvTokens; ++t) {
-                    if (t < nj) {
-                        const float xv = xs[t * KP + kk];
+                for (int r = 0; r < kGemvRows; ++r) {
+                    const int kk = k0 + r * kGemvWarps;
+                    if (kk >= kc) break;
+                    float wv[NP][8];
 #pragma unroll
-                        for (int p = 0; p < NP; ++p)
+                    for (int p = 0; p < NP; ++p) {
+                        dequant4(qv[r][p].x, p ? zp1 : zp0, &wv[p][0]);
+                        dequant4(qv[r][p].y, p ? zp1 : zp0, &wv[p][4]);
+                    }
 #pragma unroll
-                            for (int c = 0; c < 8; ++c) acc[t][p][c] = fmaf(xv, wv[p][c], acc[t][p][c]);
+                    for (int t = 0; t < kGemvTokens; ++t) {
+                        if (t < nj) {
+                            const float xv = xs[t * KP + kk];
+#pragma unroll
+                            for (int p = 0; p < NP; ++p)
+#pragma unroll
+                                for (int c = 0; c < 8; ++c) acc[t][p][c] = fmaf(xv, wv[p][c], acc[t][p][c]);
+                        }
                     }
                 }
             }
@@ -149,17 +164,31 @@ __global__ void __launch_bounds__(kGemvWarps * 32) expert_gemv_kernel(GemvArgs a
     }
 }
 
-size_t gemv_smem_bytes(int K, int KS, bool gate_up) {
+size_t gemv_smem_bytes(int K, int KS, bool gate_up, int tokens) {
     const int NP = gate_up ? 2 : 1;
     const int KP = (K + KS - 1) / KS;
-    return static_cast<size_t>(kGemvTokens * KP + kGemvWarps * kGemvTokens * NP * kGemvCols +
-                               kGemvTokens * NP * kGemvCols) * sizeof(float);
+    return static_cast<size_t>(tokens * KP + kGemvWarps * tokens * NP * kGemvCols + tokens * NP * kGemvCols) *
+           sizeof(float);
 }
 
-hmoe_status launch_expert_gemv(bool gate_up, const GemvArgs& args, int list_capacity,
+template <bool GATE_UP, int TOK>
+cudaError_t launch_gemv_variant(cudaLaunchConfig_t& cfg, const GemvArgs& args) {
+    static size_t attr_set = 0;
+    if (cfg.dynamicSmemBytes > attr_set) {
+        cudaFuncSetAttribute(expert_gemv_kernel<GATE_UP, TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(cfg.dynamicSmemBytes));
+        attr_set = cfg.dynamicSmemBytes;
+    }
+    return cudaLaunchKernelEx(&cfg, expert_gemv_kernel<GATE_UP, TOK>, args);
+}
+
+hmoe_status launch_expert_gemv(bool gate_up, const GemvArgs& args, int list_capacity, int max_tokens,
                                cudaStream_t stream) {
     if (list_capacity <= 0) return HMOE_OK;
-    const size_t smem = gemv_smem_bytes(args.K, args.KS, gate_up);
+    // One token per pass when no expert can hold more (a single-token
+    // batch without shared experts); otherwise four.
+    const int tok = max_tokens <= 1 ? 1 : 4;
+    const size_t smem = gemv_smem_bytes(args.K, args.KS, gate_up, tok);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(args.KS), static_cast<unsigned>((args.N + kGemvCols - 1) / kGemvCols),
                        static_cast<unsigned>(list_capacity));
@@ -174,17 +203,10 @@ hmoe_status launch_expert_gemv(bool gate_up, const GemvArgs& args, int list_capa
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t err;
-    static size_t attr_set[2] = {0, 0};
-    if (smem > attr_set[gate_up]) {
-        cudaFuncSetAttribute(gate_up ? expert_gemv_kernel<true> : expert_gemv_kernel<false>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        attr_set[gate_up] = smem;
-    }
-    if (gate_up) {
-        err = cudaLaunchKernelEx(&cfg, expert_gemv_kernel<true>, args);
-    } else {
-        err = cudaLaunchKernelEx(&cfg, expert_gemv_kernel<false>, args);
-    }
+    if (gate_up)
+        err = tok == 1 ? launch_gemv_variant<true, 1>(cfg, args) : launch_gemv_variant<true, 4>(cfg, args);
+    else
+        err = tok == 1 ? launch_gemv_variant<false, 1>(cfg, args) : launch_gemv_variant<false, 4>(cfg, args);
     if (err != cudaSuccess) {
         set_last_error("hmoe expert GEMV launch", err);
         return HMOE_CUDA_ERROR;

@@ -41,8 +41,17 @@ int g_variant = 0;
 cudaEvent_t g_stage_events[6];
 int g_stage_count = 0;
 
+// Records stage event i.  Under stream capture the record becomes an
+// external event node, so the caller can still synchronise on and time the
+// event after each graph launch.
 inline void stage(int i, cudaStream_t s) {
-    if (g_stage_count == 6) cudaEventRecord(g_stage_events[i], s);
+    if (g_stage_count != 6) return;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(s, &cs);
+    if (cs == cudaStreamCaptureStatusActive)
+        cudaEventRecordWithFlags(g_stage_events[i], s, cudaEventRecordExternal);
+    else
+        cudaEventRecord(g_stage_events[i], s);
 }
 
 Workspace plan_workspace(const hmoe_layer_desc& d, size_t T, int local_experts) {
@@ -180,6 +189,9 @@ hmoe_status enqueue_experts(const hmoe_layer_desc& d, const float* x, size_t T, 
     const int shared_small = (static_cast<long>(T) <= small_max) ? S : 0;
     const int small_cap = small_max <= 0 ? 0 : static_cast<int>(std::min<long>(E, assignments)) + shared_small;
     const int large_cap = static_cast<int>(std::min<long>(E, assignments / (small_max + 1))) + (S - shared_small);
+    // Largest possible group: T tokens (a shared expert, or one routed expert
+    // taking every token).
+    const int max_group = static_cast<int>(T);
     GemvArgs g{};
     g.list = reinterpret_cast<int32_t*>(ws + w.small_list);
     g.list_size = reinterpret_cast<int32_t*>(ws + w.list_sizes);
@@ -200,7 +212,7 @@ hmoe_status enqueue_experts(const hmoe_layer_desc& d, const float* x, size_t T, 
         g.K = H;
         g.N = I;
         g.KS = choose_split(small_cap, (I + 255) / 256);
-        r = launch_expert_gemv(true, g, small_cap, s);
+        r = launch_expert_gemv(true, g, small_cap, max_group, s);
         if (r != HMOE_OK) return r;
     }
     if (large_cap > 0) {
@@ -218,7 +230,7 @@ hmoe_status enqueue_experts(const hmoe_layer_desc& d, const float* x, size_t T, 
         g.K = I;
         g.N = H;
         g.KS = choose_split(small_cap, (H + 255) / 256);
-        r = launch_expert_gemv(false, g, small_cap, s);
+        r = launch_expert_gemv(false, g, small_cap, max_group, s);
         if (r != HMOE_OK) return r;
     }
     if (large_cap > 0) {

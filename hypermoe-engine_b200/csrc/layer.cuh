@@ -37,7 +37,7 @@ struct GemvArgs {
     int K, N, KS;
 };
 
-hmoe_status launch_expert_gemv(bool gate_up, const GemvArgs& args, int list_capacity,
+hmoe_status launch_expert_gemv(bool gate_up, const GemvArgs& args, int list_capacity, int max_tokens,
                                cudaStream_t stream);
 
 bool gemm_available();

@@ -28,6 +28,7 @@
 //    float(double(e)/D), selection (score desc, id asc), renormalisation by
 //    a double sum in rank order -- all as in the reference.
 #include "common.cuh"
+#include "sm100.cuh"
 
 #include <cooperative_groups.h>
 
@@ -42,6 +43,7 @@ namespace hmoe {
 constexpr int kRouteTokens = 8;  // tokens per CTA in the fused router
 constexpr int kRouteChunk = 1024; // hidden rows staged per pass (as doubles)
 constexpr int kRouteFallbacks = 64; // queued sequential recomputations per CTA
+constexpr int kRouteSlab = 32;      // router-matrix rows per bulk copy
 constexpr int kMaxExperts = 256; // E_pad <= 256 (8 candidates per lane)
 constexpr int kMaxTopK = 32;
 
@@ -98,10 +100,28 @@ __device__ void select_token(const float (&lv)[C], int E, int k, int softmax,
             if (j < E) ev_smem[j] = e;
         }
         __syncwarp();
+        // The reference sums the E floats in double in expert order.  When
+        // every term is >= 2^-22 all of them are multiples of 2^-45 and the
+        // total is below 2^8, so the double sum is exact in any order and a
+        // tree sum gives the same bits; otherwise sum sequentially.
         double den = 0.0;
-        if (lane == 0)
-            for (int j = 0; j < E; ++j) den += static_cast<double>(ev_smem[j]);
-        den = __shfl_sync(0xffffffffu, den, 0);
+        bool small = false;
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            const int j = lane + 32 * c;
+            if (j < E) {
+                den += static_cast<double>(p[c]);
+                small |= p[c] < 0x1.0p-22f;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+        if (__any_sync(0xffffffffu, small)) {
+            den = 0.0;
+            if (lane == 0)
+                for (int j = 0; j < E; ++j) den += static_cast<double>(ev_smem[j]);
+            den = __shfl_sync(0xffffffffu, den, 0);
+        }
         __syncwarp();
         if (!(isfinite(den) && den > 0.0)) ok = false;
 #pragma unroll
@@ -193,6 +213,16 @@ __device__ void select_token(const float (&lv)[C], int E, int k, int softmax,
     }
 }
 
+// Byte offset of the router-matrix slabs in the fused router's shared memory
+// (after x/partials, squared norms, token norms, logits, exp scratch and the
+// fallback queue), rounded up to 16 bytes for the bulk copies.
+__host__ __device__ inline int route_slab_offset(int E_pad, int P) {
+    const int part = (kRouteTokens * kRouteChunk * 8 > kRouteTokens * P * E_pad * 8) ? kRouteTokens * kRouteChunk * 8
+                                                                                      : kRouteTokens * P * E_pad * 8;
+    const int bytes = part + P * E_pad * 4 + kRouteTokens * 8 + 2 * kRouteTokens * E_pad * 4 + (1 + kRouteFallbacks) * 4;
+    return (bytes + 15) & ~15;
+}
+
 // The reference's sequential double accumulation for one (token, expert),
 // by a single thread (used only when the per-CTA queue overflows).
 __device__ double sequential_logit(const RouteArgs& a, int tok, int e) {
@@ -215,7 +245,7 @@ __device__ double sequential_logit(const RouteArgs& a, int tok, int e) {
 // order (rank, p).  The certificate bounds sum_i |x_i W_ie| by
 // ||x|| ||W_e|| (Cauchy-Schwarz).
 template <int C>
-__global__ void __launch_bounds__(256) route_kernel(RouteArgs a, int EQ, int P, int KS) {
+__global__ void __launch_bounds__(256, 2) route_kernel(RouteArgs a, int EQ, int P, int KS) {
     extern __shared__ __align__(16) unsigned char smem[];
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = static_cast<int>(cluster.block_rank());
@@ -230,6 +260,8 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a, int EQ, int P, 
     float* evs = logit + kRouteTokens * E_pad;                                  // [TB][E_pad]
     int* fb_count = reinterpret_cast<int*>(evs + kRouteTokens * E_pad);         // [1]
     int* fb_list = fb_count + 1;                                                // [kRouteFallbacks]
+    float* wsl = reinterpret_cast<float*>(smem + route_slab_offset(E_pad, P));  // [2][slab][E]
+    uint64_t* wbar = reinterpret_cast<uint64_t*>(wsl + 2 * kRouteSlab * E_pad); // [2]
 
     const int tid = threadIdx.x;
     const int quad = tid % EQ, p = tid / EQ;
@@ -247,37 +279,49 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a, int EQ, int P, 
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[t][j] = 0.0;
 
-    for (int c0 = h0; c0 < h1; c0 += kRouteChunk) {
-        const int cn = min(kRouteChunk, h1 - c0);
-        for (int idx = tid; idx < kRouteTokens * cn; idx += blockDim.x) {
-            const int t = idx / cn, i = idx % cn;
-            xs[t * kRouteChunk + i] = t < nt ? static_cast<double>(a.x[static_cast<size_t>(t0 + t) * H + c0 + i]) : 0.0;
+    // Router rows stream through shared memory in slabs of kRouteSlab rows
+    // (contiguous in [H, E] layout), double-buffered with bulk copies, while
+    // the token rows are staged as doubles kRouteChunk rows at a time.
+    const int nslab = (h1 - h0 + kRouteSlab - 1) / kRouteSlab;
+    if (tid == 0) {
+        sm100::mbar_init(&wbar[0], 1);
+        sm100::mbar_init(&wbar[1], 1);
+        sm100::fence_mbarrier_init();
+    }
+    __syncthreads();
+    auto issue_slab = [&](int sl) {
+        const int r0 = h0 + sl * kRouteSlab;
+        const int nr = min(kRouteSlab, h1 - r0);
+        sm100::mbar_arrive_expect_tx(&wbar[sl & 1], static_cast<uint32_t>(nr * E * 4));
+        sm100::bulk_load(wsl + (sl & 1) * kRouteSlab * E, a.w + static_cast<size_t>(r0) * E,
+                         static_cast<uint32_t>(nr * E * 4), &wbar[sl & 1]);
+    };
+    if (tid == 0 && nslab > 0) issue_slab(0);
+    for (int sl = 0; sl < nslab; ++sl) {
+        const int r0 = h0 + sl * kRouteSlab;
+        const int nr = min(kRouteSlab, h1 - r0);
+        if ((r0 - h0) % kRouteChunk == 0) { // stage the next token chunk
+            const int cn = min(kRouteChunk, h1 - r0);
+            for (int idx = tid; idx < kRouteTokens * cn; idx += blockDim.x) {
+                const int t = idx / cn, i = idx % cn;
+                xs[t * kRouteChunk + i] = t < nt ? static_cast<double>(a.x[static_cast<size_t>(t0 + t) * H + r0 + i]) : 0.0;
+            }
+            __syncthreads();
         }
-        __syncthreads();
+        if (tid == 0 && sl + 1 < nslab) issue_slab(sl + 1); // other buffer: freed by the last barrier
+        if (!sm100::mbar_wait_for(&wbar[sl & 1], (sl >> 1) & 1, 2000000000ull)) device_fail(a.st, HMOE_TIMEOUT);
+        const float* ws = wsl + (sl & 1) * kRouteSlab * E;
+        const int xoff = (r0 - h0) % kRouteChunk;
         if (active) {
-            // W rows are loaded two iterations ahead of their use.
-            auto load_w = [&](int i, float (&wv)[4]) {
-                if (i >= cn) return;
-                const float* wr = a.w + static_cast<size_t>(c0 + i) * E + 4 * quad;
+            for (int i = p; i < nr; i += P) {
+                float wv[4];
                 if (vec4) {
-                    const float4 w4 = __ldg(reinterpret_cast<const float4*>(wr));
+                    const float4 w4 = *reinterpret_cast<const float4*>(ws + i * E + 4 * quad);
                     wv[0] = w4.x; wv[1] = w4.y; wv[2] = w4.z; wv[3] = w4.w;
                 } else {
 #pragma unroll
-                    for (int j = 0; j < 4; ++j) wv[j] = 4 * quad + j < E ? wr[j] : 0.0f;
+                    for (int j = 0; j < 4; ++j) wv[j] = 4 * quad + j < E ? ws[i * E + 4 * quad + j] : 0.0f;
                 }
-            };
-            float wn1[4] = {0.f, 0.f, 0.f, 0.f}, wn2[4] = {0.f, 0.f, 0.f, 0.f};
-            load_w(p, wn1);
-            load_w(p + P, wn2);
-            for (int i = p; i < cn; i += P) {
-                float wv[4];
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    wv[j] = wn1[j];
-                    wn1[j] = wn2[j];
-                }
-                load_w(i + 2 * P, wn2);
                 double wd[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -287,7 +331,7 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a, int EQ, int P, 
 #pragma unroll
                 for (int t = 0; t < kRouteTokens; ++t) {
                     if (t < nt) {
-                        const double xv = xs[t * kRouteChunk + i];
+                        const double xv = xs[t * kRouteChunk + xoff + i];
 #pragma unroll
                         for (int j = 0; j < 4; ++j) acc[t][j] = fma(xv, wd[j], acc[t][j]);
                     }
@@ -304,6 +348,21 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a, int EQ, int P, 
 #pragma unroll
         for (int j = 0; j < 4; ++j) wsq[p * E_pad + 4 * quad + j] = sq[j];
     }
+    __syncthreads();
+    // Fold this CTA's row lanes in fixed order q = 0..P-1 into row 0 of each
+    // token's partial block (and of wsq), so the cluster reduction below
+    // reads one value per CTA.
+    for (int idx = tid; idx < kRouteTokens * E_pad; idx += blockDim.x) {
+        const int t = idx / E_pad, e = idx % E_pad;
+        double s = 0.0;
+        for (int q = 0; q < P; ++q) s += part[(t * P + q) * E_pad + e];
+        part[(t * P) * E_pad + e] = s;
+        if (t == 0) {
+            float w2 = 0.0f;
+            for (int q = 0; q < P; ++q) w2 += wsq[q * E_pad + e];
+            wsq[e] = w2;
+        }
+    }
     cluster.sync();
 
     if (rank == 0) {
@@ -312,11 +371,26 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a, int EQ, int P, 
         const int warp = tid >> 5, lane = tid & 31;
         for (int t = warp; t < kRouteTokens; t += blockDim.x >> 5) {
             double s = 0.0;
-            if (t < nt)
-                for (int i = lane; i < H; i += 32) {
-                    const double v = a.x[static_cast<size_t>(t0 + t) * H + i];
-                    s = fma(v, v, s);
+            if (t < nt) {
+                // 8 independent partial sums keep 8 loads in flight per lane
+                // (the norm only feeds an upper bound, so order is free).
+                const float* xr = a.x + static_cast<size_t>(t0 + t) * H;
+                double sp[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                int i = lane;
+                for (; i + 7 * 32 < H; i += 8 * 32) {
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) {
+                        const double v = xr[i + u * 32];
+                        sp[u] = fma(v, v, sp[u]);
+                    }
                 }
+                for (; i < H; i += 32) {
+                    const double v = xr[i];
+                    sp[0] = fma(v, v, sp[0]);
+                }
+#pragma unroll
+                for (int u = 0; u < 8; ++u) s += sp[u];
+            }
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
             if (lane == 0) xn[t] = s;
@@ -325,20 +399,21 @@ __global__ void __launch_bounds__(256) route_kernel(RouteArgs a, int EQ, int P, 
         // Phase 2: exact float logits.  Thread (quad, p) finalises token p;
         // logits the certificate cannot settle are queued and recomputed in
         // the reference's sequential order by whole warps (phase 2b).
-        for (int t = p; active && t < nt; t += P) {
+        for (int idx = tid; idx < nt * E; idx += blockDim.x) {
+            const int t = idx / E, e = idx % E;
+            {
+                double pr[8];
+                float wr[8];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int e = 4 * quad + j;
-                if (e >= E) continue;
+                for (int r = 0; r < 8; ++r) { // issue every remote load first
+                    pr[r] = r < KS ? cluster.map_shared_rank(part, r)[(t * P) * E_pad + e] : 0.0;
+                    wr[r] = r < KS ? cluster.map_shared_rank(wsq, r)[e] : 0.0f;
+                }
                 double s = 0.0;
                 float w2 = 0.0f;
                 for (int r = 0; r < KS; ++r) {
-                    const double* rp = cluster.map_shared_rank(part, r);
-                    const float* rw = cluster.map_shared_rank(wsq, r);
-                    for (int q = 0; q < P; ++q) {
-                        s += rp[(t * P + q) * E_pad + e];
-                        w2 += rw[q * E_pad + e];
-                    }
+                    s += pr[r];
+                    w2 += wr[r];
                 }
                 double A = sqrt(xn[t] * (1.0 + 0x1.0p-40)) *
                            sqrt(static_cast<double>(w2) * (1.0 + (H + 64) * 0x1.0p-22)) * (1.0 + 0x1.0p-40);
@@ -532,8 +607,7 @@ __global__ void __launch_bounds__(256) group_kernel(GroupArgs g) {
 // ------------------------------------------------------------ launchers
 
 int route_smem_bytes(int E_pad, int P) {
-    const int part = std::max(kRouteTokens * kRouteChunk * 8, kRouteTokens * P * E_pad * 8);
-    return part + P * E_pad * 4 + kRouteTokens * 8 + 2 * kRouteTokens * E_pad * 4 + (1 + kRouteFallbacks) * 4;
+    return route_slab_offset(E_pad, P) + 2 * kRouteSlab * E_pad * 4 + 16;
 }
 
 hmoe_status launch_route(const float* x, const float* w, const float* bias,
