@@ -19,9 +19,11 @@ with events the library records at stage boundaries.  `cpu_baseline` is the
 reference's own CPU implementation (oracle/_ref, compiled from its sources)
 on a bounded token sample, on this host's cores.
 
-Multi-GPU (torchrun, one process per GPU): every rank holds the whole layer
-and routes its own 4096 tokens -- independent replicas, weak scaling -- until
-expert parallelism replaces it; the time is the max over ranks.
+Multi-GPU (torchrun, one process per GPU): expert parallelism through
+hmoe_ep_moe_forward.  Rank r holds its contiguous share of the 128 routed
+experts and routes its own 4096 tokens (weak scaling); rows travel to the
+expert owners and back over NCCL point-to-point on NVLink.  The step time is
+the max over ranks.
 """
 from __future__ import annotations
 
@@ -123,19 +125,24 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def algorithmic(cfg, T, ids_np, offsets_np):
-    """Algorithmic bytes and FLOPs per stage for one layer call."""
+def algorithmic(cfg, T, U, rows_in=None, local_experts=None):
+    """Algorithmic bytes and FLOPs per stage of one layer call on one GPU.
+
+    U: experts with at least one row on this GPU (weights streamed once);
+    rows_in: expert rows this GPU computes (T*(k+S) on one GPU; the received
+    rows plus the shared-expert rows under expert parallelism)."""
     H, I, E, k, S = cfg.hidden, cfg.intermediate, cfg.experts, cfg.top_k, cfg.shared_experts
-    counts = offsets_np[1:] - offsets_np[:-1]
-    U = int((counts > 0).sum()) + S
     rows = T * (k + S)
+    rin = rows if rows_in is None else rows_in
     return {
         "route": {"bytes": T * H * 4 + H * E * 4 + T * k * 8, "flops": 2 * T * H * E},
-        "group": {"bytes": T * k * 8 * 2, "flops": 0},
-        "gate_up": {"bytes": U * 2 * H * I + rows * H * 4 + rows * I * 4, "flops": 4 * rows * H * I},
-        "down": {"bytes": U * H * I + rows * I * 4 + rows * H * 4, "flops": 2 * rows * H * I},
-        "combine": {"bytes": rows * H * 4 + T * H * 4, "flops": 0},
-        "layer": {"bytes": U * 3 * H * I + H * E * 4 + 8 * T * H, "flops": T * (2 * H * E + (k + S) * 6 * H * I)},
+        # grouping ids/scores, then each token row read once and written as BF16 rows
+        "group": {"bytes": T * k * 8 * 2 + T * H * 4 + rows * H * 2, "flops": 0},
+        "gate_up": {"bytes": U * 2 * H * I + rin * H * 2 + rin * I * 2, "flops": 4 * rin * H * I},
+        "down": {"bytes": U * H * I + rin * I * 2 + rin * H * 2, "flops": 2 * rin * H * I},
+        "combine": {"bytes": rows * H * 2 + T * H * 4, "flops": 0},
+        "layer": {"bytes": U * 3 * H * I + H * E * 4 + 8 * T * H,
+                  "flops": 2 * T * H * E + rin * 6 * H * I},
         "unique_experts": U,
     }
 
@@ -209,6 +216,7 @@ def main():
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist = None
+    comm = None
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
@@ -216,9 +224,24 @@ def main():
     H.set_variant(args.variant)
     host_layer = H.make_host_layer(cfg, seed=args.seed)
     x_np = H.make_tokens(cfg, T, seed=args.seed + 7919 * rank)
-    layer = H.DeviceLayer(host_layer, dev)
+    if world > 1:
+        # expert parallelism: this rank holds its contiguous share of the
+        # routed experts; tokens stay on their rank (weak scaling)
+        uid = [H.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = H.EpComm(uid[0], rank, world, timeout_ms=120000)
+        layer = H.EpLayer(host_layer, comm, dev)
+    else:
+        layer = H.DeviceLayer(host_layer, dev)
     x = torch.from_numpy(x_np).to(dev)
     y = torch.empty_like(x)
+
+    def forward():
+        if comm is not None:
+            layer.forward(x, y, max_tokens=T)
+        else:
+            layer.forward(x, y)
+
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
@@ -233,33 +256,42 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    # routing facts for the algorithmic byte/FLOP counts
-    ids, scores, offsets, _, _ = layer.route(x)
-    torch.cuda.synchronize()
-    alg = algorithmic(cfg, T, ids.cpu().numpy(), offsets.cpu().numpy())
-
     for _ in range(args.warmup):
-        layer.forward(x, y)
+        forward()
     barrier()
 
-    # One layer call, stage events included, captured once into a CUDA graph
-    # (hmoe_moe_forward allocates nothing and never synchronises, so it is
-    # capturable for a fixed token count); each timed step replays it.
+    # routing facts for the algorithmic byte/FLOP counts
+    if comm is None:
+        _, _, offsets, _, _ = layer.route(x)
+        torch.cuda.synchronize()
+        counts = np.diff(offsets.cpu().numpy())
+        alg = algorithmic(cfg, T, int((counts > 0).sum()) + cfg.shared_experts)
+    else:
+        plan = comm.last_plan()
+        rows_in = int(plan.recv_total) + T * cfg.shared_experts
+        # every local expert counted as touched (an upper bound on the bytes)
+        alg = algorithmic(cfg, T, int(plan.local_experts) + cfg.shared_experts, rows_in)
+        alg["rows_received"] = int(plan.recv_total)
+
+    # Single GPU: one layer call, stage events included, captured once into a
+    # CUDA graph (hmoe_moe_forward allocates nothing and never synchronises,
+    # so it is capturable for a fixed token count); each timed step replays
+    # it.  Expert parallelism reads the exchanged counts on the host once per
+    # call, so it runs eagerly.
     H.check("stage events", H.lib().hmoe_set_stage_events(arr, 6))
     graph = None
     per_forward = None
-    if not args.eager:
-        c0 = H.lib().hmoe_launch_count()
+    if not args.eager and comm is None:
         side = torch.cuda.Stream()
         side.wait_stream(stream)
         with torch.cuda.stream(side):
-            layer.forward(x, y)  # warm the side stream (attributes, tensor maps)
+            forward()  # warm the side stream (attributes, tensor maps)
         stream.wait_stream(side)
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         c1 = H.lib().hmoe_launch_count()
         with torch.cuda.graph(graph):
-            layer.forward(x, y)
+            forward()
         per_forward = H.lib().hmoe_launch_count() - c1
         torch.cuda.synchronize()
         stream = torch.cuda.current_stream()
@@ -275,7 +307,7 @@ def main():
         if graph is not None:
             graph.replay()
         else:
-            layer.forward(x, y)
+            forward()
         ev[5].synchronize()
         step_ms.append(ev[0].elapsed_time(ev[5]))
         for i, s in enumerate(STAGES):
@@ -293,18 +325,29 @@ def main():
         ms = float(t.item())
     value = world * T / (ms * 1e-3)
 
-    # e2e: host buffers through hmoe_moe_forward_host, copies inside the region
+    # e2e: host buffers in and out, both copies inside the timed region
+    # (single GPU: hmoe_moe_forward_host; expert parallelism: pinned copies
+    # around hmoe_ep_moe_forward on the same stream)
     xh = torch.from_numpy(x_np).pin_memory()
     yh = torch.empty_like(xh).pin_memory()
+
+    def forward_host():
+        if comm is None:
+            layer.forward_host(xh, yh)
+        else:
+            x.copy_(xh, non_blocking=True)
+            layer.forward(x, y, max_tokens=T)
+            yh.copy_(y, non_blocking=True)
+
     for _ in range(max(1, args.warmup // 2)):
-        layer.forward_host(xh, yh)
+        forward_host()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e2e_ms = []
     for _ in range(args.steps):
         flush.zero_()
         e0.record(stream)
-        layer.forward_host(xh, yh)
+        forward_host()
         e1.record(stream)
         e1.synchronize()
         e2e_ms.append(e0.elapsed_time(e1))
@@ -320,6 +363,7 @@ def main():
     if rank != 0:
         if dist is not None:
             dist.barrier()
+            comm.close()
             dist.destroy_process_group()
         return
 
@@ -350,7 +394,7 @@ def main():
                               alg["layer"]["flops"] / (peaks["bf16_tflops"] * 1e12))
 
     cpu = None
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and world == 1:
         threads = os.cpu_count() or 1
         rate, n, dt = cpu_reference_sample(cfg, host_layer, x_np, args.cpu_seconds, threads)
         cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "reference",
@@ -360,24 +404,27 @@ def main():
     # tensor-core GEMM present (hmoe_set_variant(2) is refused without it)?
     has_gemm = H.lib().hmoe_set_variant(2) == 0
     H.lib().hmoe_set_variant(args.variant)
-    used_gemm = has_gemm and args.variant != 1 and T * cfg.top_k / cfg.experts > 16
+    used_gemm = has_gemm and args.variant != 1 and T * (cfg.top_k + cfg.shared_experts) > 64
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp32" if not used_gemm else "bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights quantised to INT8)",
-        "config": dict(config, parallelism=("replicas" if world > 1 else "single"),
+        "config": dict(config, parallelism=(f"ep{world}" if world > 1 else "single"),
                        l2="inputs larger than L2 (604 MB INT8 arena) and a 256 MiB flush between steps"),
         "e2e": e2e, "gpu_launches": launches,
-        "timing": "cuda-graph replay of hmoe_moe_forward" if graph is not None else "eager hmoe_moe_forward",
+        "timing": ("cuda-graph replay of hmoe_moe_forward" if graph is not None else
+                   "eager hmoe_ep_moe_forward" if comm is not None else "eager hmoe_moe_forward"),
         "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
         "stages_ms": avg, "layer_roofline_ms": layer_roof_ms,
         "layer_roofline_frac": layer_roof_ms / ms, "unique_experts": alg["unique_experts"],
+        "rows_received_rank0": alg.get("rows_received"),
         "device_status": {"status": status[0], "near_ties": status[1], "sequential_logits": status[2]},
     }
     print(json.dumps(line))
     if dist is not None:
         dist.barrier()
+        comm.close()
         dist.destroy_process_group()
 
 

@@ -32,9 +32,10 @@
 //               and multicasts tcgen05.commit to both CTAs' barriers
 //   warps 3-10  dequantise INT8 -> BF16 into the swizzled A layout and
 //               signal the leader
-//   warps 11-14 epilogue: tcgen05.ld from double-buffered accumulators,
-//               projection scale, SwiGLU (gate/up -> BF16 rows) or routing
-//               weight (down -> FP32 rows), overlapping the next main loop.
+//   warps 11-18 epilogue: tcgen05.ld from double-buffered accumulators,
+//               projection scale, SwiGLU (gate/up) or routing weight (down),
+//               BF16 rows staged in shared memory and stored coalesced,
+//               overlapping the next main loop.
 // Work items are (token tile of <= 256 rows of one expert, feature block),
 // longest tiles first, dealt round-robin to the pairs.
 //
@@ -43,6 +44,7 @@
 #include "sm100.cuh"
 
 #include <cudaTypedefs.h>
+#include <cub/block/block_scan.cuh>
 
 #include <algorithm>
 #include <mutex>
@@ -52,6 +54,7 @@ namespace hmoe {
 namespace {
 
 constexpr int kTileT = 256;   // tokens per work item (pair MMA N <= 256)
+static_assert(kTileT == kTileRows, "GEMM work items are whole tiles");
 constexpr int kHalfT = 128;   // token rows per CTA (B box height)
 constexpr int kBK = 64;       // K per stage (128 bytes of BF16)
 constexpr int kWStages = 4;   // INT8 staging ring
@@ -67,7 +70,7 @@ constexpr int kABytes = 128 * kBK * 2;     // 16 KB: 128 A rows (two 64-row atom
 constexpr int kBBytes = kHalfT * kBK * 2;  // 16 KB: 128 token rows
 constexpr int kSBytes = 64 * kBK;          // 4 KB: one [64 k][64 n] INT8 box
 // Epilogue scratch per column-half group: gate/up exchange (2 x 64 x 16
-// FP32) and an output staging tile (32 tokens x 128 FP32 for down, 32 x 64
+// FP32) and an output staging tile (32 tokens x 128 BF16 for down, 32 x 64
 // BF16 for gate/up).
 constexpr int kXchBytes = 2 * 64 * 16 * 4;  // 8 KB
 constexpr int kStgBytes = 32 * 128 * 4;     // 16 KB
@@ -87,7 +90,7 @@ struct GemmArgs {
     int nblocks;                // feature blocks per pair
     const hmoe_expert_quant* quant;
     const float* perm_weight;   // down: routing weight per row
-    void* out;                  // gate/up: BF16 hmid [R,N]; down: FP32 rows [R,N]
+    void* out;                  // BF16 rows [R,N]: gate/up SwiGLU output; down weighted output
     int K, N;
     DeviceStatus* st;
 };
@@ -435,22 +438,22 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
                 } else {
                     const float sd = qp.scale[2];
                     const float wl = lane < nt ? a.perm_weight[row0 + c0 + lane] : 0.0f;
-                    float* st = reinterpret_cast<float*>(stg); // [32 t][128 f]
+                    __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(stg); // [32 t][128 f]
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
                         const float wt = __shfl_sync(0xffffffffu, wl, i);
-                        st[i * 128 + m] = wt * (sd * __uint_as_float(v[i]));
+                        st[i * 128 + m] = __float2bfloat16_rn(wt * (sd * __uint_as_float(v[i])));
                     }
                     epi_barrier(grp);
                     const int f0 = nb * 256 + 128 * static_cast<int>(rank);
-                    float* out = static_cast<float*>(a.out);
+                    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
 #pragma unroll
-                    for (int p = 0; p < 8; ++p) {
-                        const int idx = gt + 128 * p;      // 1024 pieces of 4 floats
-                        const int t = idx >> 5, c = idx & 31;
-                        if (t < nt && f0 + c * 4 < a.N)
-                            *reinterpret_cast<float4*>(out + static_cast<size_t>(row0 + c0 + t) * a.N + f0 + c * 4) =
-                                *reinterpret_cast<const float4*>(st + t * 128 + c * 4);
+                    for (int p = 0; p < 4; ++p) {
+                        const int idx = gt + 128 * p;      // 512 pieces of 8 BF16
+                        const int t = idx >> 4, c = idx & 15;
+                        if (t < nt && f0 + c * 8 < a.N)
+                            *reinterpret_cast<uint4*>(out + static_cast<size_t>(row0 + c0 + t) * a.N + f0 + c * 8) =
+                                *reinterpret_cast<const uint4*>(st + t * 128 + c * 8);
                     }
                     epi_barrier(grp);
                 }
@@ -472,70 +475,71 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
     }
 }
 
-// Cuts every expert on the large list into tiles of <= kTileT consecutive
-// permuted rows: all full tiles first, then the remainders in decreasing
-// size (ties by list position), so the persistent CTAs start with the
-// longest work items.  One CTA, one thread per listed expert.
-__global__ void __launch_bounds__(256) tile_list_kernel(const int32_t* large_list, const int32_t* list_sizes,
-                                                        const int32_t* offsets, int4* tiles,
-                                                        int32_t* tile_count, int capacity) {
-    __shared__ int full_s[256], rem_s[256], off_s[256];
-    __shared__ int total_full_s;
-    const int nl = min(list_sizes[1], 256);
+// Cuts every segment (a run of consecutive permuted rows of one expert)
+// into tiles of <= kTileRows rows: all full tiles first, then the remainders
+// in decreasing size (ties by segment order), so the persistent CTAs start
+// with the longest work items.  One CTA, one thread per segment.
+__global__ void __launch_bounds__(kMaxSegments) tile_list_kernel(SegSpec sp, int4* tiles, int32_t* tile_count,
+                                                                 int capacity) {
+    using Scan = cub::BlockScan<int, kMaxSegments>;
+    __shared__ typename Scan::TempStorage scan_s;
+    __shared__ int rem_s[kMaxSegments];
+    __shared__ int total_full_s, parts_s;
     const int i = threadIdx.x;
-    int e = -1, r0 = 0, cnt = 0;
-    if (i < nl) {
-        e = large_list[i];
-        r0 = offsets[e];
-        cnt = offsets[e + 1] - r0;
+    const bool valid = i < sp.nseg;
+    int r0 = 0, cnt = 0;
+    if (valid) {
+        if (sp.offsets) {
+            r0 = sp.offsets[i];
+            cnt = sp.offsets[i + 1] - r0;
+        } else {
+            cnt = sp.counts[(i / sp.eps) * sp.count_stride + i % sp.eps];
+        }
     }
-    full_s[i] = cnt / kTileT;
-    rem_s[i] = cnt % kTileT;
+    if (!sp.offsets) {
+        Scan(scan_s).ExclusiveSum(cnt, r0);
+        r0 += sp.row_base;
+        __syncthreads();
+    }
+    const int full = cnt / kTileRows, rem = cnt % kTileRows;
+    int full_before = 0;
+    Scan(scan_s).ExclusiveSum(full, full_before);
+    rem_s[i] = rem;
+    if (i == kMaxSegments - 1) total_full_s = full_before + full;
     __syncthreads();
-    if (i == 0) {
-        int acc = 0;
-        for (int j = 0; j < nl; ++j) {
-            off_s[j] = acc;
-            acc += full_s[j];
-        }
-        total_full_s = acc;
-    }
+    int parts_flag = rem > 0, parts_before = 0;
+    Scan(scan_s).ExclusiveSum(parts_flag, parts_before);
+    if (i == kMaxSegments - 1) parts_s = parts_before + parts_flag;
     __syncthreads();
-    if (i < nl) {
-        for (int f = 0; f < full_s[i]; ++f) {
-            const int pos = off_s[i] + f;
-            if (pos < capacity) tiles[pos] = make_int4(e, r0 + f * kTileT, kTileT, 0);
-        }
-        if (rem_s[i] > 0) {
-            int before = 0;
-            for (int j = 0; j < nl; ++j)
-                before += rem_s[j] > rem_s[i] || (rem_s[j] == rem_s[i] && j < i);
-            const int pos = total_full_s + before;
-            if (pos < capacity) tiles[pos] = make_int4(e, r0 + full_s[i] * kTileT, rem_s[i], 0);
-        }
+    if (!valid) return;
+    const int e = sp.expert_base + i % sp.eps;
+    for (int f = 0; f < full; ++f) {
+        const int pos = full_before + f;
+        if (pos < capacity) tiles[pos] = make_int4(e, r0 + f * kTileRows, kTileRows, 0);
     }
-    if (i == 0) {
-        int parts = 0;
-        for (int j = 0; j < nl; ++j) parts += rem_s[j] > 0;
-        *tile_count = min(capacity, total_full_s + parts);
+    if (rem > 0) {
+        int before = 0;
+        for (int j = 0; j < sp.nseg; ++j) before += rem_s[j] > rem || (rem_s[j] == rem && j < i);
+        const int pos = total_full_s + before;
+        if (pos < capacity) tiles[pos] = make_int4(e, r0 + full * kTileRows, rem, 0);
     }
+    if (i == 0) *tile_count = min(capacity, total_full_s + parts_s);
 }
 
-// X_perm[row] = BF16(x[perm_token[row]]) for the rows of every GEMM tile.
-__global__ void __launch_bounds__(256) permute_kernel(const float* __restrict__ x, const uint32_t* __restrict__ perm_token,
-                                                      const int4* tiles, const int32_t* tile_count, int H,
-                                                      __nv_bfloat16* __restrict__ xperm) {
-    if (static_cast<int>(blockIdx.x) >= *tile_count) return;
-    const int4 td = tiles[blockIdx.x];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int r = warp; r < td.z; r += 8) {
-        const int row = td.y + r;
-        const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(perm_token[row]) * H);
-        uint4* dst = reinterpret_cast<uint4*>(xperm + static_cast<size_t>(row) * H);
-        for (int c = lane; c < H / 8; c += 32) {
-            const float4 v0 = src[2 * c], v1 = src[2 * c + 1];
-            dst[c] = make_uint4(bf16x2(v0.x, v0.y), bf16x2(v0.z, v0.w), bf16x2(v1.x, v1.y), bf16x2(v1.z, v1.w));
-        }
+// Token-major permutation: token t's FP32 row is read once, converted to
+// BF16 and written to each of its rows inv[t, 0..slots).
+__global__ void __launch_bounds__(256) permute_kernel(const float* __restrict__ x, const int32_t* __restrict__ inv,
+                                                      int slots, int H, __nv_bfloat16* __restrict__ xrows) {
+    __shared__ int rows_s[kMaxSlots];
+    const int t = blockIdx.x;
+    for (int s = threadIdx.x; s < slots; s += blockDim.x) rows_s[s] = inv[static_cast<size_t>(t) * slots + s];
+    __syncthreads();
+    const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H);
+    for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
+        const float4 v0 = src[2 * c], v1 = src[2 * c + 1];
+        const uint4 o = make_uint4(bf16x2(v0.x, v0.y), bf16x2(v0.z, v0.w), bf16x2(v1.x, v1.y), bf16x2(v1.z, v1.w));
+        for (int s = 0; s < slots; ++s)
+            reinterpret_cast<uint4*>(xrows + static_cast<size_t>(rows_s[s]) * H)[c] = o;
     }
 }
 
@@ -619,11 +623,6 @@ hmoe_status launch_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUte
     return check_launch(GATE_UP ? "hmoe expert GEMM gate/up" : "hmoe expert GEMM down");
 }
 
-int tile_capacity(const hmoe_layer_desc& d, size_t T, int list_capacity) {
-    const long rows = static_cast<long>(T) * (d.top_k + d.shared_experts);
-    return static_cast<int>(rows / kTileT + list_capacity + 1);
-}
-
 } // namespace
 
 bool gemm_available() {
@@ -639,54 +638,50 @@ bool gemm_available() {
     return avail == 1;
 }
 
-size_t gemm_tile_bytes(size_t rows, int experts) { return (rows / kTileT + experts + 2) * sizeof(int4); }
+hmoe_status launch_tile_list(const SegSpec& spec, int4* tiles, int32_t* tile_count, int capacity,
+                             cudaStream_t s) {
+    if (spec.nseg <= 0 || spec.nseg > kMaxSegments || spec.eps <= 0 || capacity <= 0)
+        return HMOE_INVALID_ARGUMENT;
+    tile_list_kernel<<<1, kMaxSegments, 0, s>>>(spec, tiles, tile_count, capacity);
+    return check_launch("hmoe tile list");
+}
 
-hmoe_status launch_expert_gemm_gate_up(const hmoe_layer_desc& d, const float* x, size_t T, char* ws,
-                                       const Workspace& w, int list_capacity, cudaStream_t s) {
-    const int H = static_cast<int>(d.hidden), I = static_cast<int>(d.intermediate);
-    const int E = static_cast<int>(d.experts + d.shared_experts);
-    const int cap = tile_capacity(d, T, list_capacity);
-    const int R = static_cast<int>(T * (d.top_k + d.shared_experts));
-    auto* tiles = reinterpret_cast<int4*>(ws + w.tiles);
-    auto* tcount = reinterpret_cast<int32_t*>(ws + w.tile_count);
-    tile_list_kernel<<<1, 256, 0, s>>>(reinterpret_cast<int32_t*>(ws + w.large_list),
-                                       reinterpret_cast<int32_t*>(ws + w.list_sizes),
-                                       reinterpret_cast<int32_t*>(ws + w.offsets), tiles, tcount, cap);
-    hmoe_status r = check_launch("hmoe tile list");
-    if (r != HMOE_OK) return r;
-    auto* xperm = reinterpret_cast<__nv_bfloat16*>(ws + w.xperm);
-    permute_kernel<<<cap, 256, 0, s>>>(x, reinterpret_cast<uint32_t*>(ws + w.perm_token), tiles, tcount, H, xperm);
-    r = check_launch("hmoe permute");
-    if (r != HMOE_OK) return r;
+hmoe_status launch_permute(const float* x, const int32_t* inv, int tokens, int slots, int H,
+                           __nv_bfloat16* xrows, cudaStream_t s) {
+    if (tokens <= 0) return HMOE_OK;
+    permute_kernel<<<static_cast<unsigned>(tokens), 256, 0, s>>>(x, inv, slots, H, xrows);
+    return check_launch("hmoe permute");
+}
+
+// Full tiles are at most rows / kTileRows; each segment with rows adds at
+// most one partial tile, and at most `rows` segments have rows.
+int tile_capacity_for(long rows, int segments) {
+    return static_cast<int>(rows / kTileRows + std::min<long>(segments, rows) + 1);
+}
+
+hmoe_status gemm_gate_up(const ExpertRun& r, cudaStream_t s) {
     CUtensorMap mg, mu, mb;
-    if (!map_weights(&mg, d.arena + d.gate_offset, I, H, E, d.expert_stride) ||
-        !map_weights(&mu, d.arena + d.up_offset, I, H, E, d.expert_stride) || !map_rows(&mb, xperm, H, R)) {
+    if (!map_weights(&mg, r.arena + r.gate_offset, r.I, r.H, r.experts, r.stride) ||
+        !map_weights(&mu, r.arena + r.up_offset, r.I, r.H, r.experts, r.stride) ||
+        !map_rows(&mb, r.xrows, r.H, r.rows_cap)) {
         set_last_error_text("hmoe: cuTensorMapEncodeTiled failed (gate/up)");
         return HMOE_CUDA_ERROR;
     }
-    const int nb = (I + 127) / 128; // 128 features (64 per CTA) per pair
-    GemmArgs a{tiles, tcount, nb, d.quant, nullptr, ws + w.hmid16, H, I,
-               reinterpret_cast<DeviceStatus*>(ws + w.status)};
-    return launch_gemm<true>(mg, mu, mb, a, cap * nb, s);
+    const int nb = (r.I + 127) / 128; // 128 features (64 per CTA) per pair
+    GemmArgs a{r.tiles, r.tile_count, nb, r.quant, nullptr, r.hmid16, r.H, r.I, r.st};
+    return launch_gemm<true>(mg, mu, mb, a, r.tile_cap * nb, s);
 }
 
-hmoe_status launch_expert_gemm_down(const hmoe_layer_desc& d, size_t T, char* ws, const Workspace& w,
-                                    int list_capacity, cudaStream_t s) {
-    const int H = static_cast<int>(d.hidden), I = static_cast<int>(d.intermediate);
-    const int E = static_cast<int>(d.experts + d.shared_experts);
-    const int cap = tile_capacity(d, T, list_capacity);
-    const int R = static_cast<int>(T * (d.top_k + d.shared_experts));
+hmoe_status gemm_down(const ExpertRun& r, cudaStream_t s) {
     CUtensorMap md, mb;
-    if (!map_weights(&md, d.arena + d.down_offset, H, I, E, d.expert_stride) ||
-        !map_rows(&mb, ws + w.hmid16, I, R)) {
+    if (!map_weights(&md, r.arena + r.down_offset, r.H, r.I, r.experts, r.stride) ||
+        !map_rows(&mb, r.hmid16, r.I, r.rows_cap)) {
         set_last_error_text("hmoe: cuTensorMapEncodeTiled failed (down)");
         return HMOE_CUDA_ERROR;
     }
-    const int nb = (H + 255) / 256; // 256 features (128 per CTA) per pair
-    GemmArgs a{reinterpret_cast<int4*>(ws + w.tiles), reinterpret_cast<int32_t*>(ws + w.tile_count), nb, d.quant,
-               reinterpret_cast<float*>(ws + w.perm_weight), ws + w.yrows, I, H,
-               reinterpret_cast<DeviceStatus*>(ws + w.status)};
-    return launch_gemm<false>(md, md, mb, a, cap * nb, s);
+    const int nb = (r.H + 255) / 256; // 256 features (128 per CTA) per pair
+    GemmArgs a{r.tiles, r.tile_count, nb, r.quant, r.weight, r.yrows, r.I, r.H, r.st};
+    return launch_gemm<false>(md, md, mb, a, r.tile_cap * nb, s);
 }
 
 } // namespace hmoe

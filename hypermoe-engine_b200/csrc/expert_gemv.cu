@@ -7,8 +7,8 @@
 // (src/backend/cuda/CudaKernels.cu:30-107) plus activationKernel and a
 // cuBLAS multiply.
 //
-// One launch handles every expert on a device-built list.  A thread block
-// cluster of KS CTAs owns (expert, 256 output columns); CTA r of the
+// One launch handles every tile of the device-built tile list.  A thread
+// block cluster of KS CTAs owns (tile, 256 output columns); CTA r of the
 // cluster streams rows [r*K/KS, (r+1)*K/KS) of the INT8 weight matrix
 // ([K,N] row-major, each lane reading 8 consecutive columns with one 64-bit
 // load per row) and accumulates x * (q - zp) in FP32 for every token of the
@@ -39,10 +39,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32) expert_gemv_kernel(GemvArgs a
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = static_cast<int>(cluster.block_rank());
     const int KS = a.KS;
-    if (static_cast<int>(blockIdx.z) >= *a.list_size) return; // whole cluster exits together
-    const int e = a.list[blockIdx.z];
-    const int r0 = a.offsets[e];
-    const int n = a.offsets[e + 1] - r0;
+    if (static_cast<int>(blockIdx.z) >= *a.tile_count) return; // whole cluster exits together
+    const int4 td = a.tiles[blockIdx.z];
+    const int e = td.x;
+    const int r0 = td.y;
+    const int n = td.z;
     const int K = a.K, N = a.N;
     const int KP = (K + KS - 1) / KS;
     const int kb = min(K, rank * KP), ke = min(K, kb + KP);
@@ -68,9 +69,11 @@ __global__ void __launch_bounds__(kGemvWarps * 32) expert_gemv_kernel(GemvArgs a
             const int t = i / kc, kk = i % kc;
             float v = 0.0f;
             if (t < nj) {
-                const int row = r0 + j0 + t;
-                const size_t src = GATE_UP ? static_cast<size_t>(a.perm_token[row]) : static_cast<size_t>(row);
-                v = a.act[src * K + kb + kk];
+                const size_t row = static_cast<size_t>(r0 + j0 + t);
+                if constexpr (GATE_UP)
+                    v = __bfloat162float(a.act16[row * K + kb + kk]);
+                else
+                    v = a.act32[row * K + kb + kk];
             }
             xs[t * KP + kk] = v;
         }
@@ -155,9 +158,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32) expert_gemv_kernel(GemvArgs a
             if constexpr (GATE_UP) {
                 const float g = qp.scale[a.proj0] * s0;
                 const float u = qp.scale[a.proj0 + 1] * s1;
-                a.out[static_cast<size_t>(row) * N + c] = silu(g) * u;
+                a.out32[static_cast<size_t>(row) * N + c] = silu(g) * u;
             } else {
-                a.out[static_cast<size_t>(row) * N + c] = a.perm_weight[row] * (qp.scale[a.proj0] * s0);
+                a.out16[static_cast<size_t>(row) * N + c] = __float2bfloat16_rn(a.weight[row] * (qp.scale[a.proj0] * s0));
             }
         }
         cluster.sync();
@@ -185,6 +188,7 @@ cudaError_t launch_gemv_variant(cudaLaunchConfig_t& cfg, const GemvArgs& args) {
 hmoe_status launch_expert_gemv(bool gate_up, const GemvArgs& args, int list_capacity, int max_tokens,
                                cudaStream_t stream) {
     if (list_capacity <= 0) return HMOE_OK;
+    if (list_capacity > 65535) return HMOE_UNSUPPORTED;
     // One token per pass when no expert can hold more (a single-token
     // batch without shared experts); otherwise four.
     const int tok = max_tokens <= 1 ? 1 : 4;
@@ -212,6 +216,54 @@ hmoe_status launch_expert_gemv(bool gate_up, const GemvArgs& args, int list_capa
         return HMOE_CUDA_ERROR;
     }
     return check_launch("hmoe expert GEMV");
+}
+
+namespace {
+
+int gemv_split(int capacity, int col_blocks) {
+    int ks = 1;
+    while (ks < 8 && static_cast<long>(capacity) * col_blocks * ks < 2L * 148) ks *= 2;
+    return ks;
+}
+
+GemvArgs gemv_common(const ExpertRun& r) {
+    GemvArgs g{};
+    g.tiles = r.tiles;
+    g.tile_count = r.tile_count;
+    g.arena = r.arena;
+    g.stride = r.stride;
+    g.quant = r.quant;
+    return g;
+}
+
+} // namespace
+
+// gate/up of every tile, weight-streaming GEMV variant.
+hmoe_status gemv_gate_up(const ExpertRun& r, cudaStream_t s) {
+    GemvArgs g = gemv_common(r);
+    g.act16 = r.xrows;
+    g.off0 = r.gate_offset;
+    g.off1 = r.up_offset;
+    g.proj0 = 0;
+    g.out32 = r.hmid32;
+    g.K = r.H;
+    g.N = r.I;
+    g.KS = gemv_split(r.tile_cap, (r.I + 255) / 256);
+    return launch_expert_gemv(true, g, r.tile_cap, r.max_group, s);
+}
+
+// down of every tile with the routing weight, weight-streaming GEMV variant.
+hmoe_status gemv_down(const ExpertRun& r, cudaStream_t s) {
+    GemvArgs g = gemv_common(r);
+    g.act32 = r.hmid32;
+    g.weight = r.weight;
+    g.off0 = r.down_offset;
+    g.proj0 = 2;
+    g.out16 = r.yrows;
+    g.K = r.I;
+    g.N = r.H;
+    g.KS = gemv_split(r.tile_cap, (r.H + 255) / 256);
+    return launch_expert_gemv(false, g, r.tile_cap, r.max_group, s);
 }
 
 } // namespace hmoe

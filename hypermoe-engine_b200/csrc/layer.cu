@@ -11,9 +11,12 @@
 //
 //   memset(status, counts)                          (one cudaMemsetAsync)
 //   route_kernel     logits, softmax, top-k, renorm, expert histogram
-//   group_kernel     offsets, permutation, inverse map, GEMV/GEMM lists
-//   gate/up          GEMV for small groups, tcgen05 GEMM for large groups
-//   down             same split, routing weight folded into the epilogue
+//   group_kernel     offsets, permutation, inverse map
+//   permute_kernel   each token row once -> BF16 copies at its permuted rows
+//   tile_list_kernel (expert, first row, rows) tiles, longest first
+//   gate/up          tcgen05 GEMM (or the weight-streaming GEMV for
+//                    decode-sized batches), SwiGLU in the epilogue
+//   down             same variant, routing weight in the epilogue, BF16 rows
 //   combine_kernel   out[t] = sum of the token's rows in ascending expert id
 //
 // No host synchronisation, no allocation.  The combine order (ascending
@@ -28,23 +31,11 @@
 
 namespace hmoe {
 
-hmoe_status launch_route(const float* x, const float* w, const float* bias, int T, int H, int E,
-                         int k, int softmax, int renorm, uint32_t* ids, float* scores,
-                         int32_t* counts, DeviceStatus* st, cudaStream_t stream);
-hmoe_status launch_group(const uint32_t* ids, const float* scores, const int32_t* counts, int T,
-                         int k, int E, int S, int small_max, int32_t* offsets,
-                         uint32_t* perm_token, float* perm_weight, int32_t* inv,
-                         int32_t* small_list, int32_t* large_list, int32_t* list_sizes,
-                         cudaStream_t stream);
-
 int g_variant = 0;
 cudaEvent_t g_stage_events[6];
 int g_stage_count = 0;
 
-// Records stage event i.  Under stream capture the record becomes an
-// external event node, so the caller can still synchronise on and time the
-// event after each graph launch.
-inline void stage(int i, cudaStream_t s) {
+void stage(int i, cudaStream_t s) {
     if (g_stage_count != 6) return;
     cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
     cudaStreamIsCapturing(s, &cs);
@@ -54,11 +45,11 @@ inline void stage(int i, cudaStream_t s) {
         cudaEventRecord(g_stage_events[i], s);
 }
 
-Workspace plan_workspace(const hmoe_layer_desc& d, size_t T, int local_experts) {
+Workspace plan_workspace(const hmoe_layer_desc& d, size_t T) {
     Workspace w{};
     const size_t E = d.experts, S = d.shared_experts, k = d.top_k;
     const size_t slots = k + S;
-    const size_t R = T * slots; // upper bound of permuted rows on this device
+    const size_t R = T * slots; // permuted rows of this batch (exact)
     size_t off = 0;
     auto take = [&](size_t bytes) {
         const size_t at = off;
@@ -69,26 +60,23 @@ Workspace plan_workspace(const hmoe_layer_desc& d, size_t T, int local_experts) 
     w.counts = take((E + S) * 4); // zeroed together with status
     w.zero_bytes = off;
     w.offsets = take((E + S + 1) * 4);
-    w.list_sizes = take(2 * 4);
-    w.small_list = take((E + S) * 4);
-    w.large_list = take((E + S) * 4);
     w.ids = take(T * k * 4);
     w.scores = take(T * k * 4);
     w.perm_token = take(R * 4);
     w.perm_weight = take(R * 4);
-    w.inv = take(T * slots * 4);
-    w.hmid = take(R * static_cast<size_t>(d.intermediate) * 4);
-    w.yrows = take(R * static_cast<size_t>(d.hidden) * 4);
+    w.inv = take(R * 4);
     w.xperm = take(R * static_cast<size_t>(d.hidden) * 2);
-    w.hmid16 = take(R * static_cast<size_t>(d.intermediate) * 2);
+    w.hmid = take(R * static_cast<size_t>(d.intermediate) * 4);
+    w.yrows = take(R * static_cast<size_t>(d.hidden) * 2);
     w.tile_count = take(16);
-    w.tiles = take((R / 128 + E + S + 2) * 16);
+    w.tile_cap = tile_capacity_for(static_cast<long>(R), static_cast<int>(E + S));
+    w.tiles = take(static_cast<size_t>(w.tile_cap) * 16);
     w.total = off;
-    (void)local_experts;
     return w;
 }
 
-hmoe_status validate_desc(const hmoe_layer_desc* d) {
+// Checks shared by the single-GPU and expert-parallel entry points.
+hmoe_status validate_layer(const hmoe_layer_desc* d) {
     if (!d) return HMOE_INVALID_ARGUMENT;
     if (d->hidden == 0 || d->intermediate == 0 || d->experts == 0 || d->top_k == 0 ||
         d->top_k > d->experts || !d->router_weight || !d->arena || !d->quant)
@@ -99,7 +87,13 @@ hmoe_status validate_desc(const hmoe_layer_desc* d) {
     if (d->experts > 256 || d->top_k > 32 || d->shared_experts > 64 ||
         d->top_k + d->shared_experts > static_cast<uint32_t>(kMaxSlots))
         return HMOE_UNSUPPORTED;
-    if (d->ep_size != 1 || d->ep_rank != 0) return HMOE_UNSUPPORTED; // see hmoe_ep_*
+    return HMOE_OK;
+}
+
+hmoe_status validate_desc(const hmoe_layer_desc* d) {
+    const hmoe_status v = validate_layer(d);
+    if (v != HMOE_OK) return v;
+    if (d->ep_size != 1 || d->ep_rank != 0) return HMOE_UNSUPPORTED; // hmoe_ep_moe_forward
     return HMOE_OK;
 }
 
@@ -107,8 +101,9 @@ hmoe_status validate_desc(const hmoe_layer_desc* d) {
 
 // One CTA per token: gather the token's rows (routed slots, then shared),
 // order them ascending (rows are laid out in ascending expert id, so row
-// order is expert order) and accumulate in that order from zero.
-__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ yrows,
+// order is expert order) and accumulate in that order from zero, as the
+// reference's combine loop does (MoERuntime.cpp:311-325).
+__global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ yrows,
                                                       const int32_t* __restrict__ inv, int slots,
                                                       int H, float* __restrict__ out) {
     __shared__ int rows_s[kMaxSlots];
@@ -126,24 +121,36 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
         }
     }
     __syncthreads();
-    const int H4 = H / 4;
-    for (int c = threadIdx.x; c < H4; c += blockDim.x) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int H8 = H / 8;
+    for (int c = threadIdx.x; c < H8; c += blockDim.x) {
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
         for (int s = 0; s < slots; ++s) {
-            const float4 v = reinterpret_cast<const float4*>(yrows + static_cast<size_t>(rows_s[s]) * H)[c];
-            acc.x = __fadd_rn(acc.x, v.x);
-            acc.y = __fadd_rn(acc.y, v.y);
-            acc.z = __fadd_rn(acc.z, v.z);
-            acc.w = __fadd_rn(acc.w, v.w);
+            const uint4 v = reinterpret_cast<const uint4*>(yrows + static_cast<size_t>(rows_s[s]) * H)[c];
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                acc[2 * i] = __fadd_rn(acc[2 * i], __uint_as_float(w[i] << 16));
+                acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __uint_as_float(w[i] & 0xffff0000u));
+            }
         }
-        reinterpret_cast<float4*>(out + static_cast<size_t>(t) * H)[c] = acc;
+        float4* o = reinterpret_cast<float4*>(out + static_cast<size_t>(t) * H) + 2 * c;
+        o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
     }
+}
+
+hmoe_status launch_combine(const __nv_bfloat16* yrows, const int32_t* inv, int tokens, int slots, int H,
+                           float* out, cudaStream_t s) {
+    if (tokens <= 0) return HMOE_OK;
+    combine_kernel<<<static_cast<unsigned>(tokens), 256, 0, s>>>(yrows, inv, slots, H, out);
+    return check_launch("hmoe combine kernel");
 }
 
 // ------------------------------------------------------- layer driver
 
-hmoe_status enqueue_route(const hmoe_layer_desc& d, const float* x, size_t T, char* ws,
-                          const Workspace& w, int small_max, cudaStream_t s) {
+// Router, histogram, grouping and the BF16 row permutation of one batch.
+hmoe_status enqueue_route(const hmoe_layer_desc& d, const float* x, size_t T, char* ws, const Workspace& w,
+                          bool permute, cudaStream_t s) {
     cudaError_t err = cudaMemsetAsync(ws, 0, w.zero_bytes, s);
     if (err != cudaSuccess) {
         set_last_error("hmoe workspace reset", err);
@@ -159,97 +166,59 @@ hmoe_status enqueue_route(const hmoe_layer_desc& d, const float* x, size_t T, ch
     if (r != HMOE_OK) return r;
     stage(1, s);
     r = launch_group(reinterpret_cast<uint32_t*>(ws + w.ids), reinterpret_cast<float*>(ws + w.scores),
-                        reinterpret_cast<int32_t*>(ws + w.counts), static_cast<int>(T),
-                        static_cast<int>(d.top_k), static_cast<int>(d.experts),
-                        static_cast<int>(d.shared_experts), small_max,
-                        reinterpret_cast<int32_t*>(ws + w.offsets),
-                        reinterpret_cast<uint32_t*>(ws + w.perm_token),
-                        reinterpret_cast<float*>(ws + w.perm_weight),
-                        reinterpret_cast<int32_t*>(ws + w.inv),
-                        reinterpret_cast<int32_t*>(ws + w.small_list),
-                        reinterpret_cast<int32_t*>(ws + w.large_list),
-                        reinterpret_cast<int32_t*>(ws + w.list_sizes), s);
-    stage(2, s);
+                     reinterpret_cast<int32_t*>(ws + w.counts), static_cast<int>(T), static_cast<int>(d.top_k),
+                     static_cast<int>(d.experts), static_cast<int>(d.shared_experts),
+                     reinterpret_cast<int32_t*>(ws + w.offsets), reinterpret_cast<uint32_t*>(ws + w.perm_token),
+                     reinterpret_cast<float*>(ws + w.perm_weight), reinterpret_cast<int32_t*>(ws + w.inv), s);
+    if (r != HMOE_OK || !permute) return r;
+    return launch_permute(x, reinterpret_cast<int32_t*>(ws + w.inv), static_cast<int>(T),
+                          static_cast<int>(d.top_k + d.shared_experts), static_cast<int>(d.hidden),
+                          reinterpret_cast<__nv_bfloat16*>(ws + w.xperm), s);
+}
+
+// gate/up then down of every tile of `r` with the chosen variant.
+hmoe_status run_experts(const ExpertRun& r, bool gemv, bool stages, cudaStream_t s) {
+    hmoe_status st = gemv ? gemv_gate_up(r, s) : gemm_gate_up(r, s);
+    if (st != HMOE_OK) return st;
+    if (stages) stage(3, s);
+    st = gemv ? gemv_down(r, s) : gemm_down(r, s);
+    if (stages) stage(4, s);
+    return st;
+}
+
+// The GEMV streams each touched expert's weights once per 4 rows; the
+// tensor-core GEMM wins as soon as experts hold more than a few rows.  The
+// choice is made per launch from the number of permuted rows, which the host
+// knows without reading the routing.
+bool use_gemv(long rows) {
+    if (g_variant == 1 || !gemm_available()) return true;
+    if (g_variant == 2) return false;
+    return rows <= kGemvMaxAssignments;
+}
+
+ExpertRun local_run(const hmoe_layer_desc& d, size_t T, char* ws, const Workspace& w) {
+    ExpertRun r{};
+    r.xrows = reinterpret_cast<__nv_bfloat16*>(ws + w.xperm);
+    r.weight = reinterpret_cast<float*>(ws + w.perm_weight);
+    r.tiles = reinterpret_cast<int4*>(ws + w.tiles);
+    r.tile_count = reinterpret_cast<int32_t*>(ws + w.tile_count);
+    r.tile_cap = w.tile_cap;
+    r.rows_cap = static_cast<int>(T * (d.top_k + d.shared_experts));
+    r.hmid32 = reinterpret_cast<float*>(ws + w.hmid);
+    r.hmid16 = reinterpret_cast<__nv_bfloat16*>(ws + w.hmid);
+    r.yrows = reinterpret_cast<__nv_bfloat16*>(ws + w.yrows);
+    r.arena = d.arena;
+    r.stride = d.expert_stride;
+    r.gate_offset = d.gate_offset;
+    r.up_offset = d.up_offset;
+    r.down_offset = d.down_offset;
+    r.quant = d.quant;
+    r.experts = static_cast<int>(d.experts + d.shared_experts);
+    r.H = static_cast<int>(d.hidden);
+    r.I = static_cast<int>(d.intermediate);
+    r.max_group = static_cast<int>(T);
+    r.st = reinterpret_cast<DeviceStatus*>(ws + w.status);
     return r;
-}
-
-int choose_split(int capacity, int col_blocks) {
-    int ks = 1;
-    while (ks < 8 && static_cast<long>(capacity) * col_blocks * ks < 2L * 148) ks *= 2;
-    return ks;
-}
-
-hmoe_status enqueue_experts(const hmoe_layer_desc& d, const float* x, size_t T, char* ws,
-                            const Workspace& w, int small_max, cudaStream_t s) {
-    const int E = static_cast<int>(d.experts), S = static_cast<int>(d.shared_experts);
-    const int H = static_cast<int>(d.hidden), I = static_cast<int>(d.intermediate);
-    const long assignments = static_cast<long>(T) * d.top_k;
-    // Worst-case list sizes: experts that can hold >= 1 (GEMV) or > small_max
-    // (GEMM) tokens.
-    const int shared_small = (static_cast<long>(T) <= small_max) ? S : 0;
-    const int small_cap = small_max <= 0 ? 0 : static_cast<int>(std::min<long>(E, assignments)) + shared_small;
-    const int large_cap = static_cast<int>(std::min<long>(E, assignments / (small_max + 1))) + (S - shared_small);
-    // Largest possible group: T tokens (a shared expert, or one routed expert
-    // taking every token).
-    const int max_group = static_cast<int>(T);
-    GemvArgs g{};
-    g.list = reinterpret_cast<int32_t*>(ws + w.small_list);
-    g.list_size = reinterpret_cast<int32_t*>(ws + w.list_sizes);
-    g.offsets = reinterpret_cast<int32_t*>(ws + w.offsets);
-    g.perm_token = reinterpret_cast<uint32_t*>(ws + w.perm_token);
-    g.perm_weight = reinterpret_cast<float*>(ws + w.perm_weight);
-    g.arena = d.arena;
-    g.stride = d.expert_stride;
-    g.quant = d.quant;
-    hmoe_status r;
-    // gate/up
-    if (small_cap > 0) {
-        g.act = x;
-        g.off0 = d.gate_offset;
-        g.off1 = d.up_offset;
-        g.proj0 = 0;
-        g.out = reinterpret_cast<float*>(ws + w.hmid);
-        g.K = H;
-        g.N = I;
-        g.KS = choose_split(small_cap, (I + 255) / 256);
-        r = launch_expert_gemv(true, g, small_cap, max_group, s);
-        if (r != HMOE_OK) return r;
-    }
-    if (large_cap > 0) {
-        r = launch_expert_gemm_gate_up(d, x, T, ws, w, large_cap, s);
-        if (r != HMOE_OK) return r;
-    }
-    stage(3, s);
-    // down
-    if (small_cap > 0) {
-        g.act = reinterpret_cast<float*>(ws + w.hmid);
-        g.off0 = d.down_offset;
-        g.off1 = 0;
-        g.proj0 = 2;
-        g.out = reinterpret_cast<float*>(ws + w.yrows);
-        g.K = I;
-        g.N = H;
-        g.KS = choose_split(small_cap, (H + 255) / 256);
-        r = launch_expert_gemv(false, g, small_cap, max_group, s);
-        if (r != HMOE_OK) return r;
-    }
-    if (large_cap > 0) {
-        r = launch_expert_gemm_down(d, T, ws, w, large_cap, s);
-        if (r != HMOE_OK) return r;
-    }
-    stage(4, s);
-    return HMOE_OK;
-}
-
-// Experts with at most this many tokens take the GEMV.  The choice is made
-// per launch from the batch size alone (the host never reads the routing):
-// decode-sized batches stream every touched expert through the GEMV, larger
-// ones run every expert on the tensor-core GEMM.
-int small_threshold(size_t T, const hmoe_layer_desc& d) {
-    if (g_variant == 1 || !gemm_available()) return INT_MAX / 2;
-    if (g_variant == 2) return 0;
-    const size_t assignments = T * (d.top_k + d.shared_experts);
-    return assignments <= static_cast<size_t>(kGemvMaxAssignments) ? INT_MAX / 2 : 0;
 }
 
 } // namespace hmoe
@@ -282,7 +251,7 @@ hmoe_status hmoe_workspace_size(const hmoe_layer_desc* desc, size_t max_tokens, 
     if (v != HMOE_OK) return v;
     const bool host_io = (max_tokens & HMOE_WORKSPACE_HOST_IO) != 0;
     const size_t T = std::max<size_t>(max_tokens & ~HMOE_WORKSPACE_HOST_IO, 1);
-    *bytes = plan_workspace(*desc, T, static_cast<int>(desc->experts)).total;
+    *bytes = plan_workspace(*desc, T).total;
     if (host_io) *bytes += 2 * align_up(T * desc->hidden * sizeof(float), 256);
     return HMOE_OK;
 }
@@ -293,12 +262,12 @@ hmoe_status hmoe_route(const hmoe_layer_desc* desc, const float* x, size_t token
     const hmoe_status v = validate_desc(desc);
     if (v != HMOE_OK) return v;
     if (tokens == 0) return HMOE_OK;
-    if (!x || !workspace || tokens > static_cast<size_t>(INT_MAX) / 64) return HMOE_INVALID_ARGUMENT;
-    const Workspace w = plan_workspace(*desc, tokens, static_cast<int>(desc->experts));
+    if (!x || !workspace || tokens > static_cast<size_t>(INT_MAX) / 128) return HMOE_INVALID_ARGUMENT;
+    const Workspace w = plan_workspace(*desc, tokens);
     if (workspace_bytes < w.total) return HMOE_WORKSPACE_TOO_SMALL;
     char* ws = static_cast<char*>(workspace);
     cudaStream_t s = as_stream(stream);
-    hmoe_status r = enqueue_route(*desc, x, tokens, ws, w, small_threshold(tokens, *desc), s);
+    hmoe_status r = enqueue_route(*desc, x, tokens, ws, w, false, s);
     if (r != HMOE_OK) return r;
     const size_t tk = tokens * desc->top_k;
     auto copy = [&](void* dst, size_t src_off, size_t bytes) {
@@ -323,22 +292,25 @@ hmoe_status hmoe_moe_forward(const hmoe_layer_desc* desc, const float* x, float*
     const hmoe_status v = validate_desc(desc);
     if (v != HMOE_OK) return v;
     if (tokens == 0) return HMOE_OK;
-    if (!x || !y || !workspace || tokens > static_cast<size_t>(INT_MAX) / 64) return HMOE_INVALID_ARGUMENT;
-    const Workspace w = plan_workspace(*desc, tokens, static_cast<int>(desc->experts));
+    if (!x || !y || !workspace || tokens > static_cast<size_t>(INT_MAX) / 128) return HMOE_INVALID_ARGUMENT;
+    const Workspace w = plan_workspace(*desc, tokens);
     if (workspace_bytes < w.total) return HMOE_WORKSPACE_TOO_SMALL;
     char* ws = static_cast<char*>(workspace);
     cudaStream_t s = as_stream(stream);
-    const int small_max = small_threshold(tokens, *desc);
+    const int E = static_cast<int>(desc->experts), S = static_cast<int>(desc->shared_experts);
+    const int slots = static_cast<int>(desc->top_k) + S;
     stage(0, s);
-    hmoe_status r = enqueue_route(*desc, x, tokens, ws, w, small_max, s);
+    hmoe_status r = enqueue_route(*desc, x, tokens, ws, w, true, s);
     if (r != HMOE_OK) return r;
-    r = enqueue_experts(*desc, x, tokens, ws, w, small_max, s);
+    const ExpertRun run = local_run(*desc, tokens, ws, w);
+    const SegSpec seg{reinterpret_cast<int32_t*>(ws + w.offsets), nullptr, 0, E + S, E + S, 0, 0};
+    r = launch_tile_list(seg, const_cast<int4*>(run.tiles), const_cast<int32_t*>(run.tile_count), run.tile_cap, s);
     if (r != HMOE_OK) return r;
-    const int slots = static_cast<int>(desc->top_k + desc->shared_experts);
-    combine_kernel<<<static_cast<unsigned>(tokens), 256, 0, s>>>(
-        reinterpret_cast<float*>(ws + w.yrows), reinterpret_cast<int32_t*>(ws + w.inv), slots,
-        static_cast<int>(desc->hidden), y);
-    r = check_launch("hmoe combine kernel");
+    stage(2, s);
+    r = run_experts(run, use_gemv(static_cast<long>(tokens) * slots), true, s);
+    if (r != HMOE_OK) return r;
+    r = launch_combine(run.yrows, reinterpret_cast<int32_t*>(ws + w.inv), static_cast<int>(tokens), slots,
+                       static_cast<int>(desc->hidden), y, s);
     stage(5, s);
     return r;
 }
@@ -348,9 +320,9 @@ hmoe_status hmoe_moe_forward_host(const hmoe_layer_desc* desc, const float* x_ho
     const hmoe_status v = validate_desc(desc);
     if (v != HMOE_OK) return v;
     if (tokens == 0) return HMOE_OK;
-    if (!x_host || !y_host || !workspace || tokens > static_cast<size_t>(INT_MAX) / 64)
+    if (!x_host || !y_host || !workspace || tokens > static_cast<size_t>(INT_MAX) / 128)
         return HMOE_INVALID_ARGUMENT;
-    const Workspace w = plan_workspace(*desc, tokens, static_cast<int>(desc->experts));
+    const Workspace w = plan_workspace(*desc, tokens);
     const size_t io = align_up(tokens * desc->hidden * sizeof(float), 256);
     if (workspace_bytes < w.total + 2 * io) return HMOE_WORKSPACE_TOO_SMALL;
     char* ws = static_cast<char*>(workspace);

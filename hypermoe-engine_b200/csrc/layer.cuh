@@ -6,14 +6,16 @@
 namespace hmoe {
 
 // Byte offsets of the workspace segments (all 256-byte aligned).
+// hmid holds the intermediate rows: FP32 for the GEMV variant, BF16 for the
+// GEMM variant (one launch uses one of them).
 struct Workspace {
-    size_t status, counts, zero_bytes, offsets, list_sizes, small_list, large_list;
-    size_t ids, scores, perm_token, perm_weight, inv, hmid, yrows, xperm;
-    size_t hmid16, tiles, tile_count;
+    size_t status, counts, zero_bytes, offsets, ids, scores, perm_token, perm_weight, inv;
+    size_t xperm, hmid, yrows, tiles, tile_count;
+    int tile_cap;
     size_t total;
 };
 
-Workspace plan_workspace(const hmoe_layer_desc& d, size_t T, int local_experts);
+Workspace plan_workspace(const hmoe_layer_desc& d, size_t T);
 
 // Batches with at most this many (token, expert) assignments use the
 // weight-streaming GEMV for every expert; larger ones the tcgen05 GEMM.
@@ -22,29 +24,100 @@ constexpr int kGemvMaxAssignments = 64;
 // Upper bound of a token's rows (top_k routed + shared experts).
 constexpr int kMaxSlots = 96;
 
-struct GemvArgs {
-    const int32_t* list;        // experts to process
-    const int32_t* list_size;   // device count
-    const int32_t* offsets;     // [E+S+1] first permuted row of each expert
-    const uint32_t* perm_token; // gate/up: token of each permuted row
-    const float* perm_weight;   // down: routing weight of each permuted row
-    const float* act;           // gate/up: x [T,K]; down: hmid [R,K]
-    const int8_t* arena;
-    uint64_t stride, off0, off1; // expert stride; projection offsets
+// One expert-MLP pass over permuted rows.  Rows of one expert are cut into
+// tiles (expert, first row, rows, 0) of at most kTileRows rows; both
+// variants consume the same tile list.
+constexpr int kTileRows = 256;
+
+struct ExpertRun {
+    const __nv_bfloat16* xrows; // [rows_cap, H] permuted input rows (BF16)
+    const float* weight;        // [rows_cap] routing weight of each row
+    const int4* tiles;          // device tile list
+    const int32_t* tile_count;  // device count
+    int tile_cap;               // launch capacity (>= count)
+    int rows_cap;               // rows allocated in xrows / hmid / yrows
+    float* hmid32;              // [rows_cap, I] GEMV intermediate
+    __nv_bfloat16* hmid16;      // [rows_cap, I] GEMM intermediate
+    __nv_bfloat16* yrows;       // [rows_cap, H] weighted expert outputs
+    const int8_t* arena;        // experts indexed by tile expert id
+    uint64_t stride, gate_offset, up_offset, down_offset;
     const hmoe_expert_quant* quant;
-    int proj0;                  // quant index of the first projection
-    float* out;                 // gate/up: hmid [R,N]; down: y [R,N]
+    int experts;                // experts in the arena
+    int H, I;
+    int max_group;              // upper bound of rows of one expert
+    DeviceStatus* st;
+};
+
+struct GemvArgs {
+    const int4* tiles;
+    const int32_t* tile_count;
+    const __nv_bfloat16* act16; // gate/up input rows (BF16)
+    const float* act32;         // down input rows (FP32 intermediate)
+    const float* weight;        // down: routing weight per row
+    const int8_t* arena;
+    uint64_t stride, off0, off1;
+    const hmoe_expert_quant* quant;
+    int proj0;
+    float* out32;               // gate/up: FP32 intermediate
+    __nv_bfloat16* out16;       // down: BF16 weighted rows
     int K, N, KS;
 };
 
-hmoe_status launch_expert_gemv(bool gate_up, const GemvArgs& args, int list_capacity, int max_tokens,
+hmoe_status launch_expert_gemv(bool gate_up, const GemvArgs& args, int tile_capacity, int max_tokens,
                                cudaStream_t stream);
 
+// Segments of permuted rows: segment i holds rows of expert
+// expert_base + (i mod eps).  Rows come from offsets[i] .. offsets[i+1] or,
+// when offsets is null, from an exclusive scan of
+// counts[(i / eps) * count_stride + (i mod eps)] starting at row_base.
+constexpr int kMaxSegments = 512;
+
+struct SegSpec {
+    const int32_t* offsets;
+    const int32_t* counts;
+    int count_stride;
+    int nseg;
+    int eps;
+    int expert_base;
+    int row_base;
+};
+
 bool gemm_available();
-hmoe_status launch_expert_gemm_gate_up(const hmoe_layer_desc& d, const float* x, size_t T,
-                                       char* ws, const Workspace& w, int list_capacity,
-                                       cudaStream_t stream);
-hmoe_status launch_expert_gemm_down(const hmoe_layer_desc& d, size_t T, char* ws,
-                                    const Workspace& w, int list_capacity, cudaStream_t stream);
+hmoe_status gemm_gate_up(const ExpertRun& r, cudaStream_t stream);
+hmoe_status gemm_down(const ExpertRun& r, cudaStream_t stream);
+hmoe_status gemv_gate_up(const ExpertRun& r, cudaStream_t stream);
+hmoe_status gemv_down(const ExpertRun& r, cudaStream_t stream);
+
+hmoe_status launch_tile_list(const SegSpec& spec, int4* tiles, int32_t* tile_count, int capacity,
+                             cudaStream_t stream);
+// xrows[inv[t, s]] = BF16(x[t]) for every token t and slot s.
+hmoe_status launch_permute(const float* x, const int32_t* inv, int tokens, int slots, int H,
+                           __nv_bfloat16* xrows, cudaStream_t stream);
+
+// Upper bound of the tiles of `rows` rows spread over `segments` segments.
+int tile_capacity_for(long rows, int segments);
+
+hmoe_status launch_route(const float* x, const float* w, const float* bias, int T, int H, int E, int k,
+                         int softmax, int renorm, uint32_t* ids, float* scores, int32_t* counts,
+                         DeviceStatus* st, cudaStream_t stream);
+hmoe_status launch_group(const uint32_t* ids, const float* scores, const int32_t* counts, int T, int k,
+                         int E, int S, int32_t* offsets, uint32_t* perm_token, float* perm_weight,
+                         int32_t* inv, cudaStream_t stream);
+hmoe_status launch_combine(const __nv_bfloat16* yrows, const int32_t* inv, int tokens, int slots, int H,
+                           float* out, cudaStream_t stream);
+
+// Layer driver pieces shared by the single-GPU and expert-parallel paths.
+hmoe_status validate_layer(const hmoe_layer_desc* d);
+hmoe_status enqueue_route(const hmoe_layer_desc& d, const float* x, size_t T, char* ws, const Workspace& w,
+                          bool permute, cudaStream_t s);
+ExpertRun local_run(const hmoe_layer_desc& d, size_t T, char* ws, const Workspace& w);
+// gate/up then down of every tile of `r`; `stages` records stage events 3, 4.
+hmoe_status run_experts(const ExpertRun& r, bool gemv, bool stages, cudaStream_t s);
+bool use_gemv(long rows);
+
+// Records stage event i (0..5) when stage events are registered.  Under
+// stream capture the record becomes an external event node, so the caller
+// can still synchronise on and time the event after each graph launch.
+void stage(int i, cudaStream_t s);
 
 } // namespace hmoe

@@ -498,14 +498,10 @@ struct GroupArgs {
     const float* scores;   // [T, k]
     const int32_t* counts; // [E] routed counts
     int T, k, E, S;        // S shared experts
-    int small_max;         // experts with count <= small_max use the GEMV
     int32_t* offsets;      // [E+S+1]
     uint32_t* perm_token;  // [T*(k+S)] token of each permuted row
     float* perm_weight;    // [T*(k+S)] routing weight of each row
     int32_t* inv;          // [T*(k+S)] row of (token, slot); slots k.. = shared
-    int32_t* small_list;   // [E+S] experts for the GEMV, ascending id
-    int32_t* large_list;   // [E+S] experts for the tensor-core GEMM
-    int32_t* list_sizes;   // [2]
 };
 
 __device__ __forceinline__ int group_count(const GroupArgs& g, int e) {
@@ -513,55 +509,26 @@ __device__ __forceinline__ int group_count(const GroupArgs& g, int e) {
 }
 
 // One CTA per expert (routed then shared).  Tokens are placed in ascending
-// order inside the expert's group, exactly as routeBatch appends them.
+// order inside the expert's group, exactly as routeBatch appends them
+// (CpuRouterBackend.cpp:78-90); groups are laid out in ascending expert id.
 __global__ void __launch_bounds__(256) group_kernel(GroupArgs g) {
-    __shared__ int red[3][8];
+    __shared__ int red[8];
     __shared__ int warp_hits[8];
     __shared__ int base_s;
     const int e = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // Offset and list positions of expert e from the counts of e' < e.
-    int off = 0, small_before = 0, large_before = 0;
-    const int total = g.E + g.S;
-    const bool last = e == total - 1;
-    for (int j = tid; j < (last ? total : e); j += blockDim.x) {
-        const int c = group_count(g, j);
-        if (j < e) off += c;
-        const bool sm = c > 0 && c <= g.small_max;
-        const bool lg = c > g.small_max;
-        if (j < e) {
-            small_before += sm;
-            large_before += lg;
-        }
-    }
+    // Offset of expert e from the counts of e' < e.
+    int off = 0;
+    for (int j = tid; j < e; j += blockDim.x) off += group_count(g, j);
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        off += __shfl_xor_sync(0xffffffffu, off, o);
-        small_before += __shfl_xor_sync(0xffffffffu, small_before, o);
-        large_before += __shfl_xor_sync(0xffffffffu, large_before, o);
-    }
-    if (lane == 0) {
-        red[0][warp] = off;
-        red[1][warp] = small_before;
-        red[2][warp] = large_before;
-    }
+    for (int o = 16; o > 0; o >>= 1) off += __shfl_xor_sync(0xffffffffu, off, o);
+    if (lane == 0) red[warp] = off;
     __syncthreads();
     if (tid == 0) {
-        int o = 0, s = 0, l = 0;
-        for (int w = 0; w < 8; ++w) {
-            o += red[0][w];
-            s += red[1][w];
-            l += red[2][w];
-        }
-        const int c = group_count(g, e);
+        int o = 0;
+        for (int w = 0; w < 8; ++w) o += red[w];
         g.offsets[e] = o;
-        if (c > 0 && c <= g.small_max) g.small_list[s] = e;
-        if (c > g.small_max) g.large_list[l] = e;
-        if (last) {
-            g.offsets[total] = o + c;
-            g.list_sizes[0] = s + (c > 0 && c <= g.small_max);
-            g.list_sizes[1] = l + (c > g.small_max);
-        }
+        if (e == g.E + g.S - 1) g.offsets[e + 1] = o + group_count(g, e);
         base_s = o;
     }
     __syncthreads();
@@ -669,14 +636,10 @@ hmoe_status launch_route(const float* x, const float* w, const float* bias,
     return check_launch("hmoe route kernel");
 }
 
-hmoe_status launch_group(const uint32_t* ids, const float* scores,
-                         const int32_t* counts, int T, int k, int E, int S,
-                         int small_max, int32_t* offsets, uint32_t* perm_token,
-                         float* perm_weight, int32_t* inv, int32_t* small_list,
-                         int32_t* large_list, int32_t* list_sizes,
-                         cudaStream_t stream) {
-    GroupArgs g{ids, scores, counts, T, k, E, S, small_max, offsets, perm_token,
-                perm_weight, inv, small_list, large_list, list_sizes};
+hmoe_status launch_group(const uint32_t* ids, const float* scores, const int32_t* counts, int T, int k,
+                         int E, int S, int32_t* offsets, uint32_t* perm_token, float* perm_weight,
+                         int32_t* inv, cudaStream_t stream) {
+    GroupArgs g{ids, scores, counts, T, k, E, S, offsets, perm_token, perm_weight, inv};
     group_kernel<<<E + S, 256, 0, stream>>>(g);
     return check_launch("hmoe group kernel");
 }

@@ -38,7 +38,11 @@ EXPORTS = [
     "hmoe_set_variant", "hmoe_read_status", "hmoe_synth_normal",
     "hmoe_synth_zipf_bias", "hmoe_quantize_int8", "hmoe_synth_arena",
     "hmoe_set_stage_events", "hmoe_launch_count", "hmoe_moe_forward_host",
+    "hmoe_ep_expert_range", "hmoe_ep_plan", "hmoe_ep_unique_id", "hmoe_ep_comm_create",
+    "hmoe_ep_comm_destroy", "hmoe_ep_workspace_size", "hmoe_ep_moe_forward", "hmoe_ep_last_plan",
 ]
+EP_MAX_RANKS = 64
+EP_UNIQUE_ID_BYTES = 128
 HOST_IO = 1 << 62
 
 
@@ -63,6 +67,16 @@ class LayerDesc(ctypes.Structure):
         ("gate_offset", ctypes.c_uint64), ("up_offset", ctypes.c_uint64),
         ("down_offset", ctypes.c_uint64), ("quant", ctypes.c_void_p),
         ("ep_rank", ctypes.c_int32), ("ep_size", ctypes.c_int32),
+    ]
+
+
+class EpPlan(ctypes.Structure):
+    _fields_ = [
+        ("first_expert", ctypes.c_uint32), ("local_experts", ctypes.c_uint32),
+        ("tokens", ctypes.c_int64 * EP_MAX_RANKS),
+        ("send_rows", ctypes.c_int64 * EP_MAX_RANKS), ("send_offset", ctypes.c_int64 * EP_MAX_RANKS),
+        ("recv_rows", ctypes.c_int64 * EP_MAX_RANKS), ("recv_offset", ctypes.c_int64 * EP_MAX_RANKS),
+        ("recv_total", ctypes.c_int64),
     ]
 
 
@@ -100,6 +114,15 @@ def lib() -> ctypes.CDLL:
             "hmoe_set_variant": [i32],
             "hmoe_read_status": [vp, ctypes.POINTER(i32), ctypes.POINTER(i32), ctypes.POINTER(i32), vp],
             "hmoe_quantize_int8": [vp, sz, vp, vp, vp, vp],
+            "hmoe_ep_expert_range": [ctypes.c_uint32, i32, i32, ctypes.POINTER(ctypes.c_uint32),
+                                     ctypes.POINTER(ctypes.c_uint32)],
+            "hmoe_ep_plan": [vp, ctypes.c_uint32, ctypes.c_uint32, i32, i32, sz, ctypes.POINTER(EpPlan)],
+            "hmoe_ep_unique_id": [vp, sz],
+            "hmoe_ep_comm_create": [vp, i32, i32, i32, ctypes.POINTER(vp)],
+            "hmoe_ep_comm_destroy": [vp],
+            "hmoe_ep_workspace_size": [ctypes.POINTER(LayerDesc), sz, ctypes.POINTER(sz)],
+            "hmoe_ep_moe_forward": [ctypes.POINTER(LayerDesc), vp, vp, vp, sz, sz, vp, sz, vp],
+            "hmoe_ep_last_plan": [vp, ctypes.POINTER(EpPlan)],
         }
         for name, args in sigs.items():
             fn = getattr(L, name)
@@ -276,6 +299,8 @@ class DeviceLayer:
 
     def forward(self, x, y=None, stream=None):
         import torch
+        if self.desc.ep_size != 1:
+            raise ValueError("expert-parallel layer: use EpLayer.forward")
         T = x.shape[0]
         if y is None:
             y = torch.empty((T, self.cfg.hidden), dtype=torch.float32, device=x.device)
@@ -317,3 +342,95 @@ class DeviceLayer:
 
 def set_variant(v: int) -> None:
     check("hmoe_set_variant", lib().hmoe_set_variant(v))
+
+
+# ------------------------------------------------------ expert parallelism
+
+def ep_expert_range(experts: int, ep_size: int, ep_rank: int):
+    """(first, count) of the routed experts rank `ep_rank` owns."""
+    f, n = ctypes.c_uint32(), ctypes.c_uint32()
+    check("hmoe_ep_expert_range", lib().hmoe_ep_expert_range(experts, ep_size, ep_rank, ctypes.byref(f),
+                                                              ctypes.byref(n)))
+    return f.value, n.value
+
+
+def ep_plan(counts: np.ndarray, top_k: int, ep_rank: int, max_tokens: int) -> EpPlan:
+    """Transfer plan of `ep_rank` from counts[ep_size, experts] (int32)."""
+    counts = np.ascontiguousarray(counts, dtype=np.int32)
+    P, E = counts.shape
+    plan = EpPlan()
+    check("hmoe_ep_plan", lib().hmoe_ep_plan(counts.ctypes.data, E, top_k, P, ep_rank, max_tokens,
+                                             ctypes.byref(plan)))
+    return plan
+
+
+def ep_unique_id() -> bytes:
+    buf = ctypes.create_string_buffer(EP_UNIQUE_ID_BYTES)
+    check("hmoe_ep_unique_id", lib().hmoe_ep_unique_id(buf, EP_UNIQUE_ID_BYTES))
+    return buf.raw
+
+
+def local_host_layer(host: HostLayer, ep_size: int, ep_rank: int) -> HostLayer:
+    """The slice of `host` that rank `ep_rank` holds: its routed experts
+    followed by every shared expert (router replicated)."""
+    cfg = host.cfg
+    E, S, stride = cfg.experts, cfg.shared_experts, cfg.expert_stride
+    f, n = ep_expert_range(E, ep_size, ep_rank)
+    ids = list(range(f, f + n)) + list(range(E, E + S))
+    arena = np.concatenate([host.arena[e * stride:(e + 1) * stride] for e in ids])
+    qsz = ctypes.sizeof(ExpertQuant)
+    quant = np.concatenate([host.quant[e * qsz:(e + 1) * qsz] for e in ids])
+    return HostLayer(cfg, host.router_w, host.router_bias, arena, quant, host.scales[ids], host.zps[ids])
+
+
+class EpComm:
+    """One rank's NCCL communicator (collective create: every rank calls it
+    with the same unique id, on its own device)."""
+
+    def __init__(self, unique_id: bytes, rank: int, size: int, timeout_ms: int = 60000):
+        h = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(unique_id, EP_UNIQUE_ID_BYTES)
+        check("hmoe_ep_comm_create", lib().hmoe_ep_comm_create(buf, rank, size, timeout_ms, ctypes.byref(h)))
+        self.handle = h
+        self.rank, self.size = rank, size
+
+    def last_plan(self) -> EpPlan:
+        plan = EpPlan()
+        check("hmoe_ep_last_plan", lib().hmoe_ep_last_plan(self.handle, ctypes.byref(plan)))
+        return plan
+
+    def close(self):
+        if self.handle:
+            h, self.handle = self.handle, None
+            check("hmoe_ep_comm_destroy", lib().hmoe_ep_comm_destroy(h))
+
+
+class EpLayer(DeviceLayer):
+    """This rank's share of an expert-parallel layer on the current device."""
+
+    def __init__(self, host: HostLayer, comm: EpComm, device="cuda"):
+        super().__init__(local_host_layer(host, comm.size, comm.rank), device)
+        self.full_host = host
+        self.comm = comm
+        self.desc.ep_rank, self.desc.ep_size = comm.rank, comm.size
+
+    def ep_workspace(self, max_tokens: int):
+        import torch
+        n = ctypes.c_size_t()
+        check("hmoe_ep_workspace_size", lib().hmoe_ep_workspace_size(ctypes.byref(self.desc), max_tokens,
+                                                                     ctypes.byref(n)))
+        if self._ws is None or self._ws.numel() < n.value:
+            self._ws = torch.empty(n.value, dtype=torch.uint8, device=self.arena.device)
+        return self._ws
+
+    def forward(self, x, y=None, stream=None, max_tokens: Optional[int] = None):
+        import torch
+        T = x.shape[0]
+        max_tokens = max_tokens or max(T, 1)
+        if y is None:
+            y = torch.empty((T, self.cfg.hidden), dtype=torch.float32, device=x.device)
+        ws = self.ep_workspace(max_tokens)
+        check("hmoe_ep_moe_forward", lib().hmoe_ep_moe_forward(
+            ctypes.byref(self.desc), self.comm.handle, x.data_ptr() if T else None, y.data_ptr() if T else None,
+            T, max_tokens, ws.data_ptr(), ws.numel(), _stream(stream)))
+        return y

@@ -142,11 +142,12 @@ typedef struct {
  * the double accumulation (what the reference computes for a hidden row
  * extended by 1 and a router matrix extended by the bias row).
  *
- * ep_rank/ep_size: expert parallelism (1 process per GPU).  With
- * ep_size > 1 this rank owns routed experts
- * [ep_rank*experts/ep_size, (ep_rank+1)*experts/ep_size) and `arena`,
- * `quant` cover only those (plus the shared experts); see
- * hmoe_ep_moe_forward. */
+ * ep_rank/ep_size: expert parallelism (one process per GPU).  The
+ * single-GPU entry points need ep_rank = 0, ep_size = 1.  For
+ * hmoe_ep_moe_forward this rank owns the routed experts
+ * hmoe_ep_expert_range(experts, ep_size, ep_rank) returns, and `arena` /
+ * `quant` hold only those (local ids 0..count-1) followed by the shared
+ * experts, which every rank holds and applies to its own tokens. */
 typedef struct {
     uint32_t hidden;          /* H */
     uint32_t intermediate;    /* I */
@@ -214,7 +215,10 @@ hmoe_status hmoe_set_variant(int32_t variant);
  * cudaEvent_t handles (passed as void*) that every later hmoe_moe_forward
  * records on its stream at the stage boundaries: [0] start, [1] after the
  * router, [2] after the grouping, [3] after gate/up, [4] after down,
- * [5] after the combine.  count = 0 unregisters them.  Process-wide, for
+ * [5] after the combine.  count = 0 unregisters them.  Stage [2] covers
+ * the grouping, the BF16 row permutation and the tile list (for
+ * hmoe_ep_moe_forward also the count exchange and the dispatch); [5]
+ * after the return transfer and the combine.  Process-wide, for
  * benchmarks; the events are the caller's. */
 hmoe_status hmoe_set_stage_events(void *const *events, int32_t count);
 
@@ -228,6 +232,83 @@ int64_t hmoe_launch_count(void);
 hmoe_status hmoe_read_status(void *workspace, int32_t *status,
                              int32_t *near_ties, int32_t *sequential_logits,
                              void *stream);
+
+/* ------------------------------------------------ expert parallelism
+ *
+ * One process per GPU.  Routed experts are split into contiguous ranges,
+ * tokens stay data-parallel: each rank routes its own tokens, sends each
+ * row (BF16) and its routing weight to the rank owning the expert, runs its
+ * experts over what it received, and gets the weighted output rows back for
+ * a combine in ascending expert id.  Transfers are NCCL point-to-point
+ * operations over NVLink/NVSwitch, loaded with dlopen (HMOE_NCCL_LIBRARY
+ * overrides the library name).  The reference is single-process and
+ * single-device: these entry points have no counterpart there. */
+#define HMOE_EP_MAX_RANKS 64
+#define HMOE_EP_UNIQUE_ID_BYTES 128
+
+typedef struct hmoe_ep_comm hmoe_ep_comm;
+
+/* Expert ownership: rank r owns routed experts [first, first + count),
+ * first = r*(E/P) + min(r, E%P) (e.g. 60 experts on 8 ranks: 8,8,8,8,7,7,7,7).
+ * Host only. */
+hmoe_status hmoe_ep_expert_range(uint32_t experts, int32_t ep_size,
+                                 int32_t ep_rank, uint32_t *first,
+                                 uint32_t *count);
+
+/* Transfer plan of one rank, from the routed row counts of every
+ * (source rank, expert) pair, counts[ep_size][experts].  Host only; every
+ * rank computes it from the same counts, so a rejection (negative counts,
+ * a total that is not a multiple of top_k, a rank with more than max_tokens
+ * tokens -> HMOE_WORKSPACE_TOO_SMALL) happens on all ranks alike. */
+typedef struct {
+    uint32_t first_expert, local_experts;
+    int64_t tokens[HMOE_EP_MAX_RANKS];      /* tokens of each rank */
+    int64_t send_rows[HMOE_EP_MAX_RANKS];   /* rows to each peer ... */
+    int64_t send_offset[HMOE_EP_MAX_RANKS]; /* ... from this permuted row */
+    int64_t recv_rows[HMOE_EP_MAX_RANKS];   /* rows from each peer ... */
+    int64_t recv_offset[HMOE_EP_MAX_RANKS]; /* ... into this receive row */
+    int64_t recv_total;
+} hmoe_ep_plan_t;
+hmoe_status hmoe_ep_plan(const int32_t *counts, uint32_t experts,
+                         uint32_t top_k, int32_t ep_size, int32_t ep_rank,
+                         size_t max_tokens, hmoe_ep_plan_t *plan);
+
+/* NCCL unique id (HMOE_EP_UNIQUE_ID_BYTES bytes) made on one rank and
+ * shared with the others by the caller. */
+hmoe_status hmoe_ep_unique_id(void *id, size_t bytes);
+
+/* Collective over ep_size processes: creates this rank's communicator on
+ * the current device (allocates pinned host memory and an event; blocks
+ * until every rank has joined).  timeout_ms bounds every later host wait
+ * for peers; when it expires the communicator is aborted and
+ * hmoe_ep_moe_forward returns HMOE_TIMEOUT. */
+hmoe_status hmoe_ep_comm_create(const void *unique_id, int32_t rank,
+                                int32_t size, int32_t timeout_ms,
+                                hmoe_ep_comm **comm);
+hmoe_status hmoe_ep_comm_destroy(hmoe_ep_comm *comm);
+
+/* The transfer plan of the communicator's last hmoe_ep_moe_forward
+ * (observability: received rows, per-peer transfer sizes). */
+hmoe_status hmoe_ep_last_plan(const hmoe_ep_comm *comm, hmoe_ep_plan_t *plan);
+
+/* Scratch bytes of hmoe_ep_moe_forward for up to max_tokens tokens on
+ * every rank (the receive side holds ep_size*max_tokens*top_k rows, the
+ * worst case of every token of every rank choosing this rank's experts). */
+hmoe_status hmoe_ep_workspace_size(const hmoe_layer_desc *desc,
+                                   size_t max_tokens, size_t *bytes);
+
+/* Collective: one MoE layer forward of this rank's `tokens` tokens
+ * (0 allowed) with experts spread over the communicator's ranks.  Every
+ * rank passes the same desc (except arena/quant/ep_rank) and the same
+ * max_tokens.  Enqueues on `stream` and synchronises on the host once, to
+ * read the exchanged row counts (bounded by the communicator's timeout).
+ * The result equals hmoe_moe_forward on the concatenation of all ranks'
+ * tokens for the same expert-MLP variant. */
+hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc *desc,
+                                hmoe_ep_comm *comm, const float *x, float *y,
+                                size_t tokens, size_t max_tokens,
+                                void *workspace, size_t workspace_bytes,
+                                void *stream);
 
 /* ----------------------------------------- host-side synthetic inputs */
 

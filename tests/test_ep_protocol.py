@@ -1,0 +1,183 @@
+"""Expert-parallel protocol on CPU ranks (gloo), checked against the oracle.
+
+Each rank routes its own tokens with the CPU oracle, all-gathers the
+per-(rank, expert) row counts, plans its transfers with the library's
+hmoe_ep_plan (the same host code hmoe_ep_moe_forward runs), ships rows and
+routing weights to the expert owners, runs the owners' experts (oracle
+expert MLP, local arena from local_host_layer), ships weighted outputs back
+and combines in ascending expert id.  The result must equal the
+single-process oracle layer (oracle/hmoe_oracle.c hmo_moe_layer, which
+follows MoERuntime.cpp:58-349) on the concatenated batch bit for bit: the
+protocol only moves rows, so any difference is a planning or ordering bug.
+"""
+import os
+import socket
+import sys
+from datetime import timedelta
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PATHS = [os.path.join(ROOT, "hypermoe-engine_b200"), os.path.join(ROOT, "oracle")]
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _expert(hl, e):
+    c = hl.cfg
+    HI = c.proj_bytes
+    blob = hl.arena[e * c.expert_stride:e * c.expert_stride + 3 * HI]
+    return (blob[:HI].reshape(c.hidden, c.intermediate), blob[HI:2 * HI].reshape(c.hidden, c.intermediate),
+            blob[2 * HI:].reshape(c.intermediate, c.hidden), hl.scales[e], hl.zps[e])
+
+
+def _rank_main(rank, P, port, cfg_args, Ts, seed, q):
+    for p in PATHS:
+        sys.path.insert(0, p)
+    import torch
+    import torch.distributed as dist
+
+    import hmoe_api as H
+    import oracle as O
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=P, timeout=timedelta(seconds=120))
+    try:
+        cfg = H.LayerConfig(*cfg_args)
+        hl = H.make_host_layer(cfg, seed=seed, threads=1)
+        local = H.local_host_layer(hl, P, rank)
+        E, S, k, Hd = cfg.experts, cfg.shared_experts, cfg.top_k, cfg.hidden
+        x_all = H.make_tokens(cfg, sum(Ts), seed=seed, threads=1)
+        t0 = sum(Ts[:rank])
+        x = x_all[t0:t0 + Ts[rank]]
+        T = x.shape[0]
+        L = O.port()
+        if T:
+            ids, sc, off, gt, gs = O.route(L, x, hl.router_w, hl.router_bias, k, cfg.softmax, cfg.renormalize)
+        else:
+            off, gt, gs = np.zeros(E + 1, np.int32), np.zeros(0, np.uint32), np.zeros(0, np.float32)
+        counts = torch.from_numpy(np.diff(off).astype(np.int32))
+        gathered = [torch.empty_like(counts) for _ in range(P)]
+        dist.all_gather(gathered, counts)
+        counts_all = np.stack([g.numpy() for g in gathered])
+        max_tokens = max(Ts)
+        plan = H.ep_plan(counts_all, k, rank, max_tokens)
+        assert plan.tokens[rank] == T
+
+        # dispatch: routed rows grouped by expert, tokens ascending
+        xrows = x[gt.astype(np.int64)] if T else np.zeros((0, Hd), np.float32)
+        wrows = gs.astype(np.float32)
+        xin = np.zeros((plan.recv_total, Hd), np.float32)
+        win = np.zeros(plan.recv_total, np.float32)
+
+        def exchange(send_parts, recv_parts):
+            reqs = []
+            for peer in range(P):
+                sb, rb = send_parts[peer], recv_parts[peer]
+                if peer == rank:
+                    if rb is not None:
+                        rb[...] = sb
+                    continue
+                if sb is not None and sb.size:
+                    reqs.append(dist.isend(torch.from_numpy(np.ascontiguousarray(sb)), peer))
+                if rb is not None and rb.size:
+                    reqs.append((dist.irecv(torch.from_numpy(rb), peer), rb))
+            for r in reqs:
+                (r[0] if isinstance(r, tuple) else r).wait()
+
+        so, sr = plan.send_offset, plan.send_rows
+        ro, rr = plan.recv_offset, plan.recv_rows
+        exchange([xrows[so[p]:so[p] + sr[p]] for p in range(P)], [xin[ro[p]:ro[p] + rr[p]] for p in range(P)])
+        exchange([wrows[so[p]:so[p] + sr[p]] for p in range(P)], [win[ro[p]:ro[p] + rr[p]] for p in range(P)])
+
+        # owner: local experts over (source, expert) segments
+        yin = np.zeros_like(xin)
+        row = 0
+        for s in range(P):
+            for el in range(plan.local_experts):
+                n = int(counts_all[s, plan.first_expert + el])
+                if n:
+                    y = O.expert_mlp(L, xin[row:row + n], *_expert(local, el))
+                    yin[row:row + n] = win[row:row + n, None] * y
+                row += n
+        assert row == plan.recv_total
+
+        # return to the source rows
+        yrows = np.zeros_like(xrows)
+        exchange([yin[ro[p]:ro[p] + rr[p]] for p in range(P)], [yrows[so[p]:so[p] + sr[p]] for p in range(P)])
+
+        # combine: ascending expert id (row order), then shared experts
+        out = np.zeros((T, Hd), np.float32)
+        for r in range(len(gt)):
+            out[gt[r]] += yrows[r]
+        for s in range(S):
+            if T:
+                out += np.float32(1.0) * O.expert_mlp(L, x, *_expert(local, plan.local_experts + s))
+        ref = O.moe_layer_port(hl, x_all)[0][t0:t0 + T]
+        q.put((rank, bool(np.array_equal(out, ref)), float(np.abs(out - ref).max()) if T else 0.0))
+    except Exception as exc:  # reported to the parent
+        q.put((rank, False, repr(exc)))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(P, cfg_args, Ts, seed=0):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank_main, args=(r, P, port, cfg_args, Ts, seed, q)) for r in range(P)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in range(P):
+            rank, ok, info = q.get(timeout=300)
+            results[rank] = (ok, info)
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for r in range(P):
+        assert results[r][0], f"rank {r}: {results[r][1]}"
+
+
+def test_ep_protocol_c1_two_ranks():
+    # C1 layer: H256 E8 k2 I512, softmax + renormalise, ragged token counts
+    _run(2, (256, 512, 8, 2, True, True, 0, None), (5, 3))
+
+
+def test_ep_protocol_shared_uneven_three_ranks():
+    # 7 experts on 3 ranks (3, 2, 2), 2 shared experts, Zipf-biased router,
+    # no renormalisation, and a rank with no tokens
+    _run(3, (128, 128, 7, 2, True, False, 2, 1.1), (4, 0, 3), seed=1)
+
+
+def test_ep_plan_rejections():
+    for p in PATHS:
+        sys.path.insert(0, p)
+    import hmoe_api as H
+    counts = np.array([[1, 1, 2], [0, 3, 1]], np.int32)
+    plan = H.ep_plan(counts, 2, 0, 2)
+    assert (plan.first_expert, plan.local_experts) == (0, 2)
+    assert list(plan.tokens[:2]) == [2, 2]
+    assert list(plan.send_rows[:2]) == [2, 2] and list(plan.send_offset[:2]) == [0, 2]
+    assert list(plan.recv_rows[:2]) == [2, 3] and list(plan.recv_offset[:2]) == [0, 2]
+    assert plan.recv_total == 5
+    with pytest.raises(H.HmoeError) as e:
+        H.ep_plan(counts, 2, 0, 1)  # a rank with more tokens than max_tokens
+    assert e.value.code == 6
+    with pytest.raises(H.HmoeError) as e:
+        H.ep_plan(np.array([[1, 1, 1], [0, 0, 0]], np.int32), 2, 1, 4)  # 3 rows is not a multiple of k
+    assert e.value.code == 1
+    with pytest.raises(H.HmoeError):
+        H.ep_plan(np.array([[-1, 1, 2], [0, 0, 0]], np.int32), 2, 0, 4)
+    assert [H.ep_expert_range(60, 8, r) for r in range(8)] == [
+        (0, 8), (8, 8), (16, 8), (24, 8), (32, 7), (39, 7), (46, 7), (53, 7)]

@@ -1,0 +1,106 @@
+"""The reference-signature C++ launchers (hypermoe-engine_b200/host/
+CudaKernelsShim.cpp, lib/libhmoe_shim.so) over the C ABI.
+
+CPU: the shim exports exactly the seven hot-path symbols of
+src/backend/cuda/CudaKernels.hpp:10-46 (Itanium-mangled, so the signatures
+are part of the names); it compiles against the reference's own header when
+that tree is present; and a plan mismatch in int8WeightMatmulCooperative
+throws std::invalid_argument as CudaKernels.cu:330-333 does.
+GPU: the launchers, called by their mangled names, reproduce the
+reference's golden vectors (tests/phase23_tests.cpp:178-247,
+tests/phase18_19_tests.cpp:251-263).
+"""
+import ctypes
+import os
+import subprocess
+
+import pytest
+
+import hmoe_api as H
+from tolerance import assert_op_close
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG = os.path.join(ROOT, "hypermoe-engine_b200")
+SHIM = os.path.join(PKG, "lib", "libhmoe_shim.so")
+SHIM_SRC = os.path.join(PKG, "host", "CudaKernelsShim.cpp")
+REF_SRC = "/root/reference/src"
+
+SYMBOLS = {
+    "activation": "_ZN8hypermoe7backend4cuda7kernels10activationEiPKfPfmPv",
+    "gatherRows": "_ZN8hypermoe7backend4cuda7kernels10gatherRowsEPKfPfPKjmmPv",
+    "routerTopK": "_ZN8hypermoe7backend4cuda7kernels10routerTopKEPfmmmbbPjS3_Pv",
+    "scatterAddRows": "_ZN8hypermoe7backend4cuda7kernels14scatterAddRowsEPKfPfPKjS4_mmPv",
+    "int8WeightMatmul": "_ZN8hypermoe7backend4cuda7kernels16int8WeightMatmulEPKfPKaPfmmmfiPv",
+    "int8WeightMatmulCooperative":
+        "_ZN8hypermoe7backend4cuda7kernels27int8WeightMatmulCooperativeEPKfPKaPfS7_mmmmfiPv",
+    "zero": "_ZN8hypermoe7backend4cuda7kernels4zeroEPfmPv",
+}
+
+
+def _shim():
+    if not os.path.exists(SHIM):
+        pytest.fail(f"{SHIM} is not built")
+    H.lib()
+    return ctypes.CDLL(SHIM)
+
+
+def test_shim_exports_reference_symbols():
+    out = subprocess.run(["nm", "-D", "--defined-only", SHIM], check=True, capture_output=True, text=True).stdout
+    names = {ln.split()[-1] for ln in out.splitlines() if "kernels" in ln}
+    assert names == set(SYMBOLS.values())
+    lib = _shim()
+    for mangled in SYMBOLS.values():
+        getattr(lib, mangled)
+
+
+@pytest.mark.skipif(not os.path.isdir(REF_SRC), reason="reference tree not present")
+def test_shim_compiles_against_reference_header():
+    subprocess.run(["g++", "-std=c++20", "-fsyntax-only", "-DHMOE_SHIM_WITH_REFERENCE_HEADERS",
+                    "-I", os.path.join(ROOT, "include"), "-I", REF_SRC, SHIM_SRC], check=True)
+
+
+def test_shim_cooperative_mismatch_throws_invalid_argument(tmp_path):
+    exe = tmp_path / "harness"
+    subprocess.run(["g++", "-std=c++17", "-o", str(exe), os.path.join(ROOT, "tests", "shim", "shim_harness.cpp"),
+                    "-L", os.path.dirname(SHIM), "-lhmoe_shim", "-lhmoe",
+                    f"-Wl,-rpath,{os.path.dirname(SHIM)}"], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.strip()
+    assert out == "invalid_argument: cooperative INT8 GEMM scratch/partition mismatch"
+
+
+@pytest.mark.gpu
+def test_shim_launchers_on_gpu(cuda, golden):
+    import sys
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "tests", "golden"))
+    from make_golden import GEMM_SHAPES, phase23_inputs
+    lib = _shim()
+    f = {k: getattr(lib, v) for k, v in SYMBOLS.items()}
+    vp, sz = ctypes.c_void_p, ctypes.c_size_t
+    f["int8WeightMatmul"].argtypes = [vp, vp, vp, sz, sz, sz, ctypes.c_float, ctypes.c_int32, vp]
+    f["gatherRows"].argtypes = [vp, vp, vp, sz, sz, vp]
+    f["scatterAddRows"].argtypes = [vp, vp, vp, vp, sz, sz, vp]
+    f["zero"].argtypes = [vp, sz, vp]
+    for fn in f.values():
+        fn.restype = None
+    s = torch.cuda.current_stream().cuda_stream
+    g = golden("int8_gemm_phase23.npz")
+    for (r, k, n) in GEMM_SHAPES:
+        x, q = phase23_inputs(r, k, n)
+        dx, dq = torch.from_numpy(x).to(cuda), torch.from_numpy(q).to(cuda)
+        out = torch.empty((r, n), dtype=torch.float32, device=cuda)
+        f["int8WeightMatmul"](dx.data_ptr(), dq.data_ptr(), out.data_ptr(), r, k, n, 0.003, -3, s)
+        torch.cuda.synchronize()
+        assert_op_close(out.cpu().numpy(), g[f"out_{r}_{k}_{n}"])
+    # gather {2,3,-2,-1} and scatter {-4,-2,0,0,1,1.5} (phase18_19_tests.cpp:251-263)
+    src = torch.tensor([[-2.0, -1.0], [0.0, 1.0], [2.0, 3.0]], device=cuda)
+    rows = torch.tensor([2, 0], dtype=torch.int32, device=cuda)
+    gathered = torch.empty((2, 2), device=cuda)
+    f["gatherRows"](src.data_ptr(), gathered.data_ptr(), rows.data_ptr(), 2, 2, s)
+    w = torch.tensor([0.5, 2.0], device=cuda)
+    acc = torch.full((3, 2), 7.0, device=cuda)
+    f["zero"](acc.data_ptr(), 6, s)
+    f["scatterAddRows"](gathered.data_ptr(), acc.data_ptr(), rows.data_ptr(), w.data_ptr(), 2, 2, s)
+    torch.cuda.synchronize()
+    assert gathered.cpu().numpy().ravel().tolist() == [2.0, 3.0, -2.0, -1.0]
+    assert acc.cpu().numpy().ravel().tolist() == [-4.0, -2.0, 0.0, 0.0, 1.0, 1.5]
