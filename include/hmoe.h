@@ -206,6 +206,19 @@ hmoe_status hmoe_moe_forward_host(const hmoe_layer_desc *desc,
                                   size_t tokens, void *workspace,
                                   size_t workspace_bytes, void *stream);
 
+/* hmoe_moe_forward with no caller workspace: scratch is a file-scope
+ * device array of 16 MiB per device inside libhmoe.so, so the call allocates
+ * nothing.  No counterpart in the reference (whose layer path allocates
+ * through CudaMemoryPool); it serves callers that cannot allocate device
+ * memory at the call site.  Batches whose hmoe_workspace_size exceeds
+ * 16 MiB return HMOE_WORKSPACE_TOO_SMALL (C3 layer: up to 185 tokens).
+ * Calls that overlap in time on one device race on the shared scratch.
+ * The first call on a device looks the array up (cudaGetSymbolAddress);
+ * make it before any stream capture on that device. */
+hmoe_status hmoe_moe_forward_noalloc(const hmoe_layer_desc *desc,
+                                     const float *x, float *y, size_t tokens,
+                                     void *stream);
+
 /* Forces the expert-MLP variant for measurement: 0 = automatic (GEMV for
  * experts with few tokens, tensor-core GEMM otherwise), 1 = GEMV only,
  * 2 = tensor-core GEMM only.  Process-wide. */

@@ -1,0 +1,47 @@
+"""hmoe_moe_forward_noalloc (scratch in a static device array, no caller
+workspace) against hmoe_moe_forward on the same inputs: two calls in a row
+must both equal the workspace entry point bit for bit, and a batch beyond
+the 16 MiB scratch must be refused.  Collected last so it also runs after
+every other GPU test in the same process."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import hmoe_api as H
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("cfg_name,T", [("c1", 64), ("c3", 16), ("c3", 1), ("c2", 3)])
+def test_noalloc_forward_matches_workspace_forward(cuda, cfg_name, T):
+    import torch
+    cfg = H.CONFIGS[cfg_name]
+    hl = H.make_host_layer(cfg, seed=11)
+    x = torch.from_numpy(H.make_tokens(cfg, T, seed=11)).to(cuda)
+    dl = H.DeviceLayer(hl, cuda)
+    ref = dl.forward(x).cpu().numpy()
+    s = torch.cuda.current_stream().cuda_stream
+    outs = []
+    for _ in range(2):
+        y = torch.full((T, cfg.hidden), float("nan"), device=cuda)
+        H.check("hmoe_moe_forward_noalloc",
+                H.lib().hmoe_moe_forward_noalloc(ctypes.byref(dl.desc), x.data_ptr(), y.data_ptr(), T, s))
+        torch.cuda.synchronize()
+        outs.append(y.cpu().numpy())
+    for y in outs:
+        assert np.array_equal(y, ref), float(np.nanmax(np.abs(y - ref)))
+
+
+def test_noalloc_rejects_oversized_batch(cuda):
+    import torch
+    cfg = H.CONFIGS["c3"]
+    hl = H.make_host_layer(cfg, seed=11)
+    dl = H.DeviceLayer(hl, cuda)
+    T = 512
+    x = torch.zeros((T, cfg.hidden), device=cuda)
+    y = torch.zeros((T, cfg.hidden), device=cuda)
+    rc = H.lib().hmoe_moe_forward_noalloc(ctypes.byref(dl.desc), x.data_ptr(), y.data_ptr(), T,
+                                          torch.cuda.current_stream().cuda_stream)
+    assert rc == 6  # HMOE_WORKSPACE_TOO_SMALL
+    assert b"16 MiB" in H.lib().hmoe_last_error()
