@@ -61,6 +61,16 @@ __device__ __forceinline__ void dequant4(uint32_t w, float zp, float out[4]) {
     out[3] = static_cast<float>(static_cast<int8_t>(w >> 24)) - zp;
 }
 
+// Four INT8 weights -> q - zp, exact, without integer-to-float conversions:
+// float(2^23 + (q + 128)) - off with off = 2^23 + 128 + zp.
+__device__ __forceinline__ void dequant4_fast(uint32_t w, float off, float out[4]) {
+    const uint32_t u = w ^ 0x80808080u;
+    out[0] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - off;
+    out[1] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - off;
+    out[2] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - off;
+    out[3] = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - off;
+}
+
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + expf(-g)); }
 
 } // namespace hmoe

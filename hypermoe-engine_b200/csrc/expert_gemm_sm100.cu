@@ -51,6 +51,9 @@
 
 namespace hmoe {
 
+bool map_weights_box(CUtensorMap* m, const int8_t* base, int N, int K, int experts, uint64_t stride, int box_n,
+                     int box_k);
+
 namespace {
 
 constexpr int kTileT = 256;   // tokens per work item (pair MMA N <= 256)
@@ -562,14 +565,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // INT8 weights of one projection across all experts: dims {N, K, experts},
 // box [64 k][64 n].
 bool map_weights(CUtensorMap* m, const int8_t* base, int N, int K, int experts, uint64_t stride) {
-    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(K),
-                                static_cast<cuuint64_t>(experts)};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(N), stride};
-    const cuuint32_t box[3] = {64, kBK, 1};
-    const cuuint32_t es[3] = {1, 1, 1};
-    return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(base), dims, strides, box, es,
-                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return map_weights_box(m, base, N, K, experts, stride, 64, kBK);
 }
 
 // BF16 rows [rows, K] (K contiguous), 128-byte swizzle, box 64 x 128 rows.
@@ -624,6 +620,23 @@ hmoe_status launch_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUte
 }
 
 } // namespace
+
+// INT8 weights of one projection across all experts, dims {N, K, experts}
+// (the packed [in,out] layout, N contiguous), box [box_k][box_n], no swizzle.
+bool map_weights_box(CUtensorMap* m, const int8_t* base, int N, int K, int experts, uint64_t stride, int box_n,
+                     int box_k) {
+    if (!encode_fn()) return false;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(K),
+                                static_cast<cuuint64_t>(experts)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(N), stride};
+    const cuuint32_t box[3] = {static_cast<cuuint32_t>(box_n), static_cast<cuuint32_t>(box_k), 1};
+    const cuuint32_t es[3] = {1, 1, 1};
+    return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<int8_t*>(base), dims, strides, box, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int device_sm_count() { return sm_count(); }
 
 bool gemm_available() {
     static int avail = -1;

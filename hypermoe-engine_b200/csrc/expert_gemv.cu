@@ -1,216 +1,271 @@
-// expert_gemv.cu -- split-K weight-streaming INT8 expert projections for
-// expert groups with few tokens (decode), where the layer is HBM-bound.
+// expert_gemv.cu -- weight-streaming expert MLP for decode-sized groups.
 //
-// Replaces, for those groups, the per-expert projections of
-// ExpertMlpExecutor::execute (src/experts/ExpertExecutor.cpp:118-131) that
-// the reference runs as int8WeightMatmulKernel / cooperativeInt8Kernel
-// (src/backend/cuda/CudaKernels.cu:30-107) plus activationKernel and a
-// cuBLAS multiply.
+// Same math as the tensor-core path and as ExpertMlpExecutor::execute
+// (src/experts/ExpertExecutor.cpp:118-131):
+//     gate/up:  h[r,c] = SiLU(sg * sum_k x[r,k] Wg[k,c]) * (su * sum_k x[r,k] Wu[k,c])
+//     down:     y[r,c] = w_r * (sd * sum_k h[r,k] Wd[k,c])
+// with W = q - zp dequantised exactly, FP32 accumulation.
 //
-// One launch handles every tile of the device-built tile list.  A thread
-// block cluster of KS CTAs owns (tile, 256 output columns); CTA r of the
-// cluster streams rows [r*K/KS, (r+1)*K/KS) of the INT8 weight matrix
-// ([K,N] row-major, each lane reading 8 consecutive columns with one 64-bit
-// load per row) and accumulates x * (q - zp) in FP32 for every token of the
-// group.  The KS partial tiles are summed through distributed shared memory
-// in rank order -- a fixed order, so results are deterministic and no
-// global scratch or atomics are needed.  The epilogue applies the
-// projection scale and either SwiGLU (gate/up: h = SiLU(sg*G) * (su*U)) or
-// the routing weight (down: y = w * sd * D).
+// Decode touches each expert for a handful of rows, so the kernel is a
+// stream of the expert's INT8 weights at HBM speed.  A thread block cluster
+// of KS CTAs owns (tile, 256 output columns); CTA r of the cluster streams
+// K rows [r*kc, (r+1)*kc) of the projection(s) through a 4-stage ring of
+// TMA boxes [32 k][256 n] (8 KB each, issued by one thread, so each CTA
+// keeps up to 64 KB of weights in flight).  Thread (cq, kr) owns columns
+// 4cq..4cq+3 and the box rows kr (mod 4): one 32-bit shared load feeds
+// four exact dequantisations and four FMAs per token.  The four row groups
+// and the KS ranks are added in a fixed order (shared memory, then
+// distributed shared memory), so results are deterministic.
 #include "common.cuh"
 #include "layer.cuh"
+#include "sm100.cuh"
 
 #include <cooperative_groups.h>
+
+#include <algorithm>
 
 namespace cg = cooperative_groups;
 
 namespace hmoe {
 
-constexpr int kGemvWarps = 8;
-constexpr int kGemvCols = 256; // 32 lanes x 8 columns
-constexpr int kGemvRows = 8;   // weight rows in flight per lane
+namespace {
 
+constexpr int kVThreads = 256;
+constexpr int kVCols = 256;   // output columns per CTA (box width, bytes)
+constexpr int kVRows = 32;    // K rows per box
+constexpr int kVStages = 4;   // boxes (per projection) in flight
+constexpr int kVGroups = kVThreads / (kVCols / 4); // 4 row groups
+constexpr int kVMaxKc = 1024; // K rows per CTA (bounds the token staging)
+constexpr uint64_t kVWaitNs = 2000000000ull;
 
+struct GemvSmem {
+    int ring, xs, bars, total;
+};
 
-template <bool GATE_UP, int kGemvTokens>
-__global__ void __launch_bounds__(kGemvWarps * 32) expert_gemv_kernel(GemvArgs a) {
+__host__ __device__ inline GemvSmem gemv_smem(int NP, int tok, int kc) {
+    GemvSmem m{};
+    const int ring = kVStages * NP * kVRows * kVCols;
+    const int red = kVGroups * tok * NP * kVCols * 4; // partial sums, overlaid on the ring
+    m.ring = 0;
+    int off = (ring > red ? ring : red);
+    off = (off + 15) & ~15;
+    m.xs = off;
+    off += tok * kc * 4;
+    off = (off + 15) & ~15;
+    m.bars = off;
+    off += kVStages * 8;
+    m.total = off + 128; // room to align the base to 128 bytes
+    return m;
+}
+
+template <bool GATE_UP, int TOK>
+__global__ void __launch_bounds__(kVThreads, 2)
+    expert_gemv_kernel(const __grid_constant__ CUtensorMap tm0, const __grid_constant__ CUtensorMap tm1, GemvArgs a,
+                       int kc) {
     constexpr int NP = GATE_UP ? 2 : 1;
-    extern __shared__ __align__(16) float gsm[];
+    extern __shared__ __align__(128) unsigned char gsm[];
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = static_cast<int>(cluster.block_rank());
     const int KS = a.KS;
-    if (static_cast<int>(blockIdx.z) >= *a.tile_count) return; // whole cluster exits together
+    if (static_cast<int>(blockIdx.z) >= *a.tile_count) return; // the whole cluster exits together
     const int4 td = a.tiles[blockIdx.z];
-    const int e = td.x;
-    const int r0 = td.y;
-    const int n = td.z;
+    const int e = td.x, r0 = td.y, n = td.z;
     const int K = a.K, N = a.N;
-    const int KP = (K + KS - 1) / KS;
-    const int kb = min(K, rank * KP), ke = min(K, kb + KP);
-    const int kc = ke - kb;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int col = blockIdx.y * kGemvCols + lane * 8;
-    const bool col_ok = col < N;
+    const int kb = min(K, rank * kc), ke = min(K, kb + kc);
+    const int nbox = (ke - kb + kVRows - 1) / kVRows;
+    const int tid = threadIdx.x;
+    const int cq = tid % (kVCols / 4), kr = tid / (kVCols / 4);
+    const int c0 = blockIdx.y * kVCols;
 
-    float* xs = gsm;                                        // [kGemvTokens][KP]
-    float* red = xs + kGemvTokens * KP;                     // [warps][tokens][NP][256]
-    float* part = red + kGemvWarps * kGemvTokens * NP * kGemvCols; // [tokens][NP][256]
+    const GemvSmem L = gemv_smem(NP, TOK, kc);
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm) + 127) & ~uintptr_t(127));
+    uint8_t* ring = base + L.ring;                        // [stage][NP][32 k][256 n] INT8
+    float* red = reinterpret_cast<float*>(base + L.ring); // [group][TOK][NP][256] after the stream
+    float* xs = reinterpret_cast<float*>(base + L.xs);    // [TOK][kc]
+    uint64_t* full = reinterpret_cast<uint64_t*>(base + L.bars);
+    __shared__ int abort_s; // set after a timed-out wait: no further copies are issued
 
-    const int8_t* base = a.arena + static_cast<uint64_t>(e) * a.stride;
-    const int8_t* w0 = base + a.off0;
-    const int8_t* w1 = base + a.off1;
     const hmoe_expert_quant qp = a.quant[e];
-    const float zp0 = static_cast<float>(qp.zero_point[a.proj0]);
-    const float zp1 = GATE_UP ? static_cast<float>(qp.zero_point[a.proj0 + 1]) : 0.0f;
+    const float zoff0 = 8388608.0f + 128.0f + static_cast<float>(qp.zero_point[a.proj0]);
+    const float zoff1 = GATE_UP ? 8388608.0f + 128.0f + static_cast<float>(qp.zero_point[a.proj0 + 1]) : 0.0f;
+    if (tid == 0) {
+        abort_s = 0;
+        for (int s = 0; s < kVStages; ++s) sm100::mbar_init(&full[s], 1);
+        sm100::fence_mbarrier_init();
+        sm100::prefetch_tmap(&tm0);
+        if (GATE_UP) sm100::prefetch_tmap(&tm1);
+    }
+    __syncthreads();
 
-    for (int j0 = 0; j0 < n; j0 += kGemvTokens) {
-        const int nj = min(kGemvTokens, n - j0);
-        for (int i = tid; i < kGemvTokens * kc; i += blockDim.x) {
+    uint32_t it = 0; // ring slots consumed so far (phase of each slot)
+    for (int j0 = 0; j0 < n; j0 += TOK) {
+        const int nj = min(TOK, n - j0);
+        auto issue = [&](int b) {
+            const int s = (it + b) % kVStages;
+            sm100::mbar_arrive_expect_tx(&full[s], NP * kVRows * kVCols);
+            sm100::tma_load_3d(ring + (s * NP + 0) * kVRows * kVCols, &tm0, c0, kb + b * kVRows, e, &full[s]);
+            if (GATE_UP)
+                sm100::tma_load_3d(ring + (s * NP + 1) * kVRows * kVCols, &tm1, c0, kb + b * kVRows, e, &full[s]);
+        };
+        // Every thread tracks how many boxes of this pass were issued (the
+        // decision depends only on abort_s, read after a barrier).
+        int issued = abort_s ? 0 : min(kVStages, nbox);
+        if (tid == 0)
+            for (int b = 0; b < issued; ++b) issue(b);
+        // token rows of this pass (FP32 in shared memory; zero past the group)
+        for (int i = tid; i < TOK * kc; i += kVThreads) {
             const int t = i / kc, kk = i % kc;
             float v = 0.0f;
-            if (t < nj) {
+            if (t < nj && kb + kk < ke) {
                 const size_t row = static_cast<size_t>(r0 + j0 + t);
                 if constexpr (GATE_UP)
                     v = __bfloat162float(a.act16[row * K + kb + kk]);
                 else
                     v = a.act32[row * K + kb + kk];
             }
-            xs[t * KP + kk] = v;
+            xs[t * kc + kk] = v;
         }
         __syncthreads();
-        float acc[kGemvTokens][NP][8];
+        float acc[TOK][NP][4];
 #pragma unroll
-        for (int t = 0; t < kGemvTokens; ++t)
+        for (int t = 0; t < TOK; ++t)
 #pragma unroll
             for (int p = 0; p < NP; ++p)
 #pragma unroll
-                for (int c = 0; c < 8; ++c) acc[t][p][c] = 0.0f;
-        if (col_ok) {
-            // kGemvRows weight rows per lane are loaded before any is used,
-            // so every lane keeps kGemvRows x NP 8-byte loads in flight.
-            for (int k0 = warp; k0 < kc; k0 += kGemvWarps * kGemvRows) {
-                uint2 qv[kGemvRows][NP];
-#pragma unroll
-                for (int r = 0; r < kGemvRows; ++r) {
-                    const int kk = k0 + r * kGemvWarps;
-                    if (kk < kc) {
-                        const size_t off = static_cast<size_t>(kb + kk) * N + col;
-                        qv[r][0] = __ldg(reinterpret_cast<const uint2*>(w0 + off));
-                        if constexpr (GATE_UP) qv[r][1] = __ldg(reinterpret_cast<const uint2*>(w1 + off));
-                    } else {
-                        qv[r][0] = make_uint2(0u, 0u);
-                        if constexpr (GATE_UP) qv[r][1] = make_uint2(0u, 0u);
-                    }
-                }
-#pragma unroll
-                for (int r = 0; r < kGemvRows; ++r) {
-                    const int kk = k0 + r * kGemvWarps;
-                    if (kk >= kc) break;
-                    float wv[NP][8];
+                for (int c = 0; c < 4; ++c) acc[t][p][c] = 0.0f;
+        for (int b = 0; b < nbox; ++b) {
+            const int s = (it + b) % kVStages;
+            // Boxes that were issued are always waited for (bounded), so no
+            // copy is left in flight when the CTA moves on or exits.
+            if (b < issued && !sm100::mbar_wait_for(&full[s], ((it + b) / kVStages) & 1, kVWaitNs)) {
+                device_fail(a.st, HMOE_TIMEOUT);
+                abort_s = 1;
+            }
+            const int nr = min(kVRows, ke - (kb + b * kVRows));
+            const uint8_t* box = ring + s * NP * kVRows * kVCols;
+#pragma unroll 2
+            for (int rr = kr; rr < kVRows; rr += kVGroups) {
+                if (rr < nr) {
+                    float w[NP][4];
 #pragma unroll
                     for (int p = 0; p < NP; ++p) {
-                        dequant4(qv[r][p].x, p ? zp1 : zp0, &wv[p][0]);
-                        dequant4(qv[r][p].y, p ? zp1 : zp0, &wv[p][4]);
+                        const uint32_t q = *reinterpret_cast<const uint32_t*>(box + (p * kVRows + rr) * kVCols + 4 * cq);
+                        dequant4_fast(q, p ? zoff1 : zoff0, w[p]);
                     }
+                    const float* xr = xs + b * kVRows + rr;
 #pragma unroll
-                    for (int t = 0; t < kGemvTokens; ++t) {
-                        if (t < nj) {
-                            const float xv = xs[t * KP + kk];
+                    for (int t = 0; t < TOK; ++t) {
+                        const float xv = xr[t * kc];
 #pragma unroll
-                            for (int p = 0; p < NP; ++p)
+                        for (int p = 0; p < NP; ++p)
 #pragma unroll
-                                for (int c = 0; c < 8; ++c) acc[t][p][c] = fmaf(xv, wv[p][c], acc[t][p][c]);
-                        }
+                            for (int c = 0; c < 4; ++c) acc[t][p][c] = fmaf(xv, w[p][c], acc[t][p][c]);
                     }
                 }
             }
-        }
-#pragma unroll
-        for (int t = 0; t < kGemvTokens; ++t)
-#pragma unroll
-            for (int p = 0; p < NP; ++p) {
-                float4* dst = reinterpret_cast<float4*>(red + ((warp * kGemvTokens + t) * NP + p) * kGemvCols + lane * 8);
-                dst[0] = make_float4(acc[t][p][0], acc[t][p][1], acc[t][p][2], acc[t][p][3]);
-                dst[1] = make_float4(acc[t][p][4], acc[t][p][5], acc[t][p][6], acc[t][p][7]);
+            __syncthreads(); // every thread is done with this slot (and sees abort_s)
+            if (!abort_s && b + kVStages < nbox && issued == b + kVStages) {
+                if (tid == 0) issue(b + kVStages);
+                issued = b + kVStages + 1;
             }
-        __syncthreads();
-        for (int i = tid; i < kGemvTokens * NP * kGemvCols; i += blockDim.x) {
-            float s = 0.0f;
+        }
+        it += nbox;
+        // The ring is idle now (every issued box was waited for): reuse it
+        // for the row-group partial sums, then fold the groups in order.
 #pragma unroll
-            for (int w = 0; w < kGemvWarps; ++w) s += red[w * kGemvTokens * NP * kGemvCols + i];
-            part[i] = s;
+        for (int t = 0; t < TOK; ++t)
+#pragma unroll
+            for (int p = 0; p < NP; ++p)
+                *reinterpret_cast<float4*>(red + ((kr * TOK + t) * NP + p) * kVCols + 4 * cq) =
+                    make_float4(acc[t][p][0], acc[t][p][1], acc[t][p][2], acc[t][p][3]);
+        __syncthreads();
+        for (int i = tid; i < TOK * NP * kVCols; i += kVThreads) {
+            float v = red[i];
+#pragma unroll
+            for (int g = 1; g < kVGroups; ++g) v += red[g * TOK * NP * kVCols + i];
+            red[i] = v;
         }
         cluster.sync();
-        // Rank r finalises a slice of the columns, summing ranks in order.
-        const int slice = kGemvCols / KS;
-        for (int i = tid; i < kGemvTokens * slice; i += blockDim.x) {
+        // Rank r finalises a slice of the columns, adding the ranks in order.
+        const int slice = kVCols / KS;
+        for (int i = tid; i < TOK * slice; i += kVThreads) {
             const int t = i / slice;
             const int cl = rank * slice + i % slice;
-            const int c = blockIdx.y * kGemvCols + cl;
+            const int c = c0 + cl;
             if (t >= nj || c >= N) continue;
             float s0 = 0.0f, s1 = 0.0f;
             for (int r = 0; r < KS; ++r) {
-                const float* rp = cluster.map_shared_rank(part, r);
-                s0 += rp[(t * NP + 0) * kGemvCols + cl];
-                if constexpr (GATE_UP) s1 += rp[(t * NP + 1) * kGemvCols + cl];
+                const float* rp = cluster.map_shared_rank(red, r);
+                s0 += rp[(t * NP + 0) * kVCols + cl];
+                if constexpr (GATE_UP) s1 += rp[(t * NP + 1) * kVCols + cl];
             }
-            const int row = r0 + j0 + t;
+            const size_t row = static_cast<size_t>(r0 + j0 + t);
             if constexpr (GATE_UP) {
                 const float g = qp.scale[a.proj0] * s0;
                 const float u = qp.scale[a.proj0 + 1] * s1;
-                a.out32[static_cast<size_t>(row) * N + c] = silu(g) * u;
+                a.out32[row * N + c] = silu(g) * u;
             } else {
-                a.out16[static_cast<size_t>(row) * N + c] = __float2bfloat16_rn(a.weight[row] * (qp.scale[a.proj0] * s0));
+                a.out16[row * N + c] = __float2bfloat16_rn(a.weight[row] * (qp.scale[a.proj0] * s0));
             }
         }
-        cluster.sync();
+        cluster.sync(); // peers' partial sums stay alive until read; ring free again
     }
 }
 
-size_t gemv_smem_bytes(int K, int KS, bool gate_up, int tokens) {
-    const int NP = gate_up ? 2 : 1;
-    const int KP = (K + KS - 1) / KS;
-    return static_cast<size_t>(tokens * KP + kGemvWarps * tokens * NP * kGemvCols + tokens * NP * kGemvCols) *
-           sizeof(float);
-}
-
 template <bool GATE_UP, int TOK>
-cudaError_t launch_gemv_variant(cudaLaunchConfig_t& cfg, const GemvArgs& args) {
+cudaError_t launch_gemv_variant(cudaLaunchConfig_t& cfg, const CUtensorMap& m0, const CUtensorMap& m1,
+                                const GemvArgs& args, int kc) {
     static size_t attr_set = 0;
     if (cfg.dynamicSmemBytes > attr_set) {
         cudaFuncSetAttribute(expert_gemv_kernel<GATE_UP, TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(cfg.dynamicSmemBytes));
         attr_set = cfg.dynamicSmemBytes;
     }
-    return cudaLaunchKernelEx(&cfg, expert_gemv_kernel<GATE_UP, TOK>, args);
+    return cudaLaunchKernelEx(&cfg, expert_gemv_kernel<GATE_UP, TOK>, m0, m1, args, kc);
 }
 
-hmoe_status launch_expert_gemv(bool gate_up, const GemvArgs& args, int list_capacity, int max_tokens,
-                               cudaStream_t stream) {
-    if (list_capacity <= 0) return HMOE_OK;
-    if (list_capacity > 65535) return HMOE_UNSUPPORTED;
-    // One token per pass when no expert can hold more (a single-token
-    // batch without shared experts); otherwise four.
-    const int tok = max_tokens <= 1 ? 1 : 4;
-    const size_t smem = gemv_smem_bytes(args.K, args.KS, gate_up, tok);
+// Split of K over the cluster: enough CTAs for about two per SM, at most 8
+// per cluster, and at most kVMaxKc rows per CTA.
+int gemv_split(int capacity, int col_blocks, int K) {
+    int ks = 1;
+    while (ks < 8 && static_cast<long>(capacity) * col_blocks * ks < 2L * device_sm_count()) ks *= 2;
+    while (ks < 8 && (K + ks - 1) / ks > kVMaxKc) ks *= 2;
+    return ks;
+}
+
+hmoe_status launch_gemv(bool gate_up, const ExpertRun& r, const CUtensorMap& m0, const CUtensorMap& m1,
+                        GemvArgs& g, cudaStream_t stream) {
+    if (r.tile_cap <= 0) return HMOE_OK;
+    if (r.tile_cap > 65535) return HMOE_UNSUPPORTED;
+    const int col_blocks = (g.N + kVCols - 1) / kVCols;
+    g.KS = gemv_split(r.tile_cap, col_blocks, g.K);
+    int kc = (g.K + g.KS - 1) / g.KS;
+    kc = (kc + kVRows - 1) / kVRows * kVRows;
+    if (kc > kVMaxKc) return HMOE_UNSUPPORTED;
+    // One token per pass when no expert holds more (a single-token batch
+    // without shared experts); otherwise four.
+    const int tok = r.max_group <= 1 ? 1 : 4;
+    const GemvSmem L = gemv_smem(gate_up ? 2 : 1, tok, kc);
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(args.KS), static_cast<unsigned>((args.N + kGemvCols - 1) / kGemvCols),
-                       static_cast<unsigned>(list_capacity));
-    cfg.blockDim = dim3(kGemvWarps * 32);
-    cfg.dynamicSmemBytes = smem;
+    cfg.gridDim = dim3(static_cast<unsigned>(g.KS), static_cast<unsigned>(col_blocks),
+                       static_cast<unsigned>(r.tile_cap));
+    cfg.blockDim = dim3(kVThreads);
+    cfg.dynamicSmemBytes = static_cast<size_t>(L.total);
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(args.KS);
+    attr[0].val.clusterDim.x = static_cast<unsigned>(g.KS);
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     cudaError_t err;
     if (gate_up)
-        err = tok == 1 ? launch_gemv_variant<true, 1>(cfg, args) : launch_gemv_variant<true, 4>(cfg, args);
+        err = tok == 1 ? launch_gemv_variant<true, 1>(cfg, m0, m1, g, kc)
+                       : launch_gemv_variant<true, 4>(cfg, m0, m1, g, kc);
     else
-        err = tok == 1 ? launch_gemv_variant<false, 1>(cfg, args) : launch_gemv_variant<false, 4>(cfg, args);
+        err = tok == 1 ? launch_gemv_variant<false, 1>(cfg, m0, m1, g, kc)
+                       : launch_gemv_variant<false, 4>(cfg, m0, m1, g, kc);
     if (err != cudaSuccess) {
         set_last_error("hmoe expert GEMV launch", err);
         return HMOE_CUDA_ERROR;
@@ -218,21 +273,12 @@ hmoe_status launch_expert_gemv(bool gate_up, const GemvArgs& args, int list_capa
     return check_launch("hmoe expert GEMV");
 }
 
-namespace {
-
-int gemv_split(int capacity, int col_blocks) {
-    int ks = 1;
-    while (ks < 8 && static_cast<long>(capacity) * col_blocks * ks < 2L * 148) ks *= 2;
-    return ks;
-}
-
 GemvArgs gemv_common(const ExpertRun& r) {
     GemvArgs g{};
     g.tiles = r.tiles;
     g.tile_count = r.tile_count;
-    g.arena = r.arena;
-    g.stride = r.stride;
     g.quant = r.quant;
+    g.st = r.st;
     return g;
 }
 
@@ -242,14 +288,17 @@ GemvArgs gemv_common(const ExpertRun& r) {
 hmoe_status gemv_gate_up(const ExpertRun& r, cudaStream_t s) {
     GemvArgs g = gemv_common(r);
     g.act16 = r.xrows;
-    g.off0 = r.gate_offset;
-    g.off1 = r.up_offset;
     g.proj0 = 0;
     g.out32 = r.hmid32;
     g.K = r.H;
     g.N = r.I;
-    g.KS = gemv_split(r.tile_cap, (r.I + 255) / 256);
-    return launch_expert_gemv(true, g, r.tile_cap, r.max_group, s);
+    CUtensorMap mg, mu;
+    if (!map_weights_box(&mg, r.arena + r.gate_offset, r.I, r.H, r.experts, r.stride, kVCols, kVRows) ||
+        !map_weights_box(&mu, r.arena + r.up_offset, r.I, r.H, r.experts, r.stride, kVCols, kVRows)) {
+        set_last_error_text("hmoe: cuTensorMapEncodeTiled failed (GEMV gate/up)");
+        return HMOE_CUDA_ERROR;
+    }
+    return launch_gemv(true, r, mg, mu, g, s);
 }
 
 // down of every tile with the routing weight, weight-streaming GEMV variant.
@@ -257,13 +306,16 @@ hmoe_status gemv_down(const ExpertRun& r, cudaStream_t s) {
     GemvArgs g = gemv_common(r);
     g.act32 = r.hmid32;
     g.weight = r.weight;
-    g.off0 = r.down_offset;
     g.proj0 = 2;
     g.out16 = r.yrows;
     g.K = r.I;
     g.N = r.H;
-    g.KS = gemv_split(r.tile_cap, (r.H + 255) / 256);
-    return launch_expert_gemv(false, g, r.tile_cap, r.max_group, s);
+    CUtensorMap md;
+    if (!map_weights_box(&md, r.arena + r.down_offset, r.H, r.I, r.experts, r.stride, kVCols, kVRows)) {
+        set_last_error_text("hmoe: cuTensorMapEncodeTiled failed (GEMV down)");
+        return HMOE_CUDA_ERROR;
+    }
+    return launch_gemv(false, r, md, md, g, s);
 }
 
 } // namespace hmoe

@@ -3,6 +3,8 @@
 
 #include "common.cuh"
 
+#include <cuda.h>
+
 namespace hmoe {
 
 // Byte offsets of the workspace segments (all 256-byte aligned).
@@ -54,17 +56,13 @@ struct GemvArgs {
     const __nv_bfloat16* act16; // gate/up input rows (BF16)
     const float* act32;         // down input rows (FP32 intermediate)
     const float* weight;        // down: routing weight per row
-    const int8_t* arena;
-    uint64_t stride, off0, off1;
     const hmoe_expert_quant* quant;
-    int proj0;
+    int proj0;                  // 0: gate (and up), 2: down
     float* out32;               // gate/up: FP32 intermediate
     __nv_bfloat16* out16;       // down: BF16 weighted rows
     int K, N, KS;
+    DeviceStatus* st;
 };
-
-hmoe_status launch_expert_gemv(bool gate_up, const GemvArgs& args, int tile_capacity, int max_tokens,
-                               cudaStream_t stream);
 
 // Segments of permuted rows: segment i holds rows of expert
 // expert_base + (i mod eps).  Rows come from offsets[i] .. offsets[i+1] or,
@@ -83,6 +81,11 @@ struct SegSpec {
 };
 
 bool gemm_available();
+int device_sm_count();
+// TMA map of one INT8 projection over all experts: dims {N, K, experts},
+// box [box_k][box_n] (no swizzle).  False when the driver rejects it.
+bool map_weights_box(CUtensorMap* m, const int8_t* base, int N, int K, int experts, uint64_t stride, int box_n,
+                     int box_k);
 hmoe_status gemm_gate_up(const ExpertRun& r, cudaStream_t stream);
 hmoe_status gemm_down(const ExpertRun& r, cudaStream_t stream);
 hmoe_status gemv_gate_up(const ExpertRun& r, cudaStream_t stream);

@@ -40,10 +40,10 @@ namespace cg = cooperative_groups;
 
 namespace hmoe {
 
-constexpr int kRouteTokens = 8;  // tokens per CTA in the fused router
-constexpr int kRouteChunk = 1024; // hidden rows staged per pass (as doubles)
+constexpr int kRouteTokens = 8;     // tokens per CTA in the fused router
+constexpr int kRouteChunk = 256;    // hidden rows staged per pass (= threads per CTA)
 constexpr int kRouteFallbacks = 64; // queued sequential recomputations per CTA
-constexpr int kRouteSlab = 32;      // router-matrix rows per bulk copy
+constexpr int kRouteStages = 4;     // router-matrix slabs in flight
 constexpr int kMaxExperts = 256; // E_pad <= 256 (8 candidates per lane)
 constexpr int kMaxTopK = 32;
 
@@ -213,14 +213,45 @@ __device__ void select_token(const float (&lv)[C], int E, int k, int softmax,
     }
 }
 
-// Byte offset of the router-matrix slabs in the fused router's shared memory
-// (after x/partials, squared norms, token norms, logits, exp scratch and the
-// fallback queue), rounded up to 16 bytes for the bulk copies.
-__host__ __device__ inline int route_slab_offset(int E_pad, int P) {
-    const int part = (kRouteTokens * kRouteChunk * 8 > kRouteTokens * P * E_pad * 8) ? kRouteTokens * kRouteChunk * 8
-                                                                                      : kRouteTokens * P * E_pad * 8;
-    const int bytes = part + P * E_pad * 4 + kRouteTokens * 8 + 2 * kRouteTokens * E_pad * 4 + (1 + kRouteFallbacks) * 4;
-    return (bytes + 15) & ~15;
+// Shared-memory plan of the fused router (byte offsets, 16-byte aligned).
+// The router-matrix slab ring and, after the main loop, the per-row-lane
+// partial sums share one region.
+struct RouteSmem {
+    int slab_rows;                  // router rows per bulk copy (power of two)
+    int ring, xf, xs, wsq, xn, xw, logit, evs, fb, bars, total;
+};
+
+__host__ __device__ inline RouteSmem route_smem(int E, int E_pad, int P) {
+    RouteSmem m{};
+    int sr = 256;
+    while (sr > 8 && sr * E_pad * 4 > 16384) sr >>= 1;
+    m.slab_rows = sr;
+    auto al = [](int v) { return (v + 15) & ~15; };
+    const int ring_bytes = kRouteStages * sr * E * 4;
+    const int part_bytes = kRouteTokens * P * E_pad * 8;
+    int off = 0;
+    m.ring = off;
+    off = al(off + (ring_bytes > part_bytes ? ring_bytes : part_bytes));
+    m.xf = off;
+    off = al(off + kRouteTokens * kRouteChunk * 4);
+    m.xs = off;
+    off = al(off + kRouteTokens * kRouteChunk * 8);
+    m.wsq = off;
+    off = al(off + P * E_pad * 4);
+    m.xn = off;
+    off = al(off + 2 * kRouteTokens * 8);
+    m.xw = off;
+    off = al(off + 8 * kRouteTokens * 8);
+    m.logit = off;
+    off = al(off + kRouteTokens * E_pad * 4);
+    m.evs = off;
+    off = al(off + kRouteTokens * E_pad * 4);
+    m.fb = off;
+    off = al(off + (1 + kRouteFallbacks) * 4);
+    m.bars = off;
+    off = al(off + (kRouteStages + 1) * 8);
+    m.total = off;
+    return m;
 }
 
 // The reference's sequential double accumulation for one (token, expert),
@@ -239,11 +270,13 @@ __device__ double sequential_logit(const RouteArgs& a, int tok, int e) {
 // x: CTA r of a cluster sums hidden rows [r*H/KS, (r+1)*H/KS) for
 // kRouteTokens tokens and every expert.  Thread (quad = tid % EQ,
 // p = tid / EQ) owns experts 4*quad..4*quad+3 and the rows i = p (mod P)
-// of each staged chunk; the token rows are staged as doubles, so one shared
-// load feeds four DFMAs and the router matrix is read with 16-byte loads.
-// Partial sums meet in (distributed) shared memory and are added in a fixed
-// order (rank, p).  The certificate bounds sum_i |x_i W_ie| by
-// ||x|| ||W_e|| (Cauchy-Schwarz).
+// of each router slab.  Both operands arrive by bulk copies: the router
+// matrix in slabs of contiguous rows through a kRouteStages-deep ring, the
+// token rows kRouteChunk floats at a time, converted once to doubles in
+// shared memory (so one broadcast load feeds four DFMAs).  Partial sums
+// meet in (distributed) shared memory and are added in a fixed order
+// (rank, p).  The certificate bounds sum_i |x_i W_ie| by ||x|| ||W_e||
+// (Cauchy-Schwarz); ||x_t||^2 is accumulated during the conversion.
 template <int C>
 __global__ void __launch_bounds__(256, 2) route_kernel(RouteArgs a, int EQ, int P, int KS) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -251,67 +284,91 @@ __global__ void __launch_bounds__(256, 2) route_kernel(RouteArgs a, int EQ, int 
     const int rank = static_cast<int>(cluster.block_rank());
     const int H = a.H, E = a.E;
     const int E_pad = 4 * EQ;
-    const int part_bytes = max(kRouteTokens * kRouteChunk * 8, kRouteTokens * P * E_pad * 8);
-    double* xs = reinterpret_cast<double*>(smem);                               // [TB][chunk] (phase 1)
-    double* part = reinterpret_cast<double*>(smem);                             // [TB][P][E_pad] (after)
-    float* wsq = reinterpret_cast<float*>(smem + part_bytes);                   // [P][E_pad]
-    double* xn = reinterpret_cast<double*>(wsq + P * E_pad);                    // [TB]
-    float* logit = reinterpret_cast<float*>(xn + kRouteTokens);                 // [TB][E_pad]
-    float* evs = logit + kRouteTokens * E_pad;                                  // [TB][E_pad]
-    int* fb_count = reinterpret_cast<int*>(evs + kRouteTokens * E_pad);         // [1]
-    int* fb_list = fb_count + 1;                                                // [kRouteFallbacks]
-    float* wsl = reinterpret_cast<float*>(smem + route_slab_offset(E_pad, P));  // [2][slab][E]
-    uint64_t* wbar = reinterpret_cast<uint64_t*>(wsl + 2 * kRouteSlab * E_pad); // [2]
+    const RouteSmem L = route_smem(E, E_pad, P);
+    const int SR = L.slab_rows;
+    float* wsl = reinterpret_cast<float*>(smem + L.ring);                     // [stages][SR][E]
+    double* part = reinterpret_cast<double*>(smem + L.ring);                  // [TB][P][E_pad] (after)
+    float* xf = reinterpret_cast<float*>(smem + L.xf);                        // [TB][chunk] staging
+    double* xs = reinterpret_cast<double*>(smem + L.xs);                      // [TB][chunk]
+    float* wsq = reinterpret_cast<float*>(smem + L.wsq);                      // [P][E_pad]
+    double* xn_part = reinterpret_cast<double*>(smem + L.xn);                 // [TB] this CTA's rows
+    double* xn = xn_part + kRouteTokens;                                      // [TB] all rows
+    float* logit = reinterpret_cast<float*>(smem + L.logit);                  // [TB][E_pad]
+    float* evs = reinterpret_cast<float*>(smem + L.evs);                      // [TB][E_pad]
+    int* fb_count = reinterpret_cast<int*>(smem + L.fb);                      // [1]
+    int* fb_list = fb_count + 1;                                              // [kRouteFallbacks]
+    uint64_t* wbar = reinterpret_cast<uint64_t*>(smem + L.bars);              // [stages]
+    uint64_t* xbar = wbar + kRouteStages;                                     // [1]
 
     const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
     const int quad = tid % EQ, p = tid / EQ;
     const bool active = p < P;
     const int t0 = blockIdx.y * kRouteTokens;
     const int nt = min(kRouteTokens, a.T - t0);
     const int h0 = rank * (H / KS), h1 = h0 + H / KS;
     const bool vec4 = (E % 4) == 0;
-    if (tid == 0) *fb_count = 0;
+    const int nslab = (h1 - h0 + SR - 1) / SR;
+    const int nchunk = (h1 - h0 + kRouteChunk - 1) / kRouteChunk;
 
     double acc[kRouteTokens][4];
+    double xsq[kRouteTokens];
     float sq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int t = 0; t < kRouteTokens; ++t)
+    for (int t = 0; t < kRouteTokens; ++t) {
+        xsq[t] = 0.0;
 #pragma unroll
         for (int j = 0; j < 4; ++j) acc[t][j] = 0.0;
+    }
 
-    // Router rows stream through shared memory in slabs of kRouteSlab rows
-    // (contiguous in [H, E] layout), double-buffered with bulk copies, while
-    // the token rows are staged as doubles kRouteChunk rows at a time.
-    const int nslab = (h1 - h0 + kRouteSlab - 1) / kRouteSlab;
+    auto issue_slab = [&](int sl) {
+        const int r0 = h0 + sl * SR;
+        const int nr = min(SR, h1 - r0);
+        uint64_t* bar = &wbar[sl % kRouteStages];
+        sm100::mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nr * E * 4));
+        sm100::bulk_load(wsl + (sl % kRouteStages) * SR * E, a.w + static_cast<size_t>(r0) * E,
+                         static_cast<uint32_t>(nr * E * 4), bar);
+    };
+    auto issue_chunk = [&](int c) {
+        const int r0 = h0 + c * kRouteChunk;
+        const int cn = min(kRouteChunk, h1 - r0);
+        sm100::mbar_arrive_expect_tx(xbar, static_cast<uint32_t>(nt * cn * 4));
+        for (int t = 0; t < nt; ++t)
+            sm100::bulk_load(xf + t * kRouteChunk, a.x + static_cast<size_t>(t0 + t) * H + r0,
+                             static_cast<uint32_t>(cn * 4), xbar);
+    };
     if (tid == 0) {
-        sm100::mbar_init(&wbar[0], 1);
-        sm100::mbar_init(&wbar[1], 1);
+        *fb_count = 0;
+        for (int s = 0; s < kRouteStages; ++s) sm100::mbar_init(&wbar[s], 1);
+        sm100::mbar_init(xbar, 1);
         sm100::fence_mbarrier_init();
+        if (nchunk > 0) issue_chunk(0);
+        for (int sl = 0; sl < kRouteStages && sl < nslab; ++sl) issue_slab(sl);
     }
     __syncthreads();
-    auto issue_slab = [&](int sl) {
-        const int r0 = h0 + sl * kRouteSlab;
-        const int nr = min(kRouteSlab, h1 - r0);
-        sm100::mbar_arrive_expect_tx(&wbar[sl & 1], static_cast<uint32_t>(nr * E * 4));
-        sm100::bulk_load(wsl + (sl & 1) * kRouteSlab * E, a.w + static_cast<size_t>(r0) * E,
-                         static_cast<uint32_t>(nr * E * 4), &wbar[sl & 1]);
-    };
-    if (tid == 0 && nslab > 0) issue_slab(0);
+
     for (int sl = 0; sl < nslab; ++sl) {
-        const int r0 = h0 + sl * kRouteSlab;
-        const int nr = min(kRouteSlab, h1 - r0);
-        if ((r0 - h0) % kRouteChunk == 0) { // stage the next token chunk
-            const int cn = min(kRouteChunk, h1 - r0);
-            for (int idx = tid; idx < kRouteTokens * cn; idx += blockDim.x) {
-                const int t = idx / cn, i = idx % cn;
-                xs[t * kRouteChunk + i] = t < nt ? static_cast<double>(a.x[static_cast<size_t>(t0 + t) * H + r0 + i]) : 0.0;
-            }
-            __syncthreads();
-        }
-        if (tid == 0 && sl + 1 < nslab) issue_slab(sl + 1); // other buffer: freed by the last barrier
-        if (!sm100::mbar_wait_for(&wbar[sl & 1], (sl >> 1) & 1, 2000000000ull)) device_fail(a.st, HMOE_TIMEOUT);
-        const float* ws = wsl + (sl & 1) * kRouteSlab * E;
+        const int r0 = h0 + sl * SR;
+        const int nr = min(SR, h1 - r0);
         const int xoff = (r0 - h0) % kRouteChunk;
+        if (xoff == 0) { // convert the next token chunk to doubles
+            const int c = (r0 - h0) / kRouteChunk;
+            const int cn = min(kRouteChunk, h1 - r0);
+            if (!sm100::mbar_wait_for(xbar, c & 1, 2000000000ull)) device_fail(a.st, HMOE_TIMEOUT);
+            for (int i = tid; i < kRouteChunk; i += blockDim.x) {
+#pragma unroll
+                for (int t = 0; t < kRouteTokens; ++t) {
+                    const double v = (t < nt && i < cn) ? static_cast<double>(xf[t * kRouteChunk + i]) : 0.0;
+                    xs[t * kRouteChunk + i] = v;
+                    xsq[t] = fma(v, v, xsq[t]);
+                }
+            }
+            __syncthreads(); // xs complete, xf free
+            if (tid == 0 && c + 1 < nchunk) issue_chunk(c + 1);
+        }
+        if (!sm100::mbar_wait_for(&wbar[sl % kRouteStages], (sl / kRouteStages) & 1, 2000000000ull))
+            device_fail(a.st, HMOE_TIMEOUT);
+        const float* ws = wsl + (sl % kRouteStages) * SR * E;
         if (active) {
             for (int i = p; i < nr; i += P) {
                 float wv[4];
@@ -328,18 +385,31 @@ __global__ void __launch_bounds__(256, 2) route_kernel(RouteArgs a, int EQ, int 
                     wd[j] = static_cast<double>(wv[j]);
                     sq[j] = fmaf(wv[j], wv[j], sq[j]);
                 }
+                const double* xr = xs + xoff + i;
 #pragma unroll
                 for (int t = 0; t < kRouteTokens; ++t) {
-                    if (t < nt) {
-                        const double xv = xs[t * kRouteChunk + xoff + i];
+                    const double xv = xr[t * kRouteChunk];
 #pragma unroll
-                        for (int j = 0; j < 4; ++j) acc[t][j] = fma(xv, wd[j], acc[t][j]);
-                    }
+                    for (int j = 0; j < 4; ++j) acc[t][j] = fma(xv, wd[j], acc[t][j]);
                 }
             }
         }
-        __syncthreads();
+        __syncthreads(); // every warp is done with this slot
+        if (tid == 0 && sl + kRouteStages < nslab) issue_slab(sl + kRouteStages);
     }
+    // ||x_t||^2 over this CTA's rows: warp sums, then a fixed-order sum of
+    // the warps (the value only feeds an upper bound).
+#pragma unroll
+    for (int t = 0; t < kRouteTokens; ++t) {
+        double v = xsq[t];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        xsq[t] = v;
+    }
+    double* xw = reinterpret_cast<double*>(smem + L.xw); // [8 warps][TB]
+    if (lane == 0)
+#pragma unroll
+        for (int t = 0; t < kRouteTokens; ++t) xw[warp * kRouteTokens + t] = xsq[t];
     if (active) {
 #pragma unroll
         for (int t = 0; t < kRouteTokens; ++t)
@@ -349,6 +419,11 @@ __global__ void __launch_bounds__(256, 2) route_kernel(RouteArgs a, int EQ, int 
         for (int j = 0; j < 4; ++j) wsq[p * E_pad + 4 * quad + j] = sq[j];
     }
     __syncthreads();
+    if (tid < kRouteTokens) {
+        double v = 0.0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v += xw[w * kRouteTokens + tid];
+        xn_part[tid] = v;
+    }
     // Fold this CTA's row lanes in fixed order q = 0..P-1 into row 0 of each
     // token's partial block (and of wsq), so the cluster reduction below
     // reads one value per CTA.
@@ -366,34 +441,10 @@ __global__ void __launch_bounds__(256, 2) route_kernel(RouteArgs a, int EQ, int 
     cluster.sync();
 
     if (rank == 0) {
-        // ||x_t||^2 in double, one warp per token (this CTA covers all of H
-        // through the cluster, so the rows are read from global memory).
-        const int warp = tid >> 5, lane = tid & 31;
-        for (int t = warp; t < kRouteTokens; t += blockDim.x >> 5) {
-            double s = 0.0;
-            if (t < nt) {
-                // 8 independent partial sums keep 8 loads in flight per lane
-                // (the norm only feeds an upper bound, so order is free).
-                const float* xr = a.x + static_cast<size_t>(t0 + t) * H;
-                double sp[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                int i = lane;
-                for (; i + 7 * 32 < H; i += 8 * 32) {
-#pragma unroll
-                    for (int u = 0; u < 8; ++u) {
-                        const double v = xr[i + u * 32];
-                        sp[u] = fma(v, v, sp[u]);
-                    }
-                }
-                for (; i < H; i += 32) {
-                    const double v = xr[i];
-                    sp[0] = fma(v, v, sp[0]);
-                }
-#pragma unroll
-                for (int u = 0; u < 8; ++u) s += sp[u];
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-            if (lane == 0) xn[t] = s;
+        if (tid < kRouteTokens) {
+            double v = 0.0;
+            for (int r = 0; r < KS; ++r) v += cluster.map_shared_rank(xn_part, r)[tid];
+            xn[tid] = v;
         }
         __syncthreads();
         // Phase 2: exact float logits.  Thread (quad, p) finalises token p;
@@ -573,9 +624,6 @@ __global__ void __launch_bounds__(256) group_kernel(GroupArgs g) {
 
 // ------------------------------------------------------------ launchers
 
-int route_smem_bytes(int E_pad, int P) {
-    return route_slab_offset(E_pad, P) + 2 * kRouteSlab * E_pad * 4 + 16;
-}
 
 hmoe_status launch_route(const float* x, const float* w, const float* bias,
                          int T, int H, int E, int k, int softmax, int renorm,
@@ -584,14 +632,16 @@ hmoe_status launch_route(const float* x, const float* w, const float* bias,
     if (T <= 0) return HMOE_OK;
     if (E <= 0 || E > kMaxExperts || k <= 0 || k > E || k > kMaxTopK || H <= 0 || H % 8)
         return HMOE_INVALID_ARGUMENT;
+    // hidden rows and router rows arrive by bulk copies (16-byte aligned)
+    if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(w) % 16) return HMOE_INVALID_ARGUMENT;
     const int EQ = (E + 3) / 4;
     const int P = std::min(32, 256 / EQ); // row lanes; phase 2 maps token t to lane t mod P
     if (EQ * P > 256 || P < 1) return HMOE_UNSUPPORTED;
     const int E_pad = 4 * EQ;
-    const int smem = route_smem_bytes(E_pad, P);
+    const int smem = route_smem(E, E_pad, P).total;
     const int rows = (T + kRouteTokens - 1) / kRouteTokens;
-    int KS = 1; // split H over a cluster when there are few token blocks
-    while (KS < 8 && rows * KS < 74 && (H / (KS * 2)) % 8 == 0 && H / (KS * 2) >= 64) KS *= 2;
+    int KS = 1; // split H over a cluster until there are about 2 CTAs per SM
+    while (KS < 8 && rows * KS < 2 * 148 && (H / (KS * 2)) % 8 == 0 && H / (KS * 2) >= 64) KS *= 2;
     RouteArgs a{x, w, bias, T, H, E, k, softmax, renorm, ids, scores, counts, st};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(KS), static_cast<unsigned>(rows));
