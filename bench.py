@@ -136,8 +136,9 @@ def algorithmic(cfg, T, U, rows_in=None, local_experts=None):
     rin = rows if rows_in is None else rows_in
     return {
         "route": {"bytes": T * H * 4 + H * E * 4 + T * k * 8, "flops": 2 * T * H * E},
-        # grouping ids/scores, then each token row read once and written as BF16 rows
-        "group": {"bytes": T * k * 8 * 2 + T * H * 4 + rows * H * 2, "flops": 0},
+        # grouping ids/scores, then each token row read once and written as
+        # FP16 rows (plus a 4-byte scale per row)
+        "group": {"bytes": T * k * 8 * 2 + T * H * 4 + rows * (H * 2 + 4), "flops": 0},
         "gate_up": {"bytes": U * 2 * H * I + rin * H * 2 + rin * I * 2, "flops": 4 * rin * H * I},
         "down": {"bytes": U * H * I + rin * I * 2 + rin * H * 2, "flops": 2 * rin * H * I},
         "combine": {"bytes": rows * H * 2 + T * H * 4, "flops": 0},
@@ -408,7 +409,7 @@ def main():
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp32" if not used_gemm else "bf16",
+        "vs_baseline": None, "dtype": "fp32" if not used_gemm else "fp16+bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights quantised to INT8)",
         "config": dict(config, parallelism=(f"ep{world}" if world > 1 else "single"),
                        l2="inputs larger than L2 (604 MB INT8 arena) and a 256 MiB flush between steps"),

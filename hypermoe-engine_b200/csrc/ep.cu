@@ -7,8 +7,8 @@
 //   all-gather of counts      int32 [P][E] routed rows per (source, expert)
 //   one host read             the counts size every transfer (NCCL p2p
 //                             sizes are host values); bounded wait
-//   dispatch                  grouped ncclSend/ncclRecv of BF16 rows and
-//                             their routing weights to the expert owners
+//   dispatch                  grouped ncclSend/ncclRecv of FP16 rows, their
+//                             scales and routing weights to the expert owners
 //   expert MLP                the single-GPU kernels over the received
 //                             (source, expert) segments; shared experts run
 //                             locally on the rank's own rows
@@ -149,12 +149,13 @@ hmoe_status wait_counts(hmoe_ep_comm* c) {
 // receive side for up to P * max_tokens * k rows.
 struct EpWorkspace {
     Workspace local;
-    size_t counts_all, xin, win, hin, yin, tiles_in, count_in;
+    size_t counts_all, xin, win, scale_in, hin, yin, tiles_in, count_in;
     int tile_cap_in;
     size_t total;
 };
 
 EpWorkspace plan_ep(const hmoe_layer_desc& d, size_t max_tokens) {
+    static_assert(sizeof(__half) == 2, "FP16 rows");
     EpWorkspace w{};
     w.local = plan_workspace(d, max_tokens);
     const size_t P = static_cast<size_t>(d.ep_size);
@@ -170,6 +171,7 @@ EpWorkspace plan_ep(const hmoe_layer_desc& d, size_t max_tokens) {
     w.counts_all = take(P * d.experts * 4);
     w.xin = take(rin * d.hidden * 2);
     w.win = take(rin * 4);
+    w.scale_in = take(rin * 4);
     w.hin = take(rin * d.intermediate * 4);
     w.yin = take(rin * d.hidden * 2);
     w.count_in = take(16);
@@ -379,23 +381,29 @@ hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm,
     comm->last_plan = plan;
 
     // 3. dispatch rows and routing weights to the expert owners
-    auto* xperm = reinterpret_cast<__nv_bfloat16*>(ws + w.local.xperm);
+    auto* xperm = reinterpret_cast<__half*>(ws + w.local.xperm);
     auto* wperm = reinterpret_cast<float*>(ws + w.local.perm_weight);
+    auto* sperm = reinterpret_cast<float*>(ws + w.local.xscale);
     auto* yrows = reinterpret_cast<__nv_bfloat16*>(ws + w.local.yrows);
-    auto* xin = reinterpret_cast<__nv_bfloat16*>(ws + w.xin);
+    auto* xin = reinterpret_cast<__half*>(ws + w.xin);
     auto* win = reinterpret_cast<float*>(ws + w.win);
+    auto* scale_in = reinterpret_cast<float*>(ws + w.scale_in);
     auto* yin = reinterpret_cast<__nv_bfloat16*>(ws + w.yin);
     N.groupStart();
     for (int q = 0; q < P && nr == ncclSuccess; ++q) {
         if (plan.send_rows[q] > 0) {
-            nr = N.send(xperm + plan.send_offset[q] * H, plan.send_rows[q] * H, ncclBfloat16, q, comm->comm, s);
+            nr = N.send(xperm + plan.send_offset[q] * H, plan.send_rows[q] * H, ncclFloat16, q, comm->comm, s);
             if (nr == ncclSuccess)
                 nr = N.send(wperm + plan.send_offset[q], plan.send_rows[q], ncclFloat32, q, comm->comm, s);
+            if (nr == ncclSuccess)
+                nr = N.send(sperm + plan.send_offset[q], plan.send_rows[q], ncclFloat32, q, comm->comm, s);
         }
         if (plan.recv_rows[q] > 0 && nr == ncclSuccess) {
-            nr = N.recv(xin + plan.recv_offset[q] * H, plan.recv_rows[q] * H, ncclBfloat16, q, comm->comm, s);
+            nr = N.recv(xin + plan.recv_offset[q] * H, plan.recv_rows[q] * H, ncclFloat16, q, comm->comm, s);
             if (nr == ncclSuccess)
                 nr = N.recv(win + plan.recv_offset[q], plan.recv_rows[q], ncclFloat32, q, comm->comm, s);
+            if (nr == ncclSuccess)
+                nr = N.recv(scale_in + plan.recv_offset[q], plan.recv_rows[q], ncclFloat32, q, comm->comm, s);
         }
     }
     const ncclResult_t ge = N.groupEnd();
@@ -410,6 +418,7 @@ hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm,
     if (rin > 0) {
         ExpertRun in = run;
         in.xrows = xin;
+        in.xscale = scale_in;
         in.weight = win;
         in.tiles = reinterpret_cast<int4*>(ws + w.tiles_in);
         in.tile_count = reinterpret_cast<int32_t*>(ws + w.count_in);

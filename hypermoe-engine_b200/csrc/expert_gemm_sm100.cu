@@ -93,6 +93,7 @@ struct GemmArgs {
     int nblocks;                // feature blocks per pair
     const hmoe_expert_quant* quant;
     const float* perm_weight;   // down: routing weight per row
+    const float* xscale;        // gate/up: 1 / (power-of-two scale of each token row)
     void* out;                  // BF16 rows [R,N]: gate/up SwiGLU output; down weighted output
     int K, N;
     DeviceStatus* st;
@@ -103,21 +104,41 @@ __device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
     return *reinterpret_cast<const uint32_t*>(&v);
 }
 
-// 16 INT8 weights -> 16 BF16 values q - zp, exact:
-// float(2^23 + u) - (2^23 + 128 + zp) with u = q + 128; BF16 keeps the
-// integer exactly (|q - zp| <= 255 needs 8 significant bits).
-__device__ __forceinline__ void dequant16(const uint4 q, float off, uint32_t (&o)[8]) {
+__device__ __forceinline__ uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+    const __half2 r = __hsub2(*reinterpret_cast<const __half2*>(&a), *reinterpret_cast<const __half2*>(&b));
+    return *reinterpret_cast<const uint32_t*>(&r);
+}
+
+// 16 INT8 weights -> 16 16-bit values q - zp, exact.
+//  BF16: float(2^23 + u) - (2^23 + 128 + zp) with u = q + 128, packed
+//        (BF16 keeps the integer exactly: |q - zp| <= 255 needs 8 bits).
+//  FP16: two bytes at a time: the half pair (1024 + u0, 1024 + u1) built by
+//        one byte permute, minus (1152 + zp) in both halves -- exact in FP16.
+template <bool F16>
+__device__ __forceinline__ void dequant16(const uint4 q, float off, uint32_t offh2, uint32_t (&o)[8]) {
     const uint32_t w[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
         const uint32_t u = w[i] ^ 0x80808080u;
-        const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - off;
-        const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - off;
-        const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - off;
-        const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - off;
-        o[2 * i] = bf16x2(f0, f1);
-        o[2 * i + 1] = bf16x2(f2, f3);
+        if constexpr (F16) {
+            o[2 * i] = hsub2_u32(__byte_perm(u, 0x64646464u, 0x4140), offh2);
+            o[2 * i + 1] = hsub2_u32(__byte_perm(u, 0x64646464u, 0x4342), offh2);
+        } else {
+            const float f0 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7540)) - off;
+            const float f1 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7541)) - off;
+            const float f2 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7542)) - off;
+            const float f3 = __uint_as_float(__byte_perm(u, 0x4B000000u, 0x7543)) - off;
+            o[2 * i] = bf16x2(f0, f1);
+            o[2 * i + 1] = bf16x2(f2, f3);
+        }
     }
+}
+
+// (1152 + zp) in both halves of a half pair (exact: an integer below 2048).
+__device__ __forceinline__ uint32_t f16_offset_pair(int zp) {
+    const __half h = __int2half_rn(1152 + zp);
+    const __half2 p = __halves2half2(h, h);
+    return *reinterpret_cast<const uint32_t*>(&p);
 }
 
 // Two staging boxes [64 k][64 n] INT8 (atom 0 and atom 1) -> A [2 atoms of
@@ -127,8 +148,9 @@ __device__ __forceinline__ void dequant16(const uint4 q, float off, uint32_t (&o
 // read two 64-byte rows that fall in different bank halves, and their
 // 16-byte stores land in 8 distinct chunk positions (row k gets even
 // chunks, row k+1 odd ones), so neither side has bank conflicts.
+template <bool F16>
 __device__ __forceinline__ void dequant_stage(const uint8_t* s0, const uint8_t* s1, uint8_t* a, float off0,
-                                              float off1, int dt) {
+                                              float off1, uint32_t offh0, uint32_t offh1, int dt) {
 #pragma unroll
     for (int i = 0; i < 2; ++i) {
         const int u = dt + 256 * i;
@@ -136,7 +158,7 @@ __device__ __forceinline__ void dequant_stage(const uint8_t* s0, const uint8_t* 
         const int k = 2 * kp + r;
         const uint4 v = *reinterpret_cast<const uint4*>((atom ? s1 : s0) + k * 64 + q * 16);
         uint32_t o[8];
-        dequant16(v, atom ? off1 : off0, o);
+        dequant16<F16>(v, atom ? off1 : off0, atom ? offh1 : offh0, o);
         uint8_t* row = a + atom * 8192 + k * 128;
         const int cc = 2 * q;
         *reinterpret_cast<uint4*>(row + ((cc ^ (k & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
@@ -294,7 +316,8 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
             for (int item = pair; item < n_items && !*abort_s; item += npairs, ++j) {
                 const int4 td = a.tiles[item / a.nblocks];
                 const uint32_t nmma = static_cast<uint32_t>((td.z + 15) & ~15);
-                const uint32_t idesc = sm100::make_idesc_bf16(256, nmma, true, false);
+                // gate/up: FP16 operands (scaled token rows); down: BF16
+                const uint32_t idesc = sm100::make_idesc_f16kind(256, nmma, true, false, !GATE_UP);
                 const int buf = j & 1;
                 if (j >= 2 && !sm100::mbar_wait_cluster(&accempty[buf], ((j >> 1) - 1) & 1, abort_s, kWaitNs)) {
                     if (lane == 0) fail();
@@ -343,6 +366,8 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
             const hmoe_expert_quant qp = a.quant[td.x];
             const float off0 = 8388608.0f + 128.0f + static_cast<float>(qp.zero_point[GATE_UP ? 0 : 2]);
             const float off1 = 8388608.0f + 128.0f + static_cast<float>(qp.zero_point[GATE_UP ? 1 : 2]);
+            const uint32_t offh0 = f16_offset_pair(qp.zero_point[GATE_UP ? 0 : 2]);
+            const uint32_t offh1 = f16_offset_pair(qp.zero_point[GATE_UP ? 1 : 2]);
             bool ok = true;
             for (int kb = 0; kb < nkb; ++kb, ++wi, ++ai) {
                 const int ws = wi % kWStages, as = ai % kAStages;
@@ -353,7 +378,7 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
                     ok = false;
                     break;
                 }
-                dequant_stage(S(ws, 0), S(ws, 1), A(as), off0, off1, dt);
+                dequant_stage<GATE_UP>(S(ws, 0), S(ws, 1), A(as), off0, off1, offh0, offh1, dt);
                 sm100::fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) {
@@ -399,13 +424,17 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
                 if (GATE_UP) {
                     // rows 0-63: gate of features f, rows 64-127: up of the same
                     // f.  Warps q<2 finish tokens 0..15, warps q>=2 tokens 16..31.
+                    // The token rows were scaled by powers of two; xs undoes it.
                     const float sg = qp.scale[0], su = qp.scale[1];
+                    const float isl = lane < nt ? a.xscale[row0 + c0 + lane] : 0.0f;
                     if (q < 2) {
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) xg[i * 64 + m] = sg * __uint_as_float(v[16 + i]);
+                        for (int i = 0; i < 16; ++i)
+                            xg[i * 64 + m] = sg * (__uint_as_float(v[16 + i]) * __shfl_sync(0xffffffffu, isl, 16 + i));
                     } else {
 #pragma unroll
-                        for (int i = 0; i < 16; ++i) xu[i * 64 + (m - 64)] = su * __uint_as_float(v[i]);
+                        for (int i = 0; i < 16; ++i)
+                            xu[i * 64 + (m - 64)] = su * (__uint_as_float(v[i]) * __shfl_sync(0xffffffffu, isl, i));
                     }
                     epi_barrier(grp);
                     __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(stg); // [32 t][64 f]
@@ -413,7 +442,7 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
                     if (q < 2) {
 #pragma unroll
                         for (int i = 0; i < 16; ++i) {
-                            const float gv = sg * __uint_as_float(v[i]);
+                            const float gv = sg * (__uint_as_float(v[i]) * __shfl_sync(0xffffffffu, isl, i));
                             const float uv = xu[i * 64 + f];
                             st[i * 64 + f] = __float2bfloat16_rn(silu_fast(gv) * uv);
                         }
@@ -421,7 +450,7 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
 #pragma unroll
                         for (int i = 0; i < 16; ++i) {
                             const float gv = xg[i * 64 + f];
-                            const float uv = su * __uint_as_float(v[16 + i]);
+                            const float uv = su * (__uint_as_float(v[16 + i]) * __shfl_sync(0xffffffffu, isl, 16 + i));
                             st[(16 + i) * 64 + f] = __float2bfloat16_rn(silu_fast(gv) * uv);
                         }
                     }
@@ -529,18 +558,40 @@ __global__ void __launch_bounds__(kMaxSegments) tile_list_kernel(SegSpec sp, int
     if (i == 0) *tile_count = min(capacity, total_full_s + parts_s);
 }
 
-// Token-major permutation: token t's FP32 row is read once, converted to
-// BF16 and written to each of its rows inv[t, 0..slots).
+// Token-major permutation: token t's FP32 row is read once, scaled by the
+// power of two s_t that puts its largest magnitude in [2^14, 2^15),
+// converted to FP16 (11-bit significand, no overflow) and written to each of
+// its rows inv[t, 0..slots); 1/s_t is stored per row for the epilogues.
 __global__ void __launch_bounds__(256) permute_kernel(const float* __restrict__ x, const int32_t* __restrict__ inv,
-                                                      int slots, int H, __nv_bfloat16* __restrict__ xrows) {
+                                                      int slots, int H, __half* __restrict__ xrows,
+                                                      float* __restrict__ xscale) {
     __shared__ int rows_s[kMaxSlots];
+    __shared__ float red_s[8];
     const int t = blockIdx.x;
     for (int s = threadIdx.x; s < slots; s += blockDim.x) rows_s[s] = inv[static_cast<size_t>(t) * slots + s];
-    __syncthreads();
     const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H);
+    float mx = 0.0f;
+    for (int c = threadIdx.x; c < H / 4; c += blockDim.x) {
+        const float4 v = src[c];
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((threadIdx.x & 31) == 0) red_s[threadIdx.x >> 5] = mx;
+    __syncthreads();
+    mx = red_s[0];
+    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) mx = fmaxf(mx, red_s[w]);
+    int ex = 0;
+    if (mx > 0.0f && isfinite(mx)) frexpf(mx, &ex); // mx = m * 2^ex, m in [0.5, 1)
+    const int sh = (mx > 0.0f && isfinite(mx)) ? max(-126, min(126, 15 - ex)) : 0;
+    const float sc = ldexpf(1.0f, sh), isc = ldexpf(1.0f, -sh);
+    for (int s = threadIdx.x; s < slots; s += blockDim.x) xscale[rows_s[s]] = isc;
     for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
         const float4 v0 = src[2 * c], v1 = src[2 * c + 1];
-        const uint4 o = make_uint4(bf16x2(v0.x, v0.y), bf16x2(v0.z, v0.w), bf16x2(v1.x, v1.y), bf16x2(v1.z, v1.w));
+        const __half2 h0 = __floats2half2_rn(v0.x * sc, v0.y * sc), h1 = __floats2half2_rn(v0.z * sc, v0.w * sc);
+        const __half2 h2 = __floats2half2_rn(v1.x * sc, v1.y * sc), h3 = __floats2half2_rn(v1.z * sc, v1.w * sc);
+        const uint4 o = make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
+                                   *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
         for (int s = 0; s < slots; ++s)
             reinterpret_cast<uint4*>(xrows + static_cast<size_t>(rows_s[s]) * H)[c] = o;
     }
@@ -568,13 +619,14 @@ bool map_weights(CUtensorMap* m, const int8_t* base, int N, int K, int experts, 
     return map_weights_box(m, base, N, K, experts, stride, 64, kBK);
 }
 
-// BF16 rows [rows, K] (K contiguous), 128-byte swizzle, box 64 x 128 rows.
-bool map_rows(CUtensorMap* m, const void* base, int K, int rows) {
+// 16-bit rows [rows, K] (K contiguous), 128-byte swizzle, box 64 x 128 rows.
+bool map_rows(CUtensorMap* m, const void* base, int K, int rows, bool f16) {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
     const cuuint32_t box[2] = {kBK, kHalfT};
     const cuuint32_t es[2] = {1, 1};
-    return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
+    return encode_fn()(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                       const_cast<void*>(base), dims, strides, box, es,
                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -659,10 +711,10 @@ hmoe_status launch_tile_list(const SegSpec& spec, int4* tiles, int32_t* tile_cou
     return check_launch("hmoe tile list");
 }
 
-hmoe_status launch_permute(const float* x, const int32_t* inv, int tokens, int slots, int H,
-                           __nv_bfloat16* xrows, cudaStream_t s) {
+hmoe_status launch_permute(const float* x, const int32_t* inv, int tokens, int slots, int H, __half* xrows,
+                           float* xscale, cudaStream_t s) {
     if (tokens <= 0) return HMOE_OK;
-    permute_kernel<<<static_cast<unsigned>(tokens), 256, 0, s>>>(x, inv, slots, H, xrows);
+    permute_kernel<<<static_cast<unsigned>(tokens), 256, 0, s>>>(x, inv, slots, H, xrows, xscale);
     return check_launch("hmoe permute");
 }
 
@@ -676,24 +728,24 @@ hmoe_status gemm_gate_up(const ExpertRun& r, cudaStream_t s) {
     CUtensorMap mg, mu, mb;
     if (!map_weights(&mg, r.arena + r.gate_offset, r.I, r.H, r.experts, r.stride) ||
         !map_weights(&mu, r.arena + r.up_offset, r.I, r.H, r.experts, r.stride) ||
-        !map_rows(&mb, r.xrows, r.H, r.rows_cap)) {
+        !map_rows(&mb, r.xrows, r.H, r.rows_cap, true)) {
         set_last_error_text("hmoe: cuTensorMapEncodeTiled failed (gate/up)");
         return HMOE_CUDA_ERROR;
     }
     const int nb = (r.I + 127) / 128; // 128 features (64 per CTA) per pair
-    GemmArgs a{r.tiles, r.tile_count, nb, r.quant, nullptr, r.hmid16, r.H, r.I, r.st};
+    GemmArgs a{r.tiles, r.tile_count, nb, r.quant, nullptr, r.xscale, r.hmid16, r.H, r.I, r.st};
     return launch_gemm<true>(mg, mu, mb, a, r.tile_cap * nb, s);
 }
 
 hmoe_status gemm_down(const ExpertRun& r, cudaStream_t s) {
     CUtensorMap md, mb;
     if (!map_weights(&md, r.arena + r.down_offset, r.H, r.I, r.experts, r.stride) ||
-        !map_rows(&mb, r.hmid16, r.I, r.rows_cap)) {
+        !map_rows(&mb, r.hmid16, r.I, r.rows_cap, false)) {
         set_last_error_text("hmoe: cuTensorMapEncodeTiled failed (down)");
         return HMOE_CUDA_ERROR;
     }
     const int nb = (r.H + 255) / 256; // 256 features (128 per CTA) per pair
-    GemmArgs a{r.tiles, r.tile_count, nb, r.quant, r.weight, r.yrows, r.I, r.H, r.st};
+    GemmArgs a{r.tiles, r.tile_count, nb, r.quant, r.weight, nullptr, r.yrows, r.I, r.H, r.st};
     return launch_gemm<false>(md, md, mb, a, r.tile_cap * nb, s);
 }
 

@@ -119,7 +119,7 @@ __global__ void __launch_bounds__(kVThreads, 2)
             if (t < nj && kb + kk < ke) {
                 const size_t row = static_cast<size_t>(r0 + j0 + t);
                 if constexpr (GATE_UP)
-                    v = __bfloat162float(a.act16[row * K + kb + kk]);
+                    v = __half2float(a.act16[row * K + kb + kk]) * a.xscale[row];
                 else
                     v = a.act32[row * K + kb + kk];
             }
@@ -288,6 +288,7 @@ GemvArgs gemv_common(const ExpertRun& r) {
 hmoe_status gemv_gate_up(const ExpertRun& r, cudaStream_t s) {
     GemvArgs g = gemv_common(r);
     g.act16 = r.xrows;
+    g.xscale = r.xscale;
     g.proj0 = 0;
     g.out32 = r.hmid32;
     g.K = r.H;

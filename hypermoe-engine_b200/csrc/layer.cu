@@ -12,7 +12,7 @@
 //   memset(status, counts)                          (one cudaMemsetAsync)
 //   route_kernel     logits, softmax, top-k, renorm, expert histogram
 //   group_kernel     offsets, permutation, inverse map
-//   permute_kernel   each token row once -> BF16 copies at its permuted rows
+//   permute_kernel   each token row once -> FP16 copies (power-of-two scaled)
 //   tile_list_kernel (expert, first row, rows) tiles, longest first
 //   gate/up          tcgen05 GEMM (or the weight-streaming GEMV for
 //                    decode-sized batches), SwiGLU in the epilogue
@@ -66,6 +66,7 @@ Workspace plan_workspace(const hmoe_layer_desc& d, size_t T) {
     w.perm_weight = take(R * 4);
     w.inv = take(R * 4);
     w.xperm = take(R * static_cast<size_t>(d.hidden) * 2);
+    w.xscale = take(R * 4);
     w.hmid = take(R * static_cast<size_t>(d.intermediate) * 4);
     w.yrows = take(R * static_cast<size_t>(d.hidden) * 2);
     w.tile_count = take(16);
@@ -173,7 +174,7 @@ hmoe_status enqueue_route(const hmoe_layer_desc& d, const float* x, size_t T, ch
     if (r != HMOE_OK || !permute) return r;
     return launch_permute(x, reinterpret_cast<int32_t*>(ws + w.inv), static_cast<int>(T),
                           static_cast<int>(d.top_k + d.shared_experts), static_cast<int>(d.hidden),
-                          reinterpret_cast<__nv_bfloat16*>(ws + w.xperm), s);
+                          reinterpret_cast<__half*>(ws + w.xperm), reinterpret_cast<float*>(ws + w.xscale), s);
 }
 
 // gate/up then down of every tile of `r` with the chosen variant.
@@ -198,7 +199,8 @@ bool use_gemv(long rows) {
 
 ExpertRun local_run(const hmoe_layer_desc& d, size_t T, char* ws, const Workspace& w) {
     ExpertRun r{};
-    r.xrows = reinterpret_cast<__nv_bfloat16*>(ws + w.xperm);
+    r.xrows = reinterpret_cast<__half*>(ws + w.xperm);
+    r.xscale = reinterpret_cast<float*>(ws + w.xscale);
     r.weight = reinterpret_cast<float*>(ws + w.perm_weight);
     r.tiles = reinterpret_cast<int4*>(ws + w.tiles);
     r.tile_count = reinterpret_cast<int32_t*>(ws + w.tile_count);

@@ -12,7 +12,7 @@ namespace hmoe {
 // GEMM variant (one launch uses one of them).
 struct Workspace {
     size_t status, counts, zero_bytes, offsets, ids, scores, perm_token, perm_weight, inv;
-    size_t xperm, hmid, yrows, tiles, tile_count;
+    size_t xperm, xscale, hmid, yrows, tiles, tile_count;
     int tile_cap;
     size_t total;
 };
@@ -32,7 +32,8 @@ constexpr int kMaxSlots = 96;
 constexpr int kTileRows = 256;
 
 struct ExpertRun {
-    const __nv_bfloat16* xrows; // [rows_cap, H] permuted input rows (BF16)
+    const __half* xrows;        // [rows_cap, H] permuted input rows, FP16, scaled per token
+    const float* xscale;        // [rows_cap] 1 / (power-of-two scale) of each row
     const float* weight;        // [rows_cap] routing weight of each row
     const int4* tiles;          // device tile list
     const int32_t* tile_count;  // device count
@@ -53,7 +54,8 @@ struct ExpertRun {
 struct GemvArgs {
     const int4* tiles;
     const int32_t* tile_count;
-    const __nv_bfloat16* act16; // gate/up input rows (BF16)
+    const __half* act16;        // gate/up input rows (FP16, scaled per token)
+    const float* xscale;        // gate/up: 1 / scale of each row
     const float* act32;         // down input rows (FP32 intermediate)
     const float* weight;        // down: routing weight per row
     const hmoe_expert_quant* quant;
@@ -93,9 +95,10 @@ hmoe_status gemv_down(const ExpertRun& r, cudaStream_t stream);
 
 hmoe_status launch_tile_list(const SegSpec& spec, int4* tiles, int32_t* tile_count, int capacity,
                              cudaStream_t stream);
-// xrows[inv[t, s]] = BF16(x[t]) for every token t and slot s.
-hmoe_status launch_permute(const float* x, const int32_t* inv, int tokens, int slots, int H,
-                           __nv_bfloat16* xrows, cudaStream_t stream);
+// xrows[inv[t, s]] = FP16(x[t] * s_t), xscale[inv[t, s]] = 1 / s_t for
+// every token t and slot s (s_t: power of two, max |x[t]| s_t in [2^14, 2^15)).
+hmoe_status launch_permute(const float* x, const int32_t* inv, int tokens, int slots, int H, __half* xrows,
+                           float* xscale, cudaStream_t stream);
 
 // Upper bound of the tiles of `rows` rows spread over `segments` segments.
 int tile_capacity_for(long rows, int segments);

@@ -271,5 +271,13 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(uint32_t M, uint32_t N, b
            ((b_mn_major ? 1u : 0u) << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
+// Instruction descriptor, kind::f16 with FP32 accumulation: FP16 (bf16 =
+// false) or BF16 (bf16 = true) A and B of the same type.
+__host__ __device__ constexpr uint32_t make_idesc_f16kind(uint32_t M, uint32_t N, bool a_mn_major, bool b_mn_major,
+                                                          bool bf16) {
+    return (1u << 4) | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10) | ((a_mn_major ? 1u : 0u) << 15) |
+           ((b_mn_major ? 1u : 0u) << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+
 } // namespace sm100
 } // namespace hmoe

@@ -40,7 +40,7 @@ EXPORTS = [
     "hmoe_set_stage_events", "hmoe_launch_count", "hmoe_moe_forward_host",
     "hmoe_ep_expert_range", "hmoe_ep_plan", "hmoe_ep_unique_id", "hmoe_ep_comm_create",
     "hmoe_ep_comm_destroy", "hmoe_ep_workspace_size", "hmoe_ep_moe_forward", "hmoe_ep_last_plan",
-    "hmoe_moe_forward_noalloc",
+    "hmoe_moe_forward_noalloc", "hmoe_selftest_bounded_wait",
 ]
 EP_MAX_RANKS = 64
 EP_UNIQUE_ID_BYTES = 128
@@ -125,6 +125,7 @@ def lib() -> ctypes.CDLL:
             "hmoe_ep_moe_forward": [ctypes.POINTER(LayerDesc), vp, vp, vp, sz, sz, vp, sz, vp],
             "hmoe_ep_last_plan": [vp, ctypes.POINTER(EpPlan)],
             "hmoe_moe_forward_noalloc": [ctypes.POINTER(LayerDesc), vp, vp, sz, vp],
+            "hmoe_selftest_bounded_wait": [vp, ctypes.c_uint32, vp],
         }
         for name, args in sigs.items():
             fn = getattr(L, name)

@@ -323,6 +323,15 @@ hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc *desc,
                                 void *workspace, size_t workspace_bytes,
                                 void *stream);
 
+/* Failure-detection self-test (no counterpart in the reference): launches
+ * one kernel that waits on an mbarrier nothing arrives on, using the same
+ * bounded wait as every kernel of the library.  After limit_us (1..10^6)
+ * microseconds the wait gives up, HMOE_TIMEOUT is recorded in the status
+ * word at the start of `workspace` (read it with hmoe_read_status) and the
+ * kernel returns; the context stays usable. */
+hmoe_status hmoe_selftest_bounded_wait(void *workspace, uint32_t limit_us,
+                                       void *stream);
+
 /* ----------------------------------------- host-side synthetic inputs */
 
 /* Seeded counter-based normal generator (SplitMix64 + Box-Muller in double),

@@ -305,3 +305,23 @@ def test_workspace_too_small_is_rejected(cuda):
     rc = H.lib().hmoe_moe_forward(ctypes.byref(dl.desc), x.data_ptr(), y.data_ptr(), 4, ws.data_ptr(), 1024,
                                   stream())
     assert rc == 6
+
+
+def test_bounded_wait_times_out_and_context_survives(cuda):
+    # A device wait on a barrier nothing arrives on gives up after its limit,
+    # records HMOE_TIMEOUT, and the next layer call still computes correctly.
+    import time
+    cfg = H.CONFIGS["c1"]
+    hl = H.make_host_layer(cfg, seed=0)
+    x = H.make_tokens(cfg, 16, seed=0)
+    dl = H.DeviceLayer(hl, cuda)
+    ws = dl.workspace(16)
+    t0 = time.perf_counter()
+    H.check("selftest", H.lib().hmoe_selftest_bounded_wait(ws.data_ptr(), 20000, stream()))
+    st, _, _ = dl.read_status()
+    elapsed = time.perf_counter() - t0
+    assert st == 5  # HMOE_TIMEOUT
+    assert 0.015 < elapsed < 5.0
+    y = host(dl.forward(t(x, cuda)))
+    assert dl.read_status()[0] == 0
+    assert_layer_close(y, O.moe_layer_port(hl, x)[0])
