@@ -370,7 +370,44 @@ __global__ void __launch_bounds__(256, 2) route_kernel(RouteArgs a, int EQ, int 
             device_fail(a.st, HMOE_TIMEOUT);
         const float* ws = wsl + (sl % kRouteStages) * SR * E;
         if (active) {
-            for (int i = p; i < nr; i += P) {
+            // Two rows per iteration with every shared load issued before the
+            // DFMAs, so the load latency of one row overlaps the other's math.
+            int i = p;
+            for (; i + P < nr; i += 2 * P) {
+                float wv[2][4];
+                if (vec4) {
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const float4 w4 = *reinterpret_cast<const float4*>(ws + (i + u * P) * E + 4 * quad);
+                        wv[u][0] = w4.x; wv[u][1] = w4.y; wv[u][2] = w4.z; wv[u][3] = w4.w;
+                    }
+                } else {
+#pragma unroll
+                    for (int u = 0; u < 2; ++u)
+#pragma unroll
+                        for (int j = 0; j < 4; ++j)
+                            wv[u][j] = 4 * quad + j < E ? ws[(i + u * P) * E + 4 * quad + j] : 0.0f;
+                }
+                double xv[2][kRouteTokens];
+#pragma unroll
+                for (int u = 0; u < 2; ++u)
+#pragma unroll
+                    for (int t = 0; t < kRouteTokens; ++t) xv[u][t] = xs[t * kRouteChunk + xoff + i + u * P];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    double wd[4];
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        wd[j] = static_cast<double>(wv[u][j]);
+                        sq[j] = fmaf(wv[u][j], wv[u][j], sq[j]);
+                    }
+#pragma unroll
+                    for (int t = 0; t < kRouteTokens; ++t)
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) acc[t][j] = fma(xv[u][t], wd[j], acc[t][j]);
+                }
+            }
+            for (; i < nr; i += P) {
                 float wv[4];
                 if (vec4) {
                     const float4 w4 = *reinterpret_cast<const float4*>(ws + i * E + 4 * quad);
@@ -447,55 +484,72 @@ __global__ void __launch_bounds__(256, 2) route_kernel(RouteArgs a, int EQ, int 
             xn[tid] = v;
         }
         __syncthreads();
-        // Phase 2: exact float logits.  Thread (quad, p) finalises token p;
-        // logits the certificate cannot settle are queued and recomputed in
-        // the reference's sequential order by whole warps (phase 2b).
+        // Norm factors of the certificate, once per token and per expert:
+        // ||x_t|| and ||W_e|| (each rounded up).
+        double* wn = reinterpret_cast<double*>(evs); // [E_pad], free until phase 3
+        for (int e = tid; e < E; e += blockDim.x) {
+            float w2 = 0.0f;
+            for (int r = 0; r < KS; ++r) w2 += cluster.map_shared_rank(wsq, r)[e];
+            wn[e] = sqrt(static_cast<double>(w2) * (1.0 + (H + 64) * 0x1.0p-22));
+        }
+        if (tid < kRouteTokens) xn[tid] = sqrt(xn[tid] * (1.0 + 0x1.0p-40));
+        __syncthreads();
+        // Phase 2: exact float logits; logits the certificate cannot settle
+        // are queued and recomputed in the reference's sequential order by
+        // whole warps (phase 2b).
+        const int L = H / (P * KS) + 1;
+        const double gamma = static_cast<double>(H + L + P * KS + 4) * 0x1.0p-53 * 1.01;
         for (int idx = tid; idx < nt * E; idx += blockDim.x) {
             const int t = idx / E, e = idx % E;
-            {
-                double pr[8];
-                float wr[8];
+            double pr[8];
 #pragma unroll
-                for (int r = 0; r < 8; ++r) { // issue every remote load first
-                    pr[r] = r < KS ? cluster.map_shared_rank(part, r)[(t * P) * E_pad + e] : 0.0;
-                    wr[r] = r < KS ? cluster.map_shared_rank(wsq, r)[e] : 0.0f;
-                }
-                double s = 0.0;
-                float w2 = 0.0f;
-                for (int r = 0; r < KS; ++r) {
-                    s += pr[r];
-                    w2 += wr[r];
-                }
-                double A = sqrt(xn[t] * (1.0 + 0x1.0p-40)) *
-                           sqrt(static_cast<double>(w2) * (1.0 + (H + 64) * 0x1.0p-22)) * (1.0 + 0x1.0p-40);
-                if (a.bias) {
-                    s += static_cast<double>(a.bias[e]);
-                    A += fabs(static_cast<double>(a.bias[e]));
-                }
-                const int L = H / (P * KS) + 1;
-                const double beta = static_cast<double>(H + L + P * KS + 4) * 0x1.0p-53 * A * 1.01 + 0x1.0p-1060;
-                if (!rounding_certified(s, beta)) {
-                    const int slot = atomicAdd(fb_count, 1);
-                    if (slot < kRouteFallbacks) fb_list[slot] = t * 256 + e;
-                    else s = sequential_logit(a, t0 + t, e); // queue full: this thread does it
-                }
-                if (!isfinite(s)) device_fail(a.st, HMOE_NON_FINITE_ROUTER);
-                logit[t * E_pad + e] = static_cast<float>(s);
+            for (int r = 0; r < 8; ++r) // issue every remote load first
+                pr[r] = r < KS ? cluster.map_shared_rank(part, r)[(t * P) * E_pad + e] : 0.0;
+            double s = 0.0;
+            for (int r = 0; r < KS; ++r) s += pr[r];
+            double A = xn[t] * wn[e] * (1.0 + 0x1.0p-40);
+            if (a.bias) {
+                s += static_cast<double>(a.bias[e]);
+                A += fabs(static_cast<double>(a.bias[e]));
             }
+            const double beta = gamma * A + 0x1.0p-1060;
+            if (!rounding_certified(s, beta)) {
+                const int slot = atomicAdd(fb_count, 1);
+                if (slot < kRouteFallbacks) fb_list[slot] = t * 256 + e;
+                else s = sequential_logit(a, t0 + t, e); // queue full: this thread does it
+            }
+            if (!isfinite(s)) device_fail(a.st, HMOE_NON_FINITE_ROUTER);
+            logit[t * E_pad + e] = static_cast<float>(s);
         }
         __syncthreads();
-        // Phase 2b: warp-cooperative sequential recomputation.
+        // Phase 2b: warp-cooperative sequential recomputation.  Each lane
+        // forms one exact product per 32-row chunk; the chunks' products are
+        // loaded four chunks ahead of the dependent double additions.
         const int nfb = min(*fb_count, kRouteFallbacks);
         for (int f = warp; f < nfb; f += blockDim.x >> 5) {
             const int t = fb_list[f] >> 8, e = fb_list[f] & 255;
             const float* xr = a.x + static_cast<size_t>(t0 + t) * H;
-            double s = 0.0;
-            for (int i0 = 0; i0 < H; i0 += 32) {
-                const int i = i0 + lane;
-                // products of two floats are exact in double
-                const double prod = i < H ? static_cast<double>(xr[i]) * static_cast<double>(a.w[static_cast<size_t>(i) * E + e]) : 0.0;
+            auto prod_at = [&](int c) {
+                const int i = c * 32 + lane;
+                // products of two floats are exact in double; rows past H add +0.0
+                return i < H ? static_cast<double>(xr[i]) * static_cast<double>(a.w[static_cast<size_t>(i) * E + e])
+                             : 0.0;
+            };
+            const int nch = (H + 31) / 32;
+            double q[4];
 #pragma unroll
-                for (int jj = 0; jj < 32; ++jj) s += __shfl_sync(0xffffffffu, prod, jj);
+            for (int u = 0; u < 4; ++u) q[u] = prod_at(u);
+            double s = 0.0;
+            for (int c = 0; c < nch; c += 4) {
+                double nq[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) nq[u] = c + 4 + u < nch ? prod_at(c + 4 + u) : 0.0;
+#pragma unroll
+                for (int u = 0; u < 4; ++u)
+#pragma unroll
+                    for (int jj = 0; jj < 32; ++jj) s += __shfl_sync(0xffffffffu, q[u], jj);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) q[u] = nq[u];
             }
             if (a.bias) s += static_cast<double>(a.bias[e]);
             if (lane == 0) {
