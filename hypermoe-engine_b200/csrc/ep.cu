@@ -436,7 +436,7 @@ hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm,
         r = launch_tile_list(seg, const_cast<int4*>(in.tiles), const_cast<int32_t*>(in.tile_count), in.tile_cap, s);
         if (r != HMOE_OK) return r;
         stage(2, s);
-        r = run_experts(in, use_gemv(rin), true, s);
+        r = run_experts(in, use_gemv(rin, in.H, in.I), true, s);
         if (r != HMOE_OK) return r;
     } else {
         stage(2, s);
@@ -449,7 +449,7 @@ hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm,
         sh.tile_cap = tile_capacity_for(static_cast<long>(tokens) * S, S);
         const SegSpec seg{reinterpret_cast<int32_t*>(ws + w.local.offsets) + E, nullptr, 0, S, S, Eloc, 0};
         r = launch_tile_list(seg, const_cast<int4*>(sh.tiles), const_cast<int32_t*>(sh.tile_count), sh.tile_cap, s);
-        if (r == HMOE_OK) r = run_experts(sh, use_gemv(static_cast<long>(tokens) * S), false, s);
+        if (r == HMOE_OK) r = run_experts(sh, use_gemv(static_cast<long>(tokens) * S, sh.H, sh.I), false, s);
         if (r != HMOE_OK) return r;
     }
 

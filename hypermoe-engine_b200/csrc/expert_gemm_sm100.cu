@@ -10,12 +10,14 @@
 // projection pair.
 //
 // Formulation ("weights as M"): for expert e, output features n and tokens
-// t, D[n, t] = sum_k W[k, n] * X[t, k].  The INT8 weight tile W[k0:k0+64,
+// t, D[n, t] = sum_k W[k, n] * X[t, k].  The INT8 weight tile W[k0:k0+128,
 // n0:n0+128] -- the packed [in,out] layout exactly as stored -- becomes the
-// MN-major BF16 A operand after an exact in-shared-memory dequantisation
-// (q - zp is an integer in [-255, 255]); the expert's token rows (BF16, K
-// contiguous, TMA with 128-byte swizzle) are the K-major B operand.
-// M = 128 features, N = 16..256 tokens, FP32 accumulation in TMEM.
+// MN-major 16-bit A operand after an exact in-shared-memory dequantisation
+// (q - zp is an integer in [-255, 255], exact in FP16 and BF16); the
+// expert's token rows (K contiguous, TMA with 128-byte swizzle) are the
+// K-major B operand: FP16 rows scaled per token by a power of two for
+// gate/up, BF16 SwiGLU rows for down.  M = 256 features per CTA pair,
+// N = 16..256 tokens, FP32 accumulation in TMEM.
 //
 // Persistent kernel over CTA pairs (thread-block clusters of 2), one CTA per
 // SM.  The pair runs the 2-SM MMA (tcgen05 .cta_group::2, M = 256): each CTA
@@ -23,15 +25,19 @@
 // shared-memory traffic per MMA FLOP compared with one CTA.  For gate/up a
 // CTA's 128 A rows are 64 gate features and the same 64 up features, so
 // both projections come out of one MMA and SwiGLU stays inside the CTA.
-// Warp roles (15 warps per CTA):
-//   warp 0      TMA producer of INT8 weight tiles (two [64 k][64 n] boxes per
-//               stage, 4-deep staging ring)
-//   warp 1      TMA producer of this CTA's half of the BF16 token tile
-//               (4-deep ring; bytes counted on the leader's barrier)
+// K advances 128 per stage: the issuing thread checks one barrier, issues 8
+// MMAs and one commit per stage (its per-instruction issue cost, not the
+// tensor core, bounds narrow tiles).
+// Warp roles (19 warps per CTA):
+//   warp 0      TMA producer of INT8 weight tiles (two [128 k][64 n] boxes per
+//               stage, 3-deep staging ring)
+//   warp 1      TMA producer of this CTA's half of the 16-bit token tile
+//               (two 64-k boxes per stage; bytes counted on the leader's barrier)
 //   warp 2      TMEM owner; in the leader CTA one thread issues the pair MMA
 //               and multicasts tcgen05.commit to both CTAs' barriers
-//   warps 3-10  dequantise INT8 -> BF16 into the swizzled A layout and
-//               signal the leader
+//   warps 3-10  dequantise INT8 -> FP16 (gate/up) or BF16 (down) into the
+//               swizzled A layout; in the leader they also wait for the token
+//               tile, so one barrier tells the MMA issuer the stage is ready
 //   warps 11-18 epilogue: tcgen05.ld from double-buffered accumulators,
 //               projection scale, SwiGLU (gate/up) or routing weight (down),
 //               BF16 rows staged in shared memory and stored coalesced,
@@ -59,30 +65,31 @@ namespace {
 constexpr int kTileT = 256;   // tokens per work item (pair MMA N <= 256)
 static_assert(kTileT == kTileRows, "GEMM work items are whole tiles");
 constexpr int kHalfT = 128;   // token rows per CTA (B box height)
-constexpr int kBK = 64;       // K per stage (128 bytes of BF16)
-constexpr int kWStages = 4;   // INT8 staging ring
-constexpr int kAStages = 3;   // BF16 A ring (dequantised weights)
-constexpr int kBStages = 4;   // BF16 token-tile ring
+constexpr int kBK = 128;      // K per stage: 8 MMAs (K = 16 each) per barrier round trip
+constexpr int kWStages = 3;   // INT8 staging ring
+constexpr int kStages = 2;    // A (dequantised weights) + B (token rows) ring, one commit per stage
 constexpr int kDequantWarps = 8;
 constexpr int kEpiWarps = 8;                // two groups of 4 (one per column half)
 constexpr int kThreadsGemm = 32 * (3 + kDequantWarps + kEpiWarps);
 constexpr uint64_t kWaitNs = 2000000000ull; // 2 s per wait
 constexpr uint32_t kTmemCols = 512;         // 2 accumulator buffers x 256 columns
 
-constexpr int kABytes = 128 * kBK * 2;     // 16 KB: 128 A rows (two 64-row atoms)
-constexpr int kBBytes = kHalfT * kBK * 2;  // 16 KB: 128 token rows
-constexpr int kSBytes = 64 * kBK;          // 4 KB: one [64 k][64 n] INT8 box
+constexpr int kAAtom = 128 * kBK;           // one 64-row MN atom: 128 B x kBK k rows (16 KB)
+constexpr int kABytes = 2 * kAAtom;         // 32 KB: 128 A rows (two 64-row atoms)
+constexpr int kBBox = kHalfT * 64 * 2;      // 16 KB: one TMA box, 128 token rows x 64 k
+constexpr int kBBytes = 2 * kBBox;          // 32 KB: 128 token rows x 128 k
+constexpr int kSBytes = 64 * kBK;           // 8 KB: one [128 k][64 n] INT8 box
 // Epilogue scratch per column-half group: gate/up exchange (2 x 64 x 16
 // FP32) and an output staging tile (32 tokens x 128 BF16 for down, 32 x 64
 // BF16 for gate/up).
 constexpr int kXchBytes = 2 * 64 * 16 * 4;  // 8 KB
-constexpr int kStgBytes = 32 * 128 * 4;     // 16 KB
+constexpr int kStgBytes = 32 * 128 * 2;     // 8 KB
 constexpr int kXBytes = 2 * (kXchBytes + kStgBytes);
 
 constexpr int kSOff = 0;
 constexpr int kAOff = kSOff + kWStages * 2 * kSBytes;
-constexpr int kBOff = kAOff + kAStages * kABytes;
-constexpr int kXOff = kBOff + kBStages * kBBytes;
+constexpr int kBOff = kAOff + kStages * kABytes;
+constexpr int kXOff = kBOff + kStages * kBBytes;
 constexpr int kBarOff = kXOff + kXBytes;
 constexpr int kSmem = kBarOff + 512 + 1024 /*alignment slack*/;
 static_assert(kSmem <= 232448, "shared memory budget");
@@ -141,9 +148,9 @@ __device__ __forceinline__ uint32_t f16_offset_pair(int zp) {
     return *reinterpret_cast<const uint32_t*>(&p);
 }
 
-// Two staging boxes [64 k][64 n] INT8 (atom 0 and atom 1) -> A [2 atoms of
-// 64 MN][64 k][128 B] with the 128-byte swizzle (16-byte chunk index XOR
-// (k mod 8)).  256 threads, two 16-byte input chunks each.  Eight
+// Two staging boxes [kBK k][64 n] INT8 (atom 0 and atom 1) -> A [2 atoms of
+// 64 MN][kBK k][128 B] with the 128-byte swizzle (16-byte chunk index XOR
+// (k mod 8)).  256 threads, four 16-byte input chunks each.  Eight
 // consecutive threads cover rows k, k+1 (k even) of one box: their loads
 // read two 64-byte rows that fall in different bank halves, and their
 // 16-byte stores land in 8 distinct chunk positions (row k gets even
@@ -152,14 +159,14 @@ template <bool F16>
 __device__ __forceinline__ void dequant_stage(const uint8_t* s0, const uint8_t* s1, uint8_t* a, float off0,
                                               float off1, uint32_t offh0, uint32_t offh1, int dt) {
 #pragma unroll
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kBK / 32; ++i) {
         const int u = dt + 256 * i;
         const int q = u & 3, r = (u >> 2) & 1, atom = (u >> 3) & 1, kp = u >> 4;
         const int k = 2 * kp + r;
         const uint4 v = *reinterpret_cast<const uint4*>((atom ? s1 : s0) + k * 64 + q * 16);
         uint32_t o[8];
         dequant16<F16>(v, atom ? off1 : off0, atom ? offh1 : offh0, o);
-        uint8_t* row = a + atom * 8192 + k * 128;
+        uint8_t* row = a + atom * kAAtom + k * 128;
         const int cc = 2 * q;
         *reinterpret_cast<uint4*>(row + ((cc ^ (k & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
         *reinterpret_cast<uint4*>(row + (((cc + 1) ^ (k & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
@@ -191,11 +198,10 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
     uint64_t* full_w = bars;                  // [kWStages] local: weights landed
     uint64_t* empty_w = full_w + kWStages;    // [kWStages] local: staging consumed
-    uint64_t* full_b = empty_w + kWStages;    // [kBStages] leader: both token halves landed
-    uint64_t* empty_b = full_b + kBStages;    // [kBStages] both: MMA done with the slot
-    uint64_t* aready = empty_b + kBStages;    // [kAStages] leader: A written in both CTAs
-    uint64_t* empty_a = aready + kAStages;    // [kAStages] both: MMA done with A
-    uint64_t* accfull = empty_a + kAStages;   // [2] both: accumulator ready
+    uint64_t* full_b = empty_w + kWStages;    // [kStages] leader: both token halves landed
+    uint64_t* aready = full_b + kStages;      // [kStages] leader: A written in both CTAs, B landed
+    uint64_t* empty_ab = aready + kStages;    // [kStages] both: MMA done with A and B of the stage
+    uint64_t* accfull = empty_ab + kStages;   // [2] both: accumulator ready
     uint64_t* accempty = accfull + 2;         // [2] leader: both epilogues drained it
     uint64_t* drain = accempty + 2;           // [1] both: every MMA done
     uint32_t* tmem_s = reinterpret_cast<uint32_t*>(drain + 1);
@@ -213,13 +219,10 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
             sm100::mbar_init(&full_w[s], 1);
             sm100::mbar_init(&empty_w[s], kDequantWarps);
         }
-        for (int s = 0; s < kBStages; ++s) {
+        for (int s = 0; s < kStages; ++s) {
             sm100::mbar_init(&full_b[s], 1);
-            sm100::mbar_init(&empty_b[s], 1);
-        }
-        for (int s = 0; s < kAStages; ++s) {
             sm100::mbar_init(&aready[s], 2 * kDequantWarps);
-            sm100::mbar_init(&empty_a[s], 1);
+            sm100::mbar_init(&empty_ab[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             sm100::mbar_init(&accfull[b], 1);
@@ -279,7 +282,7 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
             for (uint32_t i = (it > kWStages ? it - kWStages : 0); i < it; ++i)
                 sm100::mbar_wait_for(&full_w[i % kWStages], (i / kWStages) & 1, kWaitNs);
     } else if (warp == 1) {
-        // ------------------------------------------------ BF16 token-tile producer
+        // ------------------------------------------------ 16-bit token-tile producer
         if (lane == 0) sm100::prefetch_tmap(&tm_b);
         uint32_t it = 0;
         for (int item = pair; item < n_items && !*abort_s; item += npairs) {
@@ -288,16 +291,17 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
             const int y = td.y + static_cast<int>(rank) * half;
             bool ok = true;
             for (int kb = 0; kb < nkb; ++kb, ++it) {
-                const int s = it % kBStages;
-                if (it >= kBStages &&
-                    !sm100::mbar_wait(&empty_b[s], ((it / kBStages) - 1) & 1, abort_s, kWaitNs)) {
+                const int s = it % kStages;
+                if (it >= kStages &&
+                    !sm100::mbar_wait(&empty_ab[s], ((it / kStages) - 1) & 1, abort_s, kWaitNs)) {
                     ok = false;
                     break;
                 }
                 if (lane == 0) {
+                    const uint32_t bar = sm100::map_shared(sm100::smem_u32(&full_b[s]), 0);
                     if (leader) sm100::mbar_arrive_expect_tx(&full_b[s], 2 * kBBytes);
-                    sm100::tma_load_2d_pair(B(s), &tm_b, kb * kBK, y,
-                                            sm100::map_shared(sm100::smem_u32(&full_b[s]), 0));
+                    sm100::tma_load_2d_pair(B(s), &tm_b, kb * kBK, y, bar);
+                    sm100::tma_load_2d_pair(B(s) + kBBox, &tm_b, kb * kBK + 64, y, bar);
                 }
                 __syncwarp();
             }
@@ -306,8 +310,12 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
                 break;
             }
         }
-        // Loads in flight complete on the leader's barriers; the teardown
-        // cluster barrier below keeps both CTAs alive until then.
+        // Both CTAs' token loads complete on the leader's barriers: after an
+        // abort the leader waits for the last stages it saw issued, and the
+        // teardown cluster barrier keeps the follower alive until then.
+        if (*abort_s && leader)
+            for (uint32_t i = (it > kStages ? it - kStages : 0); i < it; ++i)
+                sm100::mbar_wait_for(&full_b[i % kStages], (i / kStages) & 1, kWaitNs);
     } else if (warp == 2) {
         // ------------------------------------------------ MMA issuer (leader)
         if (leader) {
@@ -327,23 +335,24 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
                 const uint32_t d0 = tmem + static_cast<uint32_t>(buf * kTileT);
                 bool ok = true;
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
-                    const int as = it % kAStages, bs = it % kBStages;
-                    if (!sm100::mbar_wait_cluster(&full_b[bs], (it / kBStages) & 1, abort_s, kWaitNs) ||
-                        !sm100::mbar_wait_cluster(&aready[as], (it / kAStages) & 1, abort_s, kWaitNs)) {
+                    const int s = it % kStages;
+                    // aready implies the token tile landed: the leader's
+                    // dequantisation warps wait for it before arriving.
+                    if (!sm100::mbar_wait_cluster(&aready[s], (it / kStages) & 1, abort_s, kWaitNs)) {
                         ok = false;
                         break;
                     }
                     sm100::tc_fence_after();
                     if (lane == 0) {
-                        const uint32_t a0 = sm100::smem_u32(A(as)), b0 = sm100::smem_u32(B(bs));
+                        const uint32_t a0 = sm100::smem_u32(A(s)), b0 = sm100::smem_u32(B(s));
 #pragma unroll
                         for (int ks = 0; ks < kBK / 16; ++ks) {
-                            const uint64_t ad = sm100::make_smem_desc(a0 + ks * 2048, 8192, 1024, 2);
-                            const uint64_t bd = sm100::make_smem_desc(b0 + ks * 32, 16, 1024, 2);
+                            const uint64_t ad = sm100::make_smem_desc(a0 + ks * 2048, kAAtom, 1024, 2);
+                            const uint64_t bd =
+                                sm100::make_smem_desc(b0 + (ks >> 2) * kBBox + (ks & 3) * 32, 16, 1024, 2);
                             sm100::mma_bf16_pair(d0, ad, bd, idesc, (kb | ks) != 0);
                         }
-                        sm100::mma_commit_pair(&empty_a[as], 0x3);
-                        sm100::mma_commit_pair(&empty_b[bs], 0x3);
+                        sm100::mma_commit_pair(&empty_ab[s], 0x3);
                     }
                     __syncwarp();
                 }
@@ -370,10 +379,10 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
             const uint32_t offh1 = f16_offset_pair(qp.zero_point[GATE_UP ? 1 : 2]);
             bool ok = true;
             for (int kb = 0; kb < nkb; ++kb, ++wi, ++ai) {
-                const int ws = wi % kWStages, as = ai % kAStages;
+                const int ws = wi % kWStages, as = ai % kStages;
                 if (!sm100::mbar_wait(&full_w[ws], (wi / kWStages) & 1, abort_s, kWaitNs) ||
-                    (ai >= kAStages &&
-                     !sm100::mbar_wait_cluster(&empty_a[as], ((ai / kAStages) - 1) & 1, abort_s, kWaitNs))) {
+                    (ai >= kStages &&
+                     !sm100::mbar_wait_cluster(&empty_ab[as], ((ai / kStages) - 1) & 1, abort_s, kWaitNs))) {
                     fail();
                     ok = false;
                     break;
@@ -381,10 +390,13 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
                 dequant_stage<GATE_UP>(S(ws, 0), S(ws, 1), A(as), off0, off1, offh0, offh1, dt);
                 sm100::fence_proxy_async_smem();
                 __syncwarp();
-                if (lane == 0) {
-                    sm100::mbar_arrive(&empty_w[ws]);
-                    sm100::mbar_arrive_remote(sm100::map_shared(sm100::smem_u32(&aready[as]), 0));
+                if (lane == 0) sm100::mbar_arrive(&empty_w[ws]);
+                if (leader && !sm100::mbar_wait(&full_b[as], (ai / kStages) & 1, abort_s, kWaitNs)) {
+                    fail();
+                    ok = false;
+                    break;
                 }
+                if (lane == 0) sm100::mbar_arrive_remote(sm100::map_shared(sm100::smem_u32(&aready[as]), 0));
             }
             if (!ok) break;
         }
@@ -623,7 +635,7 @@ bool map_weights(CUtensorMap* m, const int8_t* base, int N, int K, int experts, 
 bool map_rows(CUtensorMap* m, const void* base, int K, int rows, bool f16) {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
-    const cuuint32_t box[2] = {kBK, kHalfT};
+    const cuuint32_t box[2] = {64, kHalfT}; // 128 bytes: the swizzle span
     const cuuint32_t es[2] = {1, 1};
     return encode_fn()(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                        const_cast<void*>(base), dims, strides, box, es,

@@ -191,8 +191,8 @@ hmoe_status run_experts(const ExpertRun& r, bool gemv, bool stages, cudaStream_t
 // tensor-core GEMM wins as soon as experts hold more than a few rows.  The
 // choice is made per launch from the number of permuted rows, which the host
 // knows without reading the routing.
-bool use_gemv(long rows) {
-    if (g_variant == 1 || !gemm_available()) return true;
+bool use_gemv(long rows, int H, int I) {
+    if (g_variant == 1 || !gemm_available() || !gemm_shape_ok(H, I)) return true;
     if (g_variant == 2) return false;
     return rows <= kGemvMaxAssignments;
 }
@@ -309,7 +309,7 @@ hmoe_status hmoe_moe_forward(const hmoe_layer_desc* desc, const float* x, float*
     r = launch_tile_list(seg, const_cast<int4*>(run.tiles), const_cast<int32_t*>(run.tile_count), run.tile_cap, s);
     if (r != HMOE_OK) return r;
     stage(2, s);
-    r = run_experts(run, use_gemv(static_cast<long>(tokens) * slots), true, s);
+    r = run_experts(run, use_gemv(static_cast<long>(tokens) * slots, run.H, run.I), true, s);
     if (r != HMOE_OK) return r;
     r = launch_combine(run.yrows, reinterpret_cast<int32_t*>(ws + w.inv), static_cast<int>(tokens), slots,
                        static_cast<int>(desc->hidden), y, s);

@@ -83,6 +83,8 @@ struct SegSpec {
 };
 
 bool gemm_available();
+// The tensor-core GEMM streams K in 128-deep stages.
+inline bool gemm_shape_ok(int H, int I) { return H % 128 == 0 && I % 128 == 0; }
 int device_sm_count();
 // TMA map of one INT8 projection over all experts: dims {N, K, experts},
 // box [box_k][box_n] (no swizzle).  False when the driver rejects it.
@@ -119,7 +121,8 @@ hmoe_status enqueue_route(const hmoe_layer_desc& d, const float* x, size_t T, ch
 ExpertRun local_run(const hmoe_layer_desc& d, size_t T, char* ws, const Workspace& w);
 // gate/up then down of every tile of `r`; `stages` records stage events 3, 4.
 hmoe_status run_experts(const ExpertRun& r, bool gemv, bool stages, cudaStream_t s);
-bool use_gemv(long rows);
+// GEMV or tensor-core GEMM for `rows` permuted rows of an [H, I] expert.
+bool use_gemv(long rows, int H, int I);
 
 // Records stage event i (0..5) when stage events are registered.  Under
 // stream capture the record becomes an external event node, so the caller
