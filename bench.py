@@ -36,6 +36,7 @@ import subprocess
 import sys
 import threading
 import time
+from typing import Optional
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "hypermoe-engine_b200"))
@@ -57,6 +58,9 @@ def parse():
     p.add_argument("--variant", type=int, default=0, help="0 auto, 1 GEMV only, 2 GEMM only")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
+    p.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
+                   help="expert placement under expert parallelism: balanced from a calibration batch's "
+                        "routing counts (EPLB-style static placement), or contiguous expert ids")
     p.add_argument("--eager", action="store_true",
                    help="time eager hmoe_moe_forward calls instead of CUDA-graph replays")
     return p.parse_args()
@@ -73,18 +77,48 @@ def load_peaks():
 
 
 class Clocks:
-    """nvidia-smi sampler for the timed region (clocks and throttle reasons)."""
+    """SM clock and throttle-reason sampler for the timed region (read-only
+    NVML queries every 5 ms; nvidia-smi every 200 ms when NVML is missing)."""
 
+    REASONS = {"hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+               "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+               "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+               "sw_power_cap": "nvmlClocksEventReasonSwPowerCap"}
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, pci_bus_id: Optional[str] = None):
         self.index = index
+        self.pci = pci_bus_id
         self.proc = None
+        self.thread = None
+        self.stop_flag = threading.Event()
+        self.sm, self.max_mhz, self.reasons = [], None, set()
         self.lines = []
 
     def start(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = (pynvml.nvmlDeviceGetHandleByPciBusId(self.pci.encode()) if self.pci
+                 else pynvml.nvmlDeviceGetHandleByIndex(self.index))
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            bits = {n: getattr(pynvml, v) for n, v in self.REASONS.items()}
+
+            def poll():
+                while not self.stop_flag.is_set():
+                    self.sm.append(float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)))
+                    r = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    for n, bit in bits.items():
+                        if r & bit:
+                            self.reasons.add(n)
+                    time.sleep(0.005)
+            self.thread = threading.Thread(target=poll, daemon=True)
+            self.thread.start()
+            return
+        except Exception:
+            pass
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200",
@@ -99,8 +133,13 @@ class Clocks:
             self.lines.append(line.strip())
 
     def stop(self):
+        if self.proc is None and self.thread is not None:  # NVML sampler
+            self.stop_flag.set()
+            self.thread.join(timeout=2)
+            return {"sm_mhz": statistics.median(self.sm) if self.sm else None, "sm_max_mhz": self.max_mhz,
+                    "reasons": sorted(self.reasons), "samples": len(self.sm), "source": "nvml 5 ms"}
         if not self.proc:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["clock sampling unavailable"]}
         time.sleep(0.25)
         self.proc.terminate()
         try:
@@ -122,7 +161,7 @@ class Clocks:
                 if v.lower().startswith("active"):
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+                "reasons": sorted(reasons), "samples": len(sm), "source": "nvidia-smi 200 ms"}
 
 
 def algorithmic(cfg, T, U, rows_in=None, local_experts=None):
@@ -231,7 +270,20 @@ def main():
         uid = [H.ep_unique_id() if rank == 0 else None]
         dist.broadcast_object_list(uid, src=0)
         comm = H.EpComm(uid[0], rank, world, timeout_ms=120000)
-        layer = H.EpLayer(host_layer, comm, dev)
+        placement = [None]
+        if args.placement == "balanced" and rank == 0:
+            # expert loads observed on a calibration batch (different seed
+            # from every timed batch), routed on this GPU
+            cal = H.DeviceLayer(host_layer, dev)
+            xc = torch.from_numpy(H.make_tokens(cfg, 4096, seed=args.seed + 104729)).to(dev)
+            _, _, off, _, _ = cal.route(xc)
+            load = np.diff(off.cpu().numpy()).astype(np.float64)
+            placement = [H.ep_balanced_placement(load, world)]
+            del cal, xc
+            torch.cuda.empty_cache()
+        if args.placement == "balanced":
+            dist.broadcast_object_list(placement, src=0)
+        layer = H.EpLayer(host_layer, comm, dev, slot_of_expert=placement[0])
     else:
         layer = H.DeviceLayer(host_layer, dev)
     x = torch.from_numpy(x_np).to(dev)
@@ -297,8 +349,12 @@ def main():
         torch.cuda.synchronize()
         stream = torch.cuda.current_stream()
     launches0 = H.lib().hmoe_launch_count()
+    props = torch.cuda.get_device_properties(dev)
+    pci = None
+    if hasattr(props, "pci_bus_id"):
+        pci = f"{getattr(props, 'pci_domain_id', 0):08X}:{props.pci_bus_id:02X}:{getattr(props, 'pci_device_id', 0):02X}.0"
     clocks = Clocks(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local])
-                    if os.environ.get("CUDA_VISIBLE_DEVICES") else local)
+                    if os.environ.get("CUDA_VISIBLE_DEVICES") else local, pci)
     clocks.start()
     stage_ms = {s: [] for s in STAGES}
     step_ms = []
@@ -412,6 +468,9 @@ def main():
         "vs_baseline": None, "dtype": "fp32" if not used_gemm else "fp16+bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights quantised to INT8)",
         "config": dict(config, parallelism=(f"ep{world}" if world > 1 else "single"),
+                       placement=(None if world == 1 else
+                                  "balanced from 4096 calibration tokens (seed+104729)" if args.placement == "balanced"
+                                  else "contiguous"),
                        l2="inputs larger than L2 (604 MB INT8 arena) and a 256 MiB flush between steps"),
         "e2e": e2e, "gpu_launches": launches,
         "timing": ("cuda-graph replay of hmoe_moe_forward" if graph is not None else

@@ -103,6 +103,11 @@ struct hmoe_ep_comm {
     cudaEvent_t counts_ready = nullptr;
     bool broken = false;
     hmoe_ep_plan_t last_plan{};
+    // Expert placement (slot of each expert; rank r owns a contiguous slot
+    // range), or identity when placement_experts == 0.
+    uint32_t placement_experts = 0;
+    int32_t slot_of_expert[256] = {};
+    int32_t* d_expert_of_slot = nullptr; // device [256]
 };
 
 namespace hmoe {
@@ -149,7 +154,7 @@ hmoe_status wait_counts(hmoe_ep_comm* c) {
 // receive side for up to P * max_tokens * k rows.
 struct EpWorkspace {
     Workspace local;
-    size_t counts_all, xin, win, scale_in, hin, yin, tiles_in, count_in;
+    size_t slot_counts, counts_all, xin, win, scale_in, hin, yin, tiles_in, count_in;
     int tile_cap_in;
     size_t total;
 };
@@ -168,6 +173,7 @@ EpWorkspace plan_ep(const hmoe_layer_desc& d, size_t max_tokens) {
         off = align_up(off + bytes, 256);
         return at;
     };
+    w.slot_counts = take(static_cast<size_t>(d.experts) * 4);
     w.counts_all = take(P * d.experts * 4);
     w.xin = take(rin * d.hidden * 2);
     w.win = take(rin * 4);
@@ -313,9 +319,70 @@ hmoe_status hmoe_ep_comm_destroy(hmoe_ep_comm* c) {
         if (r != ncclSuccess) st = nccl_fail("ncclCommDestroy", r);
     }
     if (c->counts_ready) cudaEventDestroy(c->counts_ready);
+    if (c->d_expert_of_slot) cudaFree(c->d_expert_of_slot);
     if (c->host_counts) cudaFreeHost(c->host_counts);
     delete c;
     return st;
+}
+
+hmoe_status hmoe_ep_set_placement(hmoe_ep_comm* comm, const int32_t* slot_of_expert, uint32_t experts) {
+    if (!comm) return HMOE_INVALID_ARGUMENT;
+    if (experts == 0 || !slot_of_expert) { // back to identity
+        comm->placement_experts = 0;
+        return HMOE_OK;
+    }
+    if (experts > 256) return HMOE_UNSUPPORTED;
+    int32_t expert_of_slot[256];
+    bool seen[256] = {};
+    for (uint32_t e = 0; e < experts; ++e) {
+        const int32_t sl = slot_of_expert[e];
+        if (sl < 0 || static_cast<uint32_t>(sl) >= experts || seen[sl]) return HMOE_INVALID_ARGUMENT;
+        seen[sl] = true;
+        expert_of_slot[sl] = static_cast<int32_t>(e);
+    }
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != comm->device) return HMOE_INVALID_ARGUMENT;
+    cudaError_t err = cudaSuccess;
+    if (!comm->d_expert_of_slot) err = cudaMalloc(&comm->d_expert_of_slot, 256 * sizeof(int32_t));
+    if (err == cudaSuccess)
+        err = cudaMemcpy(comm->d_expert_of_slot, expert_of_slot, experts * sizeof(int32_t), cudaMemcpyHostToDevice);
+    if (err != cudaSuccess) {
+        set_last_error("hmoe EP placement", err);
+        return HMOE_CUDA_ERROR;
+    }
+    std::memcpy(comm->slot_of_expert, slot_of_expert, experts * sizeof(int32_t));
+    comm->placement_experts = experts;
+    return HMOE_OK;
+}
+
+hmoe_status hmoe_ep_balanced_placement(const double* load, uint32_t experts, int32_t ep_size,
+                                       int32_t* slot_of_expert) {
+    if (!load || !slot_of_expert || ep_size < 1 || ep_size > HMOE_EP_MAX_RANKS || experts > 256 ||
+        experts < static_cast<uint32_t>(ep_size))
+        return HMOE_INVALID_ARGUMENT;
+    // Largest expected load first (ties by expert id), each to the rank with
+    // the least load so far among those with free slots (ties: lowest rank).
+    int32_t order[256];
+    for (uint32_t e = 0; e < experts; ++e) {
+        if (!(load[e] >= 0.0)) return HMOE_INVALID_ARGUMENT;
+        order[e] = static_cast<int32_t>(e);
+    }
+    std::stable_sort(order, order + experts, [&](int32_t a, int32_t b) { return load[a] > load[b]; });
+    double rank_load[HMOE_EP_MAX_RANKS] = {};
+    uint32_t filled[HMOE_EP_MAX_RANKS] = {};
+    for (uint32_t i = 0; i < experts; ++i) {
+        int best = -1;
+        for (int r = 0; r < ep_size; ++r) {
+            uint32_t first = 0, count = 0;
+            hmoe_ep_expert_range(experts, ep_size, r, &first, &count);
+            if (filled[r] < count && (best < 0 || rank_load[r] < rank_load[best])) best = r;
+        }
+        uint32_t first = 0, count = 0;
+        hmoe_ep_expert_range(experts, ep_size, best, &first, &count);
+        slot_of_expert[order[i]] = static_cast<int32_t>(first + filled[best]++);
+        rank_load[best] += load[order[i]];
+    }
+    return HMOE_OK;
 }
 
 hmoe_status hmoe_ep_last_plan(const hmoe_ep_comm* comm, hmoe_ep_plan_t* plan) {
@@ -356,14 +423,21 @@ hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm,
     const size_t H = desc->hidden;
     const int slots = k + S;
 
-    // 1. route, group and permute this rank's tokens (T may be 0)
+    // 1. route, group and permute this rank's tokens (T may be 0); with a
+    // placement the expert groups follow slot order, so each rank's slots
+    // are contiguous rows
+    const bool placed = comm->placement_experts != 0;
+    if (placed && comm->placement_experts != desc->experts) return HMOE_INVALID_ARGUMENT;
+    auto* slot_counts = reinterpret_cast<int32_t*>(ws + w.slot_counts);
     stage(0, s);
-    hmoe_status r = enqueue_route(*desc, x, tokens, ws, w.local, true, s);
+    hmoe_status r = enqueue_route(*desc, x, tokens, ws, w.local, true, s, placed ? comm->d_expert_of_slot : nullptr,
+                                  placed ? slot_counts : nullptr);
     if (r != HMOE_OK) return r;
 
-    // 2. counts of every (source, expert), read once on the host
+    // 2. counts of every (source, slot), read once on the host
     auto* counts_all = reinterpret_cast<int32_t*>(ws + w.counts_all);
-    ncclResult_t nr = N.allGather(ws + w.local.counts, counts_all, static_cast<size_t>(E), ncclInt32, comm->comm, s);
+    ncclResult_t nr = N.allGather(placed ? static_cast<void*>(slot_counts) : static_cast<void*>(ws + w.local.counts),
+                                  counts_all, static_cast<size_t>(E), ncclInt32, comm->comm, s);
     if (nr != ncclSuccess) return nccl_fail("EP count all-gather", nr);
     cudaError_t err = cudaMemcpyAsync(comm->host_counts, counts_all, static_cast<size_t>(P) * E * 4,
                                       cudaMemcpyDeviceToHost, s);
@@ -466,8 +540,9 @@ hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm,
     if (ge2 != ncclSuccess) return nccl_fail("EP return", ge2);
 
     // 6. combine in ascending expert id
-    r = launch_combine(yrows, reinterpret_cast<int32_t*>(ws + w.local.inv), static_cast<int>(tokens), slots,
-                       static_cast<int>(H), y, s);
+    r = launch_combine(yrows, reinterpret_cast<int32_t*>(ws + w.local.inv),
+                       placed ? reinterpret_cast<uint32_t*>(ws + w.local.ids) : nullptr, k, E,
+                       static_cast<int>(tokens), slots, static_cast<int>(H), y, s);
     stage(5, s);
     return r;
 }

@@ -105,19 +105,24 @@ hmoe_status validate_desc(const hmoe_layer_desc* d) {
 // order is expert order) and accumulate in that order from zero, as the
 // reference's combine loop does (MoERuntime.cpp:311-325).
 __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ yrows,
-                                                      const int32_t* __restrict__ inv, int slots,
+                                                      const int32_t* __restrict__ inv,
+                                                      const uint32_t* __restrict__ ids, int k, int E, int slots,
                                                       int H, float* __restrict__ out) {
     __shared__ int rows_s[kMaxSlots];
     const int t = blockIdx.x;
     if (threadIdx.x == 0) {
+        int keys[kMaxSlots];
         int n = 0;
         for (int s = 0; s < slots; ++s) {
             const int r = inv[static_cast<size_t>(t) * slots + s];
+            const int key = ids ? (s < k ? static_cast<int>(ids[static_cast<size_t>(t) * k + s]) : E + (s - k)) : r;
             int j = n++;
-            while (j > 0 && rows_s[j - 1] > r) {
+            while (j > 0 && keys[j - 1] > key) {
+                keys[j] = keys[j - 1];
                 rows_s[j] = rows_s[j - 1];
                 --j;
             }
+            keys[j] = key;
             rows_s[j] = r;
         }
     }
@@ -140,10 +145,10 @@ __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __res
     }
 }
 
-hmoe_status launch_combine(const __nv_bfloat16* yrows, const int32_t* inv, int tokens, int slots, int H,
-                           float* out, cudaStream_t s) {
+hmoe_status launch_combine(const __nv_bfloat16* yrows, const int32_t* inv, const uint32_t* ids, int k, int E,
+                           int tokens, int slots, int H, float* out, cudaStream_t s) {
     if (tokens <= 0) return HMOE_OK;
-    combine_kernel<<<static_cast<unsigned>(tokens), 256, 0, s>>>(yrows, inv, slots, H, out);
+    combine_kernel<<<static_cast<unsigned>(tokens), 256, 0, s>>>(yrows, inv, ids, k, E, slots, H, out);
     return check_launch("hmoe combine kernel");
 }
 
@@ -151,7 +156,7 @@ hmoe_status launch_combine(const __nv_bfloat16* yrows, const int32_t* inv, int t
 
 // Router, histogram, grouping and the BF16 row permutation of one batch.
 hmoe_status enqueue_route(const hmoe_layer_desc& d, const float* x, size_t T, char* ws, const Workspace& w,
-                          bool permute, cudaStream_t s) {
+                          bool permute, cudaStream_t s, const int32_t* expert_of_slot, int32_t* slot_counts) {
     cudaError_t err = cudaMemsetAsync(ws, 0, w.zero_bytes, s);
     if (err != cudaSuccess) {
         set_last_error("hmoe workspace reset", err);
@@ -170,7 +175,8 @@ hmoe_status enqueue_route(const hmoe_layer_desc& d, const float* x, size_t T, ch
                      reinterpret_cast<int32_t*>(ws + w.counts), static_cast<int>(T), static_cast<int>(d.top_k),
                      static_cast<int>(d.experts), static_cast<int>(d.shared_experts),
                      reinterpret_cast<int32_t*>(ws + w.offsets), reinterpret_cast<uint32_t*>(ws + w.perm_token),
-                     reinterpret_cast<float*>(ws + w.perm_weight), reinterpret_cast<int32_t*>(ws + w.inv), s);
+                     reinterpret_cast<float*>(ws + w.perm_weight), reinterpret_cast<int32_t*>(ws + w.inv),
+                     expert_of_slot, slot_counts, s);
     if (r != HMOE_OK || !permute) return r;
     return launch_permute(x, reinterpret_cast<int32_t*>(ws + w.inv), static_cast<int>(T),
                           static_cast<int>(d.top_k + d.shared_experts), static_cast<int>(d.hidden),
@@ -311,8 +317,8 @@ hmoe_status hmoe_moe_forward(const hmoe_layer_desc* desc, const float* x, float*
     stage(2, s);
     r = run_experts(run, use_gemv(static_cast<long>(tokens) * slots, run.H, run.I), true, s);
     if (r != HMOE_OK) return r;
-    r = launch_combine(run.yrows, reinterpret_cast<int32_t*>(ws + w.inv), static_cast<int>(tokens), slots,
-                       static_cast<int>(desc->hidden), y, s);
+    r = launch_combine(run.yrows, reinterpret_cast<int32_t*>(ws + w.inv), nullptr, 0, E, static_cast<int>(tokens),
+                       slots, static_cast<int>(desc->hidden), y, s);
     stage(5, s);
     return r;
 }

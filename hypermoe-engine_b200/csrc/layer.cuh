@@ -108,16 +108,23 @@ int tile_capacity_for(long rows, int segments);
 hmoe_status launch_route(const float* x, const float* w, const float* bias, int T, int H, int E, int k,
                          int softmax, int renorm, uint32_t* ids, float* scores, int32_t* counts,
                          DeviceStatus* st, cudaStream_t stream);
+// Expert groups in ascending expert id, or in placement-slot order when
+// expert_of_slot is given (then slot_counts[b] = rows of slot b).
 hmoe_status launch_group(const uint32_t* ids, const float* scores, const int32_t* counts, int T, int k,
                          int E, int S, int32_t* offsets, uint32_t* perm_token, float* perm_weight,
-                         int32_t* inv, cudaStream_t stream);
-hmoe_status launch_combine(const __nv_bfloat16* yrows, const int32_t* inv, int tokens, int slots, int H,
-                           float* out, cudaStream_t stream);
+                         int32_t* inv, const int32_t* expert_of_slot, int32_t* slot_counts,
+                         cudaStream_t stream);
+// out[t] = sum of the token's rows in ascending expert id: routed slot j has
+// expert ids[t, j] (when ids is null the row order is the expert order),
+// shared expert s counts as expert E + s.
+hmoe_status launch_combine(const __nv_bfloat16* yrows, const int32_t* inv, const uint32_t* ids, int k, int E,
+                           int tokens, int slots, int H, float* out, cudaStream_t stream);
 
 // Layer driver pieces shared by the single-GPU and expert-parallel paths.
 hmoe_status validate_layer(const hmoe_layer_desc* d);
 hmoe_status enqueue_route(const hmoe_layer_desc& d, const float* x, size_t T, char* ws, const Workspace& w,
-                          bool permute, cudaStream_t s);
+                          bool permute, cudaStream_t s, const int32_t* expert_of_slot = nullptr,
+                          int32_t* slot_counts = nullptr);
 ExpertRun local_run(const hmoe_layer_desc& d, size_t T, char* ws, const Workspace& w);
 // gate/up then down of every tile of `r`; `stages` records stage events 3, 4.
 hmoe_status run_experts(const ExpertRun& r, bool gemv, bool stages, cudaStream_t s);

@@ -607,10 +607,17 @@ struct GroupArgs {
     uint32_t* perm_token;  // [T*(k+S)] token of each permuted row
     float* perm_weight;    // [T*(k+S)] routing weight of each row
     int32_t* inv;          // [T*(k+S)] row of (token, slot); slots k.. = shared
+    const int32_t* expert_of_slot; // [E] placement (group b holds that expert), or null
+    int32_t* slot_counts;  // [E] routed rows per placement slot (with a placement)
 };
 
-__device__ __forceinline__ int group_count(const GroupArgs& g, int e) {
-    return e < g.E ? g.counts[e] : g.T;
+// Expert held by group b (routed groups follow the placement when given).
+__device__ __forceinline__ int group_expert(const GroupArgs& g, int b) {
+    return (b < g.E && g.expert_of_slot) ? g.expert_of_slot[b] : b;
+}
+
+__device__ __forceinline__ int group_count(const GroupArgs& g, int b) {
+    return b < g.E ? g.counts[group_expert(g, b)] : g.T;
 }
 
 // One CTA per expert (routed then shared).  Tokens are placed in ascending
@@ -620,11 +627,12 @@ __global__ void __launch_bounds__(256) group_kernel(GroupArgs g) {
     __shared__ int red[8];
     __shared__ int warp_hits[8];
     __shared__ int base_s;
-    const int e = blockIdx.x;
+    const int b = blockIdx.x;          // group (placement slot for routed experts)
+    const int e = group_expert(g, b);  // expert of the group
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // Offset of expert e from the counts of e' < e.
+    // Offset of group b from the counts of the groups before it.
     int off = 0;
-    for (int j = tid; j < e; j += blockDim.x) off += group_count(g, j);
+    for (int j = tid; j < b; j += blockDim.x) off += group_count(g, j);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) off += __shfl_xor_sync(0xffffffffu, off, o);
     if (lane == 0) red[warp] = off;
@@ -632,15 +640,16 @@ __global__ void __launch_bounds__(256) group_kernel(GroupArgs g) {
     if (tid == 0) {
         int o = 0;
         for (int w = 0; w < 8; ++w) o += red[w];
-        g.offsets[e] = o;
-        if (e == g.E + g.S - 1) g.offsets[e + 1] = o + group_count(g, e);
+        g.offsets[b] = o;
+        if (b == g.E + g.S - 1) g.offsets[b + 1] = o + group_count(g, b);
+        if (g.slot_counts && b < g.E) g.slot_counts[b] = group_count(g, b);
         base_s = o;
     }
     __syncthreads();
     int base = base_s;
     const int slots = g.k + g.S;
-    if (e >= g.E) {
-        const int s = e - g.E;
+    if (b >= g.E) {
+        const int s = b - g.E;
         for (int t = tid; t < g.T; t += blockDim.x) {
             const int row = base + t;
             g.perm_token[row] = static_cast<uint32_t>(t);
@@ -742,8 +751,10 @@ hmoe_status launch_route(const float* x, const float* w, const float* bias,
 
 hmoe_status launch_group(const uint32_t* ids, const float* scores, const int32_t* counts, int T, int k,
                          int E, int S, int32_t* offsets, uint32_t* perm_token, float* perm_weight,
-                         int32_t* inv, cudaStream_t stream) {
-    GroupArgs g{ids, scores, counts, T, k, E, S, offsets, perm_token, perm_weight, inv};
+                         int32_t* inv, const int32_t* expert_of_slot, int32_t* slot_counts,
+                         cudaStream_t stream) {
+    GroupArgs g{ids, scores, counts, T, k, E, S, offsets, perm_token, perm_weight, inv, expert_of_slot,
+                slot_counts};
     group_kernel<<<E + S, 256, 0, stream>>>(g);
     return check_launch("hmoe group kernel");
 }

@@ -40,7 +40,8 @@ EXPORTS = [
     "hmoe_set_stage_events", "hmoe_launch_count", "hmoe_moe_forward_host",
     "hmoe_ep_expert_range", "hmoe_ep_plan", "hmoe_ep_unique_id", "hmoe_ep_comm_create",
     "hmoe_ep_comm_destroy", "hmoe_ep_workspace_size", "hmoe_ep_moe_forward", "hmoe_ep_last_plan",
-    "hmoe_moe_forward_noalloc", "hmoe_selftest_bounded_wait",
+    "hmoe_moe_forward_noalloc", "hmoe_selftest_bounded_wait", "hmoe_ep_set_placement",
+    "hmoe_ep_balanced_placement",
 ]
 EP_MAX_RANKS = 64
 EP_UNIQUE_ID_BYTES = 128
@@ -126,6 +127,8 @@ def lib() -> ctypes.CDLL:
             "hmoe_ep_last_plan": [vp, ctypes.POINTER(EpPlan)],
             "hmoe_moe_forward_noalloc": [ctypes.POINTER(LayerDesc), vp, vp, sz, vp],
             "hmoe_selftest_bounded_wait": [vp, ctypes.c_uint32, vp],
+            "hmoe_ep_set_placement": [vp, vp, ctypes.c_uint32],
+            "hmoe_ep_balanced_placement": [vp, ctypes.c_uint32, i32, vp],
         }
         for name, args in sigs.items():
             fn = getattr(L, name)
@@ -373,13 +376,27 @@ def ep_unique_id() -> bytes:
     return buf.raw
 
 
-def local_host_layer(host: HostLayer, ep_size: int, ep_rank: int) -> HostLayer:
-    """The slice of `host` that rank `ep_rank` holds: its routed experts
-    followed by every shared expert (router replicated)."""
+def ep_balanced_placement(load, ep_size: int) -> np.ndarray:
+    """slot_of_expert balancing the expected per-expert `load` over ranks."""
+    load = np.ascontiguousarray(load, dtype=np.float64)
+    out = np.zeros(load.size, dtype=np.int32)
+    check("hmoe_ep_balanced_placement", lib().hmoe_ep_balanced_placement(load.ctypes.data, load.size, ep_size,
+                                                                         out.ctypes.data))
+    return out
+
+
+def local_host_layer(host: HostLayer, ep_size: int, ep_rank: int, slot_of_expert=None) -> HostLayer:
+    """The slice of `host` that rank `ep_rank` holds: its routed experts (in
+    placement-slot order) followed by every shared expert (router replicated)."""
     cfg = host.cfg
     E, S, stride = cfg.experts, cfg.shared_experts, cfg.expert_stride
     f, n = ep_expert_range(E, ep_size, ep_rank)
-    ids = list(range(f, f + n)) + list(range(E, E + S))
+    if slot_of_expert is None:
+        routed = list(range(f, f + n))
+    else:
+        expert_of_slot = np.argsort(np.asarray(slot_of_expert))
+        routed = [int(e) for e in expert_of_slot[f:f + n]]
+    ids = routed + list(range(E, E + S))
     arena = np.concatenate([host.arena[e * stride:(e + 1) * stride] for e in ids])
     qsz = ctypes.sizeof(ExpertQuant)
     quant = np.concatenate([host.quant[e * qsz:(e + 1) * qsz] for e in ids])
@@ -397,6 +414,13 @@ class EpComm:
         self.handle = h
         self.rank, self.size = rank, size
 
+    def set_placement(self, slot_of_expert) -> None:
+        if slot_of_expert is None:
+            check("hmoe_ep_set_placement", lib().hmoe_ep_set_placement(self.handle, None, 0))
+            return
+        arr = np.ascontiguousarray(slot_of_expert, dtype=np.int32)
+        check("hmoe_ep_set_placement", lib().hmoe_ep_set_placement(self.handle, arr.ctypes.data, arr.size))
+
     def last_plan(self) -> EpPlan:
         plan = EpPlan()
         check("hmoe_ep_last_plan", lib().hmoe_ep_last_plan(self.handle, ctypes.byref(plan)))
@@ -411,8 +435,9 @@ class EpComm:
 class EpLayer(DeviceLayer):
     """This rank's share of an expert-parallel layer on the current device."""
 
-    def __init__(self, host: HostLayer, comm: EpComm, device="cuda"):
-        super().__init__(local_host_layer(host, comm.size, comm.rank), device)
+    def __init__(self, host: HostLayer, comm: EpComm, device="cuda", slot_of_expert=None):
+        super().__init__(local_host_layer(host, comm.size, comm.rank, slot_of_expert), device)
+        comm.set_placement(slot_of_expert)
         self.full_host = host
         self.comm = comm
         self.desc.ep_rank, self.desc.ep_size = comm.rank, comm.size

@@ -300,6 +300,24 @@ hmoe_status hmoe_ep_comm_create(const void *unique_id, int32_t rank,
                                 hmoe_ep_comm **comm);
 hmoe_status hmoe_ep_comm_destroy(hmoe_ep_comm *comm);
 
+/* Expert placement of the communicator (all ranks must set the same one):
+ * slot_of_expert[e] is a permutation of [0, experts); rank r owns the slots
+ * hmoe_ep_expert_range returns, so its arena holds the experts whose slot
+ * is in that range, in slot order, followed by the shared experts.
+ * NULL / 0 restores the identity (contiguous expert ids).  Results do not
+ * depend on the placement: rows are combined in ascending expert id.
+ * Set-up call (allocates a small device table). */
+hmoe_status hmoe_ep_set_placement(hmoe_ep_comm *comm,
+                                  const int32_t *slot_of_expert,
+                                  uint32_t experts);
+
+/* Static load balancing of experts over ep_size ranks from an expected load
+ * per expert (e.g. a routing-frequency profile): largest load first, each to
+ * the least-loaded rank with a free slot.  Host only. */
+hmoe_status hmoe_ep_balanced_placement(const double *load, uint32_t experts,
+                                       int32_t ep_size,
+                                       int32_t *slot_of_expert);
+
 /* The transfer plan of the communicator's last hmoe_ep_moe_forward
  * (observability: received rows, per-peer transfer sizes). */
 hmoe_status hmoe_ep_last_plan(const hmoe_ep_comm *comm, hmoe_ep_plan_t *plan);

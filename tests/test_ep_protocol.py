@@ -36,7 +36,7 @@ def _expert(hl, e):
             blob[2 * HI:].reshape(c.intermediate, c.hidden), hl.scales[e], hl.zps[e])
 
 
-def _rank_main(rank, P, port, cfg_args, Ts, seed, q):
+def _rank_main(rank, P, port, cfg_args, Ts, seed, q, placement=None):
     for p in PATHS:
         sys.path.insert(0, p)
     import torch
@@ -51,7 +51,10 @@ def _rank_main(rank, P, port, cfg_args, Ts, seed, q):
     try:
         cfg = H.LayerConfig(*cfg_args)
         hl = H.make_host_layer(cfg, seed=seed, threads=1)
-        local = H.local_host_layer(hl, P, rank)
+        local = H.local_host_layer(hl, P, rank, placement)
+        # slot order of the expert groups (identity without a placement)
+        expert_of_slot = (np.argsort(np.asarray(placement)) if placement is not None
+                          else np.arange(cfg.experts))
         E, S, k, Hd = cfg.experts, cfg.shared_experts, cfg.top_k, cfg.hidden
         x_all = H.make_tokens(cfg, sum(Ts), seed=seed, threads=1)
         t0 = sum(Ts[:rank])
@@ -62,7 +65,7 @@ def _rank_main(rank, P, port, cfg_args, Ts, seed, q):
             ids, sc, off, gt, gs = O.route(L, x, hl.router_w, hl.router_bias, k, cfg.softmax, cfg.renormalize)
         else:
             off, gt, gs = np.zeros(E + 1, np.int32), np.zeros(0, np.uint32), np.zeros(0, np.float32)
-        counts = torch.from_numpy(np.diff(off).astype(np.int32))
+        counts = torch.from_numpy(np.diff(off).astype(np.int32)[expert_of_slot].copy())
         gathered = [torch.empty_like(counts) for _ in range(P)]
         dist.all_gather(gathered, counts)
         counts_all = np.stack([g.numpy() for g in gathered])
@@ -70,7 +73,11 @@ def _rank_main(rank, P, port, cfg_args, Ts, seed, q):
         plan = H.ep_plan(counts_all, k, rank, max_tokens)
         assert plan.tokens[rank] == T
 
-        # dispatch: routed rows grouped by expert, tokens ascending
+        # dispatch: routed rows grouped by slot, tokens ascending inside a group
+        order = (np.concatenate([np.arange(off[e], off[e + 1]) for e in expert_of_slot]).astype(np.int64)
+                 if T else np.zeros(0, np.int64))
+        gt, gs = gt[order], gs[order]
+        row_expert = np.concatenate([np.full(off[e + 1] - off[e], e) for e in expert_of_slot]) if T else order
         xrows = x[gt.astype(np.int64)] if T else np.zeros((0, Hd), np.float32)
         wrows = gs.astype(np.float32)
         xin = np.zeros((plan.recv_total, Hd), np.float32)
@@ -112,9 +119,9 @@ def _rank_main(rank, P, port, cfg_args, Ts, seed, q):
         yrows = np.zeros_like(xrows)
         exchange([yin[ro[p]:ro[p] + rr[p]] for p in range(P)], [yrows[so[p]:so[p] + sr[p]] for p in range(P)])
 
-        # combine: ascending expert id (row order), then shared experts
+        # combine: ascending expert id per token, then shared experts
         out = np.zeros((T, Hd), np.float32)
-        for r in range(len(gt)):
+        for r in np.lexsort((np.arange(len(gt)), row_expert)) if T else []:
             out[gt[r]] += yrows[r]
         for s in range(S):
             if T:
@@ -127,12 +134,12 @@ def _rank_main(rank, P, port, cfg_args, Ts, seed, q):
         dist.destroy_process_group()
 
 
-def _run(P, cfg_args, Ts, seed=0):
+def _run(P, cfg_args, Ts, seed=0, placement=None):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, P, port, cfg_args, Ts, seed, q)) for r in range(P)]
+    procs = [ctx.Process(target=_rank_main, args=(r, P, port, cfg_args, Ts, seed, q, placement)) for r in range(P)]
     for p in procs:
         p.start()
     results = {}
@@ -158,6 +165,27 @@ def test_ep_protocol_shared_uneven_three_ranks():
     # 7 experts on 3 ranks (3, 2, 2), 2 shared experts, Zipf-biased router,
     # no renormalisation, and a rank with no tokens
     _run(3, (128, 128, 7, 2, True, False, 2, 1.1), (4, 0, 3), seed=1)
+
+
+def test_ep_protocol_with_placement_two_ranks():
+    # a scrambled expert placement: rows travel in slot order, the combine
+    # still adds each token's rows in ascending expert id
+    placement = np.random.default_rng(7).permutation(8).astype(np.int32)
+    _run(2, (256, 512, 8, 2, True, True, 0, None), (6, 4), seed=2, placement=placement)
+
+
+def test_balanced_placement():
+    for p in PATHS:
+        sys.path.insert(0, p)
+    import hmoe_api as H
+    load = np.array([10.0, 1, 1, 1, 5, 5, 1, 1], np.float64)
+    pl = H.ep_balanced_placement(load, 2)
+    assert sorted(pl.tolist()) == list(range(8))
+    per = [load[(pl >= 4 * r) & (pl < 4 * r + 4)].sum() for r in range(2)]
+    assert per == [13.0, 12.0]  # 10+1+1+1 | 5+5+1+1
+    # uneven split (60 experts on 8 ranks: 8,8,8,8,7,7,7,7): every slot used once
+    pl = H.ep_balanced_placement(np.linspace(1, 2, 60), 8)
+    assert sorted(pl.tolist()) == list(range(60))
 
 
 def test_ep_plan_rejections():

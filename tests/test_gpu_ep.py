@@ -39,9 +39,11 @@ def _single_gpu(hl, x, dev, variant):
         H.set_variant(0)
 
 
-@pytest.mark.parametrize("cfg_name,T,variant", [("c3", 256, 0), ("c3", 256, 2), ("c3", 1, 0), ("c2", 33, 2),
-                                                ("c1", 64, 1)])
-def test_ep_one_rank_equals_forward(cuda, cfg_name, T, variant):
+@pytest.mark.parametrize("cfg_name,T,variant,placed", [("c3", 256, 0, False), ("c3", 256, 2, False),
+                                                       ("c3", 1, 0, False), ("c2", 33, 2, False),
+                                                       ("c1", 64, 1, False), ("c3", 256, 2, True),
+                                                       ("c2", 33, 2, True)])
+def test_ep_one_rank_equals_forward(cuda, cfg_name, T, variant, placed):
     import torch
     cfg = H.CONFIGS[cfg_name]
     hl = H.make_host_layer(cfg, seed=3)
@@ -50,7 +52,10 @@ def test_ep_one_rank_equals_forward(cuda, cfg_name, T, variant):
     comm = H.EpComm(H.ep_unique_id(), 0, 1, timeout_ms=30000)
     try:
         H.set_variant(variant)
-        layer = H.EpLayer(hl, comm, cuda)
+        # a scrambled placement: groups travel in slot order, rows still
+        # combine in ascending expert id
+        pl = np.random.default_rng(3).permutation(cfg.experts).astype(np.int32) if placed else None
+        layer = H.EpLayer(hl, comm, cuda, slot_of_expert=pl)
         dx = torch.from_numpy(x).to(cuda)
         y1 = layer.forward(dx, max_tokens=T + 7).cpu().numpy()
         y2 = layer.forward(dx, max_tokens=T + 7).cpu().numpy()
@@ -71,7 +76,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _ep_rank(rank, P, port, cfg_name, Ts, variant, q):
+def _ep_rank(rank, P, port, cfg_name, Ts, variant, q, balanced=False):
     for p in PATHS:
         sys.path.insert(0, p)
     import torch
@@ -94,7 +99,11 @@ def _ep_rank(rank, P, port, cfg_name, Ts, variant, q):
         t0 = sum(Ts[:rank])
         dev = torch.device("cuda", rank)
         H.set_variant(variant)
-        layer = H.EpLayer(hl, comm, dev)
+        pl = None
+        if balanced:  # placement from the router's popularity prior
+            load = np.exp(hl.router_bias.astype(np.float64)) if hl.router_bias is not None else np.ones(cfg.experts)
+            pl = H.ep_balanced_placement(load, P)
+        layer = H.EpLayer(hl, comm, dev, slot_of_expert=pl)
         dx = torch.from_numpy(x_all[t0:t0 + Ts[rank]]).to(dev)
         y = layer.forward(dx, max_tokens=max(Ts)).cpu().numpy()
         st, ties, _ = layer.read_status()
@@ -107,8 +116,9 @@ def _ep_rank(rank, P, port, cfg_name, Ts, variant, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("cfg_name,Ts,variant", [("c3", (300, 212), 2), ("c2", (40, 0), 2), ("c3", (3, 1), 0)])
-def test_ep_two_gpus_equal_single_gpu(cuda, cfg_name, Ts, variant):
+@pytest.mark.parametrize("cfg_name,Ts,variant,balanced", [("c3", (300, 212), 2, False), ("c2", (40, 0), 2, False),
+                                                          ("c3", (3, 1), 0, False), ("c3", (300, 212), 2, True)])
+def test_ep_two_gpus_equal_single_gpu(cuda, cfg_name, Ts, variant, balanced):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -120,7 +130,7 @@ def test_ep_two_gpus_equal_single_gpu(cuda, cfg_name, Ts, variant):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ep_rank, args=(r, 2, port, cfg_name, Ts, variant, q)) for r in range(2)]
+    procs = [ctx.Process(target=_ep_rank, args=(r, 2, port, cfg_name, Ts, variant, q, balanced)) for r in range(2)]
     for p in procs:
         p.start()
     out = {}
