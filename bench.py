@@ -56,6 +56,7 @@ def parse():
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--impl", default="hmoe", choices=["hmoe", "reference"])
     p.add_argument("--variant", type=int, default=0, help="0 auto, 1 GEMV only, 2 GEMM only")
+    p.add_argument("--route-variant", type=int, default=0, help="0 auto, 1 cluster router, 2 tiled router")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
@@ -262,6 +263,7 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=dev)
     H.set_variant(args.variant)
+    H.set_route_variant(args.route_variant)
     host_layer = H.make_host_layer(cfg, seed=args.seed)
     x_np = H.make_tokens(cfg, T, seed=args.seed + 7919 * rank)
     if world > 1:

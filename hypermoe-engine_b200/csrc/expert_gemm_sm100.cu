@@ -685,6 +685,21 @@ hmoe_status launch_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUte
 
 } // namespace
 
+// FP32 row-major matrix [rows][cols] (cols contiguous, cols % 4 == 0), box
+// [box_rows][box_cols] with box_cols * 4 == 128 bytes, 128-byte swizzle;
+// elements outside the matrix read as zero.
+bool map_f32_rows_sw128(CUtensorMap* m, const float* base, uint64_t cols, uint64_t rows, uint32_t box_cols,
+                        uint32_t box_rows) {
+    if (!encode_fn()) return false;
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols) * 4};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t es[2] = {1, 1};
+    return encode_fn()(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // INT8 weights of one projection across all experts, dims {N, K, experts}
 // (the packed [in,out] layout, N contiguous), box [box_k][box_n], no swizzle.
 bool map_weights_box(CUtensorMap* m, const int8_t* base, int N, int K, int experts, uint64_t stride, int box_n,

@@ -90,6 +90,10 @@ int device_sm_count();
 // box [box_k][box_n] (no swizzle).  False when the driver rejects it.
 bool map_weights_box(CUtensorMap* m, const int8_t* base, int N, int K, int experts, uint64_t stride, int box_n,
                      int box_k);
+// TMA map of an FP32 row-major matrix [rows][cols] (cols % 4 == 0): box
+// [box_rows][box_cols] of 128-byte rows, 128-byte swizzle, zero fill outside.
+bool map_f32_rows_sw128(CUtensorMap* m, const float* base, uint64_t cols, uint64_t rows, uint32_t box_cols,
+                        uint32_t box_rows);
 hmoe_status gemm_gate_up(const ExpertRun& r, cudaStream_t stream);
 hmoe_status gemm_down(const ExpertRun& r, cudaStream_t stream);
 hmoe_status gemv_gate_up(const ExpertRun& r, cudaStream_t stream);

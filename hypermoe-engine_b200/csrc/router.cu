@@ -28,6 +28,7 @@
 //    float(double(e)/D), selection (score desc, id asc), renormalisation by
 //    a double sum in rank order -- all as in the reference.
 #include "common.cuh"
+#include "layer.cuh"
 #include "sm100.cuh"
 
 #include <cooperative_groups.h>
@@ -149,7 +150,8 @@ __device__ void select_token(const float (&lv)[C], int E, int k, int softmax,
     unsigned selected = 0; // bit c: candidate c of this lane taken
     double rsum = 0.0;
     float prev_p = 0.0f, prev_l = 0.0f;
-    float chosen[kMaxTopK];
+    float mine = 0.0f; // lane r < k: the rank-r probability and expert
+    int myid = 0;
     bool tie = false;
     const int rounds = k < E ? k + 1 : k; // one extra to see rank k
     for (int r = 0; r < rounds; ++r) {
@@ -164,16 +166,20 @@ __device__ void select_token(const float (&lv)[C], int E, int k, int softmax,
                 bl = lv[c];
             }
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float op = __shfl_xor_sync(0xffffffffu, bp, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            const float ol = __shfl_xor_sync(0xffffffffu, bl, o);
-            if (better(op, oi, bp, bi)) {
-                bp = op;
-                bi = oi;
-                bl = ol;
-            }
+        // Warp argmax in the order of better(): the largest value of an
+        // order-preserving key (-0.0 keyed as +0.0, which compare equal),
+        // then the smallest index among the lanes holding it; the owner of
+        // that index holds it as its own best candidate.
+        {
+            uint32_t key = __float_as_uint(bp + 0.0f);
+            key = (key & 0x80000000u) ? ~key : (key | 0x80000000u);
+            const uint32_t kmax = __reduce_max_sync(0xffffffffu, key);
+            const uint32_t imin =
+                __reduce_min_sync(0xffffffffu, key == kmax ? static_cast<uint32_t>(bi) : 0xffffffffu);
+            const int owner = static_cast<int>(imin & 31u);
+            bp = __shfl_sync(0xffffffffu, bp, owner);
+            bl = __shfl_sync(0xffffffffu, bl, owner);
+            bi = static_cast<int>(imin);
         }
         if (r > 0 && softmax && bl != prev_l) {
             const int d = abs(__float_as_int(prev_p) - __float_as_int(bp));
@@ -187,27 +193,26 @@ __device__ void select_token(const float (&lv)[C], int E, int k, int softmax,
             ok = false;
         }
         if ((bi & 31) == lane) selected |= 1u << (bi >> 5);
-        chosen[r] = bp;
-        rsum += static_cast<double>(bp);
-        if (lane == 0) {
-            ids_out[r] = static_cast<uint32_t>(bi);
-            if (counts) atomicAdd(counts + bi, 1);
+        if (lane == r) {
+            mine = bp;
+            myid = bi;
         }
+        rsum += static_cast<double>(bp); // rank order, as the reference
+    }
+    // Lane r writes rank r: the renormalised score (a double division, as
+    // the reference) or, for a token flagged non-finite, the raw scores with
+    // NaN in slot 0 (CudaKernels.cu:201-202).
+    if (renorm && !(isfinite(rsum) && rsum != 0.0)) ok = false;
+    ok = __all_sync(0xffffffffu, ok);
+    if (lane < k) {
+        float sc = mine;
+        if (renorm && ok) sc = static_cast<float>(static_cast<double>(mine) / rsum);
+        if (!ok && lane == 0) sc = __int_as_float(0x7fc00000);
+        ids_out[lane] = static_cast<uint32_t>(myid);
+        scores_out[lane] = sc;
+        if (counts) atomicAdd(counts + myid, 1);
     }
     if (lane == 0) {
-        if (renorm) {
-            if (!(isfinite(rsum) && rsum != 0.0)) ok = false;
-            if (ok) {
-                for (int r = 0; r < k; ++r)
-                    scores_out[r] = static_cast<float>(static_cast<double>(chosen[r]) / rsum);
-            } else {
-                for (int r = 0; r < k; ++r) scores_out[r] = chosen[r];
-                scores_out[0] = __int_as_float(0x7fc00000); // NaN, CudaKernels.cu:201-202
-            }
-        } else {
-            for (int r = 0; r < k; ++r) scores_out[r] = chosen[r];
-            if (!ok) scores_out[0] = __int_as_float(0x7fc00000);
-        }
         if (!ok) device_fail(st, HMOE_NON_FINITE_ROUTER);
         if (tie && st) atomicAdd(&st->near_ties, 1);
     }
@@ -266,6 +271,164 @@ __device__ double sequential_logit(const RouteArgs& a, int tok, int e) {
     return s;
 }
 
+// The same sequential sum by a whole warp (result on every lane): each lane
+// forms one exact product per 32-row chunk, the products are loaded four
+// chunks ahead, and the dependent double additions run in row order through
+// shuffles.
+__device__ double warp_sequential_logit(const RouteArgs& a, int tok, int e) {
+    const int lane = threadIdx.x & 31;
+    const int H = a.H, E = a.E;
+    const float* xr = a.x + static_cast<size_t>(tok) * H;
+    auto prod_at = [&](int c) {
+        const int i = c * 32 + lane;
+        // products of two floats are exact in double; rows past H add +0.0
+        return i < H ? static_cast<double>(xr[i]) * static_cast<double>(a.w[static_cast<size_t>(i) * E + e]) : 0.0;
+    };
+    const int nch = (H + 31) / 32;
+    double q[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) q[u] = prod_at(u);
+    double s = 0.0;
+    for (int c = 0; c < nch; c += 4) {
+        double nq[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) nq[u] = c + 4 + u < nch ? prod_at(c + 4 + u) : 0.0;
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int jj = 0; jj < 32; ++jj) s += __shfl_sync(0xffffffffu, q[u], jj);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) q[u] = nq[u];
+    }
+    if (a.bias) s += static_cast<double>(a.bias[e]);
+    return s;
+}
+
+__device__ __forceinline__ void two_sum(double a, double b, double& s, double& err) {
+    s = a + b;
+    const double bb = s - a;
+    err = (a - (s - bb)) + (b - bb);
+}
+
+// Shared-memory doubles a warp needs to stage the H products of one logit.
+__host__ __device__ constexpr int staged_logit_doubles(int H) { return H + 32; }
+
+// The H exact products x_i * W_ie of one logit, staged by the whole warp in
+// 32 segments of H/32 rows: row i at buf[i + i/(H/32)] (one pad per
+// segment, so the lanes' segment walks below hit distinct banks).
+// Needs H % 32 == 0.
+__device__ void stage_products(const RouteArgs& a, int tok, int e, double* buf) {
+    const int lane = threadIdx.x & 31;
+    const int H = a.H, E = a.E, seg = H / 32;
+    const float* xr = a.x + static_cast<size_t>(tok) * H;
+#pragma unroll 8
+    for (int i = lane; i < H; i += 32)
+        buf[i + i / seg] = static_cast<double>(xr[i]) * static_cast<double>(a.w[static_cast<size_t>(i) * E + e]);
+    __syncwarp();
+}
+
+// Second-level certificate of one logit from its staged products, by a
+// whole warp (result on every lane), tried before the sequential
+// recomputation.  The reference's sum s_H = fl(...fl(p_1 + p_2)... + p_H)
+// differs from the exact sum S_H by at most u/(1-u) * sum_i |s_i| <=
+// u/(1-u) * sum_i |S_i| + H^2 u^2 P (S_i the exact partial sums,
+// P = sum |p_i|, u = 2^-53).  The partial sums of a random-signed sum grow
+// like sqrt(i), so this is far tighter than the (H-1) u P of the first
+// certificate.  Lane l walks segment l; S_i comes from compensated (TwoSum)
+// sums and a warp scan.  Returns whether the float logit (bias added last,
+// as the reference does) is settled, and sets *out to it.
+__device__ bool refined_logit(const RouteArgs& a, int e, const double* buf, float* out) {
+    const int lane = threadIdx.x & 31;
+    const int H = a.H, seg = H / 32;
+    const double* sb = buf + lane * (seg + 1);
+    double hi = 0.0, lo = 0.0, pabs = 0.0;
+    for (int i = 0; i < seg; ++i) {
+        const double p = sb[i];
+        double err;
+        two_sum(hi, p, hi, err);
+        lo += err;
+        pabs += fabs(p);
+    }
+    // inclusive scan of the segment sums over the lanes (double-double)
+    double ih = hi, il = lo;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double oh = __shfl_up_sync(0xffffffffu, ih, o), ol = __shfl_up_sync(0xffffffffu, il, o);
+        if (lane >= o) {
+            double err;
+            two_sum(oh, ih, ih, err);
+            il = il + ol + err;
+        }
+    }
+    double sh = __shfl_up_sync(0xffffffffu, ih, 1), sl = __shfl_up_sync(0xffffffffu, il, 1);
+    if (lane == 0) sh = sl = 0.0;
+    const double th = __shfl_sync(0xffffffffu, ih, 31), tl = __shfl_sync(0xffffffffu, il, 31);
+    // walk the segment again from its prefix: sum of |S_i|
+    double sabs = 0.0;
+    for (int i = 0; i < seg; ++i) {
+        double err;
+        two_sum(sh, sb[i], sh, err);
+        sl += err;
+        sabs += fabs(sh + sl);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        sabs += __shfl_xor_sync(0xffffffffu, sabs, o);
+        pabs += __shfl_xor_sync(0xffffffffu, pabs, o);
+    }
+    const double u = 0x1.0p-53;
+    const double hh = static_cast<double>(H + 64);
+    // |s_H - S_H| (reference) and |t - S_H| (this compensated sum), with
+    // generous slack for the roundings of the bound itself.
+    const double beta_ref = sabs * u * (1.0 + 0x1.0p-30) + 8.0 * hh * hh * u * u * pabs;
+    const double b = a.bias ? static_cast<double>(a.bias[e]) : 0.0;
+    const double z = th + (tl + b);
+    const double beta = beta_ref * (1.0 + 4.0 * u) + 8.0 * u * (fabs(z) + fabs(b) + fabs(tl) + beta_ref) +
+                        8.0 * hh * hh * u * u * pabs + 0x1.0p-1060;
+    *out = static_cast<float>(z);
+    return isfinite(z) && rounding_certified(z, beta);
+}
+
+// The reference's sequential sum over the staged products: lane 0 runs the
+// dependent additions in row order (result on lane 0).
+__device__ double staged_sequential_logit(const RouteArgs& a, int e, const double* buf) {
+    const int lane = threadIdx.x & 31;
+    const int H = a.H, seg = H / 32;
+    double s = 0.0;
+    if (lane == 0) {
+        for (int l = 0; l < 32; ++l) {
+            const double* sb = buf + l * (seg + 1);
+#pragma unroll 8
+            for (int i = 0; i < seg; ++i) s += sb[i];
+        }
+        if (a.bias) s += static_cast<double>(a.bias[e]);
+    }
+    __syncwarp(); // buf is reused by this warp's next logit
+    return s;
+}
+
+// One queued logit by a whole warp: the second-level certificate over the
+// staged products, else the sequential sum (staged when a buffer is given,
+// otherwise from global memory).  Result on lane 0; counts the sequential
+// recomputations.
+__device__ float settle_logit(const RouteArgs& a, int tok, int e, double* buf) {
+    const int lane = threadIdx.x & 31;
+    if (buf && a.H % 32 == 0) {
+        stage_products(a, tok, e, buf);
+        float lg;
+        if (refined_logit(a, e, buf, &lg)) {
+            __syncwarp();
+            return lg;
+        }
+        const double s = staged_sequential_logit(a, e, buf);
+        if (lane == 0 && a.st) atomicAdd(&a.st->sequential_logits, 1);
+        return static_cast<float>(s);
+    }
+    const double s = warp_sequential_logit(a, tok, e);
+    if (lane == 0 && a.st) atomicAdd(&a.st->sequential_logits, 1);
+    return static_cast<float>(s);
+}
+
 // Fused router.  Grid (KS, ceil(T/kRouteTokens)), clusters of KS CTAs along
 // x: CTA r of a cluster sums hidden rows [r*H/KS, (r+1)*H/KS) for
 // kRouteTokens tokens and every expert.  Thread (quad = tid % EQ,
@@ -286,6 +449,7 @@ __global__ void __launch_bounds__(256, 2) route_kernel(RouteArgs a, int EQ, int 
     const int E_pad = 4 * EQ;
     const RouteSmem L = route_smem(E, E_pad, P);
     const int SR = L.slab_rows;
+    const int stage_region = L.xf - L.ring; // the slab ring / partials region, free in phase 2b
     float* wsl = reinterpret_cast<float*>(smem + L.ring);                     // [stages][SR][E]
     double* part = reinterpret_cast<double*>(smem + L.ring);                  // [TB][P][E_pad] (after)
     float* xf = reinterpret_cast<float*>(smem + L.xf);                        // [TB][chunk] staging
@@ -522,40 +686,16 @@ __global__ void __launch_bounds__(256, 2) route_kernel(RouteArgs a, int EQ, int 
             logit[t * E_pad + e] = static_cast<float>(s);
         }
         __syncthreads();
-        // Phase 2b: warp-cooperative sequential recomputation.  Each lane
-        // forms one exact product per 32-row chunk; the chunks' products are
-        // loaded four chunks ahead of the dependent double additions.
+        // Phase 2b, a warp per queued logit (settle_logit).  This CTA's
+        // partials are consumed, so their region stages the products.
         const int nfb = min(*fb_count, kRouteFallbacks);
+        const int slots = min(8, stage_region / (8 * staged_logit_doubles(H)));
         for (int f = warp; f < nfb; f += blockDim.x >> 5) {
             const int t = fb_list[f] >> 8, e = fb_list[f] & 255;
-            const float* xr = a.x + static_cast<size_t>(t0 + t) * H;
-            auto prod_at = [&](int c) {
-                const int i = c * 32 + lane;
-                // products of two floats are exact in double; rows past H add +0.0
-                return i < H ? static_cast<double>(xr[i]) * static_cast<double>(a.w[static_cast<size_t>(i) * E + e])
-                             : 0.0;
-            };
-            const int nch = (H + 31) / 32;
-            double q[4];
-#pragma unroll
-            for (int u = 0; u < 4; ++u) q[u] = prod_at(u);
-            double s = 0.0;
-            for (int c = 0; c < nch; c += 4) {
-                double nq[4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) nq[u] = c + 4 + u < nch ? prod_at(c + 4 + u) : 0.0;
-#pragma unroll
-                for (int u = 0; u < 4; ++u)
-#pragma unroll
-                    for (int jj = 0; jj < 32; ++jj) s += __shfl_sync(0xffffffffu, q[u], jj);
-#pragma unroll
-                for (int u = 0; u < 4; ++u) q[u] = nq[u];
-            }
-            if (a.bias) s += static_cast<double>(a.bias[e]);
+            const float lg = settle_logit(a, t0 + t, e, warp < slots ? part + warp * staged_logit_doubles(H) : nullptr);
             if (lane == 0) {
-                if (!isfinite(s)) device_fail(a.st, HMOE_NON_FINITE_ROUTER);
-                logit[t * E_pad + e] = static_cast<float>(s);
-                if (a.st) atomicAdd(&a.st->sequential_logits, 1);
+                if (!isfinite(lg)) device_fail(a.st, HMOE_NON_FINITE_ROUTER);
+                logit[t * E_pad + e] = lg;
             }
         }
         __syncthreads();
@@ -573,6 +713,310 @@ __global__ void __launch_bounds__(256, 2) route_kernel(RouteArgs a, int EQ, int 
         }
     }
     cluster.sync(); // keep every CTA's shared memory alive until rank 0 is done
+}
+
+// ------------------------------------------------------------ tiled router
+//
+// Large batches.  The router is a [T, H] x [H, E] product in FP64.  The
+// per-8-token CTAs of route_kernel re-stream the whole router matrix for
+// every 8 tokens and issue one DFMA per multiply-add with operands from
+// shared memory, which holds them near a third of the FP64 rate.  The tiled
+// kernel runs the products on the FP64 tensor-core path (mma.sync m8n8k4):
+//  * a CTA owns 64 tokens and all (<= 128) experts, split over H across a
+//    cluster of KS CTAs; warp (wm, wn) owns tokens 32wm.. and experts
+//    32wn.. as 4 x 4 tiles of 8 x 8: 16 MMAs per 8 fragment loads;
+//  * 32-row chunks of the FP32 token rows (one [64][32] box) and router
+//    rows (four [32][32] boxes) arrive by TMA with the 128-byte swizzle
+//    through a four-deep ring; the swizzle keeps an A-fragment load at one
+//    shared-memory wavefront and a B-fragment load at two;
+//  * fragments are converted float -> double as they are loaded (exact);
+//  * a ring stage is refilled by the last warp to finish with it (a shared
+//    counter), so the main loop runs no CTA-wide barrier;
+//  * the certificate's norms come from the fragments themselves: ||x_t||^2
+//    from the A fragments of warps 0 and 3, ||W_e||^2 from the B fragments
+//    of warps 1, 2, 5 and 6, each summed in a fixed order.
+// Products of two floats are exact in double and the tensor-core path
+// rounds each accumulation to nearest (IEEE 754), so every output is a
+// summation tree of the exact products with at most H/KS roundings on any
+// chain: the rounding certificate of route_kernel covers it, and the
+// logits, and all that follows from them, are bit-identical to the
+// reference's (uncertified ones are recomputed sequentially).
+constexpr int kRtTokens = 64;
+constexpr int kRtRows = 32;     // hidden rows per chunk (one 128-byte swizzle row)
+constexpr int kRtCols = 128;    // expert columns (E <= 128)
+constexpr int kRtStages = 4;
+constexpr int kRtFallbacks = 64;
+constexpr int kStageW = 4 * kRtRows * 128;       // four [32 rows][32 experts] FP32 boxes
+constexpr int kStageX = kRtTokens * 128;         // one [64 tokens][32 rows] FP32 box
+constexpr int kStageBytes = kStageW + kStageX;     // 24 KB (multiple of 1024)
+
+struct TiledSmem {
+    int ring, xn, wn, xnorm, wnorm, bias, evs, fb, cnt, bars, total;
+};
+
+__host__ __device__ constexpr int tiled_al(int v) { return (v + 15) & ~15; }
+
+// Offsets from the 1024-byte aligned base; `total` includes the alignment slack.
+__host__ __device__ constexpr TiledSmem tiled_smem() {
+    TiledSmem m{};
+    int off = 0;
+    m.ring = off; // [stages][W boxes | x box]; after the main loop [64][128]
+                  // double partials, then [64][128] float logits
+    off = tiled_al(off + kRtStages * kStageBytes);
+    m.xn = off;   // [KS][64/KS] received ||x_t||^2 partials of this rank's tokens
+    off = tiled_al(off + kRtTokens * 8);
+    m.wn = off;   // [KS][128] received ||W_e||^2 partials; [8 warps][128] floats in phase 3
+    off = tiled_al(off + 8 * kRtCols * 8);
+    m.xnorm = off;
+    off = tiled_al(off + kRtTokens * 8);
+    m.wnorm = off;
+    off = tiled_al(off + kRtCols * 8);
+    m.bias = off;
+    off = tiled_al(off + kRtCols * 4);
+    m.evs = m.wn;
+    m.fb = off;
+    off = tiled_al(off + (1 + kRtFallbacks) * 4);
+    m.cnt = off;  // [stages] warps done with the stage's current chunk
+    off = tiled_al(off + kRtStages * 4);
+    m.bars = off; // full[stages]
+    off = tiled_al(off + kRtStages * 8);
+    m.total = off + 1024;
+    return m;
+}
+
+static_assert(kRtTokens * kRtCols * (8 + 4) <= kRtStages * kStageBytes,
+              "tiled router: received partials and logits fit the ring");
+static_assert(8 * kRtCols * 4 <= 8 * kRtCols * 8, "tiled router: softmax scratch fits the W-norm region");
+static_assert(kStageBytes % 1024 == 0, "tiled router: swizzled boxes need 1024-byte alignment");
+static_assert(tiled_smem().total <= 112 * 1024, "tiled router: two CTAs per SM");
+
+__device__ __forceinline__ void dmma_8x8x4(double (&d)[2], double a, double b) {
+    asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0,%1}, {%2}, {%3}, {%0,%1};"
+                 : "+d"(d[0]), "+d"(d[1])
+                 : "d"(a), "d"(b));
+}
+
+// Grid (KS, ceil(T / kRtTokens)), clusters of KS CTAs along x; CTA r sums
+// hidden rows [r*H/KS, (r+1)*H/KS).  mx: token rows [T][H], box [64][32];
+// mw: router rows [H][E], box [32][32].  Needs E <= 128, E % 4 == 0 and
+// H % (32*KS) == 0.
+template <int C>
+__global__ void __launch_bounds__(256, 2) route_tiled_kernel(const __grid_constant__ CUtensorMap mx,
+                                                             const __grid_constant__ CUtensorMap mw,
+                                                             RouteArgs a, int KS) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    unsigned char* smem =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = static_cast<int>(cluster.block_rank());
+    const int H = a.H, E = a.E;
+    constexpr TiledSmem L = tiled_smem();
+    unsigned char* ring = smem + L.ring;
+    double* recv = reinterpret_cast<double*>(ring);                            // [KS][64/KS][128]
+    float* logit = reinterpret_cast<float*>(ring + kRtTokens * kRtCols * 8);   // [64/KS][128]
+    double* xrecv = reinterpret_cast<double*>(smem + L.xn);                    // [KS][64/KS]
+    double* wrecv = reinterpret_cast<double*>(smem + L.wn);                    // [KS][128]
+    double* xnorm = reinterpret_cast<double*>(smem + L.xnorm);
+    double* wnorm = reinterpret_cast<double*>(smem + L.wnorm);
+    float* bias_s = reinterpret_cast<float*>(smem + L.bias);
+    float* evs = reinterpret_cast<float*>(smem + L.evs);
+    int* fb_count = reinterpret_cast<int*>(smem + L.fb);
+    int* fb_list = fb_count + 1;
+    int* cnt = reinterpret_cast<int*>(smem + L.cnt);
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int wm = warp & 1, wn4 = warp >> 1;
+    const int t0 = blockIdx.y * kRtTokens;
+    const int nt = min(kRtTokens, a.T - t0);
+    const int rows = H / KS, h0 = rank * rows;
+    const int nchunk = rows / kRtRows;
+
+    if (tid == 0) {
+        *fb_count = 0;
+        for (int s = 0; s < kRtStages; ++s) {
+            cnt[s] = 0;
+            sm100::mbar_init(&full[s], 1);
+        }
+        sm100::fence_mbarrier_init();
+        sm100::prefetch_tmap(&mx);
+        sm100::prefetch_tmap(&mw);
+    }
+    __syncthreads();
+
+    // Chunk c into stage c % kRtStages (one thread): the token box and the
+    // four router boxes; rows past T and columns past E read as zero.
+    auto issue = [&](int c) {
+        const int s = c % kRtStages;
+        const int r0 = h0 + c * kRtRows;
+        unsigned char* st = ring + s * kStageBytes;
+        sm100::mbar_arrive_expect_tx(&full[s], kStageBytes);
+        for (int cb = 0; cb < 4; ++cb) sm100::tma_load_2d(st + cb * kRtRows * 128, &mw, 32 * cb, r0, &full[s]);
+        sm100::tma_load_2d(st + kStageW, &mx, r0, t0, &full[s]);
+    };
+    if (tid == 0)
+        for (int c = 0; c < kRtStages && c < nchunk; ++c) issue(c);
+
+    double acc[4][4][2];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j][0] = acc[i][j][1] = 0.0;
+    // Norm roles (one warp per token block and per expert block, disjoint):
+    // role 1 (warps 0, 3): ||x||^2 of tokens 32wm + 8i + lane/4 from the A
+    // fragments; role 2 (warps 1, 2, 5, 6): ||W||^2 of experts
+    // 32wn + 8j + lane/4 from the B fragments.
+    const int role = wn4 == wm ? 1 : (wm == 1 - (wn4 & 1) ? 2 : 0);
+    double sq[4] = {0.0, 0.0, 0.0, 0.0};
+    bool failed = false;
+    const int fr = lane & 3, fc = lane >> 2; // fragment row / column within an 8 x 4 or 4 x 8 tile
+
+    for (int c = 0; c < nchunk; ++c) {
+        const int s = c % kRtStages;
+        if (!sm100::mbar_wait_for(&full[s], (c / kRtStages) & 1, 2000000000ull)) failed = true;
+        // Swizzled box rows are 128 bytes; 16-byte chunk q of row r sits at
+        // chunk q ^ (r % 8).  B: row 4kk+fr, column 8j+fc of box wn.  A:
+        // token 32wm+8i+fc (so r % 8 = fc), column 4kk+fr.
+        const unsigned char* wsb = ring + s * kStageBytes + wn4 * (kRtRows * 128) + fr * 128 + (fc & 3) * 4;
+        const unsigned char* xsb = ring + s * kStageBytes + kStageW + (32 * wm + fc) * 128 + fr * 4;
+#pragma unroll 2
+        for (int kk = 0; kk < kRtRows / 4; ++kk) {
+            double av[4], bv[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                av[i] = static_cast<double>(*reinterpret_cast<const float*>(xsb + i * 8 * 128 + ((kk ^ fc) << 4)));
+            const int rsw = (4 * kk + fr) & 7;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                bv[j] = static_cast<double>(
+                    *reinterpret_cast<const float*>(wsb + kk * 4 * 128 + (((2 * j + (fc >> 2)) ^ rsw) << 4)));
+            if (role == 1) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) sq[i] = fma(av[i], av[i], sq[i]);
+            } else if (role == 2) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) sq[j] = fma(bv[j], bv[j], sq[j]);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) dmma_8x8x4(acc[i][j], av[i], bv[j]);
+        }
+        __syncwarp(); // every lane is done with stage s
+        if (lane == 0) {
+            __threadfence_block();
+            if (atomicAdd(&cnt[s], 1) == 7) { // last warp out refills the stage
+                cnt[s] = 0;
+                __threadfence_block();
+                if (c + kRtStages < nchunk) {
+                    sm100::fence_proxy_async_smem();
+                    issue(c + kRtStages);
+                }
+            }
+        }
+    }
+    if (failed) {
+        device_fail(a.st, HMOE_TIMEOUT);
+        for (int s = 0; s < kRtStages && s < nchunk; ++s) // let issued copies land
+            sm100::mbar_wait_for(&full[s], ((nchunk - 1 - s) / kRtStages) & 1, 2000000000ull);
+    }
+    __syncthreads(); // every warp is done with the ring
+
+    // Partials of this CTA go straight to the rank that finishes them: rank
+    // q owns tokens [q*TPR, (q+1)*TPR) of the tile and receives every rank's
+    // sums for them (slot = source rank), the x-norm partials of its tokens
+    // and every rank's W-norm partials.  The norms are first summed over the
+    // four lanes of a fragment column (fixed order).
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        sq[i] += __shfl_xor_sync(0xffffffffu, sq[i], 1);
+        sq[i] += __shfl_xor_sync(0xffffffffu, sq[i], 2);
+    }
+    const int TPR = kRtTokens / KS;
+    cluster.sync(); // every CTA of the cluster is done with its ring
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int tok = 32 * wm + 8 * i + fc;
+        const int q = tok / TPR, lt = tok % TPR;
+        double* dst = cluster.map_shared_rank(recv, q) + (rank * TPR + lt) * kRtCols + 32 * wn4 + 2 * fr;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<double2*>(dst + 8 * j) = make_double2(acc[i][j][0], acc[i][j][1]);
+        if (role == 1 && fr == 0) cluster.map_shared_rank(xrecv, q)[rank * TPR + lt] = sq[i];
+    }
+    if (role == 2 && fr == 0)
+        for (int q = 0; q < KS; ++q) {
+            double* dst = cluster.map_shared_rank(wrecv, q) + rank * kRtCols + 32 * wn4 + fc;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) dst[8 * j] = sq[j];
+        }
+    cluster.sync(); // everything this rank needs is now in its own shared memory
+
+    // Epilogue: this rank finishes tokens [rank*TPR, (rank+1)*TPR) of the tile.
+    const int lt0 = rank * TPR;
+    const int ntr = max(0, min(TPR, nt - lt0));
+    for (int e = tid; e < E; e += blockDim.x) {
+        double w2 = 0.0;
+        for (int q = 0; q < KS; ++q) w2 += wrecv[q * kRtCols + e];
+        wnorm[e] = sqrt(w2 * (1.0 + (H + 64) * 0x1.0p-52));
+        bias_s[e] = a.bias ? a.bias[e] : 0.0f;
+    }
+    if (tid < ntr) {
+        double x2 = 0.0;
+        for (int q = 0; q < KS; ++q) x2 += xrecv[q * TPR + tid];
+        xnorm[tid] = sqrt(x2 * (1.0 + (H + 64) * 0x1.0p-52));
+    }
+    __syncthreads();
+    // Phase 2: float logits certified against the reference's rounding; the
+    // rest are queued for the sequential recomputation (phase 2b).
+    const double gamma = static_cast<double>(H + rows + KS + 8) * 0x1.0p-53 * 1.01;
+    for (int idx = tid; idx < ntr * E; idx += blockDim.x) {
+        const int lt = idx / E, e = idx % E;
+        double sum = 0.0;
+        for (int q = 0; q < KS; ++q) sum += recv[(q * TPR + lt) * kRtCols + e];
+        double A = xnorm[lt] * wnorm[e] * (1.0 + 0x1.0p-40);
+        if (a.bias) {
+            sum += static_cast<double>(bias_s[e]);
+            A += fabs(static_cast<double>(bias_s[e]));
+        }
+        const double beta = gamma * A + 0x1.0p-1060;
+        if (!rounding_certified(sum, beta)) {
+            const int slot = atomicAdd(fb_count, 1);
+            if (slot < kRtFallbacks) fb_list[slot] = lt * 256 + e;
+            else sum = sequential_logit(a, t0 + lt0 + lt, e); // queue full: this thread does it
+        }
+        if (!isfinite(sum)) device_fail(a.st, HMOE_NON_FINITE_ROUTER);
+        logit[lt * kRtCols + e] = static_cast<float>(sum);
+    }
+    __syncthreads();
+    // Phase 2b, a warp per queued logit (settle_logit): the second-level
+    // certificate settles almost all of them; the rest are summed in the
+    // reference's order.  The received partials are consumed, so their
+    // region stages the products.
+    const int nfb = min(*fb_count, kRtFallbacks);
+    const int slots = min(8, (kRtTokens * kRtCols * 8) / (8 * staged_logit_doubles(H)));
+    for (int f = warp; f < nfb; f += blockDim.x >> 5) {
+        const int lt = fb_list[f] >> 8, e = fb_list[f] & 255;
+        const float lg =
+            settle_logit(a, t0 + lt0 + lt, e, warp < slots ? recv + warp * staged_logit_doubles(H) : nullptr);
+        if (lane == 0) {
+            if (!isfinite(lg)) device_fail(a.st, HMOE_NON_FINITE_ROUTER);
+            logit[lt * kRtCols + e] = lg;
+        }
+    }
+    __syncthreads();
+    // Phase 3: softmax, selection, renormalisation; one warp per token.
+    for (int lt = warp; lt < ntr; lt += blockDim.x >> 5) {
+        float lv[C];
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            const int j = lane + 32 * c;
+            lv[c] = j < E ? logit[lt * kRtCols + j] : 0.0f;
+        }
+        const size_t tok = static_cast<size_t>(t0 + lt0 + lt);
+        select_token<C>(lv, E, a.k, a.softmax, a.renorm, evs + warp * kRtCols, a.ids + tok * a.k,
+                        a.scores + tok * a.k, a.counts, a.st, false, nullptr);
+    }
 }
 
 // kernels::routerTopK drop-in (CudaKernels.cu:152-204): one warp per token,
@@ -688,6 +1132,62 @@ __global__ void __launch_bounds__(256) group_kernel(GroupArgs g) {
 // ------------------------------------------------------------ launchers
 
 
+// Router kernel choice: 0 = automatic, 1 = per-8-token cluster kernel,
+// 2 = tiled kernel (hmoe_set_route_variant).
+int g_route_variant = 0;
+constexpr int kTiledMinTokens = 512;
+
+bool tiled_shape_ok(int H, int E) { return E <= kRtCols && E % 4 == 0 && H % kRtRows == 0; }
+
+hmoe_status launch_route_tiled(const RouteArgs& a, cudaStream_t stream) {
+    CUtensorMap mx, mw;
+    if (!map_f32_rows_sw128(&mx, a.x, static_cast<uint64_t>(a.H), static_cast<uint64_t>(a.T), 32, kRtTokens) ||
+        !map_f32_rows_sw128(&mw, a.w, static_cast<uint64_t>(a.E), static_cast<uint64_t>(a.H), 32, kRtRows)) {
+        set_last_error_text("hmoe: cuTensorMapEncodeTiled failed (tiled router)");
+        return HMOE_CUDA_ERROR;
+    }
+    const int tiles = (a.T + kRtTokens - 1) / kRtTokens;
+    int KS = 1; // split H over a cluster until the tiles fill about two CTAs per SM
+    while (KS < 8 && tiles * KS < 250 && a.H % (kRtRows * KS * 2) == 0) KS *= 2;
+    constexpr int smem = tiled_smem().total;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(KS), static_cast<unsigned>(tiles));
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(KS);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t err = cudaErrorInvalidValue;
+#define HMOE_TILED_CASE(CC)                                                                                 \
+    case CC: {                                                                                              \
+        static bool attr_set = false;                                                                       \
+        if (!attr_set) {                                                                                    \
+            cudaFuncSetAttribute(route_tiled_kernel<CC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
+            attr_set = true;                                                                                \
+        }                                                                                                   \
+        err = cudaLaunchKernelEx(&cfg, route_tiled_kernel<CC>, mx, mw, a, KS);                                      \
+        break;                                                                                              \
+    }
+    switch ((a.E + 31) / 32) {
+        HMOE_TILED_CASE(1)
+        HMOE_TILED_CASE(2)
+        HMOE_TILED_CASE(3)
+        HMOE_TILED_CASE(4)
+    default: return HMOE_UNSUPPORTED;
+    }
+#undef HMOE_TILED_CASE
+    if (err != cudaSuccess) {
+        set_last_error("hmoe tiled route kernel launch", err);
+        return HMOE_CUDA_ERROR;
+    }
+    return check_launch("hmoe tiled route kernel");
+}
+
 hmoe_status launch_route(const float* x, const float* w, const float* bias,
                          int T, int H, int E, int k, int softmax, int renorm,
                          uint32_t* ids, float* scores, int32_t* counts,
@@ -697,6 +1197,15 @@ hmoe_status launch_route(const float* x, const float* w, const float* bias,
         return HMOE_INVALID_ARGUMENT;
     // hidden rows and router rows arrive by bulk copies (16-byte aligned)
     if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(w) % 16) return HMOE_INVALID_ARGUMENT;
+    const bool tiled_ok = tiled_shape_ok(H, E);
+    if (g_route_variant == 2 && !tiled_ok) {
+        set_last_error_text("hmoe route: the tiled router needs E <= 128, E % 4 == 0 and H % 32 == 0");
+        return HMOE_UNSUPPORTED;
+    }
+    if (g_route_variant == 2 || (g_route_variant == 0 && tiled_ok && T >= kTiledMinTokens)) {
+        RouteArgs a{x, w, bias, T, H, E, k, softmax, renorm, ids, scores, counts, st};
+        return launch_route_tiled(a, stream);
+    }
     const int EQ = (E + 3) / 4;
     const int P = std::min(32, 256 / EQ); // row lanes; phase 2 maps token t to lane t mod P
     if (EQ * P > 256 || P < 1) return HMOE_UNSUPPORTED;
@@ -794,4 +1303,10 @@ extern "C" hmoe_status hmoe_router_topk(float* logits, size_t tokens,
     }
 #undef HMOE_TOPK_CASE
     return check_launch("CUDA router top-k kernel");
+}
+
+extern "C" hmoe_status hmoe_set_route_variant(int32_t variant) {
+    if (variant < 0 || variant > 2) return HMOE_INVALID_ARGUMENT;
+    hmoe::g_route_variant = variant;
+    return HMOE_OK;
 }

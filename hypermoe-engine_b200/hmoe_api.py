@@ -41,7 +41,7 @@ EXPORTS = [
     "hmoe_ep_expert_range", "hmoe_ep_plan", "hmoe_ep_unique_id", "hmoe_ep_comm_create",
     "hmoe_ep_comm_destroy", "hmoe_ep_workspace_size", "hmoe_ep_moe_forward", "hmoe_ep_last_plan",
     "hmoe_moe_forward_noalloc", "hmoe_selftest_bounded_wait", "hmoe_ep_set_placement",
-    "hmoe_ep_balanced_placement",
+    "hmoe_ep_balanced_placement", "hmoe_set_route_variant",
 ]
 EP_MAX_RANKS = 64
 EP_UNIQUE_ID_BYTES = 128
@@ -114,6 +114,7 @@ def lib() -> ctypes.CDLL:
             "hmoe_moe_forward": [ctypes.POINTER(LayerDesc), vp, vp, sz, vp, sz, vp],
             "hmoe_moe_forward_host": [ctypes.POINTER(LayerDesc), vp, vp, sz, vp, sz, vp],
             "hmoe_set_variant": [i32],
+            "hmoe_set_route_variant": [i32],
             "hmoe_read_status": [vp, ctypes.POINTER(i32), ctypes.POINTER(i32), ctypes.POINTER(i32), vp],
             "hmoe_quantize_int8": [vp, sz, vp, vp, vp, vp],
             "hmoe_ep_expert_range": [ctypes.c_uint32, i32, i32, ctypes.POINTER(ctypes.c_uint32),
@@ -348,6 +349,11 @@ class DeviceLayer:
 
 def set_variant(v: int) -> None:
     check("hmoe_set_variant", lib().hmoe_set_variant(v))
+
+
+def set_route_variant(v: int) -> None:
+    """0 = automatic, 1 = per-8-token cluster router, 2 = tiled router."""
+    check("hmoe_set_route_variant", lib().hmoe_set_route_variant(v))
 
 
 # ------------------------------------------------------ expert parallelism

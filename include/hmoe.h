@@ -224,6 +224,14 @@ hmoe_status hmoe_moe_forward_noalloc(const hmoe_layer_desc *desc,
  * 2 = tensor-core GEMM only.  Process-wide. */
 hmoe_status hmoe_set_variant(int32_t variant);
 
+/* Forces the router kernel for measurement: 0 = automatic (the tiled kernel
+ * for batches of 512 tokens or more when E <= 128, E % 4 == 0 and
+ * H % 32 == 0), 1 = the per-8-token cluster kernel, 2 = the tiled kernel
+ * (64-token tiles on the FP64 tensor-core path; routing calls whose shape it
+ * does not take return HMOE_UNSUPPORTED).  Both produce bit-identical
+ * results.  Process-wide. */
+hmoe_status hmoe_set_route_variant(int32_t variant);
+
 /* Measurement hooks.  hmoe_set_stage_events registers `count` (= 6)
  * cudaEvent_t handles (passed as void*) that every later hmoe_moe_forward
  * records on its stream at the stage boundaries: [0] start, [1] after the

@@ -177,9 +177,15 @@ def _pad64(x, w):
     return xp, wp
 
 
+@pytest.mark.parametrize("route_variant", [0, 2])
 @pytest.mark.parametrize("case", ["a", "b", "c", "d", "p12"])
-def test_fused_route_bit_exact(cuda, golden, case):
+def test_fused_route_bit_exact(cuda, golden, case, route_variant):
+    """Both router kernels (the per-8-token cluster kernel chosen
+    automatically at these sizes, and the 64-token tiled kernel forced)
+    against the reference's router goldens."""
     g = golden("router.npz")
+    if route_variant == 2 and case in ("d", "p12"):
+        pytest.skip("the tiled router takes E <= 128 with E % 4 == 0")
     if case == "p12":
         x, w = _pad64(g["p12_x"], g["p12_w"])
         k, sm, rn, bias = 2, 1, 1, None
@@ -191,7 +197,11 @@ def test_fused_route_bit_exact(cuda, golden, case):
     hl = H.make_host_layer(cfg, seed=0)
     hl.router_w, hl.router_bias = w, bias
     dl = H.DeviceLayer(hl, cuda)
-    ids, sc, off, gt, gs = dl.route(t(x, cuda))
+    H.set_route_variant(route_variant)
+    try:
+        ids, sc, off, gt, gs = dl.route(t(x, cuda))
+    finally:
+        H.set_route_variant(0)
     np.testing.assert_array_equal(host(ids).view(np.uint32), g[f"{case}_ids"])
     np.testing.assert_array_equal(host(off), g[f"{case}_offsets"])
     np.testing.assert_array_equal(host(gt).view(np.uint32), g[f"{case}_gtok"])
@@ -203,14 +213,21 @@ def test_fused_route_bit_exact(cuda, golden, case):
         assert groups == [[0, 2], [0, 1, 2], [1]]
 
 
-@pytest.mark.parametrize("T", [1, 16, 256, 4096])
-def test_fused_route_c3_full_sizes(cuda, T):
+@pytest.mark.parametrize("route_variant", [1, 2])
+@pytest.mark.parametrize("T", [1, 16, 256, 700, 4096])
+def test_fused_route_c3_full_sizes(cuda, T, route_variant):
+    """C3 router (H2048, E128, k8, Zipf bias) at decode to prefill sizes,
+    with each router kernel forced; 700 tokens leave a ragged last tile."""
     cfg = H.CONFIGS["c3"]
     hl = H.make_host_layer(cfg, seed=2)
     x = H.make_tokens(cfg, T, seed=2)
     ids_p, sc_p, off_p, gt_p, gs_p = O.route(O.port(), x, hl.router_w, hl.router_bias, cfg.top_k)
     dl = H.DeviceLayer(hl, cuda)
-    ids, sc, off, gt, gs = dl.route(t(x, cuda))
+    H.set_route_variant(route_variant)
+    try:
+        ids, sc, off, gt, gs = dl.route(t(x, cuda))
+    finally:
+        H.set_route_variant(0)
     np.testing.assert_array_equal(host(ids).view(np.uint32), ids_p)
     np.testing.assert_array_equal(host(off), off_p)
     np.testing.assert_array_equal(host(gt).view(np.uint32), gt_p)
