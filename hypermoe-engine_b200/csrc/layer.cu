@@ -57,7 +57,9 @@ Workspace plan_workspace(const hmoe_layer_desc& d, size_t T) {
         return at;
     };
     w.status = take(sizeof(DeviceStatus));
-    w.counts = take((E + S) * 4); // zeroed together with status
+    // zeroed together with status: routed counts, then per token block
+    w.counts = take((E + S) * 4);
+    w.block_counts = take(((T + kGroupBlock - 1) / kGroupBlock) * E * 4);
     w.zero_bytes = off;
     w.offsets = take((E + S + 1) * 4);
     w.ids = take(T * k * 4);
@@ -168,11 +170,13 @@ hmoe_status enqueue_route(const hmoe_layer_desc& d, const float* x, size_t T, ch
                                  static_cast<int>(d.top_k), d.softmax, d.renormalize,
                                  reinterpret_cast<uint32_t*>(ws + w.ids),
                                  reinterpret_cast<float*>(ws + w.scores),
-                                 reinterpret_cast<int32_t*>(ws + w.counts), st, s);
+                                 reinterpret_cast<int32_t*>(ws + w.counts),
+                                 reinterpret_cast<int32_t*>(ws + w.block_counts), st, s);
     if (r != HMOE_OK) return r;
     stage(1, s);
     r = launch_group(reinterpret_cast<uint32_t*>(ws + w.ids), reinterpret_cast<float*>(ws + w.scores),
-                     reinterpret_cast<int32_t*>(ws + w.counts), static_cast<int>(T), static_cast<int>(d.top_k),
+                     reinterpret_cast<int32_t*>(ws + w.counts), reinterpret_cast<int32_t*>(ws + w.block_counts),
+                     static_cast<int>(T), static_cast<int>(d.top_k),
                      static_cast<int>(d.experts), static_cast<int>(d.shared_experts),
                      reinterpret_cast<int32_t*>(ws + w.offsets), reinterpret_cast<uint32_t*>(ws + w.perm_token),
                      reinterpret_cast<float*>(ws + w.perm_weight), reinterpret_cast<int32_t*>(ws + w.inv),

@@ -10,8 +10,12 @@ namespace hmoe {
 // Byte offsets of the workspace segments (all 256-byte aligned).
 // hmid holds the intermediate rows: FP32 for the GEMV variant, BF16 for the
 // GEMM variant (one launch uses one of them).
+// Tokens per block of the grouping's counting sort; the router counts the
+// selected experts of each block.
+constexpr int kGroupBlock = 256;
+
 struct Workspace {
-    size_t status, counts, zero_bytes, offsets, ids, scores, perm_token, perm_weight, inv;
+    size_t status, counts, block_counts, zero_bytes, offsets, ids, scores, perm_token, perm_weight, inv;
     size_t xperm, xscale, hmid, yrows, tiles, tile_count;
     int tile_cap;
     size_t total;
@@ -111,13 +115,13 @@ int tile_capacity_for(long rows, int segments);
 
 hmoe_status launch_route(const float* x, const float* w, const float* bias, int T, int H, int E, int k,
                          int softmax, int renorm, uint32_t* ids, float* scores, int32_t* counts,
-                         DeviceStatus* st, cudaStream_t stream);
+                         int32_t* block_counts, DeviceStatus* st, cudaStream_t stream);
 // Expert groups in ascending expert id, or in placement-slot order when
 // expert_of_slot is given (then slot_counts[b] = rows of slot b).
-hmoe_status launch_group(const uint32_t* ids, const float* scores, const int32_t* counts, int T, int k,
-                         int E, int S, int32_t* offsets, uint32_t* perm_token, float* perm_weight,
-                         int32_t* inv, const int32_t* expert_of_slot, int32_t* slot_counts,
-                         cudaStream_t stream);
+hmoe_status launch_group(const uint32_t* ids, const float* scores, const int32_t* counts,
+                         const int32_t* block_counts, int T, int k, int E, int S, int32_t* offsets,
+                         uint32_t* perm_token, float* perm_weight, int32_t* inv, const int32_t* expert_of_slot,
+                         int32_t* slot_counts, cudaStream_t stream);
 // out[t] = sum of the token's rows in ascending expert id: routed slot j has
 // expert ids[t, j] (when ids is null the row order is the expert order),
 // shared expert s counts as expert E + s.

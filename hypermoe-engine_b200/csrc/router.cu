@@ -32,6 +32,7 @@
 #include "sm100.cuh"
 
 #include <cooperative_groups.h>
+#include <cub/block/block_scan.cuh>
 
 #include <cfloat>
 #include <algorithm>
@@ -57,7 +58,13 @@ struct RouteArgs {
     float* scores;      // [T, k]
     int32_t* counts;    // [E] (zeroed by the caller), may be null
     DeviceStatus* st;
+    int32_t* block_counts; // [ceil(T/kGroupBlock)][E] per token block (zeroed), may be null
 };
+
+// Selected-expert counts of token block tok / kGroupBlock (for the grouping).
+__device__ __forceinline__ int32_t* token_block_counts(const RouteArgs& a, size_t tok) {
+    return a.block_counts ? a.block_counts + (tok / kGroupBlock) * a.E : nullptr;
+}
 
 __device__ __forceinline__ bool better(float pa, int ia, float pb, int ib) {
     return pa > pb || (pa == pb && ia < ib);
@@ -77,7 +84,7 @@ __device__ __forceinline__ bool rounding_certified(double s, double beta) {
 template <int C>
 __device__ void select_token(const float (&lv)[C], int E, int k, int softmax,
                              int renorm, float* ev_smem, uint32_t* ids_out,
-                             float* scores_out, int32_t* counts,
+                             float* scores_out, int32_t* counts, int32_t* block_counts,
                              DeviceStatus* st, bool write_probs,
                              float* probs_out) {
     const int lane = threadIdx.x & 31;
@@ -211,6 +218,7 @@ __device__ void select_token(const float (&lv)[C], int E, int k, int softmax,
         ids_out[lane] = static_cast<uint32_t>(myid);
         scores_out[lane] = sc;
         if (counts) atomicAdd(counts + myid, 1);
+        if (block_counts) atomicAdd(block_counts + myid, 1);
     }
     if (lane == 0) {
         if (!ok) device_fail(st, HMOE_NON_FINITE_ROUTER);
@@ -709,7 +717,7 @@ __global__ void __launch_bounds__(256, 2) route_kernel(RouteArgs a, int EQ, int 
             }
             const size_t tok = static_cast<size_t>(t0 + t);
             select_token<C>(lv, E, a.k, a.softmax, a.renorm, evs + t * E_pad, a.ids + tok * a.k,
-                            a.scores + tok * a.k, a.counts, a.st, false, nullptr);
+                            a.scores + tok * a.k, a.counts, token_block_counts(a, tok), a.st, false, nullptr);
         }
     }
     cluster.sync(); // keep every CTA's shared memory alive until rank 0 is done
@@ -1015,7 +1023,7 @@ __global__ void __launch_bounds__(256, 2) route_tiled_kernel(const __grid_consta
         }
         const size_t tok = static_cast<size_t>(t0 + lt0 + lt);
         select_token<C>(lv, E, a.k, a.softmax, a.renorm, evs + warp * kRtCols, a.ids + tok * a.k,
-                        a.scores + tok * a.k, a.counts, a.st, false, nullptr);
+                        a.scores + tok * a.k, a.counts, token_block_counts(a, tok), a.st, false, nullptr);
     }
 }
 
@@ -1037,7 +1045,7 @@ __global__ void router_topk_kernel(float* logits, int T, int E, int k,
         lv[c] = j < E ? row[j] : 0.0f;
     }
     select_token<C>(lv, E, k, softmax, renorm, evs[warp], ids + static_cast<size_t>(t) * k,
-                    scores + static_cast<size_t>(t) * k, nullptr, nullptr, softmax != 0, row);
+                    scores + static_cast<size_t>(t) * k, nullptr, nullptr, nullptr, softmax != 0, row);
 }
 
 // ------------------------------------------------------------ grouping
@@ -1046,6 +1054,7 @@ struct GroupArgs {
     const uint32_t* ids;   // [T, k]
     const float* scores;   // [T, k]
     const int32_t* counts; // [E] routed counts
+    const int32_t* block_counts; // [ceil(T/kGroupBlock)][E] routed counts per token block
     int T, k, E, S;        // S shared experts
     int32_t* offsets;      // [E+S+1]
     uint32_t* perm_token;  // [T*(k+S)] token of each permuted row
@@ -1064,68 +1073,73 @@ __device__ __forceinline__ int group_count(const GroupArgs& g, int b) {
     return b < g.E ? g.counts[group_expert(g, b)] : g.T;
 }
 
-// One CTA per expert (routed then shared).  Tokens are placed in ascending
-// order inside the expert's group, exactly as routeBatch appends them
-// (CpuRouterBackend.cpp:78-90); groups are laid out in ascending expert id.
+// Stable counting sort of the (token, slot) assignments, one CTA per block
+// of kGroupBlock tokens.  Groups are laid out in slot order (ascending
+// expert id without a placement), then the shared experts; inside a group
+// tokens ascend, exactly as routeBatch appends them
+// (CpuRouterBackend.cpp:78-90).  A row's position is the group offset, plus
+// the group's rows in earlier token blocks (the router's per-block counts),
+// plus the rank of the token among this block's tokens of that expert (a
+// bit mask per expert).
 __global__ void __launch_bounds__(256) group_kernel(GroupArgs g) {
-    __shared__ int red[8];
-    __shared__ int warp_hits[8];
-    __shared__ int base_s;
-    const int b = blockIdx.x;          // group (placement slot for routed experts)
-    const int e = group_expert(g, b);  // expert of the group
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // Offset of group b from the counts of the groups before it.
-    int off = 0;
-    for (int j = tid; j < b; j += blockDim.x) off += group_count(g, j);
+    using Scan = cub::BlockScan<int, 256>;
+    __shared__ typename Scan::TempStorage scan_tmp;
+    __shared__ int off_s[2 * 256 + 1];
+    __shared__ int slot_of[kMaxExperts];
+    __shared__ int pre[kMaxExperts];
+    __shared__ uint32_t mask[kMaxExperts][kGroupBlock / 32];
+    const int tid = threadIdx.x, blk = blockIdx.x;
+    const int tb0 = blk * kGroupBlock;
+    const int nt = min(kGroupBlock, g.T - tb0);
+    const int nb = g.E + g.S;
+    // group offsets: exclusive scan of the group sizes (two per thread)
+    int v[2];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) off += __shfl_xor_sync(0xffffffffu, off, o);
-    if (lane == 0) red[warp] = off;
-    __syncthreads();
-    if (tid == 0) {
-        int o = 0;
-        for (int w = 0; w < 8; ++w) o += red[w];
-        g.offsets[b] = o;
-        if (b == g.E + g.S - 1) g.offsets[b + 1] = o + group_count(g, b);
-        if (g.slot_counts && b < g.E) g.slot_counts[b] = group_count(g, b);
-        base_s = o;
+    for (int q = 0; q < 2; ++q) {
+        const int b = 2 * tid + q;
+        v[q] = b < nb ? group_count(g, b) : 0;
     }
+    int total = 0;
+    Scan(scan_tmp).ExclusiveSum(v, v, total);
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+        if (2 * tid + q < nb) off_s[2 * tid + q] = v[q];
+    if (tid == 0) off_s[nb] = total;
+    for (int b = tid; b < g.E; b += blockDim.x) slot_of[group_expert(g, b)] = b;
+    for (int e = tid; e < g.E; e += blockDim.x) {
+        int p = 0;
+        for (int q = 0; q < blk; ++q) p += g.block_counts[q * g.E + e];
+        pre[e] = p;
+    }
+    for (int i = tid; i < g.E * (kGroupBlock / 32); i += blockDim.x) (&mask[0][0])[i] = 0u;
     __syncthreads();
-    int base = base_s;
+    if (blk == 0) {
+        for (int b = tid; b <= nb; b += blockDim.x) g.offsets[b] = off_s[b];
+        if (g.slot_counts)
+            for (int b = tid; b < g.E; b += blockDim.x) g.slot_counts[b] = group_count(g, b);
+    }
+    const int t = tb0 + tid;
+    const uint32_t* r = g.ids + static_cast<size_t>(t) * g.k;
+    if (tid < nt)
+        for (int j = 0; j < g.k; ++j) atomicOr(&mask[r[j]][tid >> 5], 1u << (tid & 31));
+    __syncthreads();
+    if (tid >= nt) return;
     const int slots = g.k + g.S;
-    if (b >= g.E) {
-        const int s = b - g.E;
-        for (int t = tid; t < g.T; t += blockDim.x) {
-            const int row = base + t;
-            g.perm_token[row] = static_cast<uint32_t>(t);
-            g.perm_weight[row] = 1.0f;
-            g.inv[static_cast<size_t>(t) * slots + g.k + s] = row;
-        }
-        return;
+    const int w = tid >> 5;
+    for (int j = 0; j < g.k; ++j) {
+        const int e = static_cast<int>(r[j]);
+        int rank = __popc(mask[e][w] & ((1u << (tid & 31)) - 1u));
+        for (int q = 0; q < w; ++q) rank += __popc(mask[e][q]);
+        const int row = off_s[slot_of[e]] + pre[e] + rank;
+        g.perm_token[row] = static_cast<uint32_t>(t);
+        g.perm_weight[row] = g.scores[static_cast<size_t>(t) * g.k + j];
+        g.inv[static_cast<size_t>(t) * slots + j] = row;
     }
-    for (int t0 = 0; t0 < g.T; t0 += blockDim.x) {
-        const int t = t0 + tid;
-        int slot = -1;
-        if (t < g.T) {
-            const uint32_t* r = g.ids + static_cast<size_t>(t) * g.k;
-            for (int j = 0; j < g.k; ++j)
-                if (r[j] == static_cast<uint32_t>(e)) slot = j;
-        }
-        const unsigned mask = __ballot_sync(0xffffffffu, slot >= 0);
-        if (lane == 0) warp_hits[warp] = __popc(mask);
-        __syncthreads();
-        int before = 0, chunk = 0;
-        for (int w = 0; w < 8; ++w) {
-            before += w < warp ? warp_hits[w] : 0;
-            chunk += warp_hits[w];
-        }
-        if (slot >= 0) {
-            const int row = base + before + __popc(mask & ((1u << lane) - 1u));
-            g.perm_token[row] = static_cast<uint32_t>(t);
-            g.perm_weight[row] = g.scores[static_cast<size_t>(t) * g.k + slot];
-            g.inv[static_cast<size_t>(t) * slots + slot] = row;
-        }
-        base += chunk;
-        __syncthreads();
+    for (int sx = 0; sx < g.S; ++sx) {
+        const int row = off_s[g.E + sx] + t;
+        g.perm_token[row] = static_cast<uint32_t>(t);
+        g.perm_weight[row] = 1.0f;
+        g.inv[static_cast<size_t>(t) * slots + g.k + sx] = row;
     }
 }
 
@@ -1191,7 +1205,7 @@ hmoe_status launch_route_tiled(const RouteArgs& a, cudaStream_t stream) {
 hmoe_status launch_route(const float* x, const float* w, const float* bias,
                          int T, int H, int E, int k, int softmax, int renorm,
                          uint32_t* ids, float* scores, int32_t* counts,
-                         DeviceStatus* st, cudaStream_t stream) {
+                         int32_t* block_counts, DeviceStatus* st, cudaStream_t stream) {
     if (T <= 0) return HMOE_OK;
     if (E <= 0 || E > kMaxExperts || k <= 0 || k > E || k > kMaxTopK || H <= 0 || H % 8)
         return HMOE_INVALID_ARGUMENT;
@@ -1203,7 +1217,7 @@ hmoe_status launch_route(const float* x, const float* w, const float* bias,
         return HMOE_UNSUPPORTED;
     }
     if (g_route_variant == 2 || (g_route_variant == 0 && tiled_ok && T >= kTiledMinTokens)) {
-        RouteArgs a{x, w, bias, T, H, E, k, softmax, renorm, ids, scores, counts, st};
+        RouteArgs a{x, w, bias, T, H, E, k, softmax, renorm, ids, scores, counts, st, block_counts};
         return launch_route_tiled(a, stream);
     }
     const int EQ = (E + 3) / 4;
@@ -1214,7 +1228,7 @@ hmoe_status launch_route(const float* x, const float* w, const float* bias,
     const int rows = (T + kRouteTokens - 1) / kRouteTokens;
     int KS = 1; // split H over a cluster until there are about 2 CTAs per SM
     while (KS < 8 && rows * KS < 2 * 148 && (H / (KS * 2)) % 8 == 0 && H / (KS * 2) >= 64) KS *= 2;
-    RouteArgs a{x, w, bias, T, H, E, k, softmax, renorm, ids, scores, counts, st};
+    RouteArgs a{x, w, bias, T, H, E, k, softmax, renorm, ids, scores, counts, st, block_counts};
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(KS), static_cast<unsigned>(rows));
     cfg.blockDim = dim3(256);
@@ -1258,13 +1272,15 @@ hmoe_status launch_route(const float* x, const float* w, const float* bias,
     return check_launch("hmoe route kernel");
 }
 
-hmoe_status launch_group(const uint32_t* ids, const float* scores, const int32_t* counts, int T, int k,
-                         int E, int S, int32_t* offsets, uint32_t* perm_token, float* perm_weight,
-                         int32_t* inv, const int32_t* expert_of_slot, int32_t* slot_counts,
-                         cudaStream_t stream) {
-    GroupArgs g{ids, scores, counts, T, k, E, S, offsets, perm_token, perm_weight, inv, expert_of_slot,
-                slot_counts};
-    group_kernel<<<E + S, 256, 0, stream>>>(g);
+hmoe_status launch_group(const uint32_t* ids, const float* scores, const int32_t* counts,
+                         const int32_t* block_counts, int T, int k, int E, int S, int32_t* offsets,
+                         uint32_t* perm_token, float* perm_weight, int32_t* inv, const int32_t* expert_of_slot,
+                         int32_t* slot_counts, cudaStream_t stream) {
+    if (T <= 0) return HMOE_OK;
+    if (E + S > 2 * 256) return HMOE_UNSUPPORTED;
+    GroupArgs g{ids, scores, counts, block_counts, T, k, E, S, offsets, perm_token, perm_weight, inv,
+                expert_of_slot, slot_counts};
+    group_kernel<<<(T + kGroupBlock - 1) / kGroupBlock, 256, 0, stream>>>(g);
     return check_launch("hmoe group kernel");
 }
 
