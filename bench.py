@@ -22,8 +22,9 @@ on a bounded token sample, on this host's cores.
 Multi-GPU (torchrun, one process per GPU): expert parallelism through
 hmoe_ep_moe_forward.  Rank r holds its contiguous share of the 128 routed
 experts and routes its own 4096 tokens (weak scaling); rows travel to the
-expert owners and back over NCCL point-to-point on NVLink.  The step time is
-the max over ranks.
+expert owners and back as stores into the peers' memory over NVLink
+(registered workspaces, epoch flags; --ep-path nccl: NCCL point-to-point
+instead).  The step time is the max over ranks.
 """
 from __future__ import annotations
 
@@ -57,6 +58,8 @@ def parse():
     p.add_argument("--impl", default="hmoe", choices=["hmoe", "reference"])
     p.add_argument("--variant", type=int, default=0, help="0 auto, 1 GEMV only, 2 GEMM only")
     p.add_argument("--route-variant", type=int, default=0, help="0 auto, 1 cluster router, 2 tiled router")
+    p.add_argument("--ep-path", default="peer", choices=["peer", "nccl"],
+                   help="expert parallelism: peer-memory stores (registered workspace) or NCCL send/recv")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
@@ -285,7 +288,7 @@ def main():
             torch.cuda.empty_cache()
         if args.placement == "balanced":
             dist.broadcast_object_list(placement, src=0)
-        layer = H.EpLayer(host_layer, comm, dev, slot_of_expert=placement[0])
+        layer = H.EpLayer(host_layer, comm, dev, slot_of_expert=placement[0], peer=args.ep_path == "peer")
     else:
         layer = H.DeviceLayer(host_layer, dev)
     x = torch.from_numpy(x_np).to(dev)
@@ -470,6 +473,7 @@ def main():
         "vs_baseline": None, "dtype": "fp32" if not used_gemm else "fp16+bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights quantised to INT8)",
         "config": dict(config, parallelism=(f"ep{world}" if world > 1 else "single"),
+                       ep_path=(args.ep_path if world > 1 else None),
                        placement=(None if world == 1 else
                                   "balanced from 4096 calibration tokens (seed+104729)" if args.placement == "balanced"
                                   else "contiguous"),

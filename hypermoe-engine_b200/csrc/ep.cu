@@ -108,6 +108,18 @@ struct hmoe_ep_comm {
     uint32_t placement_experts = 0;
     int32_t slot_of_expert[256] = {};
     int32_t* d_expert_of_slot = nullptr; // device [256]
+    // Peer-memory path (hmoe_ep_register_workspace): every rank's registered
+    // workspace mapped into this process; own entry = reg_ws.
+    void* reg_ws = nullptr;
+    size_t reg_bytes = 0;
+    char* peer_ws[HMOE_EP_MAX_RANKS] = {};
+    void* peer_base[HMOE_EP_MAX_RANKS] = {}; // IPC mappings to close
+    char** d_peer_ws = nullptr;              // device copy of peer_ws
+    uint64_t epoch = 0;                      // forwards since registration
+    bool last_peer = false;                  // last forward took the peer path
+    int last_parity = 0;
+    uint32_t last_E = 0, last_k = 0;        // ... and its layer shape
+    size_t last_max_tokens = 0, last_counts_off = 0;
 };
 
 namespace hmoe {
@@ -152,6 +164,24 @@ hmoe_status wait_counts(hmoe_ep_comm* c) {
 // Workspace of one EP rank: the single-GPU layout for max_tokens local
 // tokens (routing over all E experts, local and shared-expert rows) and the
 // receive side for up to P * max_tokens * k rows.
+// Peer-memory path: the first kEpSyncBytes of the workspace hold the epoch
+// flags written by the peers ([3 kinds][HMOE_EP_MAX_RANKS] uint64: counts
+// published, rows dispatched, rows returned), two CTA-completion counters
+// and the device transfer plan.  Zeroed at registration.
+struct EpDevPlan {
+    int32_t send_off[HMOE_EP_MAX_RANKS];  // this rank's rows for rank q start here ...
+    int32_t send_rows[HMOE_EP_MAX_RANKS]; // ... and are this many
+    int32_t dest_base[HMOE_EP_MAX_RANKS]; // and land at this row of q's receive rows
+    int32_t recv_base[HMOE_EP_MAX_RANKS]; // rows from rank p start at this receive row ...
+    int32_t recv_rows[HMOE_EP_MAX_RANKS]; // ... and are this many
+    int32_t ret_off[HMOE_EP_MAX_RANKS];   // and return to this row of p's permuted rows
+    int32_t recv_total, sent_total;
+};
+constexpr size_t kEpFlagsBytes = 3 * HMOE_EP_MAX_RANKS * 8;
+constexpr size_t kEpCtrOff = kEpFlagsBytes;           // 2 x int32 CTA-completion counters
+constexpr size_t kEpPlanOff = kEpFlagsBytes + 256;
+constexpr size_t kEpSyncBytes = kEpPlanOff + ((sizeof(EpDevPlan) + 255) / 256) * 256;
+
 struct EpWorkspace {
     Workspace local;
     size_t slot_counts, counts_all, xin, win, scale_in, hin, yin, tiles_in, count_in;
@@ -167,14 +197,15 @@ EpWorkspace plan_ep(const hmoe_layer_desc& d, size_t max_tokens) {
     const size_t rin = P * max_tokens * d.top_k;
     uint32_t first = 0, count = 0;
     hmoe_ep_expert_range(d.experts, d.ep_size, d.ep_rank, &first, &count);
-    size_t off = w.local.total;
+    // the single-GPU layout (offsets from ws + kEpSyncBytes) follows the sync area
+    size_t off = kEpSyncBytes + w.local.total;
     auto take = [&](size_t bytes) {
         const size_t at = off;
         off = align_up(off + bytes, 256);
         return at;
     };
     w.slot_counts = take(static_cast<size_t>(d.experts) * 4);
-    w.counts_all = take(P * d.experts * 4);
+    w.counts_all = take(2 * P * d.experts * 4); // [epoch parity][P][E]
     w.xin = take(rin * d.hidden * 2);
     w.win = take(rin * 4);
     w.scale_in = take(rin * 4);
@@ -202,6 +233,360 @@ hmoe_status validate_ep(const hmoe_layer_desc* d) {
 bool ep_rows_fit(const hmoe_layer_desc& d, size_t max_tokens) {
     const double rin = static_cast<double>(d.ep_size) * static_cast<double>(max_tokens) * d.top_k;
     return rin * std::max(d.hidden, d.intermediate) < 4e18 && rin <= static_cast<double>(INT_MAX / 2);
+}
+
+// ------------------------------------------------------------ peer-memory path
+//
+// With a registered workspace (hmoe_ep_register_workspace) every rank's
+// workspace is mapped into every process (CUDA IPC over NVLink), and the
+// layer's exchanges are plain stores into the peers' memory, ordered by
+// epoch flags: no host synchronisation, no NCCL.
+//   ep_exchange_kernel  publish this rank's slot counts into every rank's
+//                       counts (epoch-parity buffer), flag them, wait for
+//                       every rank's, build the transfer plan on the device
+//   ep_copy_rows_kernel dispatch: this rank's FP16 rows, scales and routing
+//                       weights into the owners' receive rows; return: the
+//                       weighted BF16 output rows into the sources' rows;
+//                       the last CTA to finish flags every rank
+//   ep_wait_kernel      bounded wait for every rank's flag of this epoch
+// A rank can run at most one epoch ahead of another (it needs their counts
+// of the same epoch before it writes anything into their buffers), and a
+// rank publishes the counts of epoch n only after its kernels of epoch
+// n - 1 have run, so receive rows and returned rows are never overwritten
+// while in use; the counts are double-buffered by epoch parity.
+struct PeerCtx {
+    char* const* peer; // [P] every rank's workspace base in this address space
+    int P, me;
+    uint64_t epoch;
+    uint64_t limit_ns;
+    DeviceStatus* st;
+};
+
+__device__ __forceinline__ void st_release_sys(uint64_t* p, uint64_t v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t ld_acquire_sys(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint64_t now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ uint64_t* ep_flags(char* base, int kind) {
+    return reinterpret_cast<uint64_t*>(base) + kind * HMOE_EP_MAX_RANKS;
+}
+
+// Thread-level: every rank's flag `kind` reaches `epoch`, or false after
+// limit_ns.
+__device__ bool wait_all_flags(const PeerCtx& c, int kind) {
+    const uint64_t* f = ep_flags(c.peer[c.me], kind);
+    const uint64_t t0 = now_ns();
+    for (int p = 0; p < c.P; ++p)
+        while (ld_acquire_sys(f + p) < c.epoch) {
+            if (now_ns() - t0 > c.limit_ns) return false;
+            __nanosleep(100);
+        }
+    return true;
+}
+
+__device__ void signal_all(const PeerCtx& c, int kind) {
+    __threadfence_system();
+    for (int q = 0; q < c.P; ++q) st_release_sys(ep_flags(c.peer[q], kind) + c.me, c.epoch);
+}
+
+__global__ void ep_wait_kernel(PeerCtx c, int kind) {
+    if (threadIdx.x == 0 && !wait_all_flags(c, kind)) device_fail(c.st, HMOE_TIMEOUT);
+}
+
+// One CTA.  counts_off: the [2][P][E] counts in every workspace;
+// my_counts: this rank's routed rows per slot; cap_rows: receive rows of
+// every workspace.  On a timeout or an inconsistent count the plan moves no
+// rows (and the status says why).
+__global__ void __launch_bounds__(256) ep_exchange_kernel(PeerCtx c, size_t counts_off, const int32_t* my_counts,
+                                                          int E, int parity, int cap_rows) {
+    __shared__ int R[HMOE_EP_MAX_RANKS][HMOE_EP_MAX_RANKS + 1]; // rows from p to q
+    __shared__ int ok;
+    const int P = c.P, me = c.me, tid = threadIdx.x;
+    for (int q = 0; q < P; ++q) {
+        int32_t* dst = reinterpret_cast<int32_t*>(c.peer[q] + counts_off) + (static_cast<size_t>(parity) * P + me) * E;
+        for (int e = tid; e < E; e += blockDim.x) dst[e] = my_counts[e];
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (tid == 0) {
+        signal_all(c, 0);
+        ok = wait_all_flags(c, 0);
+        if (!ok) device_fail(c.st, HMOE_TIMEOUT);
+    }
+    __syncthreads();
+    const int32_t* cnt = reinterpret_cast<const int32_t*>(c.peer[me] + counts_off) + static_cast<size_t>(parity) * P * E;
+    const int base = E / P, extra = E % P;
+    for (int idx = tid; idx < P * P; idx += blockDim.x) {
+        const int p = idx / P, q = idx % P;
+        const int f = q * base + min(q, extra), n = base + (q < extra ? 1 : 0);
+        int r = 0;
+        for (int sl = f; sl < f + n; ++sl) r += max(0, cnt[p * E + sl]);
+        R[p][q] = ok ? r : 0;
+    }
+    __syncthreads();
+    if (tid == 0) { // every rank's receive rows fit (identical verdict on every rank)
+        for (int q = 0; q < P; ++q) {
+            long in = 0;
+            for (int p = 0; p < P; ++p) in += R[p][q];
+            if (in > cap_rows) ok = 0;
+        }
+        if (!ok) device_fail(c.st, HMOE_INVALID_ARGUMENT);
+    }
+    __syncthreads();
+    EpDevPlan* plan = reinterpret_cast<EpDevPlan*>(c.peer[me] + kEpPlanOff);
+    if (tid < P) {
+        const int q = tid; // as a destination for send_*, dest_base; as a source p for recv_*, ret_off
+        int so = 0, db = 0, rb = 0, ro = 0;
+        for (int j = 0; j < q; ++j) {
+            so += R[me][j];
+            rb += R[j][me];
+        }
+        for (int p = 0; p < me; ++p) db += R[p][q];
+        for (int j = 0; j < me; ++j) ro += R[q][j];
+        plan->send_off[q] = ok ? so : 0;
+        plan->send_rows[q] = ok ? R[me][q] : 0;
+        plan->dest_base[q] = ok ? db : 0;
+        plan->recv_base[q] = ok ? rb : 0;
+        plan->recv_rows[q] = ok ? R[q][me] : 0;
+        plan->ret_off[q] = ok ? ro : 0;
+    }
+    if (tid == 0) {
+        int rt = 0, st = 0;
+        for (int p = 0; p < P; ++p) {
+            rt += R[p][me];
+            st += R[me][p];
+        }
+        plan->recv_total = ok ? rt : 0;
+        plan->sent_total = ok ? st : 0;
+    }
+}
+
+// Row copies between ranks, a warp per row.  DISPATCH: this rank's permuted
+// rows r < sent_total to rank q (the owner of r's slot) at row
+// dest_base[q] + r - send_off[q] of q's receive rows, with their scale and
+// routing weight.  RETURN: received rows i < recv_total back to their
+// source p at row ret_off[p] + i - recv_base[p] of p's permuted rows.  The
+// last CTA out flags `kind` on every rank.
+struct CopyArgs {
+    const char* src;        // local rows (FP16 or BF16, H elements)
+    size_t dst_off;         // destination rows in every workspace
+    const float* src_a;     // dispatch: scales and weights (else null)
+    const float* src_b;
+    size_t dst_a_off, dst_b_off;
+    int H;
+    int kind;               // 1 dispatch, 2 return
+};
+
+__global__ void __launch_bounds__(256) ep_copy_rows_kernel(PeerCtx c, CopyArgs a) {
+    __shared__ int s_off[HMOE_EP_MAX_RANKS], s_rows[HMOE_EP_MAX_RANKS], s_dst[HMOE_EP_MAX_RANKS];
+    __shared__ int s_total;
+    const EpDevPlan* plan = reinterpret_cast<const EpDevPlan*>(c.peer[c.me] + kEpPlanOff);
+    const bool disp = a.kind == 1;
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (tid < c.P) {
+        s_off[tid] = disp ? plan->send_off[tid] : plan->recv_base[tid];
+        s_rows[tid] = disp ? plan->send_rows[tid] : plan->recv_rows[tid];
+        s_dst[tid] = disp ? plan->dest_base[tid] : plan->ret_off[tid];
+    }
+    if (tid == 0) s_total = disp ? plan->sent_total : plan->recv_total;
+    __syncthreads();
+    const size_t row_bytes = static_cast<size_t>(a.H) * 2;
+    const int vecs = static_cast<int>(row_bytes / 16);
+    const int warps = gridDim.x * (blockDim.x >> 5);
+    int q = 0;
+    for (int r = blockIdx.x * (blockDim.x >> 5) + (tid >> 5); r < s_total; r += warps) {
+        while (q + 1 < c.P && r >= s_off[q] + s_rows[q]) ++q; // rows ascend with q
+        while (q > 0 && r < s_off[q]) --q;
+        const int d = s_dst[q] + r - s_off[q];
+        const uint4* src = reinterpret_cast<const uint4*>(a.src + static_cast<size_t>(r) * row_bytes);
+        uint4* dst = reinterpret_cast<uint4*>(c.peer[q] + a.dst_off + static_cast<size_t>(d) * row_bytes);
+        for (int v = lane; v < vecs; v += 32) dst[v] = src[v];
+        if (a.src_a && lane == 0) {
+            reinterpret_cast<float*>(c.peer[q] + a.dst_a_off)[d] = a.src_a[r];
+            reinterpret_cast<float*>(c.peer[q] + a.dst_b_off)[d] = a.src_b[r];
+        }
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (tid == 0) {
+        int* ctr = reinterpret_cast<int*>(c.peer[c.me] + kEpCtrOff) + (a.kind - 1);
+        if (atomicAdd(ctr, 1) == static_cast<int>(gridDim.x) - 1) {
+            *ctr = 0;
+            signal_all(c, a.kind);
+        }
+    }
+}
+
+// Peer-memory forward (workspace == comm->reg_ws); the steps of
+// hmoe_ep_moe_forward with the count exchange, dispatch and return done by
+// the kernels above.
+hmoe_status ep_forward_peer(const hmoe_layer_desc* desc, hmoe_ep_comm* comm, const float* x, float* y,
+                            size_t tokens, size_t max_tokens, char* ws, const EpWorkspace& w, cudaStream_t s) {
+    const int E = static_cast<int>(desc->experts), S = static_cast<int>(desc->shared_experts);
+    const int k = static_cast<int>(desc->top_k), P = comm->size;
+    const size_t H = desc->hidden;
+    const int slots = k + S;
+    char* wsl = ws + kEpSyncBytes; // the single-GPU layout
+    const bool placed = comm->placement_experts != 0;
+    if (placed && comm->placement_experts != desc->experts) return HMOE_INVALID_ARGUMENT;
+    auto* slot_counts = reinterpret_cast<int32_t*>(ws + w.slot_counts);
+    const uint64_t epoch = ++comm->epoch;
+    const int parity = static_cast<int>(epoch & 1);
+    comm->last_peer = true;
+    comm->last_parity = parity;
+    comm->last_E = desc->experts;
+    comm->last_k = desc->top_k;
+    comm->last_max_tokens = max_tokens;
+    comm->last_counts_off = w.counts_all;
+    auto* st = reinterpret_cast<DeviceStatus*>(wsl + w.local.status);
+    // every flag wait gives up after the communicator's timeout (at most 10 s)
+    const PeerCtx c{comm->d_peer_ws, P, comm->rank, epoch,
+                    static_cast<uint64_t>(std::min(comm->timeout_ms, 10000)) * 1000000ull, st};
+    const int rin_cap = static_cast<int>(static_cast<size_t>(P) * max_tokens * desc->top_k);
+
+    // 1. route, group and permute this rank's tokens
+    stage(0, s);
+    hmoe_status r = enqueue_route(*desc, x, tokens, wsl, w.local, true, s, placed ? comm->d_expert_of_slot : nullptr,
+                                  placed ? slot_counts : nullptr);
+    if (r != HMOE_OK) return r;
+    // 2. counts of every (source, slot) and the transfer plan, on the device
+    const int32_t* my_counts = placed ? slot_counts : reinterpret_cast<const int32_t*>(wsl + w.local.counts);
+    ep_exchange_kernel<<<1, 256, 0, s>>>(c, w.counts_all, my_counts, E, parity, rin_cap);
+    r = check_launch("hmoe EP count exchange");
+    if (r != HMOE_OK) return r;
+    // 3. dispatch FP16 rows, scales and routing weights to the owners
+    const int copy_grid = device_sm_count() * 4;
+    CopyArgs da{wsl + w.local.xperm, w.xin, reinterpret_cast<const float*>(wsl + w.local.xscale),
+                reinterpret_cast<const float*>(wsl + w.local.perm_weight), w.scale_in, w.win, static_cast<int>(H), 1};
+    ep_copy_rows_kernel<<<copy_grid, 256, 0, s>>>(c, da);
+    r = check_launch("hmoe EP dispatch");
+    if (r != HMOE_OK) return r;
+    uint32_t first = 0, Eloc_u = 0;
+    hmoe_ep_expert_range(desc->experts, P, comm->rank, &first, &Eloc_u);
+    const int Eloc = static_cast<int>(Eloc_u);
+    ExpertRun run = local_run(*desc, tokens, wsl, w.local);
+    run.experts = Eloc + S;
+    ExpertRun in = run;
+    in.xrows = reinterpret_cast<const __half*>(ws + w.xin);
+    in.xscale = reinterpret_cast<const float*>(ws + w.scale_in);
+    in.weight = reinterpret_cast<const float*>(ws + w.win);
+    in.tiles = reinterpret_cast<int4*>(ws + w.tiles_in);
+    in.tile_count = reinterpret_cast<int32_t*>(ws + w.count_in);
+    in.tile_cap = tile_capacity_for(rin_cap, P * Eloc);
+    in.rows_cap = rin_cap;
+    in.hmid32 = reinterpret_cast<float*>(ws + w.hin);
+    in.hmid16 = reinterpret_cast<__nv_bfloat16*>(ws + w.hin);
+    in.yrows = reinterpret_cast<__nv_bfloat16*>(ws + w.yin);
+    in.max_group = static_cast<int>(std::min<size_t>(static_cast<size_t>(P) * max_tokens, INT_MAX));
+    const int32_t* counts_all = reinterpret_cast<const int32_t*>(ws + w.counts_all) + static_cast<size_t>(parity) * P * E;
+    const SegSpec seg{nullptr, counts_all + first, E, P * Eloc, Eloc, 0, 0};
+    r = launch_tile_list(seg, const_cast<int4*>(in.tiles), const_cast<int32_t*>(in.tile_count), in.tile_cap, s);
+    if (r != HMOE_OK) return r;
+    ep_wait_kernel<<<1, 32, 0, s>>>(c, 1);
+    r = check_launch("hmoe EP dispatch wait");
+    if (r != HMOE_OK) return r;
+    stage(2, s);
+    // 4. this rank's experts over the received (source, expert) segments
+    r = run_experts(in, use_gemv(rin_cap, in.H, in.I), true, s);
+    if (r != HMOE_OK) return r;
+    if (S > 0 && tokens > 0) { // shared experts on the rank's own rows
+        ExpertRun sh = run;
+        sh.tile_cap = tile_capacity_for(static_cast<long>(tokens) * S, S);
+        const SegSpec sseg{reinterpret_cast<int32_t*>(wsl + w.local.offsets) + E, nullptr, 0, S, S, Eloc, 0};
+        r = launch_tile_list(sseg, const_cast<int4*>(sh.tiles), const_cast<int32_t*>(sh.tile_count), sh.tile_cap, s);
+        if (r == HMOE_OK) r = run_experts(sh, use_gemv(static_cast<long>(tokens) * S, sh.H, sh.I), false, s);
+        if (r != HMOE_OK) return r;
+    }
+    // 5. weighted BF16 outputs back to their source rows
+    CopyArgs ra{ws + w.yin, w.local.yrows + kEpSyncBytes, nullptr, nullptr, 0, 0, static_cast<int>(H), 2};
+    ep_copy_rows_kernel<<<copy_grid, 256, 0, s>>>(c, ra);
+    r = check_launch("hmoe EP return");
+    if (r != HMOE_OK) return r;
+    ep_wait_kernel<<<1, 32, 0, s>>>(c, 2);
+    r = check_launch("hmoe EP return wait");
+    if (r != HMOE_OK) return r;
+    // 6. combine in ascending expert id
+    r = launch_combine(reinterpret_cast<__nv_bfloat16*>(wsl + w.local.yrows), reinterpret_cast<int32_t*>(wsl + w.local.inv),
+                       placed ? reinterpret_cast<uint32_t*>(wsl + w.local.ids) : nullptr, k, E,
+                       static_cast<int>(tokens), slots, static_cast<int>(H), y, s);
+    stage(5, s);
+    return r;
+}
+
+// Base address and size of the allocation holding p (driver entry point).
+bool allocation_range(const void* p, char** base, size_t* size) {
+    using Fn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+    static Fn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, []() {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &f, 12000, cudaEnableDefault, &q) ==
+                cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<Fn>(f);
+    });
+    if (!fn) return false;
+    CUdeviceptr b = 0;
+    size_t n = 0;
+    if (fn(&b, &n, reinterpret_cast<CUdeviceptr>(p)) != CUDA_SUCCESS) return false;
+    *base = reinterpret_cast<char*>(b);
+    *size = n;
+    return true;
+}
+
+void unregister_peers(hmoe_ep_comm* c) {
+    for (int q = 0; q < HMOE_EP_MAX_RANKS; ++q) {
+        if (c->peer_base[q]) cudaIpcCloseMemHandle(c->peer_base[q]);
+        c->peer_base[q] = nullptr;
+        c->peer_ws[q] = nullptr;
+    }
+    if (c->d_peer_ws) cudaFree(c->d_peer_ws);
+    c->d_peer_ws = nullptr;
+    c->reg_ws = nullptr;
+    c->reg_bytes = 0;
+    c->epoch = 0;
+    c->last_peer = false;
+}
+
+struct PeerEntry {
+    cudaIpcMemHandle_t handle;
+    uint64_t offset, bytes;
+};
+
+// All-gather of one fixed-size record per rank through NCCL (blocking).
+hmoe_status allgather_host(hmoe_ep_comm* c, const void* mine, void* all, size_t bytes) {
+    void* d = nullptr;
+    cudaStream_t s = nullptr;
+    cudaError_t err = cudaMalloc(&d, bytes * (c->size + 1));
+    if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    if (err == cudaSuccess) err = cudaMemcpy(d, mine, bytes, cudaMemcpyHostToDevice);
+    hmoe_status r = HMOE_OK;
+    if (err == cudaSuccess) {
+        const ncclResult_t nr = nccl().allGather(d, static_cast<char*>(d) + bytes, bytes, ncclChar, c->comm, s);
+        if (nr != ncclSuccess) r = nccl_fail("EP registration all-gather", nr);
+        err = cudaStreamSynchronize(s);
+    }
+    if (err == cudaSuccess && r == HMOE_OK)
+        err = cudaMemcpy(all, static_cast<char*>(d) + bytes, bytes * c->size, cudaMemcpyDeviceToHost);
+    if (s) cudaStreamDestroy(s);
+    if (d) cudaFree(d);
+    if (err != cudaSuccess && r == HMOE_OK) {
+        set_last_error("hmoe EP registration", err);
+        r = HMOE_CUDA_ERROR;
+    }
+    return r;
 }
 
 } // namespace
@@ -318,6 +703,7 @@ hmoe_status hmoe_ep_comm_destroy(hmoe_ep_comm* c) {
         const ncclResult_t r = nccl().commDestroy(c->comm);
         if (r != ncclSuccess) st = nccl_fail("ncclCommDestroy", r);
     }
+    unregister_peers(c);
     if (c->counts_ready) cudaEventDestroy(c->counts_ready);
     if (c->d_expert_of_slot) cudaFree(c->d_expert_of_slot);
     if (c->host_counts) cudaFreeHost(c->host_counts);
@@ -387,7 +773,130 @@ hmoe_status hmoe_ep_balanced_placement(const double* load, uint32_t experts, int
 
 hmoe_status hmoe_ep_last_plan(const hmoe_ep_comm* comm, hmoe_ep_plan_t* plan) {
     if (!comm || !plan) return HMOE_INVALID_ARGUMENT;
-    *plan = comm->last_plan;
+    if (!comm->last_peer) {
+        *plan = comm->last_plan;
+        return HMOE_OK;
+    }
+    // peer path: the plan lives on the device; rebuild it from the
+    // exchanged counts (waits for the device)
+    const size_t n = static_cast<size_t>(comm->size) * comm->last_E;
+    int32_t counts[HMOE_EP_MAX_RANKS * kEpMaxExperts];
+    cudaError_t err = cudaDeviceSynchronize();
+    if (err == cudaSuccess)
+        err = cudaMemcpy(counts, static_cast<const char*>(comm->reg_ws) + comm->last_counts_off +
+                                     static_cast<size_t>(comm->last_parity) * n * 4,
+                         n * 4, cudaMemcpyDeviceToHost);
+    if (err != cudaSuccess) {
+        set_last_error("hmoe EP last plan", err);
+        return HMOE_CUDA_ERROR;
+    }
+    return hmoe_ep_plan(counts, comm->last_E, comm->last_k, comm->size, comm->rank, comm->last_max_tokens, plan);
+}
+
+hmoe_status hmoe_ep_register_workspace(hmoe_ep_comm* comm, void* workspace, size_t bytes) {
+    if (!comm || comm->broken || !comm->comm) return HMOE_INVALID_ARGUMENT;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev != comm->device) return HMOE_INVALID_ARGUMENT;
+    if (workspace && (bytes < kEpSyncBytes || reinterpret_cast<uintptr_t>(workspace) % 256)) return HMOE_INVALID_ARGUMENT;
+    // Every rank's earlier work is done before any rank touches the flags.
+    cudaError_t err = cudaDeviceSynchronize();
+    if (err != cudaSuccess) {
+        set_last_error("hmoe EP registration", err);
+        return HMOE_CUDA_ERROR;
+    }
+    unregister_peers(comm);
+    PeerEntry mine{};
+    int ok = 1;
+    if (workspace) {
+        char* base = nullptr;
+        size_t n = 0;
+        ok = allocation_range(workspace, &base, &n) &&
+             cudaIpcGetMemHandle(&mine.handle, base) == cudaSuccess &&
+             cudaMemset(workspace, 0, kEpSyncBytes) == cudaSuccess && cudaDeviceSynchronize() == cudaSuccess;
+        mine.offset = static_cast<uint64_t>(static_cast<char*>(workspace) - base);
+        mine.bytes = ok ? bytes : 0;
+    }
+    PeerEntry all[HMOE_EP_MAX_RANKS];
+    hmoe_status r = allgather_host(comm, &mine, all, sizeof(PeerEntry));
+    if (r != HMOE_OK) return r;
+    if (!workspace) return HMOE_OK; // collective unregistration
+    // Every rank registers the same size (same layer and max_tokens), or
+    // none uses the peer path.
+    for (int q = 0; q < comm->size; ++q)
+        if (all[q].bytes != bytes) {
+            set_last_error_text("hmoe EP registration: the ranks' workspaces differ or one failed to export");
+            return HMOE_UNSUPPORTED;
+        }
+    hmoe_status res = HMOE_OK;
+    for (int q = 0; q < comm->size && res == HMOE_OK; ++q) {
+        if (q == comm->rank) {
+            comm->peer_ws[q] = static_cast<char*>(workspace);
+            continue;
+        }
+        void* p = nullptr;
+        err = cudaIpcOpenMemHandle(&p, all[q].handle, cudaIpcMemLazyEnablePeerAccess);
+        if (err != cudaSuccess) {
+            set_last_error("hmoe EP registration: cudaIpcOpenMemHandle", err);
+            res = HMOE_UNSUPPORTED;
+            break;
+        }
+        comm->peer_base[q] = p;
+        comm->peer_ws[q] = static_cast<char*>(p) + all[q].offset;
+    }
+    if (res == HMOE_OK) {
+        err = cudaMalloc(&comm->d_peer_ws, sizeof(char*) * comm->size);
+        if (err == cudaSuccess)
+            err = cudaMemcpy(comm->d_peer_ws, comm->peer_ws, sizeof(char*) * comm->size, cudaMemcpyHostToDevice);
+        if (err != cudaSuccess) {
+            set_last_error("hmoe EP registration", err);
+            res = HMOE_CUDA_ERROR;
+        }
+    }
+    // Every rank learns whether every other rank mapped all peers.
+    int32_t flag = res == HMOE_OK ? 1 : 0, flags[HMOE_EP_MAX_RANKS];
+    r = allgather_host(comm, &flag, flags, sizeof(flag));
+    if (r != HMOE_OK) res = r;
+    for (int q = 0; q < comm->size && res == HMOE_OK; ++q)
+        if (!flags[q]) {
+            set_last_error_text("hmoe EP registration: a peer could not map every workspace");
+            res = HMOE_UNSUPPORTED;
+        }
+    if (res != HMOE_OK) {
+        unregister_peers(comm);
+        return res;
+    }
+    comm->reg_ws = workspace;
+    comm->reg_bytes = bytes;
+    comm->epoch = 0;
+    return HMOE_OK;
+}
+
+hmoe_status hmoe_ep_read_status(void* workspace, int32_t* status, int32_t* near_ties, int32_t* sequential_logits,
+                                void* stream) {
+    if (!workspace) return HMOE_INVALID_ARGUMENT;
+    return hmoe_read_status(static_cast<char*>(workspace) + kEpSyncBytes, status, near_ties, sequential_logits,
+                            stream);
+}
+
+hmoe_status hmoe_ep_selftest_flag_wait(hmoe_ep_comm* comm, uint64_t limit_ns, int32_t* status) {
+    if (!comm || !status || !comm->reg_ws) return HMOE_INVALID_ARGUMENT;
+    // waits for an epoch no rank will reach: the bounded wait must give up
+    auto* st = reinterpret_cast<DeviceStatus*>(static_cast<char*>(comm->reg_ws) + kEpPlanOff + sizeof(EpDevPlan));
+    static_assert(kEpPlanOff + sizeof(EpDevPlan) + sizeof(DeviceStatus) <= kEpSyncBytes, "self-test status slot");
+    cudaError_t err = cudaMemset(st, 0, sizeof(DeviceStatus));
+    const PeerCtx c{comm->d_peer_ws, comm->size, comm->rank, comm->epoch + (1ull << 40), limit_ns, st};
+    if (err == cudaSuccess) {
+        ep_wait_kernel<<<1, 32>>>(c, 1);
+        err = cudaGetLastError();
+    }
+    DeviceStatus host{};
+    if (err == cudaSuccess) err = cudaDeviceSynchronize();
+    if (err == cudaSuccess) err = cudaMemcpy(&host, st, sizeof(host), cudaMemcpyDeviceToHost);
+    if (err != cudaSuccess) {
+        set_last_error("hmoe EP flag-wait self-test", err);
+        return HMOE_CUDA_ERROR;
+    }
+    *status = host.status;
     return HMOE_OK;
 }
 
@@ -415,8 +924,13 @@ hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm,
     if (cudaGetDevice(&dev) != cudaSuccess || dev != comm->device) return HMOE_INVALID_ARGUMENT;
     const EpWorkspace w = plan_ep(*desc, max_tokens);
     if (workspace_bytes < w.total) return HMOE_WORKSPACE_TOO_SMALL;
+    if (comm->reg_ws && workspace == comm->reg_ws)
+        return ep_forward_peer(desc, comm, x, y, tokens, max_tokens, static_cast<char*>(workspace), w,
+                               as_stream(stream));
+    comm->last_peer = false;
     const NcclApi& N = nccl();
     char* ws = static_cast<char*>(workspace);
+    char* wsl = ws + kEpSyncBytes; // the single-GPU layout
     cudaStream_t s = as_stream(stream);
     const int E = static_cast<int>(desc->experts), S = static_cast<int>(desc->shared_experts);
     const int k = static_cast<int>(desc->top_k), P = comm->size;
@@ -430,13 +944,13 @@ hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm,
     if (placed && comm->placement_experts != desc->experts) return HMOE_INVALID_ARGUMENT;
     auto* slot_counts = reinterpret_cast<int32_t*>(ws + w.slot_counts);
     stage(0, s);
-    hmoe_status r = enqueue_route(*desc, x, tokens, ws, w.local, true, s, placed ? comm->d_expert_of_slot : nullptr,
+    hmoe_status r = enqueue_route(*desc, x, tokens, wsl, w.local, true, s, placed ? comm->d_expert_of_slot : nullptr,
                                   placed ? slot_counts : nullptr);
     if (r != HMOE_OK) return r;
 
     // 2. counts of every (source, slot), read once on the host
     auto* counts_all = reinterpret_cast<int32_t*>(ws + w.counts_all);
-    ncclResult_t nr = N.allGather(placed ? static_cast<void*>(slot_counts) : static_cast<void*>(ws + w.local.counts),
+    ncclResult_t nr = N.allGather(placed ? static_cast<void*>(slot_counts) : static_cast<void*>(wsl + w.local.counts),
                                   counts_all, static_cast<size_t>(E), ncclInt32, comm->comm, s);
     if (nr != ncclSuccess) return nccl_fail("EP count all-gather", nr);
     cudaError_t err = cudaMemcpyAsync(comm->host_counts, counts_all, static_cast<size_t>(P) * E * 4,
@@ -455,10 +969,10 @@ hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm,
     comm->last_plan = plan;
 
     // 3. dispatch rows and routing weights to the expert owners
-    auto* xperm = reinterpret_cast<__half*>(ws + w.local.xperm);
-    auto* wperm = reinterpret_cast<float*>(ws + w.local.perm_weight);
-    auto* sperm = reinterpret_cast<float*>(ws + w.local.xscale);
-    auto* yrows = reinterpret_cast<__nv_bfloat16*>(ws + w.local.yrows);
+    auto* xperm = reinterpret_cast<__half*>(wsl + w.local.xperm);
+    auto* wperm = reinterpret_cast<float*>(wsl + w.local.perm_weight);
+    auto* sperm = reinterpret_cast<float*>(wsl + w.local.xscale);
+    auto* yrows = reinterpret_cast<__nv_bfloat16*>(wsl + w.local.yrows);
     auto* xin = reinterpret_cast<__half*>(ws + w.xin);
     auto* win = reinterpret_cast<float*>(ws + w.win);
     auto* scale_in = reinterpret_cast<float*>(ws + w.scale_in);
@@ -487,7 +1001,7 @@ hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm,
     // 4. this rank's experts over the received (source, expert) segments
     const int Eloc = static_cast<int>(plan.local_experts);
     const int rin = static_cast<int>(plan.recv_total);
-    ExpertRun run = local_run(*desc, tokens, ws, w.local);
+    ExpertRun run = local_run(*desc, tokens, wsl, w.local);
     run.experts = Eloc + S;
     if (rin > 0) {
         ExpertRun in = run;
@@ -521,7 +1035,7 @@ hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm,
     if (S > 0 && tokens > 0) {
         ExpertRun sh = run;
         sh.tile_cap = tile_capacity_for(static_cast<long>(tokens) * S, S);
-        const SegSpec seg{reinterpret_cast<int32_t*>(ws + w.local.offsets) + E, nullptr, 0, S, S, Eloc, 0};
+        const SegSpec seg{reinterpret_cast<int32_t*>(wsl + w.local.offsets) + E, nullptr, 0, S, S, Eloc, 0};
         r = launch_tile_list(seg, const_cast<int4*>(sh.tiles), const_cast<int32_t*>(sh.tile_count), sh.tile_cap, s);
         if (r == HMOE_OK) r = run_experts(sh, use_gemv(static_cast<long>(tokens) * S, sh.H, sh.I), false, s);
         if (r != HMOE_OK) return r;
@@ -540,8 +1054,8 @@ hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm,
     if (ge2 != ncclSuccess) return nccl_fail("EP return", ge2);
 
     // 6. combine in ascending expert id
-    r = launch_combine(yrows, reinterpret_cast<int32_t*>(ws + w.local.inv),
-                       placed ? reinterpret_cast<uint32_t*>(ws + w.local.ids) : nullptr, k, E,
+    r = launch_combine(yrows, reinterpret_cast<int32_t*>(wsl + w.local.inv),
+                       placed ? reinterpret_cast<uint32_t*>(wsl + w.local.ids) : nullptr, k, E,
                        static_cast<int>(tokens), slots, static_cast<int>(H), y, s);
     stage(5, s);
     return r;

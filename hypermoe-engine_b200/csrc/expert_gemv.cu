@@ -224,12 +224,13 @@ cudaError_t launch_gemv_variant(cudaLaunchConfig_t& cfg, const CUtensorMap& m0, 
     return cudaLaunchKernelEx(&cfg, expert_gemv_kernel<GATE_UP, TOK>, m0, m1, args, kc);
 }
 
-// Split of K over the cluster: enough CTAs for about two per SM, at most 8
-// per cluster, and at most kVMaxKc rows per CTA.
-int gemv_split(int capacity, int col_blocks, int K) {
-    int ks = 1;
-    while (ks < 8 && static_cast<long>(capacity) * col_blocks * ks < 2L * device_sm_count()) ks *= 2;
-    while (ks < 8 && (K + ks - 1) / ks > kVMaxKc) ks *= 2;
+// Split of K over the cluster: 8 CTAs (fewer only when a CTA would get
+// under one box of rows).  It depends on K alone, so a row's result does not
+// depend on how many tiles the launch covers (the expert-parallel path sizes
+// its launches by capacity, the single-GPU path by the batch).
+int gemv_split(int K) {
+    int ks = 8;
+    while (ks > 1 && (K + ks - 1) / ks < kVRows) ks /= 2;
     return ks;
 }
 
@@ -238,7 +239,7 @@ hmoe_status launch_gemv(bool gate_up, const ExpertRun& r, const CUtensorMap& m0,
     if (r.tile_cap <= 0) return HMOE_OK;
     if (r.tile_cap > 65535) return HMOE_UNSUPPORTED;
     const int col_blocks = (g.N + kVCols - 1) / kVCols;
-    g.KS = gemv_split(r.tile_cap, col_blocks, g.K);
+    g.KS = gemv_split(g.K);
     int kc = (g.K + g.KS - 1) / g.KS;
     kc = (kc + kVRows - 1) / kVRows * kVRows;
     if (kc > kVMaxKc) return HMOE_UNSUPPORTED;

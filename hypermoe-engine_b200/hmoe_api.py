@@ -41,7 +41,8 @@ EXPORTS = [
     "hmoe_ep_expert_range", "hmoe_ep_plan", "hmoe_ep_unique_id", "hmoe_ep_comm_create",
     "hmoe_ep_comm_destroy", "hmoe_ep_workspace_size", "hmoe_ep_moe_forward", "hmoe_ep_last_plan",
     "hmoe_moe_forward_noalloc", "hmoe_selftest_bounded_wait", "hmoe_ep_set_placement",
-    "hmoe_ep_balanced_placement", "hmoe_set_route_variant",
+    "hmoe_ep_balanced_placement", "hmoe_set_route_variant", "hmoe_ep_register_workspace",
+    "hmoe_ep_selftest_flag_wait", "hmoe_ep_read_status",
 ]
 EP_MAX_RANKS = 64
 EP_UNIQUE_ID_BYTES = 128
@@ -126,6 +127,9 @@ def lib() -> ctypes.CDLL:
             "hmoe_ep_workspace_size": [ctypes.POINTER(LayerDesc), sz, ctypes.POINTER(sz)],
             "hmoe_ep_moe_forward": [ctypes.POINTER(LayerDesc), vp, vp, vp, sz, sz, vp, sz, vp],
             "hmoe_ep_last_plan": [vp, ctypes.POINTER(EpPlan)],
+            "hmoe_ep_register_workspace": [vp, vp, sz],
+            "hmoe_ep_selftest_flag_wait": [vp, ctypes.c_uint64, ctypes.POINTER(i32)],
+            "hmoe_ep_read_status": [vp, ctypes.POINTER(i32), ctypes.POINTER(i32), ctypes.POINTER(i32), vp],
             "hmoe_moe_forward_noalloc": [ctypes.POINTER(LayerDesc), vp, vp, sz, vp],
             "hmoe_selftest_bounded_wait": [vp, ctypes.c_uint32, vp],
             "hmoe_ep_set_placement": [vp, vp, ctypes.c_uint32],
@@ -432,6 +436,16 @@ class EpComm:
         check("hmoe_ep_last_plan", lib().hmoe_ep_last_plan(self.handle, ctypes.byref(plan)))
         return plan
 
+    def register_workspace(self, ws) -> None:
+        """Collective: peer-memory path for this workspace (None unregisters)."""
+        check("hmoe_ep_register_workspace", lib().hmoe_ep_register_workspace(
+            self.handle, ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0))
+
+    def selftest_flag_wait(self, limit_ns: int) -> int:
+        st = ctypes.c_int32()
+        check("hmoe_ep_selftest_flag_wait", lib().hmoe_ep_selftest_flag_wait(self.handle, limit_ns, ctypes.byref(st)))
+        return st.value
+
     def close(self):
         if self.handle:
             h, self.handle = self.handle, None
@@ -441,11 +455,14 @@ class EpComm:
 class EpLayer(DeviceLayer):
     """This rank's share of an expert-parallel layer on the current device."""
 
-    def __init__(self, host: HostLayer, comm: EpComm, device="cuda", slot_of_expert=None):
+    def __init__(self, host: HostLayer, comm: EpComm, device="cuda", slot_of_expert=None, peer: bool = True):
+        """peer: register the workspace for the peer-memory path (collective;
+        every rank must pass the same value); False keeps the NCCL path."""
         super().__init__(local_host_layer(host, comm.size, comm.rank, slot_of_expert), device)
         comm.set_placement(slot_of_expert)
         self.full_host = host
         self.comm = comm
+        self.peer = peer
         self.desc.ep_rank, self.desc.ep_size = comm.rank, comm.size
 
     def ep_workspace(self, max_tokens: int):
@@ -454,8 +471,17 @@ class EpLayer(DeviceLayer):
         check("hmoe_ep_workspace_size", lib().hmoe_ep_workspace_size(ctypes.byref(self.desc), max_tokens,
                                                                      ctypes.byref(n)))
         if self._ws is None or self._ws.numel() < n.value:
+            # every rank sizes the same, so every rank re-registers together
             self._ws = torch.empty(n.value, dtype=torch.uint8, device=self.arena.device)
+            if self.peer:
+                self.comm.register_workspace(self._ws)
         return self._ws
+
+    def read_status(self, stream=None):
+        st, ties, seq = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        check("hmoe_ep_read_status", lib().hmoe_ep_read_status(
+            self._ws.data_ptr(), ctypes.byref(st), ctypes.byref(ties), ctypes.byref(seq), _stream(stream)))
+        return st.value, ties.value, seq.value
 
     def forward(self, x, y=None, stream=None, max_tokens: Optional[int] = None):
         import torch

@@ -330,6 +330,33 @@ hmoe_status hmoe_ep_balanced_placement(const double *load, uint32_t experts,
  * (observability: received rows, per-peer transfer sizes). */
 hmoe_status hmoe_ep_last_plan(const hmoe_ep_comm *comm, hmoe_ep_plan_t *plan);
 
+/* Collective: maps this rank's EP workspace (from cudaMalloc, the size
+ * hmoe_ep_workspace_size returns, the same on every rank) into every other
+ * rank's process (CUDA IPC over NVLink/NVSwitch) and every other rank's into
+ * this one.  hmoe_ep_moe_forward called with exactly this workspace then
+ * runs the peer-memory path: the count exchange, the dispatch of rows and
+ * the return of expert outputs are stores into the peers' memory ordered by
+ * epoch flags, with no host synchronisation and no NCCL; any other
+ * workspace takes the NCCL path.  Waits for the device first; NULL
+ * unregisters (also collective).  HMOE_UNSUPPORTED on every rank when any
+ * rank cannot map every workspace.  Each flag wait gives up after the
+ * communicator's timeout and reports HMOE_TIMEOUT in the status word
+ * (hmoe_read_status on the workspace's single-GPU part). */
+hmoe_status hmoe_ep_register_workspace(hmoe_ep_comm *comm, void *workspace,
+                                       size_t bytes);
+
+/* hmoe_read_status for an EP workspace (its single-GPU part follows the
+ * peer path's flag area). */
+hmoe_status hmoe_ep_read_status(void *workspace, int32_t *status,
+                                int32_t *near_ties, int32_t *sequential_logits,
+                                void *stream);
+
+/* Self-test of the peer path's bounded flag wait (registered workspace
+ * needed): waits for a flag epoch no rank reaches, with the given limit,
+ * and returns the status the wait reported (HMOE_TIMEOUT).  Synchronous. */
+hmoe_status hmoe_ep_selftest_flag_wait(hmoe_ep_comm *comm, uint64_t limit_ns,
+                                       int32_t *status);
+
 /* Scratch bytes of hmoe_ep_moe_forward for up to max_tokens tokens on
  * every rank (the receive side holds ep_size*max_tokens*top_k rows, the
  * worst case of every token of every rank choosing this rank's experts). */
@@ -339,8 +366,9 @@ hmoe_status hmoe_ep_workspace_size(const hmoe_layer_desc *desc,
 /* Collective: one MoE layer forward of this rank's `tokens` tokens
  * (0 allowed) with experts spread over the communicator's ranks.  Every
  * rank passes the same desc (except arena/quant/ep_rank) and the same
- * max_tokens.  Enqueues on `stream` and synchronises on the host once, to
- * read the exchanged row counts (bounded by the communicator's timeout).
+ * max_tokens.  Enqueues on `stream`; without a registered workspace it
+ * synchronises on the host once, to read the exchanged row counts (bounded
+ * by the communicator's timeout).
  * The result equals hmoe_moe_forward on the concatenation of all ranks'
  * tokens for the same expert-MLP variant. */
 hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc *desc,

@@ -1,8 +1,10 @@
 """Expert parallelism on the GPU through the C ABI (hmoe_ep_*).
 
-* One GPU: a communicator of one rank runs the whole EP path (count
-  all-gather, host plan, NCCL send/recv to itself, received-segment tiles,
-  return, combine); its output must equal hmoe_moe_forward bit for bit.
+* One GPU: a communicator of one rank runs the whole EP path -- the
+  peer-memory path (registered workspace: device count exchange and plan,
+  row stores, epoch flags) and the NCCL path (count all-gather, host plan,
+  send/recv to itself) -- through received-segment tiles, return and
+  combine; its output must equal hmoe_moe_forward bit for bit.
 * Two or more GPUs: two ranks, one process per GPU, each with its own
   slice of the batch and half of the experts; every rank's output must equal
   the single-GPU hmoe_moe_forward on the concatenated batch bit for bit
@@ -39,11 +41,12 @@ def _single_gpu(hl, x, dev, variant):
         H.set_variant(0)
 
 
+@pytest.mark.parametrize("peer", [True, False])
 @pytest.mark.parametrize("cfg_name,T,variant,placed", [("c3", 256, 0, False), ("c3", 256, 2, False),
                                                        ("c3", 1, 0, False), ("c2", 33, 2, False),
                                                        ("c1", 64, 1, False), ("c3", 256, 2, True),
                                                        ("c2", 33, 2, True)])
-def test_ep_one_rank_equals_forward(cuda, cfg_name, T, variant, placed):
+def test_ep_one_rank_equals_forward(cuda, cfg_name, T, variant, placed, peer):
     import torch
     cfg = H.CONFIGS[cfg_name]
     hl = H.make_host_layer(cfg, seed=3)
@@ -55,11 +58,13 @@ def test_ep_one_rank_equals_forward(cuda, cfg_name, T, variant, placed):
         # a scrambled placement: groups travel in slot order, rows still
         # combine in ascending expert id
         pl = np.random.default_rng(3).permutation(cfg.experts).astype(np.int32) if placed else None
-        layer = H.EpLayer(hl, comm, cuda, slot_of_expert=pl)
+        layer = H.EpLayer(hl, comm, cuda, slot_of_expert=pl, peer=peer)
         dx = torch.from_numpy(x).to(cuda)
         y1 = layer.forward(dx, max_tokens=T + 7).cpu().numpy()
         y2 = layer.forward(dx, max_tokens=T + 7).cpu().numpy()
         st, ties, _ = layer.read_status()
+        plan = comm.last_plan()
+        assert plan.recv_total == T * cfg.top_k
     finally:
         H.set_variant(0)
         comm.close()
@@ -76,7 +81,27 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _ep_rank(rank, P, port, cfg_name, Ts, variant, q, balanced=False):
+def test_ep_peer_flag_wait_times_out(cuda):
+    """The peer path's flag wait is bounded: waiting for an epoch no rank
+    reaches gives up after the limit, reports HMOE_TIMEOUT, and the context
+    stays usable."""
+    import torch
+    cfg = H.CONFIGS["c1"]
+    hl = H.make_host_layer(cfg, seed=1)
+    comm = H.EpComm(H.ep_unique_id(), 0, 1, timeout_ms=30000)
+    try:
+        layer = H.EpLayer(hl, comm, cuda)
+        x = torch.from_numpy(H.make_tokens(cfg, 8, seed=1)).to(cuda)
+        layer.forward(x, max_tokens=8)
+        assert comm.selftest_flag_wait(20_000_000) == 5  # HMOE_TIMEOUT
+        y = layer.forward(x, max_tokens=8).cpu().numpy()  # still works
+        assert layer.read_status()[0] == 0
+        assert np.isfinite(y).all()
+    finally:
+        comm.close()
+
+
+def _ep_rank(rank, P, port, cfg_name, Ts, variant, q, balanced=False, peer=True):
     for p in PATHS:
         sys.path.insert(0, p)
     import torch
@@ -103,9 +128,11 @@ def _ep_rank(rank, P, port, cfg_name, Ts, variant, q, balanced=False):
         if balanced:  # placement from the router's popularity prior
             load = np.exp(hl.router_bias.astype(np.float64)) if hl.router_bias is not None else np.ones(cfg.experts)
             pl = H.ep_balanced_placement(load, P)
-        layer = H.EpLayer(hl, comm, dev, slot_of_expert=pl)
+        layer = H.EpLayer(hl, comm, dev, slot_of_expert=pl, peer=peer)
         dx = torch.from_numpy(x_all[t0:t0 + Ts[rank]]).to(dev)
         y = layer.forward(dx, max_tokens=max(Ts)).cpu().numpy()
+        y2 = layer.forward(dx, max_tokens=max(Ts)).cpu().numpy()  # a second epoch
+        assert np.array_equal(y, y2)
         st, ties, _ = layer.read_status()
         q.put((rank, st, y))
     except Exception as exc:
@@ -116,9 +143,12 @@ def _ep_rank(rank, P, port, cfg_name, Ts, variant, q, balanced=False):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("cfg_name,Ts,variant,balanced", [("c3", (300, 212), 2, False), ("c2", (40, 0), 2, False),
-                                                          ("c3", (3, 1), 0, False), ("c3", (300, 212), 2, True)])
-def test_ep_two_gpus_equal_single_gpu(cuda, cfg_name, Ts, variant, balanced):
+@pytest.mark.parametrize("cfg_name,Ts,variant,balanced,peer", [("c3", (300, 212), 2, False, True),
+                                                               ("c2", (40, 0), 2, False, True),
+                                                               ("c3", (3, 1), 0, False, True),
+                                                               ("c3", (300, 212), 2, True, True),
+                                                               ("c3", (300, 212), 2, True, False)])
+def test_ep_two_gpus_equal_single_gpu(cuda, cfg_name, Ts, variant, balanced, peer):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -130,7 +160,8 @@ def test_ep_two_gpus_equal_single_gpu(cuda, cfg_name, Ts, variant, balanced):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ep_rank, args=(r, 2, port, cfg_name, Ts, variant, q, balanced)) for r in range(2)]
+    procs = [ctx.Process(target=_ep_rank, args=(r, 2, port, cfg_name, Ts, variant, q, balanced, peer))
+             for r in range(2)]
     for p in procs:
         p.start()
     out = {}
