@@ -30,6 +30,7 @@
 // (MoERuntime.cpp:58-349).
 #include "common.cuh"
 #include "layer.cuh"
+#include "rows.cuh"
 
 #include <nccl.h> // types and enums only; the functions are resolved with dlsym
 
@@ -178,7 +179,7 @@ struct EpDevPlan {
     int32_t recv_total, sent_total;
 };
 constexpr size_t kEpFlagsBytes = 3 * HMOE_EP_MAX_RANKS * 8;
-constexpr size_t kEpCtrOff = kEpFlagsBytes;           // 2 x int32 CTA-completion counters
+constexpr size_t kEpCtrOff = kEpFlagsBytes;           // int32 CTA-completion counter of the dispatch
 constexpr size_t kEpPlanOff = kEpFlagsBytes + 256;
 constexpr size_t kEpSyncBytes = kEpPlanOff + ((sizeof(EpDevPlan) + 255) / 256) * 256;
 
@@ -244,16 +245,21 @@ bool ep_rows_fit(const hmoe_layer_desc& d, size_t max_tokens) {
 //   ep_exchange_kernel  publish this rank's slot counts into every rank's
 //                       counts (epoch-parity buffer), flag them, wait for
 //                       every rank's, build the transfer plan on the device
-//   ep_copy_rows_kernel dispatch: this rank's FP16 rows, scales and routing
-//                       weights into the owners' receive rows; return: the
-//                       weighted BF16 output rows into the sources' rows;
-//                       the last CTA to finish flags every rank
+//   ep_permute_kernel   the permutation fused with the dispatch: routed FP16
+//                       rows, their scales and routing weights go straight
+//                       into the owners' receive rows; the last CTA to
+//                       finish flags every rank
+//   ep_combine_kernel   the combine fused with the return: each routed row's
+//                       output is read from its owner's output rows once
+//                       every owner has flagged them
 //   ep_wait_kernel      bounded wait for every rank's flag of this epoch
 // A rank can run at most one epoch ahead of another (it needs their counts
 // of the same epoch before it writes anything into their buffers), and a
 // rank publishes the counts of epoch n only after its kernels of epoch
-// n - 1 have run, so receive rows and returned rows are never overwritten
-// while in use; the counts are double-buffered by epoch parity.
+// n - 1 have run.  So receive rows are never overwritten while their owner
+// computes on them, and an owner's output rows of epoch n are rewritten only
+// after every source has combined them (it needs their epoch n + 1 rows
+// first); the counts are double-buffered by epoch parity.
 struct PeerCtx {
     char* const* peer; // [P] every rank's workspace base in this address space
     int P, me;
@@ -372,60 +378,106 @@ __global__ void __launch_bounds__(256) ep_exchange_kernel(PeerCtx c, size_t coun
     }
 }
 
-// Row copies between ranks, a warp per row.  DISPATCH: this rank's permuted
-// rows r < sent_total to rank q (the owner of r's slot) at row
-// dest_base[q] + r - send_off[q] of q's receive rows, with their scale and
-// routing weight.  RETURN: received rows i < recv_total back to their
-// source p at row ret_off[p] + i - recv_base[p] of p's permuted rows.  The
-// last CTA out flags `kind` on every rank.
-struct CopyArgs {
-    const char* src;        // local rows (FP16 or BF16, H elements)
-    size_t dst_off;         // destination rows in every workspace
-    const float* src_a;     // dispatch: scales and weights (else null)
-    const float* src_b;
-    size_t dst_a_off, dst_b_off;
-    int H;
-    int kind;               // 1 dispatch, 2 return
+// Routed rows of this rank live in the expert owners' workspaces: row
+// r < routed (a routed slot; shared-expert rows stay local) belongs to the
+// rank q whose send range holds it, at q's receive row
+// dest_base[q] + r - send_off[q].
+struct PeerRowMap {
+    char* const* peer;
+    int P;
+    int routed;
+    int send_off[HMOE_EP_MAX_RANKS], send_rows[HMOE_EP_MAX_RANKS], dest_base[HMOE_EP_MAX_RANKS];
+    __device__ int owner(int r) const {
+        int q = 0;
+        while (q + 1 < P && r >= send_off[q] + send_rows[q]) ++q;
+        return q;
+    }
 };
 
-__global__ void __launch_bounds__(256) ep_copy_rows_kernel(PeerCtx c, CopyArgs a) {
-    __shared__ int s_off[HMOE_EP_MAX_RANKS], s_rows[HMOE_EP_MAX_RANKS], s_dst[HMOE_EP_MAX_RANKS];
-    __shared__ int s_total;
+// Dispatch fused into the permutation: routed rows go straight into the
+// owners' receive rows (with their scale and routing weight).
+struct PeerRows {
+    const PeerRowMap* map; // shared memory
+    __half* xrows;         // local rows (shared experts)
+    float* xscale;
+    const float* weight;   // perm_weight
+    size_t x_off, s_off, w_off;
+    int H;
+    __device__ RowDst operator()(int r) const {
+        if (r >= map->routed)
+            return RowDst{xrows + static_cast<size_t>(r) * H, xscale + r, nullptr, 0.0f};
+        const int q = map->owner(r);
+        const int d = map->dest_base[q] + r - map->send_off[q];
+        char* b = map->peer[q];
+        return RowDst{reinterpret_cast<__half*>(b + x_off) + static_cast<size_t>(d) * H,
+                      reinterpret_cast<float*>(b + s_off) + d, reinterpret_cast<float*>(b + w_off) + d, weight[r]};
+    }
+};
+
+// Return fused into the combine: a routed row's output is read from its
+// owner's expert-output rows (same receive-row index).
+struct PeerOut {
+    const PeerRowMap* map;
+    const __nv_bfloat16* yrows; // local rows (shared experts)
+    size_t y_off;
+    int H;
+    __device__ const __nv_bfloat16* operator()(int r) const {
+        if (r >= map->routed) return yrows + static_cast<size_t>(r) * H;
+        const int q = map->owner(r);
+        const int d = map->dest_base[q] + r - map->send_off[q];
+        return reinterpret_cast<const __nv_bfloat16*>(map->peer[q] + y_off) + static_cast<size_t>(d) * H;
+    }
+};
+
+__device__ void load_row_map(const PeerCtx& c, int routed, PeerRowMap* m) {
     const EpDevPlan* plan = reinterpret_cast<const EpDevPlan*>(c.peer[c.me] + kEpPlanOff);
-    const bool disp = a.kind == 1;
-    const int tid = threadIdx.x, lane = tid & 31;
-    if (tid < c.P) {
-        s_off[tid] = disp ? plan->send_off[tid] : plan->recv_base[tid];
-        s_rows[tid] = disp ? plan->send_rows[tid] : plan->recv_rows[tid];
-        s_dst[tid] = disp ? plan->dest_base[tid] : plan->ret_off[tid];
+    if (threadIdx.x < c.P) {
+        m->send_off[threadIdx.x] = plan->send_off[threadIdx.x];
+        m->send_rows[threadIdx.x] = plan->send_rows[threadIdx.x];
+        m->dest_base[threadIdx.x] = plan->dest_base[threadIdx.x];
     }
-    if (tid == 0) s_total = disp ? plan->sent_total : plan->recv_total;
+    if (threadIdx.x == 0) {
+        m->peer = c.peer;
+        m->P = c.P;
+        // rows past the plan's routed total (a failed exchange moves nothing)
+        // stay local
+        m->routed = min(routed, plan->sent_total);
+    }
     __syncthreads();
-    const size_t row_bytes = static_cast<size_t>(a.H) * 2;
-    const int vecs = static_cast<int>(row_bytes / 16);
-    const int warps = gridDim.x * (blockDim.x >> 5);
-    int q = 0;
-    for (int r = blockIdx.x * (blockDim.x >> 5) + (tid >> 5); r < s_total; r += warps) {
-        while (q + 1 < c.P && r >= s_off[q] + s_rows[q]) ++q; // rows ascend with q
-        while (q > 0 && r < s_off[q]) --q;
-        const int d = s_dst[q] + r - s_off[q];
-        const uint4* src = reinterpret_cast<const uint4*>(a.src + static_cast<size_t>(r) * row_bytes);
-        uint4* dst = reinterpret_cast<uint4*>(c.peer[q] + a.dst_off + static_cast<size_t>(d) * row_bytes);
-        for (int v = lane; v < vecs; v += 32) dst[v] = src[v];
-        if (a.src_a && lane == 0) {
-            reinterpret_cast<float*>(c.peer[q] + a.dst_a_off)[d] = a.src_a[r];
-            reinterpret_cast<float*>(c.peer[q] + a.dst_b_off)[d] = a.src_b[r];
-        }
-    }
+}
+
+// One CTA per token; the last CTA out flags the dispatch (kind 1) on every
+// rank once every CTA's stores are fenced.
+__global__ void __launch_bounds__(256) ep_permute_kernel(PeerCtx c, const float* __restrict__ x,
+                                                         const int32_t* __restrict__ inv, int slots, int routed, int H,
+                                                         __half* xrows, float* xscale, const float* weight,
+                                                         size_t x_off, size_t s_off, size_t w_off) {
+    __shared__ PeerRowMap map;
+    load_row_map(c, routed, &map);
+    permute_token(x, inv, slots, H, blockIdx.x, PeerRows{&map, xrows, xscale, weight, x_off, s_off, w_off, H});
     __threadfence_system();
     __syncthreads();
-    if (tid == 0) {
-        int* ctr = reinterpret_cast<int*>(c.peer[c.me] + kEpCtrOff) + (a.kind - 1);
+    if (threadIdx.x == 0) {
+        int* ctr = reinterpret_cast<int*>(c.peer[c.me] + kEpCtrOff);
         if (atomicAdd(ctr, 1) == static_cast<int>(gridDim.x) - 1) {
             *ctr = 0;
-            signal_all(c, a.kind);
+            signal_all(c, 1);
         }
     }
+}
+
+// No rows to dispatch (this rank has no tokens): flag the dispatch anyway.
+__global__ void ep_signal_kernel(PeerCtx c, int kind) {
+    if (threadIdx.x == 0) signal_all(c, kind);
+}
+
+__global__ void __launch_bounds__(256) ep_combine_kernel(PeerCtx c, const int32_t* __restrict__ inv,
+                                                         const uint32_t* __restrict__ ids, int k, int E, int slots,
+                                                         int routed, int H, const __nv_bfloat16* yrows, size_t y_off,
+                                                         float* __restrict__ out) {
+    __shared__ PeerRowMap map;
+    load_row_map(c, routed, &map);
+    combine_token(inv, ids, k, E, slots, H, blockIdx.x, out, PeerOut{&map, yrows, y_off, H});
 }
 
 // Peer-memory forward (workspace == comm->reg_ws); the steps of
@@ -455,22 +507,27 @@ hmoe_status ep_forward_peer(const hmoe_layer_desc* desc, hmoe_ep_comm* comm, con
                     static_cast<uint64_t>(std::min(comm->timeout_ms, 10000)) * 1000000ull, st};
     const int rin_cap = static_cast<int>(static_cast<size_t>(P) * max_tokens * desc->top_k);
 
-    // 1. route, group and permute this rank's tokens
+    // 1. route and group this rank's tokens
     stage(0, s);
-    hmoe_status r = enqueue_route(*desc, x, tokens, wsl, w.local, true, s, placed ? comm->d_expert_of_slot : nullptr,
-                                  placed ? slot_counts : nullptr);
+    hmoe_status r = enqueue_route(*desc, x, tokens, wsl, w.local, false, s,
+                                  placed ? comm->d_expert_of_slot : nullptr, placed ? slot_counts : nullptr);
     if (r != HMOE_OK) return r;
     // 2. counts of every (source, slot) and the transfer plan, on the device
     const int32_t* my_counts = placed ? slot_counts : reinterpret_cast<const int32_t*>(wsl + w.local.counts);
     ep_exchange_kernel<<<1, 256, 0, s>>>(c, w.counts_all, my_counts, E, parity, rin_cap);
     r = check_launch("hmoe EP count exchange");
     if (r != HMOE_OK) return r;
-    // 3. dispatch FP16 rows, scales and routing weights to the owners
-    const int copy_grid = device_sm_count() * 4;
-    CopyArgs da{wsl + w.local.xperm, w.xin, reinterpret_cast<const float*>(wsl + w.local.xscale),
-                reinterpret_cast<const float*>(wsl + w.local.perm_weight), w.scale_in, w.win, static_cast<int>(H), 1};
-    ep_copy_rows_kernel<<<copy_grid, 256, 0, s>>>(c, da);
-    r = check_launch("hmoe EP dispatch");
+    // 3. permutation fused with the dispatch: routed FP16 rows, their scales
+    // and routing weights straight into the owners' receive rows
+    const int routed = static_cast<int>(tokens) * k;
+    if (tokens > 0)
+        ep_permute_kernel<<<static_cast<unsigned>(tokens), 256, 0, s>>>(
+            c, x, reinterpret_cast<const int32_t*>(wsl + w.local.inv), slots, routed, static_cast<int>(H),
+            reinterpret_cast<__half*>(wsl + w.local.xperm), reinterpret_cast<float*>(wsl + w.local.xscale),
+            reinterpret_cast<const float*>(wsl + w.local.perm_weight), w.xin, w.scale_in, w.win);
+    else
+        ep_signal_kernel<<<1, 32, 0, s>>>(c, 1);
+    r = check_launch("hmoe EP permute + dispatch");
     if (r != HMOE_OK) return r;
     uint32_t first = 0, Eloc_u = 0;
     hmoe_ep_expert_range(desc->experts, P, comm->rank, &first, &Eloc_u);
@@ -493,14 +550,7 @@ hmoe_status ep_forward_peer(const hmoe_layer_desc* desc, hmoe_ep_comm* comm, con
     const SegSpec seg{nullptr, counts_all + first, E, P * Eloc, Eloc, 0, 0};
     r = launch_tile_list(seg, const_cast<int4*>(in.tiles), const_cast<int32_t*>(in.tile_count), in.tile_cap, s);
     if (r != HMOE_OK) return r;
-    ep_wait_kernel<<<1, 32, 0, s>>>(c, 1);
-    r = check_launch("hmoe EP dispatch wait");
-    if (r != HMOE_OK) return r;
-    stage(2, s);
-    // 4. this rank's experts over the received (source, expert) segments
-    r = run_experts(in, use_gemv(rin_cap, in.H, in.I), true, s);
-    if (r != HMOE_OK) return r;
-    if (S > 0 && tokens > 0) { // shared experts on the rank's own rows
+    if (S > 0 && tokens > 0) { // shared experts on the rank's own rows, while the rows arrive
         ExpertRun sh = run;
         sh.tile_cap = tile_capacity_for(static_cast<long>(tokens) * S, S);
         const SegSpec sseg{reinterpret_cast<int32_t*>(wsl + w.local.offsets) + E, nullptr, 0, S, S, Eloc, 0};
@@ -508,18 +558,28 @@ hmoe_status ep_forward_peer(const hmoe_layer_desc* desc, hmoe_ep_comm* comm, con
         if (r == HMOE_OK) r = run_experts(sh, use_gemv(static_cast<long>(tokens) * S, sh.H, sh.I), false, s);
         if (r != HMOE_OK) return r;
     }
-    // 5. weighted BF16 outputs back to their source rows
-    CopyArgs ra{ws + w.yin, w.local.yrows + kEpSyncBytes, nullptr, nullptr, 0, 0, static_cast<int>(H), 2};
-    ep_copy_rows_kernel<<<copy_grid, 256, 0, s>>>(c, ra);
-    r = check_launch("hmoe EP return");
+    ep_wait_kernel<<<1, 32, 0, s>>>(c, 1);
+    r = check_launch("hmoe EP dispatch wait");
+    if (r != HMOE_OK) return r;
+    stage(2, s);
+    // 4. this rank's experts over the received (source, expert) segments
+    r = run_experts(in, use_gemv(rin_cap, in.H, in.I), true, s);
+    if (r != HMOE_OK) return r;
+    // 5. the outputs are ready for their sources
+    ep_signal_kernel<<<1, 32, 0, s>>>(c, 2);
+    r = check_launch("hmoe EP return signal");
     if (r != HMOE_OK) return r;
     ep_wait_kernel<<<1, 32, 0, s>>>(c, 2);
     r = check_launch("hmoe EP return wait");
     if (r != HMOE_OK) return r;
-    // 6. combine in ascending expert id
-    r = launch_combine(reinterpret_cast<__nv_bfloat16*>(wsl + w.local.yrows), reinterpret_cast<int32_t*>(wsl + w.local.inv),
-                       placed ? reinterpret_cast<uint32_t*>(wsl + w.local.ids) : nullptr, k, E,
-                       static_cast<int>(tokens), slots, static_cast<int>(H), y, s);
+    // 6. combine fused with the return: each routed row is read from its
+    // owner's output rows, in ascending expert id
+    if (tokens > 0)
+        ep_combine_kernel<<<static_cast<unsigned>(tokens), 256, 0, s>>>(
+            c, reinterpret_cast<const int32_t*>(wsl + w.local.inv),
+            placed ? reinterpret_cast<const uint32_t*>(wsl + w.local.ids) : nullptr, k, E, slots, routed,
+            static_cast<int>(H), reinterpret_cast<const __nv_bfloat16*>(wsl + w.local.yrows), w.yin, y);
+    r = check_launch("hmoe EP combine");
     stage(5, s);
     return r;
 }

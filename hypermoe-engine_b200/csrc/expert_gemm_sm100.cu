@@ -47,6 +47,7 @@
 //
 #include "common.cuh"
 #include "layer.cuh"
+#include "rows.cuh"
 #include "sm100.cuh"
 
 #include <cudaTypedefs.h>
@@ -570,43 +571,20 @@ __global__ void __launch_bounds__(kMaxSegments) tile_list_kernel(SegSpec sp, int
     if (i == 0) *tile_count = min(capacity, total_full_s + parts_s);
 }
 
-// Token-major permutation: token t's FP32 row is read once, scaled by the
-// power of two s_t that puts its largest magnitude in [2^14, 2^15),
-// converted to FP16 (11-bit significand, no overflow) and written to each of
-// its rows inv[t, 0..slots); 1/s_t is stored per row for the epilogues.
+// Token-major permutation (permute_token) into this GPU's rows.
+struct LocalRows {
+    __half* xrows;
+    float* xscale;
+    int H;
+    __device__ RowDst operator()(int r) const {
+        return RowDst{xrows + static_cast<size_t>(r) * H, xscale + r, nullptr, 0.0f};
+    }
+};
+
 __global__ void __launch_bounds__(256) permute_kernel(const float* __restrict__ x, const int32_t* __restrict__ inv,
                                                       int slots, int H, __half* __restrict__ xrows,
                                                       float* __restrict__ xscale) {
-    __shared__ int rows_s[kMaxSlots];
-    __shared__ float red_s[8];
-    const int t = blockIdx.x;
-    for (int s = threadIdx.x; s < slots; s += blockDim.x) rows_s[s] = inv[static_cast<size_t>(t) * slots + s];
-    const float4* src = reinterpret_cast<const float4*>(x + static_cast<size_t>(t) * H);
-    float mx = 0.0f;
-    for (int c = threadIdx.x; c < H / 4; c += blockDim.x) {
-        const float4 v = src[c];
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    if ((threadIdx.x & 31) == 0) red_s[threadIdx.x >> 5] = mx;
-    __syncthreads();
-    mx = red_s[0];
-    for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) mx = fmaxf(mx, red_s[w]);
-    int ex = 0;
-    if (mx > 0.0f && isfinite(mx)) frexpf(mx, &ex); // mx = m * 2^ex, m in [0.5, 1)
-    const int sh = (mx > 0.0f && isfinite(mx)) ? max(-126, min(126, 15 - ex)) : 0;
-    const float sc = ldexpf(1.0f, sh), isc = ldexpf(1.0f, -sh);
-    for (int s = threadIdx.x; s < slots; s += blockDim.x) xscale[rows_s[s]] = isc;
-    for (int c = threadIdx.x; c < H / 8; c += blockDim.x) {
-        const float4 v0 = src[2 * c], v1 = src[2 * c + 1];
-        const __half2 h0 = __floats2half2_rn(v0.x * sc, v0.y * sc), h1 = __floats2half2_rn(v0.z * sc, v0.w * sc);
-        const __half2 h2 = __floats2half2_rn(v1.x * sc, v1.y * sc), h3 = __floats2half2_rn(v1.z * sc, v1.w * sc);
-        const uint4 o = make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
-                                   *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
-        for (int s = 0; s < slots; ++s)
-            reinterpret_cast<uint4*>(xrows + static_cast<size_t>(rows_s[s]) * H)[c] = o;
-    }
+    permute_token(x, inv, slots, H, blockIdx.x, LocalRows{xrows, xscale, H});
 }
 
 // ---------------------------------------------------------------- host

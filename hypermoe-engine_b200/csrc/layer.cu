@@ -25,6 +25,7 @@
 // were split between kernels, launches or GPUs.
 #include "common.cuh"
 #include "layer.cuh"
+#include "rows.cuh"
 
 #include <algorithm>
 #include <climits>
@@ -102,49 +103,18 @@ hmoe_status validate_desc(const hmoe_layer_desc* d) {
 
 // ------------------------------------------------------------- combine
 
-// One CTA per token: gather the token's rows (routed slots, then shared),
-// order them ascending (rows are laid out in ascending expert id, so row
-// order is expert order) and accumulate in that order from zero, as the
-// reference's combine loop does (MoERuntime.cpp:311-325).
+// One CTA per token (combine_token) over this GPU's rows.
+struct LocalOut {
+    const __nv_bfloat16* yrows;
+    int H;
+    __device__ const __nv_bfloat16* operator()(int r) const { return yrows + static_cast<size_t>(r) * H; }
+};
+
 __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ yrows,
                                                       const int32_t* __restrict__ inv,
                                                       const uint32_t* __restrict__ ids, int k, int E, int slots,
                                                       int H, float* __restrict__ out) {
-    __shared__ int rows_s[kMaxSlots];
-    const int t = blockIdx.x;
-    if (threadIdx.x == 0) {
-        int keys[kMaxSlots];
-        int n = 0;
-        for (int s = 0; s < slots; ++s) {
-            const int r = inv[static_cast<size_t>(t) * slots + s];
-            const int key = ids ? (s < k ? static_cast<int>(ids[static_cast<size_t>(t) * k + s]) : E + (s - k)) : r;
-            int j = n++;
-            while (j > 0 && keys[j - 1] > key) {
-                keys[j] = keys[j - 1];
-                rows_s[j] = rows_s[j - 1];
-                --j;
-            }
-            keys[j] = key;
-            rows_s[j] = r;
-        }
-    }
-    __syncthreads();
-    const int H8 = H / 8;
-    for (int c = threadIdx.x; c < H8; c += blockDim.x) {
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int s = 0; s < slots; ++s) {
-            const uint4 v = reinterpret_cast<const uint4*>(yrows + static_cast<size_t>(rows_s[s]) * H)[c];
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                acc[2 * i] = __fadd_rn(acc[2 * i], __uint_as_float(w[i] << 16));
-                acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __uint_as_float(w[i] & 0xffff0000u));
-            }
-        }
-        float4* o = reinterpret_cast<float4*>(out + static_cast<size_t>(t) * H) + 2 * c;
-        o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-        o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
-    }
+    combine_token(inv, ids, k, E, slots, H, blockIdx.x, out, LocalOut{yrows, H});
 }
 
 hmoe_status launch_combine(const __nv_bfloat16* yrows, const int32_t* inv, const uint32_t* ids, int k, int E,
