@@ -474,7 +474,15 @@ class EpLayer(DeviceLayer):
             # every rank sizes the same, so every rank re-registers together
             self._ws = torch.empty(n.value, dtype=torch.uint8, device=self.arena.device)
             if self.peer:
-                self.comm.register_workspace(self._ws)
+                try:
+                    self.comm.register_workspace(self._ws)
+                except HmoeError as exc:
+                    if exc.code != 7:  # HMOE_UNSUPPORTED: some rank cannot map every peer
+                        raise
+                    # returned on every rank alike, so every rank keeps the NCCL path
+                    import warnings
+                    warnings.warn(f"expert parallelism: peer-memory path unavailable ({exc}); using NCCL")
+                    self.peer = False
         return self._ws
 
     def read_status(self, stream=None):
