@@ -61,6 +61,8 @@ Workspace plan_workspace(const hmoe_layer_desc& d, size_t T) {
     // zeroed together with status: routed counts, then per token block
     w.counts = take((E + S) * 4);
     w.block_counts = take(((T + kGroupBlock - 1) / kGroupBlock) * E * 4);
+    w.route_acc_bytes = route_decode_scratch_bytes(T, static_cast<int>(d.hidden), static_cast<int>(E));
+    w.route_acc = take(w.route_acc_bytes); // decode router partials (zeroed)
     w.zero_bytes = off;
     w.offsets = take((E + S + 1) * 4);
     w.ids = take(T * k * 4);
@@ -141,7 +143,8 @@ hmoe_status enqueue_route(const hmoe_layer_desc& d, const float* x, size_t T, ch
                                  reinterpret_cast<uint32_t*>(ws + w.ids),
                                  reinterpret_cast<float*>(ws + w.scores),
                                  reinterpret_cast<int32_t*>(ws + w.counts),
-                                 reinterpret_cast<int32_t*>(ws + w.block_counts), st, s);
+                                 reinterpret_cast<int32_t*>(ws + w.block_counts),
+                                 w.route_acc_bytes ? reinterpret_cast<double*>(ws + w.route_acc) : nullptr, st, s);
     if (r != HMOE_OK) return r;
     stage(1, s);
     r = launch_group(reinterpret_cast<uint32_t*>(ws + w.ids), reinterpret_cast<float*>(ws + w.scores),

@@ -15,7 +15,7 @@ namespace hmoe {
 constexpr int kGroupBlock = 256;
 
 struct Workspace {
-    size_t status, counts, block_counts, zero_bytes, offsets, ids, scores, perm_token, perm_weight, inv;
+    size_t status, counts, block_counts, route_acc, route_acc_bytes, zero_bytes, offsets, ids, scores, perm_token, perm_weight, inv;
     size_t xperm, xscale, hmid, yrows, tiles, tile_count;
     int tile_cap;
     size_t total;
@@ -115,7 +115,10 @@ int tile_capacity_for(long rows, int segments);
 
 hmoe_status launch_route(const float* x, const float* w, const float* bias, int T, int H, int E, int k,
                          int softmax, int renorm, uint32_t* ids, float* scores, int32_t* counts,
-                         int32_t* block_counts, DeviceStatus* st, cudaStream_t stream);
+                         int32_t* block_counts, double* decode_scratch, DeviceStatus* st, cudaStream_t stream);
+// Zeroed scratch bytes the decode router needs for T tokens (0 when it does
+// not take the shape).
+size_t route_decode_scratch_bytes(size_t T, int H, int E);
 // Expert groups in ascending expert id, or in placement-slot order when
 // expert_of_slot is given (then slot_counts[b] = rows of slot b).
 hmoe_status launch_group(const uint32_t* ids, const float* scores, const int32_t* counts,

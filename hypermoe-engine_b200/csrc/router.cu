@@ -1027,6 +1027,151 @@ __global__ void __launch_bounds__(256, 2) route_tiled_kernel(const __grid_consta
     }
 }
 
+// ------------------------------------------------------------ decode router
+//
+// Decode-sized batches (T <= 16).  The per-8-token and tiled kernels split
+// H over at most one cluster, so at T = 1 a handful of CTAs stream the whole
+// router matrix and the SMs wait on that latency.  Here a grid of
+// (H/128) x (E/32) small CTAs each forms FP64 partial dots of all T tokens
+// with 32 experts over 128 hidden rows (lane = expert, warp = 16 rows, the
+// 8 warps added in a fixed order) and adds them to zeroed [T][E] doubles
+// with atomics, together with the norms of the certificate.  Atomic order
+// varies from run to run, but every partial is a rounded sum of exact
+// products with at most 24 + H/128 roundings on any chain, so the rounding
+// certificate holds; certified logits are the reference's exact floats and
+// the rest are settled as in the other kernels, so the result does not
+// depend on that order.  The last CTA to finish (a ticket) certifies,
+// settles and selects.
+constexpr int kDecMaxTokens = 16;
+constexpr int kDecAutoTokens = 2; // chosen automatically up to here (T=1: 22.5 us vs 29.5 us for route_kernel;
+                                  // at T=16 its serial selection tail makes it slower)
+constexpr int kDecRows = 128;  // hidden rows per CTA
+constexpr int kDecCols = 32;   // experts per CTA
+constexpr int kDecSlots = 2;   // staging buffers for settle_logit
+
+struct DecodeArgs {
+    RouteArgs a;
+    double* acc; // [T][E] partial sums (zeroed)
+    double* xn2; // [T] squared token norms (zeroed)
+    double* wn2; // [E] squared expert-column norms (zeroed)
+    int* ticket; // CTAs done (zeroed)
+};
+
+// Doubles of zeroed scratch the decode router needs for T tokens.
+__host__ __device__ inline size_t decode_scratch_doubles(int T, int E) {
+    return static_cast<size_t>(T) * E + T + E + 2;
+}
+
+template <int C>
+__global__ void __launch_bounds__(256) route_decode_kernel(DecodeArgs d) {
+    extern __shared__ __align__(16) double stage_buf[]; // [kDecSlots][H + 32]
+    __shared__ float xs[kDecMaxTokens][kDecRows];       // token rows; softmax scratch at the end
+    __shared__ double red[8][kDecMaxTokens][kDecCols];  // warp partials; logits at the end
+    __shared__ double wred[8][kDecCols];
+    __shared__ int last, fb_count, fb_list[kRouteFallbacks];
+    const RouteArgs& a = d.a;
+    const int T = a.T, H = a.H, E = a.E;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int r0 = blockIdx.x * kDecRows, e0 = blockIdx.y * kDecCols;
+    for (int i = tid; i < T * kDecRows; i += blockDim.x)
+        xs[i / kDecRows][i % kDecRows] = a.x[static_cast<size_t>(i / kDecRows) * H + r0 + i % kDecRows];
+    __syncthreads();
+    const int e = e0 + lane;
+    double acc[kDecMaxTokens];
+#pragma unroll
+    for (int t = 0; t < kDecMaxTokens; ++t) acc[t] = 0.0;
+    double wsq = 0.0;
+#pragma unroll 4
+    for (int j = 0; j < kDecRows / 8; ++j) {
+        const int i = warp * (kDecRows / 8) + j;
+        const double wd = e < E ? static_cast<double>(a.w[static_cast<size_t>(r0 + i) * E + e]) : 0.0;
+        wsq = fma(wd, wd, wsq);
+#pragma unroll
+        for (int t = 0; t < kDecMaxTokens; ++t)
+            if (t < T) acc[t] = fma(static_cast<double>(xs[t][i]), wd, acc[t]);
+    }
+#pragma unroll
+    for (int t = 0; t < kDecMaxTokens; ++t)
+        if (t < T) red[warp][t][lane] = acc[t];
+    wred[warp][lane] = wsq;
+    __syncthreads();
+    for (int idx = tid; idx < T * kDecCols; idx += blockDim.x) {
+        const int t = idx / kDecCols, l = idx % kDecCols;
+        double s = 0.0;
+        for (int w = 0; w < 8; ++w) s += red[w][t][l];
+        if (e0 + l < E) atomicAdd(d.acc + static_cast<size_t>(t) * E + e0 + l, s);
+    }
+    if (tid < kDecCols && e0 + tid < E) {
+        double s = 0.0;
+        for (int w = 0; w < 8; ++w) s += wred[w][tid];
+        atomicAdd(d.wn2 + e0 + tid, s);
+    }
+    if (blockIdx.y == 0 && tid < T) {
+        double s = 0.0;
+        for (int i = 0; i < kDecRows; ++i) {
+            const double v = static_cast<double>(xs[tid][i]);
+            s = fma(v, v, s);
+        }
+        atomicAdd(d.xn2 + tid, s);
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        last = atomicAdd(d.ticket, 1) == static_cast<int>(gridDim.x * gridDim.y) - 1;
+        fb_count = 0;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    // The last CTA: certify every logit, settle the queued ones, select.
+    float* logit = reinterpret_cast<float*>(&red[0][0][0]); // [T][E] floats (E <= 256)
+    const double gamma = static_cast<double>(H + H / kDecRows + 40) * 0x1.0p-53 * 1.01;
+    for (int idx = tid; idx < T * E; idx += blockDim.x) {
+        const int t = idx / E, ee = idx % E;
+        double s = __ldcg(d.acc + idx);
+        const double xn = sqrt(__ldcg(d.xn2 + t) * (1.0 + (H + 64) * 0x1.0p-52));
+        const double wn = sqrt(__ldcg(d.wn2 + ee) * (1.0 + (H + 64) * 0x1.0p-52));
+        double A = xn * wn * (1.0 + 0x1.0p-40);
+        if (a.bias) {
+            s += static_cast<double>(a.bias[ee]);
+            A += fabs(static_cast<double>(a.bias[ee]));
+        }
+        if (!rounding_certified(s, gamma * A + 0x1.0p-1060)) {
+            const int slot = atomicAdd(&fb_count, 1);
+            if (slot < kRouteFallbacks) fb_list[slot] = t * 256 + ee;
+            else s = sequential_logit(a, t, ee); // queue full: this thread does it
+        }
+        if (!isfinite(s)) device_fail(a.st, HMOE_NON_FINITE_ROUTER);
+        logit[idx] = static_cast<float>(s);
+    }
+    __syncthreads();
+    const int nfb = min(fb_count, kRouteFallbacks);
+    for (int f = warp; f < nfb; f += blockDim.x >> 5) {
+        const int t = fb_list[f] >> 8, ee = fb_list[f] & 255;
+        const float lg = settle_logit(a, t, ee, warp < kDecSlots ? stage_buf + warp * staged_logit_doubles(H) : nullptr);
+        if (lane == 0) {
+            if (!isfinite(lg)) device_fail(a.st, HMOE_NON_FINITE_ROUTER);
+            logit[t * E + ee] = lg;
+        }
+    }
+    __syncthreads();
+    float* evs = &xs[0][0]; // [8 warps][256] floats
+    for (int t = warp; t < T; t += blockDim.x >> 5) {
+        float lv[C];
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            const int j = lane + 32 * c;
+            lv[c] = j < E ? logit[t * E + j] : 0.0f;
+        }
+        select_token<C>(lv, E, a.k, a.softmax, a.renorm, evs + warp * kMaxExperts, a.ids + static_cast<size_t>(t) * a.k,
+                        a.scores + static_cast<size_t>(t) * a.k, a.counts, token_block_counts(a, t), a.st, false,
+                        nullptr);
+    }
+}
+
+static_assert(kDecMaxTokens * kDecRows * 4 >= 8 * kMaxExperts * 4, "decode router: softmax scratch fits");
+static_assert(8 * kDecMaxTokens * kDecCols * 8 >= kDecMaxTokens * kMaxExperts * 4, "decode router: logits fit");
+
 // kernels::routerTopK drop-in (CudaKernels.cu:152-204): one warp per token,
 // logits given, probabilities written back in place when softmax != 0.
 template <int C>
@@ -1147,9 +1292,52 @@ __global__ void __launch_bounds__(256) group_kernel(GroupArgs g) {
 
 
 // Router kernel choice: 0 = automatic, 1 = per-8-token cluster kernel,
-// 2 = tiled kernel (hmoe_set_route_variant).
+// 2 = tiled kernel, 3 = decode kernel (hmoe_set_route_variant).
 int g_route_variant = 0;
 constexpr int kTiledMinTokens = 512;
+
+bool decode_shape_ok(int T, int H, int E) { return T <= kDecMaxTokens && H % kDecRows == 0 && E <= kMaxExperts; }
+
+size_t route_decode_scratch_bytes(size_t T, int H, int E) {
+    if (!decode_shape_ok(static_cast<int>(std::min<size_t>(T, INT_MAX)), H, E)) return 0;
+    return decode_scratch_doubles(static_cast<int>(T), E) * 8;
+}
+
+hmoe_status launch_route_decode(const RouteArgs& a, double* scratch, cudaStream_t stream) {
+    DecodeArgs d{a, scratch, scratch + static_cast<size_t>(a.T) * a.E, scratch + static_cast<size_t>(a.T) * a.E + a.T,
+                 reinterpret_cast<int*>(scratch + static_cast<size_t>(a.T) * a.E + a.T + a.E)};
+    const dim3 grid(static_cast<unsigned>(a.H / kDecRows), static_cast<unsigned>((a.E + kDecCols - 1) / kDecCols));
+    const int smem = kDecSlots * staged_logit_doubles(a.H) * 8;
+    cudaError_t err = cudaErrorInvalidValue;
+#define HMOE_DECODE_CASE(CC)                                                                                 \
+    case CC: {                                                                                               \
+        static int attr_set = 0;                                                                             \
+        if (smem > attr_set) {                                                                               \
+            cudaFuncSetAttribute(route_decode_kernel<CC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
+            attr_set = smem;                                                                                 \
+        }                                                                                                    \
+        route_decode_kernel<CC><<<grid, 256, smem, stream>>>(d);                                             \
+        err = cudaGetLastError();                                                                            \
+        break;                                                                                               \
+    }
+    switch ((a.E + 31) / 32) {
+        HMOE_DECODE_CASE(1)
+        HMOE_DECODE_CASE(2)
+        HMOE_DECODE_CASE(3)
+        HMOE_DECODE_CASE(4)
+        HMOE_DECODE_CASE(5)
+        HMOE_DECODE_CASE(6)
+        HMOE_DECODE_CASE(7)
+        HMOE_DECODE_CASE(8)
+    default: return HMOE_UNSUPPORTED;
+    }
+#undef HMOE_DECODE_CASE
+    if (err != cudaSuccess) {
+        set_last_error("hmoe decode route kernel launch", err);
+        return HMOE_CUDA_ERROR;
+    }
+    return check_launch("hmoe decode route kernel");
+}
 
 bool tiled_shape_ok(int H, int E) { return E <= kRtCols && E % 4 == 0 && H % kRtRows == 0; }
 
@@ -1205,7 +1393,7 @@ hmoe_status launch_route_tiled(const RouteArgs& a, cudaStream_t stream) {
 hmoe_status launch_route(const float* x, const float* w, const float* bias,
                          int T, int H, int E, int k, int softmax, int renorm,
                          uint32_t* ids, float* scores, int32_t* counts,
-                         int32_t* block_counts, DeviceStatus* st, cudaStream_t stream) {
+                         int32_t* block_counts, double* decode_scratch, DeviceStatus* st, cudaStream_t stream) {
     if (T <= 0) return HMOE_OK;
     if (E <= 0 || E > kMaxExperts || k <= 0 || k > E || k > kMaxTopK || H <= 0 || H % 8)
         return HMOE_INVALID_ARGUMENT;
@@ -1219,6 +1407,15 @@ hmoe_status launch_route(const float* x, const float* w, const float* bias,
     if (g_route_variant == 2 || (g_route_variant == 0 && tiled_ok && T >= kTiledMinTokens)) {
         RouteArgs a{x, w, bias, T, H, E, k, softmax, renorm, ids, scores, counts, st, block_counts};
         return launch_route_tiled(a, stream);
+    }
+    const bool decode_ok = decode_shape_ok(T, H, E) && decode_scratch;
+    if (g_route_variant == 3 && !decode_ok) {
+        set_last_error_text("hmoe route: the decode router needs T <= 16, H % 128 == 0 and its scratch");
+        return HMOE_UNSUPPORTED;
+    }
+    if (g_route_variant == 3 || (g_route_variant == 0 && decode_ok && T <= kDecAutoTokens)) {
+        RouteArgs a{x, w, bias, T, H, E, k, softmax, renorm, ids, scores, counts, st, block_counts};
+        return launch_route_decode(a, decode_scratch, stream);
     }
     const int EQ = (E + 3) / 4;
     const int P = std::min(32, 256 / EQ); // row lanes; phase 2 maps token t to lane t mod P
@@ -1322,7 +1519,7 @@ extern "C" hmoe_status hmoe_router_topk(float* logits, size_t tokens,
 }
 
 extern "C" hmoe_status hmoe_set_route_variant(int32_t variant) {
-    if (variant < 0 || variant > 2) return HMOE_INVALID_ARGUMENT;
+    if (variant < 0 || variant > 3) return HMOE_INVALID_ARGUMENT;
     hmoe::g_route_variant = variant;
     return HMOE_OK;
 }

@@ -356,7 +356,7 @@ def set_variant(v: int) -> None:
 
 
 def set_route_variant(v: int) -> None:
-    """0 = automatic, 1 = per-8-token cluster router, 2 = tiled router."""
+    """0 = automatic, 1 = per-8-token cluster router, 2 = tiled router, 3 = decode router."""
     check("hmoe_set_route_variant", lib().hmoe_set_route_variant(v))
 
 

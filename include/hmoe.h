@@ -226,10 +226,12 @@ hmoe_status hmoe_set_variant(int32_t variant);
 
 /* Forces the router kernel for measurement: 0 = automatic (the tiled kernel
  * for batches of 512 tokens or more when E <= 128, E % 4 == 0 and
- * H % 32 == 0), 1 = the per-8-token cluster kernel, 2 = the tiled kernel
- * (64-token tiles on the FP64 tensor-core path; routing calls whose shape it
- * does not take return HMOE_UNSUPPORTED).  Both produce bit-identical
- * results.  Process-wide. */
+ * H % 32 == 0; the decode kernel for 1 or 2 tokens when H % 128 == 0),
+ * 1 = the per-8-token cluster kernel, 2 = the tiled kernel (64-token tiles
+ * on the FP64 tensor-core path), 3 = the decode kernel (a grid over H and
+ * the experts, up to 16 tokens); routing calls whose shape a forced kernel does not take
+ * return HMOE_UNSUPPORTED.  All produce bit-identical results.  Process-wide;
+ * query hmoe_workspace_size after setting it. */
 hmoe_status hmoe_set_route_variant(int32_t variant);
 
 /* Measurement hooks.  hmoe_set_stage_events registers `count` (= 6)

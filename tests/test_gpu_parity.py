@@ -165,11 +165,12 @@ def test_router_topk_dropin_matches_cpu_router(cuda, golden):
 
 # ------------------------------------------------------------- fused router
 
-def _pad64(x, w):
-    """Zero-pads the hidden dimension to a multiple of 64.  The extra terms
-    are exact zeros, which leave every double partial sum unchanged."""
+def _pad64(x, w, mult=64):
+    """Zero-pads the hidden dimension to a multiple of `mult` (64).  The
+    extra terms are exact zeros, which leave every double partial sum
+    unchanged."""
     Hd = x.shape[1]
-    Hp = (Hd + 63) // 64 * 64
+    Hp = (Hd + mult - 1) // mult * mult
     xp = np.zeros((x.shape[0], Hp), np.float32)
     xp[:, :Hd] = x
     wp = np.zeros((Hp, w.shape[1]), np.float32)
@@ -177,21 +178,24 @@ def _pad64(x, w):
     return xp, wp
 
 
-@pytest.mark.parametrize("route_variant", [0, 2])
+@pytest.mark.parametrize("route_variant", [0, 2, 3])
 @pytest.mark.parametrize("case", ["a", "b", "c", "d", "p12"])
 def test_fused_route_bit_exact(cuda, golden, case, route_variant):
-    """Both router kernels (the per-8-token cluster kernel chosen
-    automatically at these sizes, and the 64-token tiled kernel forced)
-    against the reference's router goldens."""
+    """Every router kernel against the reference's router goldens: the
+    per-8-token cluster kernel (chosen automatically at these sizes), the
+    64-token tiled kernel and the decode kernel (forced)."""
     g = golden("router.npz")
     if route_variant == 2 and case in ("d", "p12"):
         pytest.skip("the tiled router takes E <= 128 with E % 4 == 0")
+    if route_variant == 3 and case in ("a", "b", "d"):
+        pytest.skip("the decode router takes at most 16 tokens")
+    mult = 128 if route_variant == 3 else 64  # the decode router takes H % 128 == 0
     if case == "p12":
-        x, w = _pad64(g["p12_x"], g["p12_w"])
+        x, w = _pad64(g["p12_x"], g["p12_w"], mult)
         k, sm, rn, bias = 2, 1, 1, None
     else:
         T, Hd, E, k, sm, rn, has_bias = (int(v) for v in g[f"{case}_cfg"])
-        x, w = _pad64(g[f"{case}_x"], g[f"{case}_w"])
+        x, w = _pad64(g[f"{case}_x"], g[f"{case}_w"], mult)
         bias = g[f"{case}_bias"] if has_bias else None
     cfg = H.LayerConfig(x.shape[1], 64, w.shape[1], k, bool(sm), bool(rn))
     hl = H.make_host_layer(cfg, seed=0)
@@ -213,11 +217,14 @@ def test_fused_route_bit_exact(cuda, golden, case, route_variant):
         assert groups == [[0, 2], [0, 1, 2], [1]]
 
 
-@pytest.mark.parametrize("route_variant", [1, 2])
-@pytest.mark.parametrize("T", [1, 16, 256, 700, 4096])
+@pytest.mark.parametrize("route_variant", [1, 2, 3])
+@pytest.mark.parametrize("T", [1, 5, 16, 256, 700, 4096])
 def test_fused_route_c3_full_sizes(cuda, T, route_variant):
     """C3 router (H2048, E128, k8, Zipf bias) at decode to prefill sizes,
-    with each router kernel forced; 700 tokens leave a ragged last tile."""
+    with each router kernel forced (the decode kernel up to 16 tokens); 700
+    tokens leave a ragged last tile."""
+    if route_variant == 3 and T > 16:
+        pytest.skip("the decode router takes at most 16 tokens")
     cfg = H.CONFIGS["c3"]
     hl = H.make_host_layer(cfg, seed=2)
     x = H.make_tokens(cfg, T, seed=2)
@@ -286,6 +293,27 @@ def test_layer_configs_gemm_and_gemv_agree_with_port(cuda, cfg, T):
         finally:
             H.set_variant(0)
         assert_layer_close(y, out_p)
+
+
+@pytest.mark.parametrize("T", [1, 300])
+def test_forward_host_equals_forward(cuda, T):
+    """hmoe_moe_forward_host (page-locked host buffers in and out, copies on
+    the caller's stream) returns what hmoe_moe_forward returns on the same
+    tokens, bit for bit, on two calls in a row."""
+    import torch
+    cfg = H.CONFIGS["c3"]
+    hl = H.make_host_layer(cfg, seed=8)
+    x = H.make_tokens(cfg, T, seed=8)
+    dl = H.DeviceLayer(hl, cuda)
+    ref = host(dl.forward(t(x, cuda)))
+    xh = torch.from_numpy(x).pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    for _ in range(2):
+        yh.fill_(float("nan"))
+        dl.forward_host(xh, yh)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(yh.numpy(), ref)
+    assert dl.read_status()[0] == 0
 
 
 def test_layer_is_deterministic(cuda):
