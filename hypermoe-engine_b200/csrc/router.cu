@@ -1069,6 +1069,8 @@ __global__ void __launch_bounds__(256) route_decode_kernel(DecodeArgs d) {
     __shared__ double red[8][kDecMaxTokens][kDecCols];  // warp partials; logits at the end
     __shared__ double wred[8][kDecCols];
     __shared__ int last, fb_count, fb_list[kRouteFallbacks];
+    __shared__ double wnorm_s[kMaxExperts], xnorm_s[kDecMaxTokens];
+    __shared__ float bias_s[kMaxExperts];
     const RouteArgs& a = d.a;
     const int T = a.T, H = a.H, E = a.E;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1125,16 +1127,21 @@ __global__ void __launch_bounds__(256) route_decode_kernel(DecodeArgs d) {
     __threadfence();
     // The last CTA: certify every logit, settle the queued ones, select.
     float* logit = reinterpret_cast<float*>(&red[0][0][0]); // [T][E] floats (E <= 256)
+    for (int ee = tid; ee < E; ee += blockDim.x) {
+        wnorm_s[ee] = sqrt(__ldcg(d.wn2 + ee) * (1.0 + (H + 64) * 0x1.0p-52));
+        bias_s[ee] = a.bias ? a.bias[ee] : 0.0f;
+    }
+    if (tid < T) xnorm_s[tid] = sqrt(__ldcg(d.xn2 + tid) * (1.0 + (H + 64) * 0x1.0p-52));
+    __syncthreads();
     const double gamma = static_cast<double>(H + H / kDecRows + 40) * 0x1.0p-53 * 1.01;
+#pragma unroll 4
     for (int idx = tid; idx < T * E; idx += blockDim.x) {
         const int t = idx / E, ee = idx % E;
         double s = __ldcg(d.acc + idx);
-        const double xn = sqrt(__ldcg(d.xn2 + t) * (1.0 + (H + 64) * 0x1.0p-52));
-        const double wn = sqrt(__ldcg(d.wn2 + ee) * (1.0 + (H + 64) * 0x1.0p-52));
-        double A = xn * wn * (1.0 + 0x1.0p-40);
+        double A = xnorm_s[t] * wnorm_s[ee] * (1.0 + 0x1.0p-40);
         if (a.bias) {
-            s += static_cast<double>(a.bias[ee]);
-            A += fabs(static_cast<double>(a.bias[ee]));
+            s += static_cast<double>(bias_s[ee]);
+            A += fabs(static_cast<double>(bias_s[ee]));
         }
         if (!rounding_certified(s, gamma * A + 0x1.0p-1060)) {
             const int slot = atomicAdd(&fb_count, 1);
