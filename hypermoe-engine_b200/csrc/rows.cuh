@@ -91,15 +91,23 @@ __device__ __forceinline__ void combine_token(const int32_t* __restrict__ inv, c
     }
     __syncthreads();
     const int H8 = H / 8;
+    constexpr int kBatch = 8; // rows whose loads are in flight together
     for (int c = threadIdx.x; c < H8; c += blockDim.x) {
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int s = 0; s < slots; ++s) {
-            const uint4 v = reinterpret_cast<const uint4*>(rows_s[s])[c];
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        for (int s0 = 0; s0 < slots; s0 += kBatch) {
+            uint4 v[kBatch];
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                acc[2 * i] = __fadd_rn(acc[2 * i], __uint_as_float(w[i] << 16));
-                acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __uint_as_float(w[i] & 0xffff0000u));
+            for (int b = 0; b < kBatch; ++b)
+                if (s0 + b < slots) v[b] = reinterpret_cast<const uint4*>(rows_s[s0 + b])[c];
+#pragma unroll
+            for (int b = 0; b < kBatch; ++b) { // still added in row order
+                if (s0 + b >= slots) break;
+                const uint32_t w[4] = {v[b].x, v[b].y, v[b].z, v[b].w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    acc[2 * i] = __fadd_rn(acc[2 * i], __uint_as_float(w[i] << 16));
+                    acc[2 * i + 1] = __fadd_rn(acc[2 * i + 1], __uint_as_float(w[i] & 0xffff0000u));
+                }
             }
         }
         float4* o = reinterpret_cast<float4*>(out + static_cast<size_t>(t) * H) + 2 * c;
