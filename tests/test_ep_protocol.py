@@ -1,4 +1,4 @@
-"""Expert-parallel protocol on CPU ranks (gloo), checked against the oracle.
+"""Expert-parallel protocols on CPU ranks (gloo), checked against the oracle.
 
 Each rank routes its own tokens with the CPU oracle, all-gathers the
 per-(rank, expert) row counts, plans its transfers with the library's
@@ -9,6 +9,10 @@ and combines in ascending expert id.  The result must equal the
 single-process oracle layer (oracle/hmoe_oracle.c hmo_moe_layer, which
 follows MoERuntime.cpp:58-349) on the concatenated batch bit for bit: the
 protocol only moves rows, so any difference is a planning or ordering bug.
+
+The *_peer_* tests restate the peer-memory path's layout instead (rows
+stored into and read back from the owners' receive rows at indices derived
+on every rank from the exchanged counts) and hold it to the same standard.
 """
 import os
 import socket
@@ -134,12 +138,127 @@ def _rank_main(rank, P, port, cfg_args, Ts, seed, q, placement=None):
         dist.destroy_process_group()
 
 
-def _run(P, cfg_args, Ts, seed=0, placement=None):
+def _peer_rank_main(rank, P, port, cfg_args, Ts, seed, q, placement=None):
+    """The peer-memory layout of hmoe_ep_moe_forward with a registered
+    workspace (ep.cu: ep_exchange_kernel, ep_permute_kernel,
+    ep_combine_kernel), restated on gloo ranks: every rank derives the plan
+    from the exchanged counts; each routed row is stored by its source at
+    row dest_base[q] + r - send_off[q] of its owner q's receive rows; the
+    owner runs its experts over (source, slot) segments in receive order; the
+    source reads each output back from the owner at the same row."""
+    for p in PATHS:
+        sys.path.insert(0, p)
+    import torch.distributed as dist
+
+    import hmoe_api as H
+    import oracle as O
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=P, timeout=timedelta(seconds=120))
+    try:
+        cfg = H.LayerConfig(*cfg_args)
+        hl = H.make_host_layer(cfg, seed=seed, threads=1)
+        local = H.local_host_layer(hl, P, rank, placement)
+        expert_of_slot = (np.argsort(np.asarray(placement)) if placement is not None
+                          else np.arange(cfg.experts))
+        E, S, k, Hd = cfg.experts, cfg.shared_experts, cfg.top_k, cfg.hidden
+        x_all = H.make_tokens(cfg, sum(Ts), seed=seed, threads=1)
+        t0 = sum(Ts[:rank])
+        x = x_all[t0:t0 + Ts[rank]]
+        T = x.shape[0]
+        L = O.port()
+        if T:
+            ids, sc, off, gt, gs = O.route(L, x, hl.router_w, hl.router_bias, k, cfg.softmax, cfg.renormalize)
+        else:
+            off, gt, gs = np.zeros(E + 1, np.int32), np.zeros(0, np.uint32), np.zeros(0, np.float32)
+        counts = np.diff(off).astype(np.int64)[expert_of_slot]  # per slot
+        counts_all = np.stack(_all_gather(dist, P, counts))      # [P][E]
+        # plan, as ep_exchange_kernel forms it
+        base, extra = E // P, E % P
+        first = [r * base + min(r, extra) for r in range(P)]
+        nslot = [base + (1 if r < extra else 0) for r in range(P)]
+        R = np.array([[counts_all[p, first[qq]:first[qq] + nslot[qq]].sum() for qq in range(P)] for p in range(P)])
+        send_off = [int(R[rank, :qq].sum()) for qq in range(P)]
+        dest_base = [int(R[:rank, qq].sum()) for qq in range(P)]
+        recv_base = [int(R[:p, rank].sum()) for p in range(P)]
+        recv_total = int(R[:, rank].sum())
+        # routed rows in slot order, tokens ascending inside a slot
+        order = (np.concatenate([np.arange(off[e], off[e + 1]) for e in expert_of_slot]).astype(np.int64)
+                 if T else np.zeros(0, np.int64))
+        gt, gs = gt[order], gs[order]
+        row_expert = np.concatenate([np.full(off[e + 1] - off[e], e) for e in expert_of_slot]) if T else order
+
+        def owner(r):
+            qq = 0
+            while qq + 1 < P and r >= send_off[qq] + R[rank, qq]:
+                qq += 1
+            return qq
+
+        # dispatch: (owner, receive row, x row, weight) -- the stores of ep_permute_kernel
+        sent = [(owner(r), dest_base[owner(r)] + r - send_off[owner(r)], int(gt[r]), float(gs[r]))
+                for r in range(len(gt))]
+        everything = _all_gather_obj(dist, P, (t0, sent))
+        xin = np.full((recv_total, Hd), np.nan, np.float32)
+        win = np.full(recv_total, np.nan, np.float32)
+        for p, (tp, items) in enumerate(everything):
+            for (qq, d, tok, wgt) in items:
+                if qq != rank:
+                    continue
+                assert recv_base[p] <= d < recv_base[p] + int(R[p, rank]), (p, d)
+                assert np.isnan(win[d])  # each receive row written once
+                xin[d] = x_all[tp + tok]
+                win[d] = wgt
+        assert not np.isnan(win).any()
+        # owner: (source, local slot) segments in receive order
+        yin = np.zeros_like(xin)
+        row = 0
+        for p in range(P):
+            for el in range(nslot[rank]):
+                n = int(counts_all[p, first[rank] + el])
+                if n:
+                    y = O.expert_mlp(L, xin[row:row + n], *_expert(local, el))
+                    yin[row:row + n] = win[row:row + n, None] * y
+                row += n
+        assert row == recv_total
+        # combine: each routed row read back from its owner -- the loads of ep_combine_kernel
+        yins = _all_gather_obj(dist, P, yin)
+        out = np.zeros((T, Hd), np.float32)
+        for r in np.lexsort((np.arange(len(gt)), row_expert)) if T else []:
+            qq = owner(int(r))
+            out[gt[r]] += yins[qq][dest_base[qq] + int(r) - send_off[qq]]
+        for sx in range(S):
+            if T:
+                out += np.float32(1.0) * O.expert_mlp(L, x, *_expert(local, nslot[rank] + sx))
+        ref = O.moe_layer_port(hl, x_all)[0][t0:t0 + T]
+        q.put((rank, bool(np.array_equal(out, ref)), float(np.abs(out - ref).max()) if T else 0.0))
+    except Exception as exc:  # reported to the parent
+        q.put((rank, False, repr(exc)))
+    finally:
+        dist.destroy_process_group()
+
+
+def _all_gather(dist, P, arr):
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(arr))
+    out = [torch.empty_like(t) for _ in range(P)]
+    dist.all_gather(out, t)
+    return [o.numpy() for o in out]
+
+
+def _all_gather_obj(dist, P, obj):
+    out = [None] * P
+    dist.all_gather_object(out, obj)
+    return out
+
+
+def _run(P, cfg_args, Ts, seed=0, placement=None, target=None):
     import torch.multiprocessing as mp
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, P, port, cfg_args, Ts, seed, q, placement)) for r in range(P)]
+    target = target or _rank_main
+    procs = [ctx.Process(target=target, args=(r, P, port, cfg_args, Ts, seed, q, placement)) for r in range(P)]
     for p in procs:
         p.start()
     results = {}
@@ -172,6 +291,18 @@ def test_ep_protocol_with_placement_two_ranks():
     # still adds each token's rows in ascending expert id
     placement = np.random.default_rng(7).permutation(8).astype(np.int32)
     _run(2, (256, 512, 8, 2, True, True, 0, None), (6, 4), seed=2, placement=placement)
+
+
+def test_ep_peer_layout_two_ranks_with_placement():
+    # the peer-memory path's row layout on 2 ranks, scrambled placement
+    placement = np.random.default_rng(7).permutation(8).astype(np.int32)
+    _run(2, (256, 512, 8, 2, True, True, 0, None), (6, 4), seed=2, placement=placement, target=_peer_rank_main)
+
+
+def test_ep_peer_layout_three_ranks_shared_uneven():
+    # 7 experts on 3 ranks (3, 2, 2), 2 shared experts, Zipf-biased router,
+    # no renormalisation, and a rank with no tokens
+    _run(3, (128, 128, 7, 2, True, False, 2, 1.1), (4, 0, 3), seed=1, target=_peer_rank_main)
 
 
 def test_balanced_placement():
