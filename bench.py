@@ -61,6 +61,8 @@ def parse():
     p.add_argument("--ep-path", default="peer", choices=["peer", "nccl"],
                    help="expert parallelism: peer-memory stores (registered workspace) or NCCL send/recv")
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-reference-cuda", action="store_true",
+                   help="skip timing the reference's own CUDA path on this GPU")
     p.add_argument("--cpu-seconds", type=float, default=12.0)
     p.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                    help="expert placement under expert parallelism: balanced from a calibration batch's "
@@ -209,6 +211,86 @@ def cpu_reference_sample(cfg, host_layer, x_all, seconds, threads):
         n = min(x_all.shape[0], max(n + 1, int(n * min(8.0, 1.2 * seconds / max(dt, 1e-3)))))
 
 
+def reference_arm(args, cfg, config, rank):
+    """The reference's own CPU implementation of the layer (oracle/_ref: its
+    CpuRouterBackend, CpuTensorBackend INT8 GEMMs and ExpertMlpExecutor
+    compiled from its sources) on this host's cores.  Inputs come from the
+    standalone build of the seeded generator, so libhmoe.so is never loaded
+    in this process.  Rank 0 only."""
+    import hmoe_api as H
+    if rank != 0:
+        return
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    if not os.path.exists(O.SYNTH_PATH):
+        O.build(reference=False)
+    H.use_synth_library(O.SYNTH_PATH)
+    T = args.tokens
+    threads = os.cpu_count() or 1
+    host_layer = H.make_host_layer(cfg, seed=args.seed)
+    x = H.make_tokens(cfg, max(T, 1), seed=args.seed)
+    per_step = max(1.0, min(6.0, 150.0 / max(1, args.steps + args.warmup)))
+    rate, n, dt = cpu_reference_sample(cfg, host_layer, x, per_step, threads)
+    rl = O.RefLayer(host_layer)
+    for _ in range(args.warmup):
+        rl.forward(x[:n], threads=threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        rl.forward(x[:n], threads=threads)
+        times.append(time.perf_counter() - t0)
+    value = n / statistics.mean(times)
+    # the reference's own loop is single-threaded by construction
+    # (CpuTensorBackend.cpp:173-186): one thread on a smaller sample
+    rate1, n1, dt1 = cpu_reference_sample(cfg, host_layer, x, min(per_step, 5.0), 1)
+    sample = (f"{n} of the {T} tokens per step (reference MoERuntime CPU branch: CpuRouterBackend + "
+              f"CpuTensorBackend INT8 GEMMs; aggregate over {threads} host threads, one expert group per "
+              f"thread at a time)")
+    print(json.dumps({
+        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.mean(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights quantised to INT8)",
+        "config": config,
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample},
+        "single_thread": {"value": rate1, "unit": UNIT, "cores": 1,
+                          "sample": f"{n1} tokens in {dt1:.1f} s on one thread (the reference's own loop)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def reference_cuda(cfg, T, seed, steps, warmup, gpu_index, pci, timeout=600):
+    """Times the reference's own CUDA path (oracle/_ref/ref_cuda_bench: its
+    CudaRouterBackend, per-expert gatherRows, ExpertMlpExecutor on
+    CudaTensorBackend with planInt8Gemm's Auto mode, scatterAddRows) on this
+    GPU, in a process of its own, with its own clock record.  Same seeded
+    layer and tokens as the measured workload."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    exe = O.REF_CUDA_BENCH
+    if not os.path.exists(exe):
+        return {"unavailable": "oracle/_ref/ref_cuda_bench is not built (needs the reference sources)"}
+    cmd = [exe, "--hidden", str(cfg.hidden), "--inter", str(cfg.intermediate), "--experts", str(cfg.experts),
+           "--topk", str(cfg.top_k), "--softmax", str(int(cfg.softmax)), "--renorm", str(int(cfg.renormalize)),
+           "--shared", str(cfg.shared_experts), "--zipf", str(cfg.zipf_alpha or 0), "--tokens", str(T),
+           "--seed", str(seed), "--steps", str(steps), "--warmup", str(warmup)]
+    clocks = Clocks(gpu_index, pci)
+    clocks.start()
+    try:
+        p = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout)
+    except subprocess.TimeoutExpired:
+        clocks.stop()
+        return {"unavailable": f"reference CUDA path did not finish within {timeout} s"}
+    clk = clocks.stop()
+    if p.returncode != 0:
+        return {"unavailable": f"ref_cuda_bench exited {p.returncode}: {p.stderr.strip()[-300:]}"}
+    out = json.loads(p.stdout.strip().splitlines()[-1])
+    out["unit"] = UNIT
+    out["clocks"] = clk
+    out["timing"] = "wall clock per step (the path synchronises with the device inside each step), median"
+    return out
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -223,37 +305,16 @@ def main():
               "hidden": cfg.hidden, "experts": cfg.experts, "top_k": cfg.top_k,
               "intermediate": cfg.intermediate, "shared_experts": cfg.shared_experts,
               "tokens_per_gpu": T, "routing": "zipf1.1" if cfg.zipf_alpha else "uniform",
-              "weights": "int8 per-projection affine", "seed": args.seed}
+              "weights": "int8 per-projection affine", "seed": args.seed,
+              "parallelism": (f"ep{world}" if world > 1 else "single"),
+              "ep_path": (args.ep_path if world > 1 else None),
+              "placement": (None if world == 1 else
+                            "balanced from 4096 calibration tokens (seed+104729)" if args.placement == "balanced"
+                            else "contiguous"),
+              "l2": "inputs larger than L2 (INT8 expert arena) and a 256 MiB flush between steps"}
 
     if args.impl == "reference":
-        if rank != 0:
-            return
-        threads = os.cpu_count() or 1
-        host_layer = H.make_host_layer(cfg, seed=args.seed)
-        x = H.make_tokens(cfg, max(T, 1), seed=args.seed)
-        per_step = max(1.0, min(6.0, 150.0 / max(1, args.steps + args.warmup)))
-        rate, n, dt = cpu_reference_sample(cfg, host_layer, x, per_step, threads)
-        sys.path.insert(0, os.path.join(ROOT, "oracle"))
-        import oracle as O
-        rl = O.RefLayer(host_layer)
-        for _ in range(args.warmup):
-            rl.forward(x[:n], threads=threads)
-        times = []
-        for _ in range(args.steps):
-            t0 = time.perf_counter()
-            rl.forward(x[:n], threads=threads)
-            times.append(time.perf_counter() - t0)
-        value = n / statistics.mean(times)
-        sample = (f"{n} of the {T} tokens per step (reference MoERuntime CPU branch: CpuRouterBackend + "
-                  f"CpuTensorBackend INT8 GEMMs, expert groups spread over {threads} host threads)")
-        print(json.dumps({
-            "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.mean(times),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-            "data": "synthetic (seeded)", "config": config,
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample},
-            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        }))
+        reference_arm(args, cfg, config, rank)
         return
 
     import torch
@@ -463,6 +524,14 @@ def main():
                "sample": f"{n} tokens of this workload through the reference CPU path "
                          f"(oracle/_ref), {dt:.1f} s, expert groups over {threads} threads"}
 
+    ref_cuda = None
+    ref_cuda_decode = None
+    if world == 1 and not args.no_reference_cuda:
+        gpu_index = clocks.index
+        ref_cuda = reference_cuda(cfg, T, args.seed, 5, 2, gpu_index, pci)
+        if T > 1:
+            ref_cuda_decode = reference_cuda(cfg, 1, args.seed, 20, 3, gpu_index, pci)
+
     # tensor-core GEMM present (hmoe_set_variant(2) is refused without it)?
     has_gemm = H.lib().hmoe_set_variant(2) == 0
     H.lib().hmoe_set_variant(args.variant)
@@ -472,12 +541,7 @@ def main():
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp32" if not used_gemm else "fp16+bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights quantised to INT8)",
-        "config": dict(config, parallelism=(f"ep{world}" if world > 1 else "single"),
-                       ep_path=(args.ep_path if world > 1 else None),
-                       placement=(None if world == 1 else
-                                  "balanced from 4096 calibration tokens (seed+104729)" if args.placement == "balanced"
-                                  else "contiguous"),
-                       l2="inputs larger than L2 (604 MB INT8 arena) and a 256 MiB flush between steps"),
+        "config": config,
         "e2e": e2e, "gpu_launches": launches,
         "timing": ("cuda-graph replay of hmoe_moe_forward" if graph is not None else
                    "eager hmoe_ep_moe_forward" if comm is not None else "eager hmoe_moe_forward"),
@@ -486,6 +550,8 @@ def main():
         "layer_roofline_frac": layer_roof_ms / ms, "unique_experts": alg["unique_experts"],
         "rows_received_rank0": alg.get("rows_received"),
         "device_status": {"status": status[0], "near_ties": status[1], "sequential_logits": status[2]},
+        "reference_cuda": ref_cuda,
+        "reference_cuda_decode_t1": ref_cuda_decode,
     }
     print(json.dumps(line))
     if dist is not None:

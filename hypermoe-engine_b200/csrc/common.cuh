@@ -27,6 +27,15 @@ void set_last_error_text(const char* text);
 // Counts this library's kernel launches (hmoe_launch_count).
 void count_launch();
 
+// Raises `func`'s dynamic shared-memory limit to at least `bytes` on the
+// current device.  Function attributes belong to a device context, so the
+// setting is remembered per (kernel, device ordinal); several host threads
+// may call this at once.
+cudaError_t set_smem_limit(const void* func, int bytes);
+
+// Multiprocessor count of the current device (remembered per ordinal).
+int current_sm_count();
+
 // checkLaunch (reference CudaKernels.cu:293-299) as a status.
 inline hmoe_status check_launch(const char* what) {
     count_launch();

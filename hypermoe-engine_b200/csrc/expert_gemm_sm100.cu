@@ -54,6 +54,7 @@
 #include <cub/block/block_scan.cuh>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 namespace hmoe {
@@ -621,24 +622,15 @@ bool map_rows(CUtensorMap* m, const void* base, int K, int rows, bool f16) {
                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-int sm_count() {
-    static int n = 0;
-    if (n == 0) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-        if (n <= 0) n = 148;
-    }
-    return n;
-}
+int sm_count() { return current_sm_count(); }
 
 template <bool GATE_UP>
 hmoe_status launch_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& b, const GemmArgs& args,
                         int item_capacity, cudaStream_t s) {
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(expert_gemm_kernel<GATE_UP>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
-        attr = true;
+    const cudaError_t aerr = set_smem_limit(reinterpret_cast<const void*>(expert_gemm_kernel<GATE_UP>), kSmem);
+    if (aerr != cudaSuccess) {
+        set_last_error("hmoe expert GEMM shared-memory limit", aerr);
+        return HMOE_CUDA_ERROR;
     }
     const int pairs = std::max(1, std::min(sm_count() / 2, item_capacity));
     cudaLaunchConfig_t cfg = {};
@@ -695,17 +687,26 @@ bool map_weights_box(CUtensorMap* m, const int8_t* base, int N, int K, int exper
 
 int device_sm_count() { return sm_count(); }
 
+// Per device ordinal (a process may drive devices of different kinds):
+// 0 unknown, 1 no, 2 yes.  Racing first calls compute the same answer.
 bool gemm_available() {
-    static int avail = -1;
-    if (avail < 0) {
-        int dev = 0, major = 0, minor = 0;
-        avail = cudaGetDevice(&dev) == cudaSuccess &&
-                cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) == cudaSuccess &&
-                cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) == cudaSuccess &&
-                major == 10 && minor == 0 && encode_fn() != nullptr;
+    static std::atomic<int> avail[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
         cudaGetLastError();
+        return false;
     }
-    return avail == 1;
+    int v = avail[dev].load();
+    if (v == 0) {
+        int major = 0, minor = 0;
+        const bool ok = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) == cudaSuccess &&
+                        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) == cudaSuccess &&
+                        major == 10 && minor == 0 && encode_fn() != nullptr;
+        cudaGetLastError();
+        v = ok ? 2 : 1;
+        avail[dev].store(v);
+    }
+    return v == 2;
 }
 
 hmoe_status launch_tile_list(const SegSpec& spec, int4* tiles, int32_t* tile_count, int capacity,

@@ -215,12 +215,9 @@ __global__ void __launch_bounds__(kVThreads, 2)
 template <bool GATE_UP, int TOK>
 cudaError_t launch_gemv_variant(cudaLaunchConfig_t& cfg, const CUtensorMap& m0, const CUtensorMap& m1,
                                 const GemvArgs& args, int kc) {
-    static size_t attr_set = 0;
-    if (cfg.dynamicSmemBytes > attr_set) {
-        cudaFuncSetAttribute(expert_gemv_kernel<GATE_UP, TOK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(cfg.dynamicSmemBytes));
-        attr_set = cfg.dynamicSmemBytes;
-    }
+    const cudaError_t err = set_smem_limit(reinterpret_cast<const void*>(expert_gemv_kernel<GATE_UP, TOK>),
+                                           static_cast<int>(cfg.dynamicSmemBytes));
+    if (err != cudaSuccess) return err;
     return cudaLaunchKernelEx(&cfg, expert_gemv_kernel<GATE_UP, TOK>, m0, m1, args, kc);
 }
 

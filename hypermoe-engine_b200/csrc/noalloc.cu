@@ -12,7 +12,12 @@
 // call on that device: calls that overlap in time -- on different streams,
 // or from different host threads -- race on it.  The first call on a device
 // looks the array up with cudaGetSymbolAddress; make that first call before
-// any stream capture on that device.
+// any stream capture on that device.  The address is remembered for the life
+// of the process, so it is not valid across cudaDeviceReset.
+//
+// The layer's device status word (router non-finite input, bounded-wait
+// timeouts, near-tie counts) sits at the start of the array, as it sits at
+// the start of a caller workspace; hmoe_noalloc_read_status reads it.
 #include "common.cuh"
 
 #include <mutex>
@@ -79,4 +84,15 @@ extern "C" hmoe_status hmoe_moe_forward_noalloc(const hmoe_layer_desc* desc, con
     // hmoe_moe_forward clears the status word and the expert counters (the
     // parts that must start at zero) with one cudaMemsetAsync on `stream`.
     return hmoe_moe_forward(desc, x, y, tokens, scratch, kNoAllocScratchBytes, stream);
+}
+
+// The status word the last hmoe_moe_forward_noalloc on this device left in
+// the static scratch (hmoe_read_status on the array).
+extern "C" hmoe_status hmoe_noalloc_read_status(int32_t* status, int32_t* near_ties, int32_t* sequential_logits,
+                                                void* stream) {
+    using namespace hmoe;
+    void* scratch = nullptr;
+    const hmoe_status st = noalloc_scratch(&scratch);
+    if (st != HMOE_OK) return st;
+    return hmoe_read_status(scratch, status, near_ties, sequential_logits, stream);
 }

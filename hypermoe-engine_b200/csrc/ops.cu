@@ -10,7 +10,10 @@
 #include <climits>
 #include <cstring>
 #include <limits>
+#include <map>
+#include <mutex>
 #include <string>
+#include <utility>
 
 namespace cg = cooperative_groups;
 
@@ -22,6 +25,38 @@ std::atomic<long long> g_launches{0};
 }
 
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+namespace {
+std::mutex g_attr_mutex;
+std::map<std::pair<const void*, int>, int> g_smem_limit; // (kernel, device) -> bytes set
+std::map<int, int> g_sm_count;                           // device -> multiprocessors
+}
+
+cudaError_t set_smem_limit(const void* func, int bytes) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    std::lock_guard<std::mutex> lock(g_attr_mutex);
+    int& have = g_smem_limit[{func, dev}];
+    if (bytes <= have) return cudaSuccess;
+    err = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (err == cudaSuccess) have = bytes;
+    return err;
+}
+
+int current_sm_count() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    std::lock_guard<std::mutex> lock(g_attr_mutex);
+    int& n = g_sm_count[dev];
+    if (n <= 0) {
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            return 148;
+        }
+    }
+    return n;
+}
 
 void set_last_error(const char* what, cudaError_t err) {
     g_last_error = std::string(what) + ": " + cudaGetErrorString(err);
@@ -127,12 +162,9 @@ hmoe_status launch_int8_matmul(const float* left, const int8_t* right, float* ou
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    static size_t attr_set = 0;
-    if (smem > attr_set) {
-        cudaFuncSetAttribute(int8_matmul_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-        attr_set = smem;
-    }
-    const cudaError_t err = cudaLaunchKernelEx(&cfg, int8_matmul_kernel, left, right, out,
+    cudaError_t err = set_smem_limit(reinterpret_cast<const void*>(int8_matmul_kernel), static_cast<int>(smem));
+    if (err == cudaSuccess)
+        err = cudaLaunchKernelEx(&cfg, int8_matmul_kernel, left, right, out,
                                                static_cast<int>(rows), static_cast<int>(K),
                                                static_cast<int>(N), scale, static_cast<int>(zp), KS);
     if (err != cudaSuccess) {

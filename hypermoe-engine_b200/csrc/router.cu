@@ -1318,11 +1318,8 @@ hmoe_status launch_route_decode(const RouteArgs& a, double* scratch, cudaStream_
     cudaError_t err = cudaErrorInvalidValue;
 #define HMOE_DECODE_CASE(CC)                                                                                 \
     case CC: {                                                                                               \
-        static int attr_set = 0;                                                                             \
-        if (smem > attr_set) {                                                                               \
-            cudaFuncSetAttribute(route_decode_kernel<CC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
-            attr_set = smem;                                                                                 \
-        }                                                                                                    \
+        err = set_smem_limit(reinterpret_cast<const void*>(route_decode_kernel<CC>), smem);                  \
+        if (err != cudaSuccess) break;                                                                       \
         route_decode_kernel<CC><<<grid, 256, smem, stream>>>(d);                                             \
         err = cudaGetLastError();                                                                            \
         break;                                                                                               \
@@ -1374,12 +1371,9 @@ hmoe_status launch_route_tiled(const RouteArgs& a, cudaStream_t stream) {
     cudaError_t err = cudaErrorInvalidValue;
 #define HMOE_TILED_CASE(CC)                                                                                 \
     case CC: {                                                                                              \
-        static bool attr_set = false;                                                                       \
-        if (!attr_set) {                                                                                    \
-            cudaFuncSetAttribute(route_tiled_kernel<CC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
-            attr_set = true;                                                                                \
-        }                                                                                                   \
-        err = cudaLaunchKernelEx(&cfg, route_tiled_kernel<CC>, mx, mw, a, KS);                                      \
+        err = set_smem_limit(reinterpret_cast<const void*>(route_tiled_kernel<CC>), smem);                  \
+        if (err != cudaSuccess) break;                                                                      \
+        err = cudaLaunchKernelEx(&cfg, route_tiled_kernel<CC>, mx, mw, a, KS);                              \
         break;                                                                                              \
     }
     switch ((a.E + 31) / 32) {
@@ -1449,11 +1443,8 @@ hmoe_status launch_route(const float* x, const float* w, const float* bias,
     cudaError_t err = cudaErrorInvalidValue;
 #define HMOE_ROUTE_CASE(CC)                                                                          \
     case CC: {                                                                                       \
-        static int attr_set = 0;                                                                     \
-        if (smem > attr_set) {                                                                       \
-            cudaFuncSetAttribute(route_kernel<CC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem); \
-            attr_set = smem;                                                                         \
-        }                                                                                            \
+        err = set_smem_limit(reinterpret_cast<const void*>(route_kernel<CC>), smem);                \
+        if (err != cudaSuccess) break;                                                               \
         err = cudaLaunchKernelEx(&cfg, route_kernel<CC>, a, EQ, P, KS);                              \
         break;                                                                                       \
     }

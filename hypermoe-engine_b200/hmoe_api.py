@@ -42,7 +42,7 @@ EXPORTS = [
     "hmoe_ep_comm_destroy", "hmoe_ep_workspace_size", "hmoe_ep_moe_forward", "hmoe_ep_last_plan",
     "hmoe_moe_forward_noalloc", "hmoe_selftest_bounded_wait", "hmoe_ep_set_placement",
     "hmoe_ep_balanced_placement", "hmoe_set_route_variant", "hmoe_ep_register_workspace",
-    "hmoe_ep_selftest_flag_wait", "hmoe_ep_read_status",
+    "hmoe_ep_selftest_flag_wait", "hmoe_ep_read_status", "hmoe_noalloc_read_status",
 ]
 EP_MAX_RANKS = 64
 EP_UNIQUE_ID_BYTES = 128
@@ -131,6 +131,7 @@ def lib() -> ctypes.CDLL:
             "hmoe_ep_selftest_flag_wait": [vp, ctypes.c_uint64, ctypes.POINTER(i32)],
             "hmoe_ep_read_status": [vp, ctypes.POINTER(i32), ctypes.POINTER(i32), ctypes.POINTER(i32), vp],
             "hmoe_moe_forward_noalloc": [ctypes.POINTER(LayerDesc), vp, vp, sz, vp],
+            "hmoe_noalloc_read_status": [ctypes.POINTER(i32), ctypes.POINTER(i32), ctypes.POINTER(i32), vp],
             "hmoe_selftest_bounded_wait": [vp, ctypes.c_uint32, vp],
             "hmoe_ep_set_placement": [vp, vp, ctypes.c_uint32],
             "hmoe_ep_balanced_placement": [vp, ctypes.c_uint32, i32, vp],
@@ -153,6 +154,33 @@ def lib() -> ctypes.CDLL:
         L.hmoe_synth_arena.restype = None
         _lib = L
     return _lib
+
+
+_synth = None
+
+
+def use_synth_library(path: str) -> None:
+    """Takes the seeded-input functions (synth_normal, synth_zipf_bias,
+    make_host_layer, make_tokens) from `path`, a standalone build of the
+    same generator source (host/synth.cpp), instead of libhmoe.so.  The
+    benchmark's reference arm uses it so that it never loads the product
+    library; the values are identical."""
+    global _synth
+    L = ctypes.CDLL(path)
+    u64, f32, vp, sz = ctypes.c_uint64, ctypes.c_float, ctypes.c_void_p, ctypes.c_size_t
+    L.hmoe_synth_normal.argtypes = [u64, u64, f32, vp, sz, ctypes.c_int]
+    L.hmoe_synth_normal.restype = None
+    L.hmoe_synth_zipf_bias.argtypes = [u64, f32, vp, sz]
+    L.hmoe_synth_zipf_bias.restype = None
+    L.hmoe_synth_arena.argtypes = [u64, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                   ctypes.c_uint32, ctypes.c_uint32, f32, vp, u64, u64, u64, u64,
+                                   vp, ctypes.c_int]
+    L.hmoe_synth_arena.restype = None
+    _synth = L
+
+
+def _synth_lib() -> ctypes.CDLL:
+    return _synth if _synth is not None else lib()
 
 
 def check(fn: str, code: int) -> None:
@@ -182,13 +210,13 @@ def _stream(stream) -> int:
 def synth_normal(seed: int, stream: int, sigma: float, shape, threads: int = 0) -> np.ndarray:
     n = int(np.prod(shape))
     out = np.empty(n, dtype=np.float32)
-    lib().hmoe_synth_normal(seed, stream, sigma, out.ctypes.data, n, threads or os.cpu_count() or 1)
+    _synth_lib().hmoe_synth_normal(seed, stream, sigma, out.ctypes.data, n, threads or os.cpu_count() or 1)
     return out.reshape(shape)
 
 
 def synth_zipf_bias(seed: int, alpha: float, E: int) -> np.ndarray:
     out = np.empty(E, dtype=np.float32)
-    lib().hmoe_synth_zipf_bias(seed, alpha, out.ctypes.data, E)
+    _synth_lib().hmoe_synth_zipf_bias(seed, alpha, out.ctypes.data, E)
     return out
 
 
@@ -257,7 +285,7 @@ def make_host_layer(cfg: LayerConfig, seed: int = 0, layer: int = 0, threads: in
     stride = cfg.expert_stride
     arena = np.zeros(total * stride, dtype=np.int8)
     quant = (ExpertQuant * total)()
-    lib().hmoe_synth_arena(seed, layer, 0, total, H, I, cfg.sigma, arena.ctypes.data, stride,
+    _synth_lib().hmoe_synth_arena(seed, layer, 0, total, H, I, cfg.sigma, arena.ctypes.data, stride,
                            0, cfg.proj_bytes, 2 * cfg.proj_bytes, ctypes.addressof(quant), threads)
     qbytes = np.frombuffer(bytes(quant), dtype=np.uint8).copy()
     scales = np.array([[quant[e].scale[p] for p in range(3)] for e in range(total)], dtype=np.float32)

@@ -214,10 +214,21 @@ hmoe_status hmoe_moe_forward_host(const hmoe_layer_desc *desc,
  * 16 MiB return HMOE_WORKSPACE_TOO_SMALL (C3 layer: up to 185 tokens).
  * Calls that overlap in time on one device race on the shared scratch.
  * The first call on a device looks the array up (cudaGetSymbolAddress);
- * make it before any stream capture on that device. */
+ * make it before any stream capture on that device.  The looked-up address
+ * is kept for the life of the process: it is not valid across
+ * cudaDeviceReset. */
 hmoe_status hmoe_moe_forward_noalloc(const hmoe_layer_desc *desc,
                                      const float *x, float *y, size_t tokens,
                                      void *stream);
+
+/* hmoe_read_status for hmoe_moe_forward_noalloc: reads (and resets) the
+ * device status word the last no-allocation call on the current device left
+ * at the start of the static scratch -- HMOE_NON_FINITE_ROUTER for a NaN or
+ * Inf router input, HMOE_TIMEOUT from a bounded device wait, the near-tie
+ * and sequential-logit counts.  Synchronises `stream`.  Like the forward
+ * call it has no counterpart in the reference. */
+hmoe_status hmoe_noalloc_read_status(int32_t *status, int32_t *near_ties,
+                                     int32_t *sequential_logits, void *stream);
 
 /* Forces the expert-MLP variant for measurement: 0 = automatic (GEMV for
  * experts with few tokens, tensor-core GEMM otherwise), 1 = GEMV only,

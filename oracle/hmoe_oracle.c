@@ -15,7 +15,8 @@
  *   hmo_int8_matmul     src/tensor/backend/CpuTensorBackend.cpp:133-190
  *   hmo_silu            src/tensor/activation/Activation.cpp:44
  *   hmo_expert_mlp      src/experts/ExpertExecutor.cpp:43-138
- *   hmo_moe_layer       src/core/runtime/MoERuntime.cpp:58-349 (CPU branch:
+ *   hmo_moe_layer[_threads]
+ *                       src/core/runtime/MoERuntime.cpp:58-349 (CPU branch:
  *                       host gather :288-298, combine :311-325)
  *   hmo_quantize_int8   src/tensor/quantization/Quantization.cpp:45-79
  *
@@ -28,6 +29,7 @@
  * build does (no FMA in the baseline ISA).
  */
 #include <math.h>
+#include <pthread.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -197,14 +199,72 @@ void hmo_expert_mlp(const float *x, size_t rows, size_t H, size_t I,
  * experts (PackedModelRuntime.cpp:267-270 rejects them); this is the
  * build's definition for the Qwen1.5-MoE configuration.
  *
+ * hmo_moe_layer_threads computes the experts' MLPs on `threads` host
+ * threads (each expert's rows are independent: gather, three INT8 GEMMs,
+ * SiLU and multiply see exactly the numbers and order of the sequential
+ * loop), then combines `out[tok] += w * y` in ascending expert id on one
+ * thread (MoERuntime.cpp:311-325).  The result is bit-identical for any
+ * thread count.
+ *
  * Optional outputs (may be NULL): ids/scores [T,k], offsets [E+1]. */
-int hmo_moe_layer(const float *x, size_t T, size_t H, size_t I, size_t E,
-                  size_t k, int softmax, int renorm, const float *router_w,
-                  const float *router_bias, size_t n_shared,
-                  const int8_t *arena, size_t stride, size_t gate_off,
-                  size_t up_off, size_t down_off, const float *qscale,
-                  const int32_t *qzp, float *out, uint32_t *ids_out,
-                  float *scores_out, int32_t *offsets_out) {
+typedef struct {
+    const float *x;
+    size_t T, H, I, E;
+    const int8_t *arena;
+    size_t stride, gate_off, up_off, down_off;
+    const float *qscale;
+    const int32_t *qzp;
+    const int32_t *off;
+    const uint32_t *gt;
+    const size_t *row0; /* first row of expert e in yall */
+    float *yall;
+    size_t total;
+    size_t next; /* work counter (guarded by lock) */
+    pthread_mutex_t lock;
+} hmo_layer_job;
+
+static size_t expert_rows(const hmo_layer_job *j, size_t e) {
+    return e < j->E ? (size_t)(j->off[e + 1] - j->off[e]) : j->T;
+}
+
+static void *layer_worker(void *arg) {
+    hmo_layer_job *j = (hmo_layer_job *)arg;
+    float *xin = NULL;
+    size_t cap = 0;
+    for (;;) {
+        pthread_mutex_lock(&j->lock);
+        const size_t e = j->next++;
+        pthread_mutex_unlock(&j->lock);
+        if (e >= j->total) break;
+        const size_t n = expert_rows(j, e);
+        if (n == 0) continue;
+        if (n > cap) {
+            free(xin);
+            cap = n;
+            xin = (float *)malloc(cap * j->H * sizeof(float));
+        }
+        const uint32_t *toks = e < j->E ? j->gt + j->off[e] : NULL;
+        for (size_t r = 0; r < n; ++r) {
+            const size_t tok = toks ? toks[r] : r;
+            memcpy(xin + r * j->H, j->x + tok * j->H, j->H * sizeof(float));
+        }
+        const int8_t *blob = j->arena + e * j->stride;
+        hmo_expert_mlp(xin, n, j->H, j->I, blob + j->gate_off, blob + j->up_off,
+                       blob + j->down_off, j->qscale + 3 * e, j->qzp + 3 * e,
+                       j->yall + j->row0[e] * j->H);
+    }
+    free(xin);
+    return NULL;
+}
+
+int hmo_moe_layer_threads(const float *x, size_t T, size_t H, size_t I,
+                          size_t E, size_t k, int softmax, int renorm,
+                          const float *router_w, const float *router_bias,
+                          size_t n_shared, const int8_t *arena, size_t stride,
+                          size_t gate_off, size_t up_off, size_t down_off,
+                          const float *qscale, const int32_t *qzp, float *out,
+                          uint32_t *ids_out, float *scores_out,
+                          int32_t *offsets_out, int threads) {
     uint32_t *ids = (uint32_t *)malloc(T * k * sizeof(uint32_t));
     float *scores = (float *)malloc(T * k * sizeof(float));
     int32_t *off = (int32_t *)malloc((E + 1) * sizeof(int32_t));
@@ -213,29 +273,36 @@ int hmo_moe_layer(const float *x, size_t T, size_t H, size_t I, size_t E,
     int st = hmo_route_batch(x, router_w, router_bias, T, H, E, k, softmax,
                              renorm, ids, scores, off, gt, gs, NULL);
     if (st == HMO_OK) {
-        memset(out, 0, T * H * sizeof(float));
         const size_t total = E + n_shared;
-        float *xin = (float *)malloc(T * H * sizeof(float));
-        float *yout = (float *)malloc(T * H * sizeof(float));
+        hmo_layer_job j;
+        memset(&j, 0, sizeof(j));
+        j.x = x; j.T = T; j.H = H; j.I = I; j.E = E;
+        j.arena = arena; j.stride = stride;
+        j.gate_off = gate_off; j.up_off = up_off; j.down_off = down_off;
+        j.qscale = qscale; j.qzp = qzp; j.off = off; j.gt = gt;
+        j.total = total;
+        size_t *row0 = (size_t *)malloc((total + 1) * sizeof(size_t));
+        row0[0] = 0;
+        for (size_t e = 0; e < total; ++e) row0[e + 1] = row0[e] + expert_rows(&j, e);
+        j.row0 = row0;
+        j.yall = (float *)malloc((row0[total] ? row0[total] : 1) * H * sizeof(float));
+        pthread_mutex_init(&j.lock, NULL);
+        int nt = threads < 1 ? 1 : threads;
+        if ((size_t)nt > total) nt = (int)total;
+        pthread_t *tid = (pthread_t *)malloc((size_t)nt * sizeof(pthread_t));
+        int started = 0;
+        for (int i = 1; i < nt; ++i)
+            if (pthread_create(&tid[started], NULL, layer_worker, &j) == 0) ++started;
+        layer_worker(&j);
+        for (int i = 0; i < started; ++i) pthread_join(tid[i], NULL);
+        pthread_mutex_destroy(&j.lock);
+        free(tid);
+        memset(out, 0, T * H * sizeof(float));
         for (size_t e = 0; e < total; ++e) {
-            size_t n;
-            const uint32_t *toks = NULL;
-            const float *w = NULL;
-            if (e < E) {
-                n = (size_t)(off[e + 1] - off[e]);
-                toks = gt + off[e];
-                w = gs + off[e];
-            } else {
-                n = T;
-            }
-            if (n == 0) continue;
-            for (size_t r = 0; r < n; ++r) {
-                const size_t tok = toks ? toks[r] : r;
-                memcpy(xin + r * H, x + tok * H, H * sizeof(float));
-            }
-            const int8_t *blob = arena + e * stride;
-            hmo_expert_mlp(xin, n, H, I, blob + gate_off, blob + up_off,
-                           blob + down_off, qscale + 3 * e, qzp + 3 * e, yout);
+            const size_t n = expert_rows(&j, e);
+            const uint32_t *toks = e < E ? gt + off[e] : NULL;
+            const float *w = e < E ? gs + off[e] : NULL;
+            const float *yout = j.yall + row0[e] * H;
             for (size_t r = 0; r < n; ++r) {
                 const size_t tok = toks ? toks[r] : r;
                 const float wt = w ? w[r] : 1.0f;
@@ -243,8 +310,8 @@ int hmo_moe_layer(const float *x, size_t T, size_t H, size_t I, size_t E,
                     out[tok * H + h] += wt * yout[r * H + h];
             }
         }
-        free(xin);
-        free(yout);
+        free(j.yall);
+        free(row0);
         if (ids_out) memcpy(ids_out, ids, T * k * sizeof(uint32_t));
         if (scores_out) memcpy(scores_out, scores, T * k * sizeof(float));
         if (offsets_out) memcpy(offsets_out, off, (E + 1) * sizeof(int32_t));
@@ -255,6 +322,19 @@ int hmo_moe_layer(const float *x, size_t T, size_t H, size_t I, size_t E,
     free(gt);
     free(gs);
     return st;
+}
+
+int hmo_moe_layer(const float *x, size_t T, size_t H, size_t I, size_t E,
+                  size_t k, int softmax, int renorm, const float *router_w,
+                  const float *router_bias, size_t n_shared,
+                  const int8_t *arena, size_t stride, size_t gate_off,
+                  size_t up_off, size_t down_off, const float *qscale,
+                  const int32_t *qzp, float *out, uint32_t *ids_out,
+                  float *scores_out, int32_t *offsets_out) {
+    return hmo_moe_layer_threads(x, T, H, I, E, k, softmax, renorm, router_w,
+                                 router_bias, n_shared, arena, stride,
+                                 gate_off, up_off, down_off, qscale, qzp, out,
+                                 ids_out, scores_out, offsets_out, 1);
 }
 
 /* ---------------------------------------------------------- quantisation */

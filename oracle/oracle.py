@@ -19,6 +19,10 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 PORT_PATH = os.path.join(HERE, "_build", "libhmoe_oracle.so")
 REF_PATH = os.path.join(HERE, "_ref", "libhmoe_ref.so")
+# the seeded input generator built apart from libhmoe.so (oracle/Makefile)
+SYNTH_PATH = os.path.join(HERE, "_build", "libhmoe_synth.so")
+# the reference's own CUDA path, timed as the bar to beat (ref_cuda_bench.cpp)
+REF_CUDA_BENCH = os.path.join(HERE, "_ref", "ref_cuda_bench")
 
 _port = None
 _ref = None
@@ -26,14 +30,22 @@ _ref = None
 vp, sz, i32, f32 = ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int32, ctypes.c_float
 
 
+def reference_dir():
+    """The reference's source tree: $HMOE_REFERENCE, else a checkout named
+    `reference` beside this repository; None when neither holds `src/`
+    (e.g. on a GPU box, which uses the prebuilt oracle/_ref)."""
+    d = os.environ.get("HMOE_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return d if os.path.isdir(os.path.join(d, "src")) else None
+
+
 def build(reference: bool = True) -> None:
     """Builds the port (always) and the reference library (when its sources exist)."""
     targets = ["oracle"]
-    if reference and os.path.isdir(os.environ.get("HMOE_REFERENCE", "/root/reference")):
-        targets.append("ref")
     env = dict(os.environ)
-    if "HMOE_REFERENCE" in os.environ:
-        env["REF"] = os.environ["HMOE_REFERENCE"]
+    ref_dir = reference_dir()
+    if reference and ref_dir:
+        targets.append("ref")
+        env["REF"] = ref_dir
     subprocess.run(["make", "-C", HERE, "-j8", *targets], check=True, env=env,
                    stdout=subprocess.DEVNULL)
 
@@ -56,6 +68,7 @@ def port() -> ctypes.CDLL:
         L.hmo_expert_mlp.restype = None
         L.hmo_moe_layer.argtypes = [vp, sz, sz, sz, sz, sz, ctypes.c_int, ctypes.c_int, vp, vp, sz,
                                     vp, sz, sz, sz, sz, vp, vp, vp, vp, vp, vp]
+        L.hmo_moe_layer_threads.argtypes = L.hmo_moe_layer.argtypes + [ctypes.c_int]
         L.hmo_quantize_int8.argtypes = [vp, sz, vp, vp, vp, vp]
         L.hmo_silu.argtypes = [f32]
         L.hmo_silu.restype = f32
@@ -161,8 +174,10 @@ def quantize(lib, w):
     return q, s.value, z.value, e.value
 
 
-def moe_layer_port(host_layer, x):
-    """Full layer through the C port: (out [T,H], ids, scores, offsets)."""
+def moe_layer_port(host_layer, x, threads=None):
+    """Full layer through the C port: (out [T,H], ids, scores, offsets).
+    Expert MLPs run on `threads` host threads (default: every core); the
+    result is bit-identical for any thread count."""
     L = port()
     c = host_layer.cfg
     x = np.ascontiguousarray(x, np.float32)
@@ -171,11 +186,11 @@ def moe_layer_port(host_layer, x):
     ids = np.zeros((T, c.top_k), np.uint32)
     sc = np.zeros((T, c.top_k), np.float32)
     off = np.zeros(c.experts + 1, np.int32)
-    st = L.hmo_moe_layer(_p(x), T, c.hidden, c.intermediate, c.experts, c.top_k, int(c.softmax),
-                         int(c.renormalize), _p(host_layer.router_w), _p(host_layer.router_bias),
-                         c.shared_experts, _p(host_layer.arena), c.expert_stride, 0, c.proj_bytes,
-                         2 * c.proj_bytes, _p(host_layer.scales), _p(host_layer.zps), _p(out), _p(ids),
-                         _p(sc), _p(off))
+    st = L.hmo_moe_layer_threads(_p(x), T, c.hidden, c.intermediate, c.experts, c.top_k, int(c.softmax),
+                                 int(c.renormalize), _p(host_layer.router_w), _p(host_layer.router_bias),
+                                 c.shared_experts, _p(host_layer.arena), c.expert_stride, 0, c.proj_bytes,
+                                 2 * c.proj_bytes, _p(host_layer.scales), _p(host_layer.zps), _p(out), _p(ids),
+                                 _p(sc), _p(off), int(threads or os.cpu_count() or 1))
     if st != 0:
         raise OracleError(f"moe layer failed with status {st}")
     return out, ids, sc, off

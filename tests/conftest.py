@@ -18,6 +18,21 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200, sm_100a)")
 
 
+_HOST_LAYERS = {}
+
+
+def host_layer(cfg_name, seed):
+    """Seeded synthetic layer of a named configuration, synthesized once per
+    test session (the C5 arena is 2.4 GB and takes seconds to generate)."""
+    import hmoe_api
+    key = (cfg_name, seed)
+    if key not in _HOST_LAYERS:
+        if len(_HOST_LAYERS) >= 2:
+            _HOST_LAYERS.clear()
+        _HOST_LAYERS[key] = hmoe_api.make_host_layer(hmoe_api.CONFIGS[cfg_name], seed=seed)
+    return _HOST_LAYERS[key]
+
+
 def load_golden(name):
     return np.load(os.path.join(GOLDEN, name), allow_pickle=False)
 

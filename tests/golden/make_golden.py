@@ -144,6 +144,7 @@ def main():
     gen_layer("c1_t64", "c1", 64, 0)
     gen_layer("c3_t16", "c3", 16, 0)
     gen_layer("c2_t3", "c2", 3, 1)
+    gen_layer("c5_t4", "c5", 4, 2)
     for f in sorted(os.listdir(OUT)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(OUT, f)))

@@ -12,6 +12,7 @@ import pytest
 
 import hmoe_api as H
 import oracle as O
+from conftest import host_layer
 
 
 def sha(a):
@@ -98,10 +99,10 @@ def test_quantizer_matches_reference(port, golden):
 
 
 @pytest.mark.parametrize("name,cfg,T,seed", [("c1_t64", "c1", 64, 0), ("c3_t16", "c3", 16, 0),
-                                              ("c2_t3", "c2", 3, 1)])
+                                              ("c2_t3", "c2", 3, 1), ("c5_t4", "c5", 4, 2)])
 def test_layer_matches_reference_fixture(port, golden, name, cfg, T, seed):
     g = golden(f"layer_{name}.npz")
-    hl = H.make_host_layer(H.CONFIGS[cfg], seed=seed)
+    hl = host_layer(cfg, seed)
     x = H.make_tokens(H.CONFIGS[cfg], T, seed=seed)
     # the regenerated inputs are the ones the fixture was made from
     assert sha(x) == str(g["sha_x"])

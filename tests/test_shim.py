@@ -17,13 +17,15 @@ import subprocess
 import pytest
 
 import hmoe_api as H
+import oracle as O
 from tolerance import assert_op_close
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PKG = os.path.join(ROOT, "hypermoe-engine_b200")
 SHIM = os.path.join(PKG, "lib", "libhmoe_shim.so")
 SHIM_SRC = os.path.join(PKG, "host", "CudaKernelsShim.cpp")
-REF_SRC = "/root/reference/src"
+REF_DIR = O.reference_dir()
+REF_SRC = os.path.join(REF_DIR, "src") if REF_DIR else None
 
 SYMBOLS = {
     "activation": "_ZN8hypermoe7backend4cuda7kernels10activationEiPKfPfmPv",
@@ -53,7 +55,7 @@ def test_shim_exports_reference_symbols():
         getattr(lib, mangled)
 
 
-@pytest.mark.skipif(not os.path.isdir(REF_SRC), reason="reference tree not present")
+@pytest.mark.skipif(REF_SRC is None, reason="reference tree not present")
 def test_shim_compiles_against_reference_header():
     subprocess.run(["g++", "-std=c++20", "-fsyntax-only", "-DHMOE_SHIM_WITH_REFERENCE_HEADERS",
                     "-I", os.path.join(ROOT, "include"), "-I", REF_SRC, SHIM_SRC], check=True)

@@ -1,8 +1,11 @@
 """hmoe_moe_forward_noalloc (scratch in a static device array, no caller
 workspace) against hmoe_moe_forward on the same inputs: two calls in a row
-must both equal the workspace entry point bit for bit, and a batch beyond
-the 16 MiB scratch must be refused.  Collected last so it also runs after
-every other GPU test in the same process."""
+must both equal the workspace entry point bit for bit, the device status
+word it leaves in the static scratch must read back through
+hmoe_noalloc_read_status (zero after a clean call, HMOE_NON_FINITE_ROUTER
+after a NaN or Inf router input), and a batch beyond the 16 MiB scratch must
+be refused.  Collected last so it also runs after every other GPU test in
+the same process."""
 import ctypes
 
 import numpy as np
@@ -11,6 +14,14 @@ import pytest
 import hmoe_api as H
 
 pytestmark = pytest.mark.gpu
+
+
+def noalloc_status():
+    import torch
+    st, ties, seq = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+    H.check("hmoe_noalloc_read_status", H.lib().hmoe_noalloc_read_status(
+        ctypes.byref(st), ctypes.byref(ties), ctypes.byref(seq), torch.cuda.current_stream().cuda_stream))
+    return st.value, ties.value, seq.value
 
 
 @pytest.mark.parametrize("cfg_name,T", [("c1", 64), ("c3", 16), ("c3", 1), ("c2", 3)])
@@ -29,8 +40,29 @@ def test_noalloc_forward_matches_workspace_forward(cuda, cfg_name, T):
                 H.lib().hmoe_moe_forward_noalloc(ctypes.byref(dl.desc), x.data_ptr(), y.data_ptr(), T, s))
         torch.cuda.synchronize()
         outs.append(y.cpu().numpy())
+        assert noalloc_status()[0] == 0
     for y in outs:
         assert np.array_equal(y, ref), float(np.nanmax(np.abs(y - ref)))
+
+
+@pytest.mark.parametrize("bad", [float("inf"), float("nan")])
+def test_noalloc_reports_non_finite_router_input(cuda, bad):
+    import torch
+    cfg = H.CONFIGS["c1"]
+    dl = H.DeviceLayer(H.make_host_layer(cfg, seed=3), cuda)
+    x_np = H.make_tokens(cfg, 8, seed=3)
+    x_np[5, 17] = bad
+    x = torch.from_numpy(x_np).to(cuda)
+    y = torch.empty_like(x)
+    s = torch.cuda.current_stream().cuda_stream
+    H.check("hmoe_moe_forward_noalloc",
+            H.lib().hmoe_moe_forward_noalloc(ctypes.byref(dl.desc), x.data_ptr(), y.data_ptr(), 8, s))
+    assert noalloc_status()[0] == 2  # HMOE_NON_FINITE_ROUTER
+    assert noalloc_status()[0] == 0  # reading resets the word
+    x[5, 17] = 0.0
+    H.check("hmoe_moe_forward_noalloc",
+            H.lib().hmoe_moe_forward_noalloc(ctypes.byref(dl.desc), x.data_ptr(), y.data_ptr(), 8, s))
+    assert noalloc_status()[0] == 0
 
 
 def test_noalloc_rejects_oversized_batch(cuda):
