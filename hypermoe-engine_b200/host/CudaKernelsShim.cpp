@@ -14,6 +14,10 @@
 // rmsNorm, rope and causalAttention are not on the MoE hot path and stay
 // the reference's own.
 //
+// With HMOE_SHIM_TRACE set in the environment, the process prints at exit
+// how often each launcher here was called (stderr, one line), so a caller
+// can see that its kernel launches went through this file.
+//
 // Build modes:
 //   * inside the reference tree: -DHMOE_SHIM_WITH_REFERENCE_HEADERS and the
 //     reference's src/ on the include path; the header's declarations are
@@ -23,8 +27,11 @@
 //     below, which spell the same signatures.
 #include "hmoe.h"
 
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
+#include <cstdio>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 #include <type_traits>
@@ -57,6 +64,22 @@ void zero(float* output, std::size_t elements, StreamHandle stream);
 namespace hypermoe::backend::cuda::kernels {
 namespace {
 
+enum Op { kActivation, kMatmul, kCooperative, kRouterTopK, kGather, kScatter, kZero, kOps };
+const char* const kOpNames[kOps] = {"activation", "int8WeightMatmul", "int8WeightMatmulCooperative",
+                                    "routerTopK", "gatherRows", "scatterAddRows", "zero"};
+std::atomic<long long> g_calls[kOps];
+
+struct CallReport {
+    ~CallReport() {
+        if (!std::getenv("HMOE_SHIM_TRACE")) return;
+        std::fprintf(stderr, "hmoe shim calls:");
+        for (int i = 0; i < kOps; ++i) std::fprintf(stderr, " %s=%lld", kOpNames[i], g_calls[i].load());
+        std::fprintf(stderr, "\n");
+    }
+} g_report;
+
+void note(Op op) { g_calls[op].fetch_add(1, std::memory_order_relaxed); }
+
 // Converts a status into the reference's exception for that failure.
 void raise(hmoe_status status, const char* operation) {
     if (status == HMOE_OK) return;
@@ -68,12 +91,14 @@ void raise(hmoe_status status, const char* operation) {
 } // namespace
 
 void activation(int type, const float* input, float* output, std::size_t elements, StreamHandle stream) {
+    note(kActivation);
     raise(hmoe_activation(type, input, output, elements, stream), "CUDA activation kernel");
 }
 
 void int8WeightMatmul(const float* left, const std::int8_t* right, float* output, std::size_t rows,
                       std::size_t inner, std::size_t columns, float scale, std::int32_t zeroPoint,
                       StreamHandle stream) {
+    note(kMatmul);
     raise(hmoe_int8_weight_matmul(left, right, output, rows, inner, columns, scale, zeroPoint, stream),
           "CUDA INT8 weight matmul kernel");
 }
@@ -82,6 +107,7 @@ void int8WeightMatmulCooperative(const float* left, const std::int8_t* right, fl
                                  std::size_t rows, std::size_t inner, std::size_t columns,
                                  std::size_t partitions, float scale, std::int32_t zeroPoint,
                                  StreamHandle stream) {
+    note(kCooperative);
     const hmoe_status st = hmoe_int8_weight_matmul_cooperative(left, right, output, partials, rows, inner, columns,
                                                                partitions, scale, zeroPoint, stream);
     if (st == HMOE_INVALID_ARGUMENT)
@@ -91,6 +117,7 @@ void int8WeightMatmulCooperative(const float* left, const std::int8_t* right, fl
 
 void routerTopK(float* logits, std::size_t tokens, std::size_t experts, std::size_t topK, bool softmax,
                 bool renormalize, std::uint32_t* selectedIds, float* selectedScores, StreamHandle stream) {
+    note(kRouterTopK);
     raise(hmoe_router_topk(logits, tokens, experts, topK, softmax ? 1 : 0, renormalize ? 1 : 0, selectedIds,
                            selectedScores, stream),
           "CUDA router top-k kernel");
@@ -98,15 +125,18 @@ void routerTopK(float* logits, std::size_t tokens, std::size_t experts, std::siz
 
 void gatherRows(const float* input, float* output, const std::uint32_t* rows, std::size_t rowCount,
                 std::size_t width, StreamHandle stream) {
+    note(kGather);
     raise(hmoe_gather_rows(input, output, rows, rowCount, width, stream), "CUDA gather kernel");
 }
 
 void scatterAddRows(const float* input, float* output, const std::uint32_t* rows, const float* weights,
                     std::size_t rowCount, std::size_t width, StreamHandle stream) {
+    note(kScatter);
     raise(hmoe_scatter_add_rows(input, output, rows, weights, rowCount, width, stream), "CUDA scatter kernel");
 }
 
 void zero(float* output, std::size_t elements, StreamHandle stream) {
+    note(kZero);
     raise(hmoe_zero(output, elements, stream), "CUDA zero kernel");
 }
 
