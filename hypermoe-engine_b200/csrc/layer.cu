@@ -115,14 +115,17 @@ struct LocalOut {
 __global__ void __launch_bounds__(256) combine_kernel(const __nv_bfloat16* __restrict__ yrows,
                                                       const int32_t* __restrict__ inv,
                                                       const uint32_t* __restrict__ ids, int k, int E, int slots,
-                                                      int H, float* __restrict__ out) {
-    combine_token(inv, ids, k, E, slots, H, blockIdx.x, out, LocalOut{yrows, H});
+                                                      int H, float* out, const float* residual,
+                                                      __nv_bfloat16* __restrict__ out16) {
+    combine_token(inv, ids, k, E, slots, H, blockIdx.x, out, LocalOut{yrows, H}, residual, out16);
 }
 
 hmoe_status launch_combine(const __nv_bfloat16* yrows, const int32_t* inv, const uint32_t* ids, int k, int E,
-                           int tokens, int slots, int H, float* out, cudaStream_t s) {
+                           int tokens, int slots, int H, float* out, cudaStream_t s, const float* residual,
+                           __nv_bfloat16* out16) {
     if (tokens <= 0) return HMOE_OK;
-    combine_kernel<<<static_cast<unsigned>(tokens), 256, 0, s>>>(yrows, inv, ids, k, E, slots, H, out);
+    combine_kernel<<<static_cast<unsigned>(tokens), 256, 0, s>>>(yrows, inv, ids, k, E, slots, H, out, residual,
+                                                                 out16);
     return check_launch("hmoe combine kernel");
 }
 
@@ -272,8 +275,15 @@ hmoe_status hmoe_route(const hmoe_layer_desc* desc, const float* x, size_t token
     return HMOE_OK;
 }
 
-hmoe_status hmoe_moe_forward(const hmoe_layer_desc* desc, const float* x, float* y, size_t tokens,
-                             void* workspace, size_t workspace_bytes, void* stream) {
+} // extern "C"
+
+namespace hmoe {
+
+// The fused layer; residual and y16 are optional (see
+// hmoe_moe_forward_residual).
+hmoe_status forward_layer(const hmoe_layer_desc* desc, const float* x, const float* residual, float* y,
+                          __nv_bfloat16* y16, size_t tokens, void* workspace, size_t workspace_bytes,
+                          void* stream) {
     const hmoe_status v = validate_desc(desc);
     if (v != HMOE_OK) return v;
     if (tokens == 0) return HMOE_OK;
@@ -295,9 +305,25 @@ hmoe_status hmoe_moe_forward(const hmoe_layer_desc* desc, const float* x, float*
     r = run_experts(run, use_gemv(static_cast<long>(tokens) * slots, run.H, run.I), true, s);
     if (r != HMOE_OK) return r;
     r = launch_combine(run.yrows, reinterpret_cast<int32_t*>(ws + w.inv), nullptr, 0, E, static_cast<int>(tokens),
-                       slots, static_cast<int>(desc->hidden), y, s);
+                       slots, static_cast<int>(desc->hidden), y, s, residual, y16);
     stage(5, s);
     return r;
+}
+
+} // namespace hmoe
+
+extern "C" {
+
+hmoe_status hmoe_moe_forward(const hmoe_layer_desc* desc, const float* x, float* y, size_t tokens,
+                             void* workspace, size_t workspace_bytes, void* stream) {
+    return forward_layer(desc, x, nullptr, y, nullptr, tokens, workspace, workspace_bytes, stream);
+}
+
+hmoe_status hmoe_moe_forward_residual(const hmoe_layer_desc* desc, const float* x, const float* residual,
+                                      float* y, uint16_t* y_bf16, size_t tokens, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+    return forward_layer(desc, x, residual, y, reinterpret_cast<__nv_bfloat16*>(y_bf16), tokens, workspace,
+                         workspace_bytes, stream);
 }
 
 hmoe_status hmoe_moe_forward_host(const hmoe_layer_desc* desc, const float* x_host, float* y_host,

@@ -128,8 +128,11 @@ hmoe_status launch_group(const uint32_t* ids, const float* scores, const int32_t
 // out[t] = sum of the token's rows in ascending expert id: routed slot j has
 // expert ids[t, j] (when ids is null the row order is the expert order),
 // shared expert s counts as expert E + s.
+// residual (may be null, may equal out): out[t] = residual[t] + sum, one
+// FP32 rounding; out16 (may be null): a BF16 copy of out.
 hmoe_status launch_combine(const __nv_bfloat16* yrows, const int32_t* inv, const uint32_t* ids, int k, int E,
-                           int tokens, int slots, int H, float* out, cudaStream_t stream);
+                           int tokens, int slots, int H, float* out, cudaStream_t stream,
+                           const float* residual = nullptr, __nv_bfloat16* out16 = nullptr);
 
 // Layer driver pieces shared by the single-GPU and expert-parallel paths.
 hmoe_status validate_layer(const hmoe_layer_desc* d);

@@ -65,11 +65,16 @@ __device__ __forceinline__ void permute_token(const float* __restrict__ x, const
 // ascending by expert id (routing ids when given, else row order, which is
 // expert order without a placement) and accumulated in that order from zero,
 // as the reference's combine loop does (MoERuntime.cpp:311-325).  src(row)
-// gives the BF16 row.  One CTA.
+// gives the BF16 row.  With `residual`, the finished sum is added to
+// residual[t] with one FP32 rounding, as the reference's layer adds the MoE
+// output to its residual (MoELayer.cpp:37-39); residual may be `out`
+// itself.  With `out16`, the result is also written as BF16 (round to
+// nearest even).  One CTA.
 template <class Src>
 __device__ __forceinline__ void combine_token(const int32_t* __restrict__ inv, const uint32_t* __restrict__ ids,
-                                              int k, int E, int slots, int H, int t, float* __restrict__ out,
-                                              const Src& src) {
+                                              int k, int E, int slots, int H, int t, float* out,
+                                              const Src& src, const float* residual = nullptr,
+                                              __nv_bfloat16* __restrict__ out16 = nullptr) {
     __shared__ const __nv_bfloat16* rows_s[kMaxSlots];
     if (threadIdx.x == 0) {
         int keys[kMaxSlots];
@@ -110,9 +115,25 @@ __device__ __forceinline__ void combine_token(const int32_t* __restrict__ inv, c
                 }
             }
         }
+        if (residual) {
+            const float4* rs = reinterpret_cast<const float4*>(residual + static_cast<size_t>(t) * H) + 2 * c;
+            const float4 r0 = rs[0], r1 = rs[1];
+            const float r[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(r[i], acc[i]);
+        }
         float4* o = reinterpret_cast<float4*>(out + static_cast<size_t>(t) * H) + 2 * c;
         o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
         o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        if (out16) {
+            uint32_t b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                const __nv_bfloat162 v = __floats2bfloat162_rn(acc[2 * i], acc[2 * i + 1]);
+                b[i] = *reinterpret_cast<const uint32_t*>(&v);
+            }
+            reinterpret_cast<uint4*>(out16 + static_cast<size_t>(t) * H)[c] = make_uint4(b[0], b[1], b[2], b[3]);
+        }
     }
 }
 

@@ -43,6 +43,7 @@ EXPORTS = [
     "hmoe_moe_forward_noalloc", "hmoe_selftest_bounded_wait", "hmoe_ep_set_placement",
     "hmoe_ep_balanced_placement", "hmoe_set_route_variant", "hmoe_ep_register_workspace",
     "hmoe_ep_selftest_flag_wait", "hmoe_ep_read_status", "hmoe_noalloc_read_status",
+    "hmoe_moe_forward_residual",
 ]
 EP_MAX_RANKS = 64
 EP_UNIQUE_ID_BYTES = 128
@@ -114,6 +115,7 @@ def lib() -> ctypes.CDLL:
             "hmoe_route": [ctypes.POINTER(LayerDesc), vp, sz, vp, vp, vp, vp, vp, vp, sz, vp],
             "hmoe_moe_forward": [ctypes.POINTER(LayerDesc), vp, vp, sz, vp, sz, vp],
             "hmoe_moe_forward_host": [ctypes.POINTER(LayerDesc), vp, vp, sz, vp, sz, vp],
+            "hmoe_moe_forward_residual": [ctypes.POINTER(LayerDesc), vp, vp, vp, vp, sz, vp, sz, vp],
             "hmoe_set_variant": [i32],
             "hmoe_set_route_variant": [i32],
             "hmoe_read_status": [vp, ctypes.POINTER(i32), ctypes.POINTER(i32), ctypes.POINTER(i32), vp],
@@ -348,10 +350,26 @@ class DeviceLayer:
             ctypes.byref(self.desc), x.data_ptr(), y.data_ptr(), T, ws.data_ptr(), ws.numel(), _stream(stream)))
         return y
 
-    def forward_host(self, x_host, y_host, stream=None):
-        """x_host/y_host: page-locked CPU tensors [T, H] FP32."""
+    def forward_residual(self, x, residual=None, y=None, y_bf16=None, stream=None):
+        """y = residual + layer(x) (FP32, one rounding), and optionally its
+        BF16 copy y_bf16 (a torch.bfloat16 tensor [T, H])."""
+        import torch
+        T = x.shape[0]
+        if y is None:
+            y = torch.empty((T, self.cfg.hidden), dtype=torch.float32, device=x.device)
+        ws = self.workspace(T)
+        check("hmoe_moe_forward_residual", lib().hmoe_moe_forward_residual(
+            ctypes.byref(self.desc), x.data_ptr(), _ptr(residual), y.data_ptr(), _ptr(y_bf16), T,
+            ws.data_ptr(), ws.numel(), _stream(stream)))
+        return y
+
+    def forward_host(self, x_host, y_host, stream=None, workspace=None):
+        """x_host/y_host: page-locked CPU tensors [T, H] FP32.  `workspace`
+        (a device uint8 tensor of at least workspace_bytes(T, host_io=True))
+        replaces the layer's own, so that calls on different streams can be
+        in flight together."""
         T = x_host.shape[0]
-        ws = self.workspace(T, host_io=True)
+        ws = workspace if workspace is not None else self.workspace(T, host_io=True)
         check("hmoe_moe_forward_host", lib().hmoe_moe_forward_host(
             ctypes.byref(self.desc), x_host.data_ptr(), y_host.data_ptr(), T, ws.data_ptr(), ws.numel(),
             _stream(stream)))

@@ -206,6 +206,23 @@ hmoe_status hmoe_moe_forward_host(const hmoe_layer_desc *desc,
                                   size_t tokens, void *workspace,
                                   size_t workspace_bytes, void *stream);
 
+/* hmoe_moe_forward with the transformer layer's residual add and its
+ * activation boundary fused into the combine (MoELayer::execute,
+ * src/transformer/MoELayer.cpp:19-48: output = attention + moe.output
+ * followed by a host synchronisation; TransformerBlock.cpp:101-104):
+ *   y[t]      = residual[t] + moe(x)[t], one FP32 rounding after the
+ *               token's expert outputs are summed (the reference's add);
+ *   y_bf16[t] = BF16(y[t]) (round to nearest even), for a next layer that
+ *               reads BF16 activations; [T, H] of uint16_t bit patterns.
+ * residual == NULL gives hmoe_moe_forward's y; y_bf16 may be NULL.
+ * residual may alias x or y (in place); y may alias x.  Same workspace and
+ * stream rules as hmoe_moe_forward; no host synchronisation. */
+hmoe_status hmoe_moe_forward_residual(const hmoe_layer_desc *desc,
+                                      const float *x, const float *residual,
+                                      float *y, uint16_t *y_bf16,
+                                      size_t tokens, void *workspace,
+                                      size_t workspace_bytes, void *stream);
+
 /* hmoe_moe_forward with no caller workspace: scratch is a file-scope
  * device array of 16 MiB per device inside libhmoe.so, so the call allocates
  * nothing.  No counterpart in the reference (whose layer path allocates

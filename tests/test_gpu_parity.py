@@ -409,3 +409,37 @@ def test_bounded_wait_times_out_and_context_survives(cuda):
     y = host(dl.forward(t(x, cuda)))
     assert dl.read_status()[0] == 0
     assert_layer_close(y, O.moe_layer_port(hl, x)[0])
+
+
+# ------------------------------------------------- residual / BF16 boundary
+
+@pytest.mark.parametrize("cfg_name,T", [("c1", 64), ("c3", 300)])
+def test_forward_residual_fuses_the_layer_add(cuda, cfg_name, T):
+    """hmoe_moe_forward_residual against MoELayer::execute's arithmetic
+    (src/transformer/MoELayer.cpp:19-48): y = residual + moe(x) with one FP32
+    rounding, bit for bit against the plain layer output plus the residual;
+    its BF16 copy is round-to-nearest-even of y; in place (y = residual)
+    gives the same bits; and against the port's layer plus x, within the
+    layer tolerance."""
+    import torch
+    cfg = H.CONFIGS[cfg_name]
+    hl = H.make_host_layer(cfg, seed=12)
+    x_np = H.make_tokens(cfg, T, seed=12)
+    dl = H.DeviceLayer(hl, cuda)
+    x = t(x_np, cuda)
+    plain = host(dl.forward(x))
+    res_np = H.make_tokens(cfg, T, seed=13)
+    res = t(res_np, cuda)
+    y16 = torch.empty((T, cfg.hidden), dtype=torch.bfloat16, device=cuda)
+    y = host(dl.forward_residual(x, res, y_bf16=y16))
+    np.testing.assert_array_equal(y, (res_np + plain).astype(np.float32))
+    np.testing.assert_array_equal(host(y16.float()), torch.from_numpy(y).bfloat16().float().numpy())
+    # no residual: the plain layer
+    np.testing.assert_array_equal(host(dl.forward_residual(x)), plain)
+    # the transformer layer's own use: residual = the layer input, in place
+    inplace = x.clone()
+    dl.forward_residual(x, inplace, y=inplace)
+    np.testing.assert_array_equal(host(inplace), (x_np + plain).astype(np.float32))
+    out_p, *_ = O.moe_layer_port(hl, x_np)
+    assert_layer_close(host(inplace), x_np + out_p)
+    assert dl.read_status()[0] == 0
