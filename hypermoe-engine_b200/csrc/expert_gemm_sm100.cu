@@ -69,7 +69,8 @@ static_assert(kTileT == kTileRows, "GEMM work items are whole tiles");
 constexpr int kHalfT = 128;   // token rows per CTA (B box height)
 constexpr int kBK = 128;      // K per stage: 8 MMAs (K = 16 each) per barrier round trip
 constexpr int kWStages = 3;   // INT8 staging ring
-constexpr int kStages = 2;    // A (dequantised weights) + B (token rows) ring, one commit per stage
+constexpr int kAStages = 2;   // A ring (dequantised weights)
+constexpr int kBStages = 3;   // B ring (token rows): one more stage hides the L2 latency of a 32 KB tile
 constexpr int kDequantWarps = 8;
 constexpr int kEpiWarps = 8;                // two groups of 4 (one per column half)
 constexpr int kThreadsGemm = 32 * (3 + kDequantWarps + kEpiWarps);
@@ -81,17 +82,17 @@ constexpr int kABytes = 2 * kAAtom;         // 32 KB: 128 A rows (two 64-row ato
 constexpr int kBBox = kHalfT * 64 * 2;      // 16 KB: one TMA box, 128 token rows x 64 k
 constexpr int kBBytes = 2 * kBBox;          // 32 KB: 128 token rows x 128 k
 constexpr int kSBytes = 64 * kBK;           // 8 KB: one [128 k][64 n] INT8 box
-// Epilogue scratch per column-half group: gate/up exchange (2 x 64 x 16
-// FP32) and an output staging tile (32 tokens x 128 BF16 for down, 32 x 64
-// BF16 for gate/up).
+// Epilogue scratch per column-half group, 8 KB: the gate/up exchange (2 x 64
+// x 16 FP32), whose outputs are stored straight from registers (a warp's 32
+// lanes hold 32 consecutive features of a token: one 64-byte run per token
+// row); for down, the staging tile of 32 tokens x 128 BF16 features.
 constexpr int kXchBytes = 2 * 64 * 16 * 4;  // 8 KB
-constexpr int kStgBytes = 32 * 128 * 2;     // 8 KB
-constexpr int kXBytes = 2 * (kXchBytes + kStgBytes);
+constexpr int kXBytes = 2 * kXchBytes;
 
 constexpr int kSOff = 0;
 constexpr int kAOff = kSOff + kWStages * 2 * kSBytes;
-constexpr int kBOff = kAOff + kStages * kABytes;
-constexpr int kXOff = kBOff + kStages * kBBytes;
+constexpr int kBOff = kAOff + kAStages * kABytes;
+constexpr int kXOff = kBOff + kBStages * kBBytes;
 constexpr int kBarOff = kXOff + kXBytes;
 constexpr int kSmem = kBarOff + 512 + 1024 /*alignment slack*/;
 static_assert(kSmem <= 232448, "shared memory budget");
@@ -200,10 +201,11 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
     uint64_t* full_w = bars;                  // [kWStages] local: weights landed
     uint64_t* empty_w = full_w + kWStages;    // [kWStages] local: staging consumed
-    uint64_t* full_b = empty_w + kWStages;    // [kStages] leader: both token halves landed
-    uint64_t* aready = full_b + kStages;      // [kStages] leader: A written in both CTAs, B landed
-    uint64_t* empty_ab = aready + kStages;    // [kStages] both: MMA done with A and B of the stage
-    uint64_t* accfull = empty_ab + kStages;   // [2] both: accumulator ready
+    uint64_t* full_b = empty_w + kWStages;    // [kBStages] leader: both token halves landed
+    uint64_t* empty_b = full_b + kBStages;    // [kBStages] both: MMA done with the token stage
+    uint64_t* aready = empty_b + kBStages;    // [kAStages] leader: A written in both CTAs, B landed
+    uint64_t* empty_a = aready + kAStages;    // [kAStages] both: MMA done with the A stage
+    uint64_t* accfull = empty_a + kAStages;   // [2] both: accumulator ready
     uint64_t* accempty = accfull + 2;         // [2] leader: both epilogues drained it
     uint64_t* drain = accempty + 2;           // [1] both: every MMA done
     uint32_t* tmem_s = reinterpret_cast<uint32_t*>(drain + 1);
@@ -221,10 +223,13 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
             sm100::mbar_init(&full_w[s], 1);
             sm100::mbar_init(&empty_w[s], kDequantWarps);
         }
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < kBStages; ++s) {
             sm100::mbar_init(&full_b[s], 1);
+            sm100::mbar_init(&empty_b[s], 1);
+        }
+        for (int s = 0; s < kAStages; ++s) {
             sm100::mbar_init(&aready[s], 2 * kDequantWarps);
-            sm100::mbar_init(&empty_ab[s], 1);
+            sm100::mbar_init(&empty_a[s], 1);
         }
         for (int b = 0; b < 2; ++b) {
             sm100::mbar_init(&accfull[b], 1);
@@ -293,9 +298,9 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
             const int y = td.y + static_cast<int>(rank) * half;
             bool ok = true;
             for (int kb = 0; kb < nkb; ++kb, ++it) {
-                const int s = it % kStages;
-                if (it >= kStages &&
-                    !sm100::mbar_wait(&empty_ab[s], ((it / kStages) - 1) & 1, abort_s, kWaitNs)) {
+                const int s = it % kBStages;
+                if (it >= kBStages &&
+                    !sm100::mbar_wait(&empty_b[s], ((it / kBStages) - 1) & 1, abort_s, kWaitNs)) {
                     ok = false;
                     break;
                 }
@@ -316,8 +321,8 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
         // abort the leader waits for the last stages it saw issued, and the
         // teardown cluster barrier keeps the follower alive until then.
         if (*abort_s && leader)
-            for (uint32_t i = (it > kStages ? it - kStages : 0); i < it; ++i)
-                sm100::mbar_wait_for(&full_b[i % kStages], (i / kStages) & 1, kWaitNs);
+            for (uint32_t i = (it > kBStages ? it - kBStages : 0); i < it; ++i)
+                sm100::mbar_wait_for(&full_b[i % kBStages], (i / kBStages) & 1, kWaitNs);
     } else if (warp == 2) {
         // ------------------------------------------------ MMA issuer (leader)
         if (leader) {
@@ -337,16 +342,16 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
                 const uint32_t d0 = tmem + static_cast<uint32_t>(buf * kTileT);
                 bool ok = true;
                 for (int kb = 0; kb < nkb; ++kb, ++it) {
-                    const int s = it % kStages;
+                    const int s = it % kAStages, bs = it % kBStages;
                     // aready implies the token tile landed: the leader's
                     // dequantisation warps wait for it before arriving.
-                    if (!sm100::mbar_wait_cluster(&aready[s], (it / kStages) & 1, abort_s, kWaitNs)) {
+                    if (!sm100::mbar_wait_cluster(&aready[s], (it / kAStages) & 1, abort_s, kWaitNs)) {
                         ok = false;
                         break;
                     }
                     sm100::tc_fence_after();
                     if (lane == 0) {
-                        const uint32_t a0 = sm100::smem_u32(A(s)), b0 = sm100::smem_u32(B(s));
+                        const uint32_t a0 = sm100::smem_u32(A(s)), b0 = sm100::smem_u32(B(bs));
 #pragma unroll
                         for (int ks = 0; ks < kBK / 16; ++ks) {
                             const uint64_t ad = sm100::make_smem_desc(a0 + ks * 2048, kAAtom, 1024, 2);
@@ -354,7 +359,8 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
                                 sm100::make_smem_desc(b0 + (ks >> 2) * kBBox + (ks & 3) * 32, 16, 1024, 2);
                             sm100::mma_bf16_pair(d0, ad, bd, idesc, (kb | ks) != 0);
                         }
-                        sm100::mma_commit_pair(&empty_ab[s], 0x3);
+                        sm100::mma_commit_pair(&empty_a[s], 0x3);
+                        sm100::mma_commit_pair(&empty_b[bs], 0x3);
                     }
                     __syncwarp();
                 }
@@ -381,10 +387,10 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
             const uint32_t offh1 = f16_offset_pair(qp.zero_point[GATE_UP ? 1 : 2]);
             bool ok = true;
             for (int kb = 0; kb < nkb; ++kb, ++wi, ++ai) {
-                const int ws = wi % kWStages, as = ai % kStages;
+                const int ws = wi % kWStages, as = ai % kAStages, bs = ai % kBStages;
                 if (!sm100::mbar_wait(&full_w[ws], (wi / kWStages) & 1, abort_s, kWaitNs) ||
-                    (ai >= kStages &&
-                     !sm100::mbar_wait_cluster(&empty_ab[as], ((ai / kStages) - 1) & 1, abort_s, kWaitNs))) {
+                    (ai >= kAStages &&
+                     !sm100::mbar_wait_cluster(&empty_a[as], ((ai / kAStages) - 1) & 1, abort_s, kWaitNs))) {
                     fail();
                     ok = false;
                     break;
@@ -393,7 +399,7 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
                 sm100::fence_proxy_async_smem();
                 __syncwarp();
                 if (lane == 0) sm100::mbar_arrive(&empty_w[ws]);
-                if (leader && !sm100::mbar_wait(&full_b[as], (ai / kStages) & 1, abort_s, kWaitNs)) {
+                if (leader && !sm100::mbar_wait(&full_b[bs], (ai / kBStages) & 1, abort_s, kWaitNs)) {
                     fail();
                     ok = false;
                     break;
@@ -410,12 +416,10 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
         const int grp = e >> 2;
         const int q = warp & 3;                 // TMEM lane quarter of this warp
         const int m = q * 32 + lane;            // accumulator row (TMEM lane)
-        const int gt = (q & 3) * 32 + lane;     // thread index inside the group
         const uint32_t lane_addr = tmem + (static_cast<uint32_t>(q * 32) << 16);
-        uint8_t* xbase = smem + kXOff + grp * (kXchBytes + kStgBytes);
+        uint8_t* xbase = smem + kXOff + grp * kXchBytes;
         float* xg = reinterpret_cast<float*>(xbase);            // [16 t][64 f] gate, tokens 16..31
         float* xu = xg + 64 * 16;                               // [16 t][64 f] up, tokens 0..15
-        uint8_t* stg = xbase + kXchBytes;                       // output staging
         int j = 0;
         for (int item = pair; item < n_items && !*abort_s; item += npairs, ++j) {
             const int4 td = a.tiles[item / a.nblocks];
@@ -451,40 +455,38 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
                             xu[i * 64 + (m - 64)] = su * (__uint_as_float(v[i]) * __shfl_sync(0xffffffffu, isl, i));
                     }
                     epi_barrier(grp);
-                    __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(stg); // [32 t][64 f]
+                    // SwiGLU of feature f0 + f for 16 tokens per thread,
+                    // stored straight to the row (lanes: consecutive f)
                     const int f = m & 63;
+                    const int f0 = nb * 128 + 64 * static_cast<int>(rank);
+                    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out) + f0 + f;
+                    const bool fin = f0 + f < a.N;
                     if (q < 2) {
 #pragma unroll
                         for (int i = 0; i < 16; ++i) {
                             const float gv = sg * (__uint_as_float(v[i]) * __shfl_sync(0xffffffffu, isl, i));
                             const float uv = xu[i * 64 + f];
-                            st[i * 64 + f] = __float2bfloat16_rn(silu_fast(gv) * uv);
+                            if (i < nt && fin)
+                                out[static_cast<size_t>(row0 + c0 + i) * a.N] = __float2bfloat16_rn(silu_fast(gv) * uv);
                         }
                     } else {
 #pragma unroll
                         for (int i = 0; i < 16; ++i) {
                             const float gv = xg[i * 64 + f];
                             const float uv = su * (__uint_as_float(v[16 + i]) * __shfl_sync(0xffffffffu, isl, 16 + i));
-                            st[(16 + i) * 64 + f] = __float2bfloat16_rn(silu_fast(gv) * uv);
+                            if (16 + i < nt && fin)
+                                out[static_cast<size_t>(row0 + c0 + 16 + i) * a.N] =
+                                    __float2bfloat16_rn(silu_fast(gv) * uv);
                         }
                     }
-                    epi_barrier(grp);
-                    // 32 rows x 128 B, 16-byte pieces, coalesced per row
-                    const int f0 = nb * 128 + 64 * static_cast<int>(rank);
-                    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
-#pragma unroll
-                    for (int p = 0; p < 2; ++p) {
-                        const int idx = gt + 128 * p;      // 256 pieces
-                        const int t = idx >> 3, c = idx & 7;
-                        if (t < nt && f0 + c * 8 < a.N)
-                            *reinterpret_cast<uint4*>(out + static_cast<size_t>(row0 + c0 + t) * a.N + f0 + c * 8) =
-                                *reinterpret_cast<const uint4*>(st + t * 64 + c * 8);
-                    }
-                    epi_barrier(grp);
+                    epi_barrier(grp); // exchange buffers free for the next chunk
                 } else {
+                    // weighted rows: [32 t][128 f] BF16 staged in the group's
+                    // (otherwise unused) exchange buffer, then stored as
+                    // 16-byte pieces, coalesced per row
                     const float sd = qp.scale[2];
                     const float wl = lane < nt ? a.perm_weight[row0 + c0 + lane] : 0.0f;
-                    __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(stg); // [32 t][128 f]
+                    __nv_bfloat16* st = reinterpret_cast<__nv_bfloat16*>(xbase);
 #pragma unroll
                     for (int i = 0; i < 32; ++i) {
                         const float wt = __shfl_sync(0xffffffffu, wl, i);
@@ -493,9 +495,10 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
                     epi_barrier(grp);
                     const int f0 = nb * 256 + 128 * static_cast<int>(rank);
                     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
+                    const int gt = q * 32 + lane; // thread index inside the group
 #pragma unroll
                     for (int p = 0; p < 4; ++p) {
-                        const int idx = gt + 128 * p;      // 512 pieces of 8 BF16
+                        const int idx = gt + 128 * p; // 512 pieces of 8 BF16
                         const int t = idx >> 4, c = idx & 15;
                         if (t < nt && f0 + c * 8 < a.N)
                             *reinterpret_cast<uint4*>(out + static_cast<size_t>(row0 + c0 + t) * a.N + f0 + c * 8) =
@@ -522,15 +525,17 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
 }
 
 // Cuts every segment (a run of consecutive permuted rows of one expert)
-// into tiles of <= kTileRows rows: all full tiles first, then the remainders
-// in decreasing size (ties by segment order), so the persistent CTAs start
-// with the longest work items.  One CTA, one thread per segment.
+// into ceil(rows / kTileRows) tiles of near-equal size (the first rows %
+// tiles of them one row longer), so no expert leaves a sliver tile that
+// runs at the MMA issue floor.  Segments are ordered by their longest tile,
+// largest first (ties by segment order), all tiles of a segment together,
+// so the persistent CTAs start with the longest work items.  One CTA, one
+// thread per segment.
 __global__ void __launch_bounds__(kMaxSegments) tile_list_kernel(SegSpec sp, int4* tiles, int32_t* tile_count,
                                                                  int capacity) {
     using Scan = cub::BlockScan<int, kMaxSegments>;
     __shared__ typename Scan::TempStorage scan_s;
-    __shared__ int rem_s[kMaxSegments];
-    __shared__ int total_full_s, parts_s;
+    __shared__ int key_s[kMaxSegments], ntile_s[kMaxSegments];
     const int i = threadIdx.x;
     const bool valid = i < sp.nseg;
     int r0 = 0, cnt = 0;
@@ -547,29 +552,28 @@ __global__ void __launch_bounds__(kMaxSegments) tile_list_kernel(SegSpec sp, int
         r0 += sp.row_base;
         __syncthreads();
     }
-    const int full = cnt / kTileRows, rem = cnt % kTileRows;
-    int full_before = 0;
-    Scan(scan_s).ExclusiveSum(full, full_before);
-    rem_s[i] = rem;
-    if (i == kMaxSegments - 1) total_full_s = full_before + full;
+    const int ntile = cnt > 0 ? (cnt + kTileRows - 1) / kTileRows : 0;
+    const int base = ntile > 0 ? cnt / ntile : 0, extra = ntile > 0 ? cnt % ntile : 0;
+    key_s[i] = ntile > 0 ? base + (extra > 0) : 0; // longest tile of the segment
+    ntile_s[i] = ntile;
+    int total = 0;
+    Scan(scan_s).ExclusiveSum(ntile, total); // only the last thread's sum is used below
+    __shared__ int total_s;
+    if (i == kMaxSegments - 1) total_s = total + ntile;
     __syncthreads();
-    int parts_flag = rem > 0, parts_before = 0;
-    Scan(scan_s).ExclusiveSum(parts_flag, parts_before);
-    if (i == kMaxSegments - 1) parts_s = parts_before + parts_flag;
-    __syncthreads();
-    if (!valid) return;
+    if (i == 0) *tile_count = min(capacity, total_s);
+    if (!valid || ntile == 0) return;
+    const int key = key_s[i];
+    int pos = 0;
+    for (int j = 0; j < sp.nseg; ++j)
+        pos += (key_s[j] > key || (key_s[j] == key && j < i)) ? ntile_s[j] : 0;
     const int e = sp.expert_base + i % sp.eps;
-    for (int f = 0; f < full; ++f) {
-        const int pos = full_before + f;
-        if (pos < capacity) tiles[pos] = make_int4(e, r0 + f * kTileRows, kTileRows, 0);
+    int row = r0;
+    for (int f = 0; f < ntile; ++f) {
+        const int rows = base + (f < extra);
+        if (pos + f < capacity) tiles[pos + f] = make_int4(e, row, rows, 0);
+        row += rows;
     }
-    if (rem > 0) {
-        int before = 0;
-        for (int j = 0; j < sp.nseg; ++j) before += rem_s[j] > rem || (rem_s[j] == rem && j < i);
-        const int pos = total_full_s + before;
-        if (pos < capacity) tiles[pos] = make_int4(e, r0 + full * kTileRows, rem, 0);
-    }
-    if (i == 0) *tile_count = min(capacity, total_full_s + parts_s);
 }
 
 // Token-major permutation (permute_token) into this GPU's rows.
