@@ -167,19 +167,53 @@ hmoe_status wait_counts(hmoe_ep_comm* c) {
 // receive side for up to P * max_tokens * k rows.
 // Peer-memory path: the first kEpSyncBytes of the workspace hold the epoch
 // flags written by the peers ([3 kinds][HMOE_EP_MAX_RANKS] uint64: counts
-// published, rows dispatched, rows returned), two CTA-completion counters
-// and the device transfer plan.  Zeroed at registration.
-struct EpDevPlan {
-    int32_t send_off[HMOE_EP_MAX_RANKS];  // this rank's rows for rank q start here ...
-    int32_t send_rows[HMOE_EP_MAX_RANKS]; // ... and are this many
-    int32_t dest_base[HMOE_EP_MAX_RANKS]; // and land at this row of q's receive rows
-    int32_t recv_base[HMOE_EP_MAX_RANKS]; // rows from rank p start at this receive row ...
-    int32_t recv_rows[HMOE_EP_MAX_RANKS]; // ... and are this many
-    int32_t ret_off[HMOE_EP_MAX_RANKS];   // and return to this row of p's permuted rows
-    int32_t recv_total, sent_total;
-};
+// published, rows dispatched, rows returned), a CTA-completion counter, the
+// sticky abort word and the device transfer plan.  Zeroed at registration,
+// and only there: an abort stays set until the workspace is registered
+// again.
+// The device transfer plan (see hmoe_ep_peer_plan_t in hmoe.h).
+using EpDevPlan = hmoe_ep_peer_plan_t;
+
+// Rows source p sends to owner q: p's routed rows in q's slot range.
+// Negative counts count as zero, as the exchange kernel reads them.
+__host__ __device__ inline int ep_rows_to_owner(const int32_t* counts, int E, int P, int p, int q) {
+    const int base = E / P, extra = E % P;
+    const int f = q * base + (q < extra ? q : extra), n = base + (q < extra ? 1 : 0);
+    int r = 0;
+    for (int sl = f; sl < f + n; ++sl) r += counts[p * E + sl] > 0 ? counts[p * E + sl] : 0;
+    return r;
+}
+
+// Rank me's plan from R[p * stride + q] = rows of source p for owner q.
+// Rows travel source-major into every owner's receive rows (source 0's
+// first), and leave a source in owner order (its rows are grouped by slot,
+// slots by owner).  `ok` false: a plan that moves nothing.
+__host__ __device__ inline void ep_plan_from_rows(const int* R, int stride, int P, int me, bool ok,
+                                                   EpDevPlan* plan) {
+    int rt = 0, st = 0;
+    for (int q = 0; q < P; ++q) {
+        int so = 0, db = 0, rb = 0, ro = 0;
+        for (int j = 0; j < q; ++j) {
+            so += R[me * stride + j];
+            rb += R[j * stride + me];
+        }
+        for (int p = 0; p < me; ++p) db += R[p * stride + q];
+        for (int j = 0; j < me; ++j) ro += R[q * stride + j];
+        plan->send_off[q] = ok ? so : 0;
+        plan->send_rows[q] = ok ? R[me * stride + q] : 0;
+        plan->dest_base[q] = ok ? db : 0;
+        plan->recv_base[q] = ok ? rb : 0;
+        plan->recv_rows[q] = ok ? R[q * stride + me] : 0;
+        plan->ret_off[q] = ok ? ro : 0;
+        rt += R[q * stride + me];
+        st += R[me * stride + q];
+    }
+    plan->recv_total = ok ? rt : 0;
+    plan->sent_total = ok ? st : 0;
+}
 constexpr size_t kEpFlagsBytes = 3 * HMOE_EP_MAX_RANKS * 8;
 constexpr size_t kEpCtrOff = kEpFlagsBytes;           // int32 CTA-completion counter of the dispatch
+constexpr size_t kEpAbortOff = kEpFlagsBytes + 64;    // uint32 sticky abort word (any rank may set it)
 constexpr size_t kEpPlanOff = kEpFlagsBytes + 256;
 constexpr size_t kEpSyncBytes = kEpPlanOff + ((sizeof(EpDevPlan) + 255) / 256) * 256;
 
@@ -260,6 +294,19 @@ bool ep_rows_fit(const hmoe_layer_desc& d, size_t max_tokens) {
 // computes on them, and an owner's output rows of epoch n are rewritten only
 // after every source has combined them (it needs their epoch n + 1 rows
 // first); the counts are double-buffered by epoch parity.
+//
+// Failure: a rank whose flag wait runs out, or whose count exchange fails,
+// stores the abort word into every rank's sync area (its own included)
+// before anything else it would signal.  Every wait checks the word while it
+// spins and once more after its flags arrived (the flag loads acquire, so a
+// peer's abort stored before its flag is seen), and fails at once when it is
+// set; an aborted rank raises no further flags, moves no rows and reads no
+// peer's output rows; every later forward on the workspace fails at its
+// count exchange without touching the peers.  All ranks therefore report
+// HMOE_TIMEOUT for the failed forward (or, for a rank that was still ahead,
+// the next one), nobody computes on rows that were never sent, and epochs
+// stop advancing until the ranks register the workspace again, which
+// clears the word.
 struct PeerCtx {
     char* const* peer; // [P] every rank's workspace base in this address space
     int P, me;
@@ -288,17 +335,37 @@ __device__ __forceinline__ uint64_t* ep_flags(char* base, int kind) {
     return reinterpret_cast<uint64_t*>(base) + kind * HMOE_EP_MAX_RANKS;
 }
 
+__device__ __forceinline__ uint32_t* ep_abort_word(char* base) {
+    return reinterpret_cast<uint32_t*>(base + kEpAbortOff);
+}
+
+__device__ __forceinline__ bool ep_aborted(const PeerCtx& c) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ep_abort_word(c.peer[c.me])) : "memory");
+    return v != 0;
+}
+
+// Marks the failure on every rank (its own workspace included) and in this
+// rank's status word.
+__device__ void ep_abort_all(const PeerCtx& c) {
+    for (int q = 0; q < c.P; ++q)
+        asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(ep_abort_word(c.peer[q])), "r"(1u) : "memory");
+    __threadfence_system();
+    device_fail(c.st, HMOE_TIMEOUT);
+}
+
 // Thread-level: every rank's flag `kind` reaches `epoch`, or false after
-// limit_ns.
+// limit_ns or as soon as the abort word is set (also when it was set before
+// the last flag arrived).
 __device__ bool wait_all_flags(const PeerCtx& c, int kind) {
     const uint64_t* f = ep_flags(c.peer[c.me], kind);
     const uint64_t t0 = now_ns();
     for (int p = 0; p < c.P; ++p)
         while (ld_acquire_sys(f + p) < c.epoch) {
-            if (now_ns() - t0 > c.limit_ns) return false;
+            if (ep_aborted(c) || now_ns() - t0 > c.limit_ns) return false;
             __nanosleep(100);
         }
-    return true;
+    return !ep_aborted(c);
 }
 
 __device__ void signal_all(const PeerCtx& c, int kind) {
@@ -306,8 +373,13 @@ __device__ void signal_all(const PeerCtx& c, int kind) {
     for (int q = 0; q < c.P; ++q) st_release_sys(ep_flags(c.peer[q], kind) + c.me, c.epoch);
 }
 
-__global__ void ep_wait_kernel(PeerCtx c, int kind) {
-    if (threadIdx.x == 0 && !wait_all_flags(c, kind)) device_fail(c.st, HMOE_TIMEOUT);
+// sticky: a wait of a forward (a failure aborts every rank); the flag-wait
+// self-test passes false and only records the timeout.
+__global__ void ep_wait_kernel(PeerCtx c, int kind, bool sticky) {
+    if (threadIdx.x == 0 && !wait_all_flags(c, kind)) {
+        if (sticky) ep_abort_all(c);
+        else device_fail(c.st, HMOE_TIMEOUT);
+    }
 }
 
 // One CTA.  counts_off: the [2][P][E] counts in every workspace;
@@ -319,26 +391,28 @@ __global__ void __launch_bounds__(256) ep_exchange_kernel(PeerCtx c, size_t coun
     __shared__ int R[HMOE_EP_MAX_RANKS][HMOE_EP_MAX_RANKS + 1]; // rows from p to q
     __shared__ int ok;
     const int P = c.P, me = c.me, tid = threadIdx.x;
-    for (int q = 0; q < P; ++q) {
+    if (tid == 0) ok = ep_aborted(c) ? 0 : 1; // an earlier forward failed on some rank
+    __syncthreads();
+    for (int q = 0; q < P && ok; ++q) {
         int32_t* dst = reinterpret_cast<int32_t*>(c.peer[q] + counts_off) + (static_cast<size_t>(parity) * P + me) * E;
         for (int e = tid; e < E; e += blockDim.x) dst[e] = my_counts[e];
     }
     __threadfence_system();
     __syncthreads();
     if (tid == 0) {
-        signal_all(c, 0);
-        ok = wait_all_flags(c, 0);
-        if (!ok) device_fail(c.st, HMOE_TIMEOUT);
+        if (!ok) {
+            device_fail(c.st, HMOE_TIMEOUT);
+        } else {
+            signal_all(c, 0);
+            ok = wait_all_flags(c, 0);
+            if (!ok) ep_abort_all(c);
+        }
     }
     __syncthreads();
     const int32_t* cnt = reinterpret_cast<const int32_t*>(c.peer[me] + counts_off) + static_cast<size_t>(parity) * P * E;
-    const int base = E / P, extra = E % P;
     for (int idx = tid; idx < P * P; idx += blockDim.x) {
         const int p = idx / P, q = idx % P;
-        const int f = q * base + min(q, extra), n = base + (q < extra ? 1 : 0);
-        int r = 0;
-        for (int sl = f; sl < f + n; ++sl) r += max(0, cnt[p * E + sl]);
-        R[p][q] = ok ? r : 0;
+        R[p][q] = ok ? ep_rows_to_owner(cnt, E, P, p, q) : 0;
     }
     __syncthreads();
     if (tid == 0) { // every rank's receive rows fit (identical verdict on every rank)
@@ -347,34 +421,10 @@ __global__ void __launch_bounds__(256) ep_exchange_kernel(PeerCtx c, size_t coun
             for (int p = 0; p < P; ++p) in += R[p][q];
             if (in > cap_rows) ok = 0;
         }
-        if (!ok) device_fail(c.st, HMOE_INVALID_ARGUMENT);
-    }
-    __syncthreads();
-    EpDevPlan* plan = reinterpret_cast<EpDevPlan*>(c.peer[me] + kEpPlanOff);
-    if (tid < P) {
-        const int q = tid; // as a destination for send_*, dest_base; as a source p for recv_*, ret_off
-        int so = 0, db = 0, rb = 0, ro = 0;
-        for (int j = 0; j < q; ++j) {
-            so += R[me][j];
-            rb += R[j][me];
-        }
-        for (int p = 0; p < me; ++p) db += R[p][q];
-        for (int j = 0; j < me; ++j) ro += R[q][j];
-        plan->send_off[q] = ok ? so : 0;
-        plan->send_rows[q] = ok ? R[me][q] : 0;
-        plan->dest_base[q] = ok ? db : 0;
-        plan->recv_base[q] = ok ? rb : 0;
-        plan->recv_rows[q] = ok ? R[q][me] : 0;
-        plan->ret_off[q] = ok ? ro : 0;
-    }
-    if (tid == 0) {
-        int rt = 0, st = 0;
-        for (int p = 0; p < P; ++p) {
-            rt += R[p][me];
-            st += R[me][p];
-        }
-        plan->recv_total = ok ? rt : 0;
-        plan->sent_total = ok ? st : 0;
+        // every rank computes the same verdict, so a rejection needs no abort
+        if (!ok && !ep_aborted(c)) device_fail(c.st, HMOE_INVALID_ARGUMENT);
+        ep_plan_from_rows(&R[0][0], HMOE_EP_MAX_RANKS + 1, P, me, ok != 0,
+                          reinterpret_cast<EpDevPlan*>(c.peer[me] + kEpPlanOff));
     }
 }
 
@@ -461,14 +511,15 @@ __global__ void __launch_bounds__(256) ep_permute_kernel(PeerCtx c, const float*
         int* ctr = reinterpret_cast<int*>(c.peer[c.me] + kEpCtrOff);
         if (atomicAdd(ctr, 1) == static_cast<int>(gridDim.x) - 1) {
             *ctr = 0;
-            signal_all(c, 1);
+            if (!ep_aborted(c)) signal_all(c, 1);
         }
     }
 }
 
-// No rows to dispatch (this rank has no tokens): flag the dispatch anyway.
+// No rows to dispatch (this rank has no tokens): flag the dispatch anyway;
+// also flags the return.  An aborted rank raises no flags.
 __global__ void ep_signal_kernel(PeerCtx c, int kind) {
-    if (threadIdx.x == 0) signal_all(c, kind);
+    if (threadIdx.x == 0 && !ep_aborted(c)) signal_all(c, kind);
 }
 
 __global__ void __launch_bounds__(256) ep_combine_kernel(PeerCtx c, const int32_t* __restrict__ inv,
@@ -476,7 +527,14 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(PeerCtx c, const int32_
                                                          int routed, int H, const __nv_bfloat16* yrows, size_t y_off,
                                                          float* __restrict__ out) {
     __shared__ PeerRowMap map;
-    load_row_map(c, routed, &map);
+    __shared__ int aborted_s;
+    if (threadIdx.x == 0) aborted_s = ep_aborted(c) ? 1 : 0;
+    load_row_map(c, routed, &map); // synchronises the CTA
+    if (aborted_s) { // no peer's rows are read after a failure: the token's output is zero
+        float* o = out + static_cast<size_t>(blockIdx.x) * H;
+        for (int h = threadIdx.x; h < H; h += blockDim.x) o[h] = 0.0f;
+        return;
+    }
     combine_token(inv, ids, k, E, slots, H, blockIdx.x, out, PeerOut{&map, yrows, y_off, H});
 }
 
@@ -558,7 +616,7 @@ hmoe_status ep_forward_peer(const hmoe_layer_desc* desc, hmoe_ep_comm* comm, con
         if (r == HMOE_OK) r = run_experts(sh, use_gemv(static_cast<long>(tokens) * S, sh.H, sh.I), false, s);
         if (r != HMOE_OK) return r;
     }
-    ep_wait_kernel<<<1, 32, 0, s>>>(c, 1);
+    ep_wait_kernel<<<1, 32, 0, s>>>(c, 1, true);
     r = check_launch("hmoe EP dispatch wait");
     if (r != HMOE_OK) return r;
     stage(2, s);
@@ -569,7 +627,7 @@ hmoe_status ep_forward_peer(const hmoe_layer_desc* desc, hmoe_ep_comm* comm, con
     ep_signal_kernel<<<1, 32, 0, s>>>(c, 2);
     r = check_launch("hmoe EP return signal");
     if (r != HMOE_OK) return r;
-    ep_wait_kernel<<<1, 32, 0, s>>>(c, 2);
+    ep_wait_kernel<<<1, 32, 0, s>>>(c, 2, true);
     r = check_launch("hmoe EP return wait");
     if (r != HMOE_OK) return r;
     // 6. combine fused with the return: each routed row is read from its
@@ -931,6 +989,28 @@ hmoe_status hmoe_ep_register_workspace(hmoe_ep_comm* comm, void* workspace, size
     return HMOE_OK;
 }
 
+hmoe_status hmoe_ep_peer_plan(const int32_t* slot_counts, uint32_t experts, int32_t ep_size, int32_t ep_rank,
+                              int64_t capacity_rows, hmoe_ep_peer_plan_t* plan) {
+    if (!slot_counts || !plan || experts == 0 || ep_size < 1 || ep_size > HMOE_EP_MAX_RANKS || ep_rank < 0 ||
+        ep_rank >= ep_size || capacity_rows < 0)
+        return HMOE_INVALID_ARGUMENT;
+    static int R[HMOE_EP_MAX_RANKS * HMOE_EP_MAX_RANKS];
+    static std::mutex mu;
+    std::lock_guard<std::mutex> lock(mu);
+    const int P = ep_size, E = static_cast<int>(experts);
+    for (int p = 0; p < P; ++p)
+        for (int q = 0; q < P; ++q) R[p * P + q] = ep_rows_to_owner(slot_counts, E, P, p, q);
+    bool ok = true;
+    for (int q = 0; q < P; ++q) {
+        long long in = 0;
+        for (int p = 0; p < P; ++p) in += R[p * P + q];
+        if (in > capacity_rows) ok = false;
+    }
+    std::memset(plan, 0, sizeof(*plan));
+    ep_plan_from_rows(R, P, P, ep_rank, ok, plan);
+    return ok ? HMOE_OK : HMOE_INVALID_ARGUMENT;
+}
+
 hmoe_status hmoe_ep_read_status(void* workspace, int32_t* status, int32_t* near_ties, int32_t* sequential_logits,
                                 void* stream) {
     if (!workspace) return HMOE_INVALID_ARGUMENT;
@@ -946,7 +1026,7 @@ hmoe_status hmoe_ep_selftest_flag_wait(hmoe_ep_comm* comm, uint64_t limit_ns, in
     cudaError_t err = cudaMemset(st, 0, sizeof(DeviceStatus));
     const PeerCtx c{comm->d_peer_ws, comm->size, comm->rank, comm->epoch + (1ull << 40), limit_ns, st};
     if (err == cudaSuccess) {
-        ep_wait_kernel<<<1, 32>>>(c, 1);
+        ep_wait_kernel<<<1, 32>>>(c, 1, false);
         err = cudaGetLastError();
     }
     DeviceStatus host{};

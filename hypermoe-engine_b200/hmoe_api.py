@@ -43,7 +43,7 @@ EXPORTS = [
     "hmoe_moe_forward_noalloc", "hmoe_selftest_bounded_wait", "hmoe_ep_set_placement",
     "hmoe_ep_balanced_placement", "hmoe_set_route_variant", "hmoe_ep_register_workspace",
     "hmoe_ep_selftest_flag_wait", "hmoe_ep_read_status", "hmoe_noalloc_read_status",
-    "hmoe_moe_forward_residual",
+    "hmoe_moe_forward_residual", "hmoe_ep_peer_plan",
 ]
 EP_MAX_RANKS = 64
 EP_UNIQUE_ID_BYTES = 128
@@ -82,6 +82,12 @@ class EpPlan(ctypes.Structure):
         ("recv_rows", ctypes.c_int64 * EP_MAX_RANKS), ("recv_offset", ctypes.c_int64 * EP_MAX_RANKS),
         ("recv_total", ctypes.c_int64),
     ]
+
+
+class EpPeerPlan(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32 * EP_MAX_RANKS) for n in
+                ("send_off", "send_rows", "dest_base", "recv_base", "recv_rows", "ret_off")] + \
+               [("recv_total", ctypes.c_int32), ("sent_total", ctypes.c_int32)]
 
 
 class GemmPlan(ctypes.Structure):
@@ -123,6 +129,7 @@ def lib() -> ctypes.CDLL:
             "hmoe_ep_expert_range": [ctypes.c_uint32, i32, i32, ctypes.POINTER(ctypes.c_uint32),
                                      ctypes.POINTER(ctypes.c_uint32)],
             "hmoe_ep_plan": [vp, ctypes.c_uint32, ctypes.c_uint32, i32, i32, sz, ctypes.POINTER(EpPlan)],
+            "hmoe_ep_peer_plan": [vp, ctypes.c_uint32, i32, i32, ctypes.c_int64, ctypes.POINTER(EpPeerPlan)],
             "hmoe_ep_unique_id": [vp, sz],
             "hmoe_ep_comm_create": [vp, i32, i32, i32, ctypes.POINTER(vp)],
             "hmoe_ep_comm_destroy": [vp],
@@ -424,6 +431,16 @@ def ep_plan(counts: np.ndarray, top_k: int, ep_rank: int, max_tokens: int) -> Ep
     check("hmoe_ep_plan", lib().hmoe_ep_plan(counts.ctypes.data, E, top_k, P, ep_rank, max_tokens,
                                              ctypes.byref(plan)))
     return plan
+
+
+def ep_peer_plan(slot_counts: np.ndarray, ep_rank: int, capacity_rows: int):
+    """(status, plan) of the peer-memory path's device transfer plan for
+    `ep_rank` from slot_counts[ep_size, experts] (int32)."""
+    counts = np.ascontiguousarray(slot_counts, dtype=np.int32)
+    P, E = counts.shape
+    plan = EpPeerPlan()
+    st = lib().hmoe_ep_peer_plan(counts.ctypes.data, E, P, ep_rank, capacity_rows, ctypes.byref(plan))
+    return st, plan
 
 
 def ep_unique_id() -> bytes:

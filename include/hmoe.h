@@ -324,6 +324,29 @@ hmoe_status hmoe_ep_plan(const int32_t *counts, uint32_t experts,
                          uint32_t top_k, int32_t ep_size, int32_t ep_rank,
                          size_t max_tokens, hmoe_ep_plan_t *plan);
 
+/* Transfer plan of one rank on the peer-memory path (a registered
+ * workspace), as ep_exchange_kernel builds it on the device from the
+ * exchanged per-slot row counts slot_counts[ep_size][experts] (negative
+ * counts count as zero).  Owner q holds the slots hmoe_ep_expert_range
+ * gives it; every owner's receive rows hold its sources' rows source by
+ * source.  Host only (the device kernel runs the same code).  A rank
+ * receiving more than capacity_rows rows (ep_size * max_tokens * top_k on
+ * the device) gives HMOE_INVALID_ARGUMENT and a plan that moves nothing,
+ * on every rank alike.  No counterpart in the reference (single process). */
+typedef struct {
+    int32_t send_off[HMOE_EP_MAX_RANKS];  /* this rank's rows for owner q start here ... */
+    int32_t send_rows[HMOE_EP_MAX_RANKS]; /* ... and are this many */
+    int32_t dest_base[HMOE_EP_MAX_RANKS]; /* and land at this row of q's receive rows */
+    int32_t recv_base[HMOE_EP_MAX_RANKS]; /* rows from source p start at this receive row ... */
+    int32_t recv_rows[HMOE_EP_MAX_RANKS]; /* ... and are this many */
+    int32_t ret_off[HMOE_EP_MAX_RANKS];   /* and return to this row of p's permuted rows */
+    int32_t recv_total, sent_total;
+} hmoe_ep_peer_plan_t;
+hmoe_status hmoe_ep_peer_plan(const int32_t *slot_counts, uint32_t experts,
+                              int32_t ep_size, int32_t ep_rank,
+                              int64_t capacity_rows,
+                              hmoe_ep_peer_plan_t *plan);
+
 /* NCCL unique id (HMOE_EP_UNIQUE_ID_BYTES bytes) made on one rank and
  * shared with the others by the caller. */
 hmoe_status hmoe_ep_unique_id(void *id, size_t bytes);
@@ -371,7 +394,12 @@ hmoe_status hmoe_ep_last_plan(const hmoe_ep_comm *comm, hmoe_ep_plan_t *plan);
  * unregisters (also collective).  HMOE_UNSUPPORTED on every rank when any
  * rank cannot map every workspace.  Each flag wait gives up after the
  * communicator's timeout and reports HMOE_TIMEOUT in the status word
- * (hmoe_read_status on the workspace's single-GPU part). */
+ * (hmoe_ep_read_status).  A rank that times out (or whose count exchange
+ * fails) marks every rank's workspace aborted before it signals anything:
+ * the other ranks' waits then fail at once, so every rank reports
+ * HMOE_TIMEOUT instead of computing on rows that were never sent, and every
+ * later forward on these workspaces fails the same way until the ranks
+ * register them again (which clears the mark). */
 hmoe_status hmoe_ep_register_workspace(hmoe_ep_comm *comm, void *workspace,
                                        size_t bytes);
 

@@ -22,6 +22,8 @@ from datetime import timedelta
 import numpy as np
 import pytest
 
+import hmoe_api as H
+
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PATHS = [os.path.join(ROOT, "hypermoe-engine_b200"), os.path.join(ROOT, "oracle")]
 
@@ -340,3 +342,41 @@ def test_ep_plan_rejections():
         H.ep_plan(np.array([[-1, 1, 2], [0, 0, 0]], np.int32), 2, 0, 4)
     assert [H.ep_expert_range(60, 8, r) for r in range(8)] == [
         (0, 8), (8, 8), (16, 8), (24, 8), (32, 7), (39, 7), (46, 7), (53, 7)]
+
+
+@pytest.mark.parametrize("P", [2, 3, 4, 5, 8])
+@pytest.mark.parametrize("E", [7, 60, 128])
+def test_ep_peer_plan_matches_layout(P, E):
+    """The device transfer plan (ep_exchange_kernel's code, exported as
+    hmoe_ep_peer_plan) against the layout the *_peer_* tests restate:
+    send ranges in owner order, receive ranges source-major, rows returned
+    to the same positions; ragged counts, empty ranks and sources."""
+    if E < P:
+        pytest.skip("fewer experts than ranks")
+    rng = np.random.default_rng(P * 1000 + E)
+    counts = rng.integers(0, 40, size=(P, E)).astype(np.int32)
+    counts[rng.random((P, E)) < 0.3] = 0
+    counts[P - 1] = 0  # a rank with no tokens
+    base, extra = E // P, E % P
+    first = [r * base + min(r, extra) for r in range(P)]
+    nslot = [base + (1 if r < extra else 0) for r in range(P)]
+    R = np.array([[counts[p, first[q]:first[q] + nslot[q]].sum() for q in range(P)] for p in range(P)])
+    for me in range(P):
+        st, plan = H.ep_peer_plan(counts, me, capacity_rows=10 ** 9)
+        assert st == 0
+        np.testing.assert_array_equal(plan.send_off[:P], [R[me, :q].sum() for q in range(P)])
+        np.testing.assert_array_equal(plan.send_rows[:P], R[me, :])
+        np.testing.assert_array_equal(plan.dest_base[:P], [R[:me, q].sum() for q in range(P)])
+        np.testing.assert_array_equal(plan.recv_base[:P], [R[:p, me].sum() for p in range(P)])
+        np.testing.assert_array_equal(plan.recv_rows[:P], R[:, me])
+        np.testing.assert_array_equal(plan.ret_off[:P], [R[p, :me].sum() for p in range(P)])
+        assert plan.recv_total == R[:, me].sum() and plan.sent_total == R[me].sum()
+        # what a source sends to owner q arrives exactly where q expects it from that source
+        for q in range(P):
+            _, pq = H.ep_peer_plan(counts, q, capacity_rows=10 ** 9)
+            assert plan.dest_base[q] == pq.recv_base[me] and plan.send_rows[q] == pq.recv_rows[me]
+    # more rows than the receive capacity: rejected on every rank, nothing moves
+    cap = int(R.sum(axis=0).max()) - 1
+    for me in range(P):
+        st, plan = H.ep_peer_plan(counts, me, capacity_rows=cap)
+        assert st == 1 and plan.recv_total == 0 and plan.sent_total == 0 and not any(plan.send_rows[:P])

@@ -143,16 +143,29 @@ def _ep_rank(rank, P, port, cfg_name, Ts, variant, q, balanced=False, peer=True)
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("cfg_name,Ts,variant,balanced,peer", [("c3", (300, 212), 2, False, True),
-                                                               ("c2", (40, 0), 2, False, True),
-                                                               ("c3", (3, 1), 0, False, True),
-                                                               ("c3", (300, 212), 2, True, True),
-                                                               ("c3", (300, 212), 2, True, False)])
-def test_ep_two_gpus_equal_single_gpu(cuda, cfg_name, Ts, variant, balanced, peer):
+@pytest.mark.parametrize("cfg_name,Ts,variant,balanced,peer", [
+    ("c3", (300, 212), 2, False, True),
+    ("c2", (40, 0), 2, False, True),
+    ("c3", (3, 1), 0, False, True),
+    ("c3", (300, 212), 2, True, True),
+    ("c3", (300, 212), 2, True, False),
+    ("c3", (300, 212, 77, 0), 2, True, True),
+    ("c2", (40, 0, 17, 3), 2, False, True),
+    ("c3", (300, 212, 77, 0), 2, False, False),
+    ("c3", (300, 212, 77, 0, 140, 5, 256, 31), 2, True, True),
+    ("c3", (1, 2, 0, 1, 3, 1, 1, 2), 0, False, True),
+    ("c3", (300, 212, 77, 0, 140, 5, 256, 31), 2, False, False),
+])
+def test_ep_ranks_equal_single_gpu(cuda, cfg_name, Ts, variant, balanced, peer):
+    """P = len(Ts) ranks (one process per GPU, skipped with fewer GPUs): each
+    rank's slice of the output equals the single-GPU layer on the
+    concatenated batch (bit for bit for the tensor-core variant) and the
+    oracle within the layer tolerance; ragged batches and empty ranks."""
     import torch
     import torch.multiprocessing as mp
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+    P = len(Ts)
+    if torch.cuda.device_count() < P:
+        pytest.skip(f"needs {P} GPUs")
     cfg = H.CONFIGS[cfg_name]
     hl = H.make_host_layer(cfg, seed=5)
     x_all = H.make_tokens(cfg, sum(Ts), seed=5)
@@ -160,13 +173,13 @@ def test_ep_two_gpus_equal_single_gpu(cuda, cfg_name, Ts, variant, balanced, pee
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_ep_rank, args=(r, 2, port, cfg_name, Ts, variant, q, balanced, peer))
-             for r in range(2)]
+    procs = [ctx.Process(target=_ep_rank, args=(r, P, port, cfg_name, Ts, variant, q, balanced, peer))
+             for r in range(P)]
     for p in procs:
         p.start()
     out = {}
     try:
-        for _ in range(2):
+        for _ in range(P):
             rank, st, y = q.get(timeout=600)
             out[rank] = (st, y)
     finally:
@@ -174,9 +187,100 @@ def test_ep_two_gpus_equal_single_gpu(cuda, cfg_name, Ts, variant, balanced, pee
             p.join(timeout=120)
             if p.is_alive():
                 p.kill()
-    for r in range(2):
+    for r in range(P):
         assert out[r][0] == 0, out[r][1]
-    y = np.concatenate([out[0][1], out[1][1]])
+    y = np.concatenate([out[r][1] for r in range(P)])
     if variant == 2:
         assert np.array_equal(y, ref), float(np.abs(y - ref).max())
+    assert_layer_close(y, O.moe_layer_port(hl, x_all)[0])
+
+
+def _ep_abort_rank(rank, port, q):
+    """Rank 1 holds back while rank 0 runs a forward on the peer path, so
+    rank 0's flag wait runs out; both then report the failure, and a fresh
+    registration brings the path back."""
+    for p in PATHS:
+        sys.path.insert(0, p)
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    import hmoe_api as H
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=timedelta(seconds=120))
+    comm = None
+    try:
+        obj = [H.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        comm = H.EpComm(obj[0], rank, 2, timeout_ms=2000)  # flag waits give up after 2 s
+        cfg = H.CONFIGS["c1"]
+        hl = H.make_host_layer(cfg, seed=9)
+        x_all = H.make_tokens(cfg, 24, seed=9)
+        dev = torch.device("cuda", rank)
+        layer = H.EpLayer(hl, comm, dev, peer=True)
+        ws = layer.ep_workspace(16)  # collective registration
+        dx = torch.from_numpy(x_all[rank * 12:(rank + 1) * 12]).to(dev)
+        res = {}
+        if rank == 0:
+            t0 = time.perf_counter()
+            layer.forward(dx, max_tokens=16)
+            res["first"] = layer.read_status()[0]
+            res["first_s"] = time.perf_counter() - t0
+        dist.barrier()  # rank 0's wait has run out before rank 1 starts
+        if rank == 1:
+            t0 = time.perf_counter()
+            layer.forward(dx, max_tokens=16)
+            res["first"] = layer.read_status()[0]
+            res["first_s"] = time.perf_counter() - t0
+        dist.barrier()
+        layer.forward(dx, max_tokens=16)  # still aborted: fails at the count exchange
+        res["second"] = layer.read_status()[0]
+        dist.barrier()
+        comm.register_workspace(ws)  # collective: clears the abort mark
+        y = layer.forward(dx, max_tokens=16).cpu().numpy()
+        res["after"] = layer.read_status()[0]
+        q.put((rank, res, y))
+    except Exception as exc:
+        q.put((rank, {"error": repr(exc)}, None))
+    finally:
+        if comm is not None:
+            comm.close()
+        dist.destroy_process_group()
+
+
+def test_ep_peer_timeout_aborts_every_rank(cuda):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    cfg = H.CONFIGS["c1"]
+    hl = H.make_host_layer(cfg, seed=9)
+    x_all = H.make_tokens(cfg, 24, seed=9)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_ep_abort_rank, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = {}
+    try:
+        for _ in range(2):
+            rank, res, y = q.get(timeout=300)
+            out[rank] = (res, y)
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    for r in range(2):
+        res = out[r][0]
+        assert "error" not in res, res
+        assert res["first"] == 5 and res["second"] == 5 and res["after"] == 0, (r, res)
+    assert 1.5 < out[0][0]["first_s"] < 30   # rank 0 waited out its limit
+    assert out[1][0]["first_s"] < 1.5        # rank 1 failed at once
+    y = np.concatenate([out[0][1], out[1][1]])
     assert_layer_close(y, O.moe_layer_port(hl, x_all)[0])
