@@ -535,7 +535,7 @@ __global__ void __launch_bounds__(kMaxSegments) tile_list_kernel(SegSpec sp, int
                                                                  int capacity) {
     using Scan = cub::BlockScan<int, kMaxSegments>;
     __shared__ typename Scan::TempStorage scan_s;
-    __shared__ int key_s[kMaxSegments], ntile_s[kMaxSegments];
+    __shared__ int2 kn_s[kMaxSegments]; // (longest tile, tiles) of each segment
     const int i = threadIdx.x;
     const bool valid = i < sp.nseg;
     int r0 = 0, cnt = 0;
@@ -554,8 +554,8 @@ __global__ void __launch_bounds__(kMaxSegments) tile_list_kernel(SegSpec sp, int
     }
     const int ntile = cnt > 0 ? (cnt + kTileRows - 1) / kTileRows : 0;
     const int base = ntile > 0 ? cnt / ntile : 0, extra = ntile > 0 ? cnt % ntile : 0;
-    key_s[i] = ntile > 0 ? base + (extra > 0) : 0; // longest tile of the segment
-    ntile_s[i] = ntile;
+    const int key = ntile > 0 ? base + (extra > 0) : 0; // longest tile of the segment
+    kn_s[i] = make_int2(key, ntile);
     int total = 0;
     Scan(scan_s).ExclusiveSum(ntile, total); // only the last thread's sum is used below
     __shared__ int total_s;
@@ -563,10 +563,17 @@ __global__ void __launch_bounds__(kMaxSegments) tile_list_kernel(SegSpec sp, int
     __syncthreads();
     if (i == 0) *tile_count = min(capacity, total_s);
     if (!valid || ntile == 0) return;
-    const int key = key_s[i];
-    int pos = 0;
-    for (int j = 0; j < sp.nseg; ++j)
-        pos += (key_s[j] > key || (key_s[j] == key && j < i)) ? ntile_s[j] : 0;
+    // tiles of segments ordered before this one: longer tiles, or equal
+    // tiles and a lower segment index (independent partial sums so that the
+    // shared-memory loads pipeline)
+    int pos4[4] = {0, 0, 0, 0};
+    const int nseg = sp.nseg;
+#pragma unroll 4
+    for (int j = 0; j < nseg; ++j) {
+        const int2 kj = kn_s[j];
+        pos4[j & 3] += (kj.x > key || (kj.x == key && j < i)) ? kj.y : 0;
+    }
+    const int pos = pos4[0] + pos4[1] + pos4[2] + pos4[3];
     const int e = sp.expert_base + i % sp.eps;
     int row = r0;
     for (int f = 0; f < ntile; ++f) {

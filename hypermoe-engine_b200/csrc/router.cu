@@ -1043,8 +1043,9 @@ __global__ void __launch_bounds__(256, 2) route_tiled_kernel(const __grid_consta
 // depend on that order.  The last CTA to finish (a ticket) certifies,
 // settles and selects.
 constexpr int kDecMaxTokens = 16;
-constexpr int kDecAutoTokens = 2; // chosen automatically up to here (T=1: 22.5 us vs 29.5 us for route_kernel;
-                                  // at T=16 its serial selection tail makes it slower)
+constexpr int kDecAutoTokens = 8; // chosen automatically up to here (T=1: 26.6 us vs 30.7 us for route_kernel,
+                                  // T=4: 26.6 vs 32.7; at T=16 its serial selection tail makes it slower:
+                                  // 47.1 vs 36.9)
 constexpr int kDecRows = 128;  // hidden rows per CTA
 constexpr int kDecCols = 32;   // experts per CTA
 constexpr int kDecSlots = 2;   // staging buffers for settle_logit
