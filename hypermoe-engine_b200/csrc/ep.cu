@@ -283,17 +283,20 @@ bool ep_rows_fit(const hmoe_layer_desc& d, size_t max_tokens) {
 //                       rows, their scales and routing weights go straight
 //                       into the owners' receive rows; the last CTA to
 //                       finish flags every rank
-//   ep_combine_kernel   the combine fused with the return: each routed row's
-//                       output is read from its owner's output rows once
-//                       every owner has flagged them
+//   the down projection the return fused into its epilogue: each output
+//                       row is stored straight into its source's own
+//                       permuted output rows (PushRows); the owner flags
+//                       every rank once its down kernel is done, and each
+//                       rank then combines its own rows locally
 //   ep_wait_kernel      bounded wait for every rank's flag of this epoch
 // A rank can run at most one epoch ahead of another (it needs their counts
 // of the same epoch before it writes anything into their buffers), and a
 // rank publishes the counts of epoch n only after its kernels of epoch
 // n - 1 have run.  So receive rows are never overwritten while their owner
-// computes on them, and an owner's output rows of epoch n are rewritten only
-// after every source has combined them (it needs their epoch n + 1 rows
-// first); the counts are double-buffered by epoch parity.
+// computes on them, and a source's output rows of epoch n + 1 are written
+// by the owners only after the source has combined epoch n (the owners need
+// its epoch n + 1 counts first); the counts are double-buffered by epoch
+// parity.
 //
 // Failure: a rank whose flag wait runs out, or whose count exchange fails,
 // stores the abort word into every rank's sync area (its own included)
@@ -464,21 +467,6 @@ struct PeerRows {
     }
 };
 
-// Return fused into the combine: a routed row's output is read from its
-// owner's expert-output rows (same receive-row index).
-struct PeerOut {
-    const PeerRowMap* map;
-    const __nv_bfloat16* yrows; // local rows (shared experts)
-    size_t y_off;
-    int H;
-    __device__ const __nv_bfloat16* operator()(int r) const {
-        if (r >= map->routed) return yrows + static_cast<size_t>(r) * H;
-        const int q = map->owner(r);
-        const int d = map->dest_base[q] + r - map->send_off[q];
-        return reinterpret_cast<const __nv_bfloat16*>(map->peer[q] + y_off) + static_cast<size_t>(d) * H;
-    }
-};
-
 __device__ void load_row_map(const PeerCtx& c, int routed, PeerRowMap* m) {
     const EpDevPlan* plan = reinterpret_cast<const EpDevPlan*>(c.peer[c.me] + kEpPlanOff);
     if (threadIdx.x < c.P) {
@@ -520,22 +508,6 @@ __global__ void __launch_bounds__(256) ep_permute_kernel(PeerCtx c, const float*
 // also flags the return.  An aborted rank raises no flags.
 __global__ void ep_signal_kernel(PeerCtx c, int kind) {
     if (threadIdx.x == 0 && !ep_aborted(c)) signal_all(c, kind);
-}
-
-__global__ void __launch_bounds__(256) ep_combine_kernel(PeerCtx c, const int32_t* __restrict__ inv,
-                                                         const uint32_t* __restrict__ ids, int k, int E, int slots,
-                                                         int routed, int H, const __nv_bfloat16* yrows, size_t y_off,
-                                                         float* __restrict__ out) {
-    __shared__ PeerRowMap map;
-    __shared__ int aborted_s;
-    if (threadIdx.x == 0) aborted_s = ep_aborted(c) ? 1 : 0;
-    load_row_map(c, routed, &map); // synchronises the CTA
-    if (aborted_s) { // no peer's rows are read after a failure: the token's output is zero
-        float* o = out + static_cast<size_t>(blockIdx.x) * H;
-        for (int h = threadIdx.x; h < H; h += blockDim.x) o[h] = 0.0f;
-        return;
-    }
-    combine_token(inv, ids, k, E, slots, H, blockIdx.x, out, PeerOut{&map, yrows, y_off, H});
 }
 
 // Peer-memory forward (workspace == comm->reg_ws); the steps of
@@ -604,6 +576,11 @@ hmoe_status ep_forward_peer(const hmoe_layer_desc* desc, hmoe_ep_comm* comm, con
     in.hmid16 = reinterpret_cast<__nv_bfloat16*>(ws + w.hin);
     in.yrows = reinterpret_cast<__nv_bfloat16*>(ws + w.yin);
     in.max_group = static_cast<int>(std::min<size_t>(static_cast<size_t>(P) * max_tokens, INT_MAX));
+    // the return fused into the down projection: each output row goes
+    // straight into its source's own permuted output rows
+    const EpDevPlan* dplan = reinterpret_cast<const EpDevPlan*>(ws + kEpPlanOff);
+    in.push = PushRows{comm->d_peer_ws, kEpSyncBytes + w.local.yrows, dplan->ret_off, dplan->recv_base,
+                       reinterpret_cast<const uint32_t*>(ws + kEpAbortOff)};
     const int32_t* counts_all = reinterpret_cast<const int32_t*>(ws + w.counts_all) + static_cast<size_t>(parity) * P * E;
     const SegSpec seg{nullptr, counts_all + first, E, P * Eloc, Eloc, 0, 0};
     r = launch_tile_list(seg, const_cast<int4*>(in.tiles), const_cast<int32_t*>(in.tile_count), in.tile_cap, s);
@@ -623,21 +600,20 @@ hmoe_status ep_forward_peer(const hmoe_layer_desc* desc, hmoe_ep_comm* comm, con
     // 4. this rank's experts over the received (source, expert) segments
     r = run_experts(in, use_gemv(rin_cap, in.H, in.I), true, s);
     if (r != HMOE_OK) return r;
-    // 5. the outputs are ready for their sources
+    // 5. every output row has been stored into its source: flag it
     ep_signal_kernel<<<1, 32, 0, s>>>(c, 2);
     r = check_launch("hmoe EP return signal");
     if (r != HMOE_OK) return r;
     ep_wait_kernel<<<1, 32, 0, s>>>(c, 2, true);
     r = check_launch("hmoe EP return wait");
     if (r != HMOE_OK) return r;
-    // 6. combine fused with the return: each routed row is read from its
-    // owner's output rows, in ascending expert id
-    if (tokens > 0)
-        ep_combine_kernel<<<static_cast<unsigned>(tokens), 256, 0, s>>>(
-            c, reinterpret_cast<const int32_t*>(wsl + w.local.inv),
-            placed ? reinterpret_cast<const uint32_t*>(wsl + w.local.ids) : nullptr, k, E, slots, routed,
-            static_cast<int>(H), reinterpret_cast<const __nv_bfloat16*>(wsl + w.local.yrows), w.yin, y);
-    r = check_launch("hmoe EP combine");
+    // 6. the combine over this rank's own rows (the owners wrote the routed
+    // ones), in ascending expert id
+    r = launch_combine(reinterpret_cast<const __nv_bfloat16*>(wsl + w.local.yrows),
+                       reinterpret_cast<const int32_t*>(wsl + w.local.inv),
+                       placed ? reinterpret_cast<const uint32_t*>(wsl + w.local.ids) : nullptr, placed ? k : 0, E,
+                       static_cast<int>(tokens), slots, static_cast<int>(H), y, s);
+
     stage(5, s);
     return r;
 }

@@ -107,6 +107,7 @@ struct GemmArgs {
     void* out;                  // BF16 rows [R,N]: gate/up SwiGLU output; down weighted output
     int K, N;
     DeviceStatus* st;
+    PushRows push;              // down: rows pushed to their sources (peer != null)
 };
 
 __device__ __forceinline__ uint32_t bf16x2(float lo, float hi) {
@@ -496,12 +497,14 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
                     const int f0 = nb * 256 + 128 * static_cast<int>(rank);
                     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
                     const int gt = q * 32 + lane; // thread index inside the group
+                    // pushed rows: none after an abort (no store into a peer)
+                    const bool store = !a.push.peer || *reinterpret_cast<const volatile uint32_t*>(a.push.abort) == 0;
 #pragma unroll
                     for (int p = 0; p < 4; ++p) {
                         const int idx = gt + 128 * p; // 512 pieces of 8 BF16
                         const int t = idx >> 4, c = idx & 15;
-                        if (t < nt && f0 + c * 8 < a.N)
-                            *reinterpret_cast<uint4*>(out + static_cast<size_t>(row0 + c0 + t) * a.N + f0 + c * 8) =
+                        if (store && t < nt && f0 + c * 8 < a.N)
+                            *reinterpret_cast<uint4*>(pushed_row(a.push, out, td.w, row0 + c0 + t, a.N) + f0 + c * 8) =
                                 *reinterpret_cast<const uint4*>(st + t * 128 + c * 8);
                     }
                     epi_barrier(grp);
@@ -511,6 +514,7 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
             __syncwarp();
             if (lane == 0) sm100::mbar_arrive_remote(sm100::map_shared(sm100::smem_u32(&accempty[buf]), 0));
         }
+        if (a.push.peer) __threadfence_system(); // pushed rows visible to their sources before the return flag
     }
     // teardown: every thread of both CTAs arrives here, also after an abort
     if (warp == 2) {
@@ -563,6 +567,7 @@ __global__ void __launch_bounds__(kMaxSegments) tile_list_kernel(SegSpec sp, int
     __syncthreads();
     if (i == 0) *tile_count = min(capacity, total_s);
     if (!valid || ntile == 0) return;
+    const int group = i / sp.eps;
     // tiles of segments ordered before this one: longer tiles, or equal
     // tiles and a lower segment index (independent partial sums so that the
     // shared-memory loads pipeline)
@@ -578,7 +583,7 @@ __global__ void __launch_bounds__(kMaxSegments) tile_list_kernel(SegSpec sp, int
     int row = r0;
     for (int f = 0; f < ntile; ++f) {
         const int rows = base + (f < extra);
-        if (pos + f < capacity) tiles[pos + f] = make_int4(e, row, rows, 0);
+        if (pos + f < capacity) tiles[pos + f] = make_int4(e, row, rows, group);
         row += rows;
     }
 }
@@ -750,7 +755,7 @@ hmoe_status gemm_gate_up(const ExpertRun& r, cudaStream_t s) {
         return HMOE_CUDA_ERROR;
     }
     const int nb = (r.I + 127) / 128; // 128 features (64 per CTA) per pair
-    GemmArgs a{r.tiles, r.tile_count, nb, r.quant, nullptr, r.xscale, r.hmid16, r.H, r.I, r.st};
+    GemmArgs a{r.tiles, r.tile_count, nb, r.quant, nullptr, r.xscale, r.hmid16, r.H, r.I, r.st, PushRows{}};
     return launch_gemm<true>(mg, mu, mb, a, r.tile_cap * nb, s);
 }
 
@@ -762,7 +767,7 @@ hmoe_status gemm_down(const ExpertRun& r, cudaStream_t s) {
         return HMOE_CUDA_ERROR;
     }
     const int nb = (r.H + 255) / 256; // 256 features (128 per CTA) per pair
-    GemmArgs a{r.tiles, r.tile_count, nb, r.quant, r.weight, nullptr, r.yrows, r.I, r.H, r.st};
+    GemmArgs a{r.tiles, r.tile_count, nb, r.quant, r.weight, nullptr, r.yrows, r.I, r.H, r.st, r.push};
     return launch_gemm<false>(md, md, mb, a, r.tile_cap * nb, s);
 }
 

@@ -204,12 +204,14 @@ __global__ void __launch_bounds__(kVThreads, 2)
                 const float g = qp.scale[a.proj0] * s0;
                 const float u = qp.scale[a.proj0 + 1] * s1;
                 a.out32[row * N + c] = silu(g) * u;
-            } else {
-                a.out16[row * N + c] = __float2bfloat16_rn(a.weight[row] * (qp.scale[a.proj0] * s0));
+            } else if (!a.push.peer || *reinterpret_cast<const volatile uint32_t*>(a.push.abort) == 0) {
+                pushed_row(a.push, a.out16, td.w, static_cast<int>(row), N)[c] =
+                    __float2bfloat16_rn(a.weight[row] * (qp.scale[a.proj0] * s0));
             }
         }
         cluster.sync(); // peers' partial sums stay alive until read; ring free again
     }
+    if (!GATE_UP && a.push.peer) __threadfence_system(); // pushed rows visible before the return flag
 }
 
 template <bool GATE_UP, int TOK>
@@ -307,6 +309,7 @@ hmoe_status gemv_down(const ExpertRun& r, cudaStream_t s) {
     g.weight = r.weight;
     g.proj0 = 2;
     g.out16 = r.yrows;
+    g.push = r.push;
     g.K = r.I;
     g.N = r.H;
     CUtensorMap md;

@@ -31,9 +31,30 @@ constexpr int kGemvMaxAssignments = 64;
 constexpr int kMaxSlots = 96;
 
 // One expert-MLP pass over permuted rows.  Rows of one expert are cut into
-// tiles (expert, first row, rows, 0) of at most kTileRows rows; both
-// variants consume the same tile list.
+// tiles (expert, first row, rows, segment group) of at most kTileRows rows;
+// both variants consume the same tile list.  The segment group is the
+// source rank under expert parallelism (0 on one GPU).
 constexpr int kTileRows = 256;
+
+// Where the down projection's output rows go when they are pushed back to
+// their source ranks (expert parallelism, peer-memory path): receive row d
+// of a tile from source p is stored at row ret_off[p] + d - recv_base[p] of
+// the BF16 rows at byte offset `off` of source p's workspace peer[p], unless
+// the abort word is set.  peer == null: rows stay in ExpertRun::yrows.
+struct PushRows {
+    char* const* peer;
+    size_t off;
+    const int32_t* ret_off;
+    const int32_t* recv_base;
+    const uint32_t* abort;
+};
+
+// Row d of a pushed tile from source p (or row d of `local`).
+__device__ __forceinline__ __nv_bfloat16* pushed_row(const PushRows& p, __nv_bfloat16* local, int src, int d, int N) {
+    if (!p.peer) return local + static_cast<size_t>(d) * N;
+    return reinterpret_cast<__nv_bfloat16*>(p.peer[src] + p.off) +
+           static_cast<size_t>(p.ret_off[src] + d - p.recv_base[src]) * N;
+}
 
 struct ExpertRun {
     const __half* xrows;        // [rows_cap, H] permuted input rows, FP16, scaled per token
@@ -53,6 +74,7 @@ struct ExpertRun {
     int H, I;
     int max_group;              // upper bound of rows of one expert
     DeviceStatus* st;
+    PushRows push;              // down outputs pushed to their sources (peer == null: yrows)
 };
 
 struct GemvArgs {
@@ -66,6 +88,7 @@ struct GemvArgs {
     int proj0;                  // 0: gate (and up), 2: down
     float* out32;               // gate/up: FP32 intermediate
     __nv_bfloat16* out16;       // down: BF16 weighted rows
+    PushRows push;              // down: rows pushed to their sources instead (peer != null)
     int K, N, KS;
     DeviceStatus* st;
 };
