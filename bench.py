@@ -293,6 +293,62 @@ def reference_cuda(cfg, T, seed, steps, warmup, gpu_index, pci, timeout=600):
     return out
 
 
+def decode_split(layer, cfg, T, seed, dev, flush, events, peaks, steps=20):
+    """Device-timed stage split of a decode-sized batch of T tokens on the
+    resident layer: a CUDA-graph replay per step with the library's stage
+    events, the L2 flushed before each step (a decode step touches fewer
+    expert bytes than the L2 holds)."""
+    import ctypes
+    import numpy as np
+    import torch
+    import hmoe_api as H
+    x = torch.from_numpy(H.make_tokens(cfg, T, seed=seed + 31)).to(dev)
+    y = torch.empty_like(x)
+    _, _, off, _, _ = layer.route(x)
+    torch.cuda.synchronize()
+    U = int((np.diff(off.cpu().numpy()) > 0).sum()) + cfg.shared_experts
+    arr = (ctypes.c_void_p * 6)(*[e.cuda_event for e in events])
+    H.check("stage events", H.lib().hmoe_set_stage_events(arr, 6))
+    try:
+        for _ in range(3):
+            layer.forward(x, y)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            layer.forward(x, y)
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            layer.forward(x, y)
+        torch.cuda.synchronize()
+        st = {s_: [] for s_ in STAGES}
+        tot = []
+        for _ in range(steps):
+            flush.zero_()
+            graph.replay()
+            events[5].synchronize()
+            tot.append(events[0].elapsed_time(events[5]))
+            for i, s_ in enumerate(STAGES):
+                st[s_].append(events[i].elapsed_time(events[i + 1]))
+        del graph
+    finally:
+        H.check("stage events", H.lib().hmoe_set_stage_events(None, 0))
+    ms = statistics.median(tot)
+    med = {k: statistics.median(v) for k, v in st.items()}
+    alg = algorithmic(cfg, T, U)
+    roof_ms = 1e3 * max(alg["layer"]["bytes"] / (peaks["hbm_gbs"] * 1e9),
+                        alg["layer"]["flops"] / (peaks["bf16_tflops"] * 1e12))
+    expert_bytes = alg["gate_up"]["bytes"] + alg["down"]["bytes"]
+    expert_ms = med["gate_up"] + med["down"]
+    return {"tokens": T, "ms_per_step": ms, "value": T / (ms * 1e-3), "unit": UNIT,
+            "stages_ms": med, "unique_experts": U, "layer_roofline_ms": roof_ms,
+            "layer_roofline_frac": roof_ms / ms,
+            "expert_hbm_gbs": expert_bytes / (expert_ms * 1e-3) / 1e9,
+            "expert_hbm_frac": expert_bytes / (expert_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+            "timing": "cuda-graph replay, median of %d steps, 256 MiB L2 flush before each" % steps}
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -571,6 +627,10 @@ def main():
                "sample": f"{n} tokens of this workload through the reference CPU path "
                          f"(oracle/_ref), {dt:.1f} s, expert groups over {threads} threads"}
 
+    decode = None
+    if world == 1 and T > 16:
+        decode = [decode_split(layer, cfg, t, args.seed, dev, flush, ev, peaks) for t in (1, 16)]
+
     ref_cuda = None
     ref_cuda_decode = None
     if world == 1 and not args.no_reference_cuda:
@@ -597,6 +657,7 @@ def main():
         "layer_roofline_frac": layer_roof_ms / ms, "unique_experts": alg["unique_experts"],
         "rows_received_rank0": alg.get("rows_received"),
         "device_status": {"status": status[0], "near_ties": status[1], "sequential_logits": status[2]},
+        "decode": decode,
         "reference_cuda": ref_cuda,
         "reference_cuda_decode_t1": ref_cuda_decode,
     }

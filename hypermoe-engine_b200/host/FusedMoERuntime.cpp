@@ -8,6 +8,7 @@
 
 #include <cuda_runtime_api.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cstring>
 #include <stdexcept>
@@ -36,6 +37,7 @@ struct FusedMoERuntime::Impl {
     router::RouterConfig config;
     std::size_t H, I, S, stride, gateOffset, upOffset, downOffset;
     tensor::TensorView arena, bias;
+    tensor::Tensor ownedArena; // fromPackedStore: the device arena the runtime owns
     tensor::Tensor quant;     // device hmoe_expert_quant[E + S]
     tensor::Tensor workspace; // device scratch, grown to the largest batch seen
     cudaStream_t stream{};
@@ -219,6 +221,102 @@ BatchLayerExecutionResult FusedMoERuntime::executeBatch(LayerId layerId, tensor:
     }
     result.execution.uniqueExperts = result.routing.expertGroups.size();
     return result;
+}
+
+std::unique_ptr<FusedMoERuntime> FusedMoERuntime::fromPackedStore(std::shared_ptr<tensor::TensorBackend> backend,
+                                                                   const storage::ExpertStore& store,
+                                                                   const models::ExpertWeightMap& weights,
+                                                                   LayerId layer, router::RouterConfig config,
+                                                                   tensor::TensorView routerBias) {
+    config.validate();
+    if (!backend || !backend->available())
+        throw std::invalid_argument("fused MoE runtime requires an available CUDA tensor backend");
+    const std::size_t E = config.expertCount;
+    std::size_t H = 0, I = 0;
+    tensor::CpuTensorBackend cpu;
+    std::vector<ExpertQuantization> quant(E);
+    tensor::Tensor host;
+    std::size_t stride = 0;
+    for (std::size_t e = 0; e < E; ++e) {
+        const auto id = static_cast<std::uint32_t>(e);
+        const auto record = store.index().find(layer, id);
+        if (!record) throw std::invalid_argument("packed store lacks an expert of the layer");
+        const auto payload = store.mappedExpert(layer, id); // CRC-checked
+        // a TensorView does not own its storage: keep the buffer alive here
+        const auto buffer = std::make_shared<const std::vector<std::byte>>(payload.begin(), payload.end());
+        const auto view = tensor::TensorView::fromHostBuffer({payload.size()}, tensor::DType::INT8, buffer, false);
+        const auto w = weights.createViews(layer, id, view, record->offset);
+        const auto& g = w.gateProjection.shape().dimensions();
+        const auto& d = w.downProjection.shape().dimensions();
+        if (w.gateProjection.dtype() != tensor::DType::INT8 || w.upProjection.dtype() != tensor::DType::INT8 ||
+            w.downProjection.dtype() != tensor::DType::INT8 || g.size() != 2 || d.size() != 2 ||
+            w.upProjection.shape() != w.gateProjection.shape() || d[0] != g[1] || d[1] != g[0] ||
+            !w.gateQuantization || !w.upQuantization || !w.downQuantization)
+            throw std::invalid_argument("fused MoE runtime needs INT8 [H,I] gate/up and [I,H] down projections");
+        if (e == 0) {
+            H = g[0];
+            I = g[1];
+            stride = (3 * H * I + 4095) / 4096 * 4096; // ExpertPacker's blob alignment
+            host = cpu.allocateTensor({E * stride}, tensor::DType::INT8);
+            std::memset(host.data(), 0, E * stride);
+        } else if (g[0] != H || g[1] != I) {
+            throw std::invalid_argument("experts of one layer differ in shape");
+        }
+        auto* dst = static_cast<std::byte*>(host.data()) + e * stride;
+        std::memcpy(dst, w.gateProjection.data(), H * I);
+        std::memcpy(dst + H * I, w.upProjection.data(), H * I);
+        std::memcpy(dst + 2 * H * I, w.downProjection.data(), H * I);
+        quant[e] = {*w.gateQuantization, *w.upQuantization, *w.downQuantization};
+    }
+    auto arena = backend->allocateTensor(host.shape(), tensor::DType::INT8);
+    backend->copyTensor(host.view(), arena.view());
+    auto runtime = std::make_unique<FusedMoERuntime>(backend, config, H, I, arena.view(), stride, 0, H * I,
+                                                     2 * H * I, std::move(quant), 0, routerBias);
+    runtime->impl_->ownedArena = std::move(arena);
+    return runtime;
+}
+
+bool FusedMoERuntime::coversAllExperts(std::size_t deviceBudgetBytes, const storage::ExpertStore& store) {
+    std::size_t total = 0;
+    for (const auto& record : store.index().records()) {
+        if (record.size > deviceBudgetBytes - std::min(total, deviceBudgetBytes)) return false;
+        total += static_cast<std::size_t>(record.size);
+    }
+    return true;
+}
+
+tensor::Tensor FusedMoERuntime::executeWithResidual(LayerId, tensor::TensorView hiddenStates,
+                                                    tensor::TensorView routerWeights, tensor::TensorView residual,
+                                                    tensor::Tensor* bf16Output) {
+    auto& m = *impl_;
+    std::lock_guard<std::mutex> lock(m.mutex);
+    m.validate(hiddenStates, routerWeights);
+    const std::size_t T = hiddenStates.shape().dimensions()[0], H = m.H;
+    if (T == 0) throw std::invalid_argument("fused MoE runtime requires at least one token");
+    if (!residual || residual.shape() != hiddenStates.shape() || residual.dtype() != tensor::DType::FP32 ||
+        residual.device() != m.backend->device() || !residual.isContiguous())
+        throw std::invalid_argument("MoE output is incompatible with residual input");
+    checkCuda(cudaSetDevice(m.backend->device().ordinal), "cudaSetDevice");
+    m.backend->synchronizeExecution();
+    auto output = m.backend->allocateTensor({T, H}, tensor::DType::FP32);
+    std::uint16_t* y16 = nullptr;
+    if (bf16Output) {
+        *bf16Output = m.backend->allocateTensor({T, H}, tensor::DType::BF16);
+        y16 = static_cast<std::uint16_t*>(bf16Output->data());
+    }
+    const hmoe_layer_desc d = m.desc(routerWeights.data());
+    std::size_t bytes = 0;
+    check(hmoe_workspace_size(&d, T, &bytes), "fused MoE runtime workspace size");
+    void* ws = m.scratch(bytes);
+    check(hmoe_moe_forward_residual(&d, static_cast<const float*>(hiddenStates.data()),
+                                    static_cast<const float*>(residual.data()), static_cast<float*>(output.data()),
+                                    y16, T, ws, bytes, m.stream),
+          "fused MoE layer with residual");
+    std::int32_t status = 0, ties = 0, sequential = 0;
+    check(hmoe_read_status(ws, &status, &ties, &sequential, m.stream), "fused MoE layer status"); // synchronises
+    if (status == HMOE_NON_FINITE_ROUTER) throw std::runtime_error("router produced a non-finite score");
+    check(static_cast<hmoe_status>(status), "fused MoE layer (device)");
+    return output;
 }
 
 LayerExecutionResult FusedMoERuntime::executeLayer(LayerId layerId, tensor::TensorView hiddenState,

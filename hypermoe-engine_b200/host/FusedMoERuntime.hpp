@@ -28,7 +28,9 @@
 #pragma once
 
 #include "core/runtime/MoERuntime.hpp"
+#include "models/ExpertWeightMap.hpp"
 #include "router/RouterConfig.hpp"
+#include "storage/ExpertStore.hpp"
 #include "tensor/Tensor.hpp"
 #include "tensor/backend/TensorBackend.hpp"
 #include "tensor/quantization/Quantization.hpp"
@@ -69,6 +71,37 @@ public:
 
     FusedMoERuntime(const FusedMoERuntime&) = delete;
     FusedMoERuntime& operator=(const FusedMoERuntime&) = delete;
+
+    // All-resident expert mode (the packed model runtime's expert path,
+    // src/models/runtime/PackedModelRuntime.cpp:345-400, with nothing left for
+    // its scheduler, residency manager or transfer workers to do): every
+    // expert of `layer` is read once from the reference's own packed store,
+    // sliced with its ExpertWeightMap (ExpertWeightMap::createViews: the
+    // same views and quantisation checks), repacked gate|up|down into one
+    // device arena owned by the returned runtime, and uploaded through
+    // `backend`.  The routed experts are ids 0..config.expertCount-1.
+    [[nodiscard]] static std::unique_ptr<FusedMoERuntime> fromPackedStore(
+        std::shared_ptr<tensor::TensorBackend> backend, const storage::ExpertStore& store,
+        const models::ExpertWeightMap& weights, LayerId layer, router::RouterConfig config,
+        tensor::TensorView routerBias = {});
+
+    // Whether a device expert budget holds every expert the store indexes
+    // (the condition under which a packed runtime can run its MoE layers on
+    // fusedRuntime instances instead of the tiered MoERuntime).
+    [[nodiscard]] static bool coversAllExperts(std::size_t deviceBudgetBytes, const storage::ExpertStore& store);
+
+    // The transformer block's MoE stage with its residual add fused into the
+    // combine (TransformerBlock.cpp:93-104, MoELayer.cpp:37-39): returns
+    // residual + moe(hiddenStates) with one FP32 rounding, as the backend's
+    // add gives, and writes its BF16 copy into *bf16Output ([T, H], DType
+    // BF16, on the device) when given.  No [T, H] MoE output is materialised
+    // and no separate add runs; the call returns once the result is complete
+    // (the reference's CUDA tensor backend exposes no stream to order later
+    // work against).
+    [[nodiscard]] tensor::Tensor executeWithResidual(LayerId layerId, tensor::TensorView hiddenStates,
+                                                     tensor::TensorView routerWeights,
+                                                     tensor::TensorView residual,
+                                                     tensor::Tensor* bf16Output = nullptr);
 
     [[nodiscard]] BatchLayerExecutionResult executeBatch(LayerId layerId,
                                                          tensor::TensorView hiddenStates,

@@ -24,8 +24,12 @@
 #include "FusedMoERuntime.hpp"
 #include "hmoe.h"
 
+#include "models/ExpertWeightMap.hpp"
+#include "storage/ExpertStore.hpp"
 #include "tensor/backend/CpuTensorBackend.hpp"
 #include "tensor/backend/CudaTensorBackend.hpp"
+
+#include <filesystem>
 
 #include <cmath>
 #include <cstdio>
@@ -37,6 +41,8 @@
 #include <string>
 #include <thread>
 #include <vector>
+
+#include <unistd.h>
 
 extern "C" {
 void* hmr_layer_create(std::size_t H, std::size_t I, std::size_t E, std::size_t k, int softmax, int renorm,
@@ -196,13 +202,77 @@ int main(int argc, char** argv) {
         const Closeness close1 = compare(out1, std::vector<float>(outRef.begin(), outRef.begin() + H));
         hmr_layer_destroy(ref);
 
-        const bool ok = idsOk && scoresOk && groupsOk && close.ok() && layerOk && close1.ok();
+        // All-resident mode from the reference's own packed store: the
+        // experts written with ExpertStore::create (blob = gate|up|down) and
+        // mapped as the packer's manifest maps them; the runtime built from
+        // it must give the arena-built runtime's output bit for bit, and the
+        // fused residual stage out + residual (one FP32 rounding) with its
+        // BF16 copy.
+        bool packedOk = true, residualOk = true, coversOk = true;
+        if (S == 0) {
+            const auto dir = std::filesystem::temp_directory_path() /
+                             ("hmoe_packed_" + std::to_string(static_cast<long>(::getpid())));
+            std::filesystem::remove_all(dir);
+            std::filesystem::create_directories(dir);
+            std::vector<storage::ExpertBlob> blobs(E);
+            for (std::size_t e = 0; e < E; ++e) {
+                blobs[e].layerId = 3;
+                blobs[e].expertId = static_cast<std::uint32_t>(e);
+                blobs[e].quantizationType = 1;
+                const auto* src = reinterpret_cast<const std::byte*>(arena.data() + e * stride);
+                blobs[e].data.assign(src, src + 3 * proj);
+            }
+            storage::ExpertStore::create(dir, blobs, "{}");
+            storage::ExpertStore store(dir);
+            models::ExpertWeightMap mappings;
+            const models::ExpertWeightType types[3] = {models::ExpertWeightType::GATE, models::ExpertWeightType::UP,
+                                                       models::ExpertWeightType::DOWN};
+            for (std::size_t e = 0; e < E; ++e) {
+                const auto rec = store.index().find(3, static_cast<std::uint32_t>(e)).value();
+                for (int p = 0; p < 3; ++p)
+                    mappings.add(3, static_cast<std::uint32_t>(e), types[p],
+                                 {"expert", p < 2 ? tensor::Shape{H, I} : tensor::Shape{I, H}, DType::INT8,
+                                  tensor::quantization::QuantizedDType::INT8, rec.offset + p * proj, proj, 3,
+                                  static_cast<std::uint32_t>(e),
+                                  tensor::quantization::QuantizationParameters{q[e].scale[p], q[e].zero_point[p]}});
+            }
+            std::size_t totalBytes = 0;
+            for (const auto& rec : store.index().records()) totalBytes += static_cast<std::size_t>(rec.size);
+            coversOk = runtime::FusedMoERuntime::coversAllExperts(totalBytes, store) &&
+                       !runtime::FusedMoERuntime::coversAllExperts(totalBytes - 1, store);
+            auto packed = runtime::FusedMoERuntime::fromPackedStore(
+                cuda, store, mappings, 3, config, zipf > 0 ? tensor::TensorView(dBias) : tensor::TensorView());
+            auto pres = packed->executeBatch(3, dX.view(), dW.view());
+            packedOk = download(*cuda, pres.output) == out;
+            tensor::Tensor out16;
+            auto withRes = packed->executeWithResidual(3, dX.view(), dW.view(), dX.view(), &out16);
+            const auto yr = download(*cuda, withRes);
+            tensor::CpuTensorBackend cpu;
+            auto h16 = cpu.allocateTensor({T, H}, DType::BF16);
+            cuda->copyTensor(out16.view(), h16.view());
+            const auto* b16 = static_cast<const std::uint16_t*>(h16.data());
+            for (std::size_t i = 0; i < T * H && residualOk; ++i) {
+                const float sum = x[i] + out[i];
+                residualOk = yr[i] == sum;
+                // round to nearest even of the FP32 result
+                std::uint32_t u;
+                std::memcpy(&u, &sum, 4);
+                const std::uint32_t r = (u + 0x7fffu + ((u >> 16) & 1u)) >> 16;
+                residualOk = residualOk && b16[i] == static_cast<std::uint16_t>(r);
+            }
+            std::filesystem::remove_all(dir);
+        }
+
+        const bool ok = idsOk && scoresOk && groupsOk && close.ok() && layerOk && close1.ok() && packedOk &&
+                        residualOk && coversOk;
         std::printf("{\"ok\": %s, \"tokens\": %zu, \"ids_equal\": %s, \"scores_equal\": %s, \"groups_equal\": %s, "
                     "\"elementwise\": %s, \"normwise\": %.3e, \"cosine\": %.7f, \"max_abs\": %.3e, "
-                    "\"execute_layer_ok\": %s, \"unique_experts\": %zu, \"backend\": \"%s\"}\n",
+                    "\"execute_layer_ok\": %s, \"packed_store_ok\": %s, \"residual_ok\": %s, \"covers_ok\": %s, "
+                    "\"unique_experts\": %zu, \"backend\": \"%s\"}\n",
                     ok ? "true" : "false", T, idsOk ? "true" : "false", scoresOk ? "true" : "false",
                     groupsOk ? "true" : "false", close.elementwise ? "true" : "false", close.normwise, close.cosine,
-                    close.maxAbs, (layerOk && close1.ok()) ? "true" : "false", touched,
+                    close.maxAbs, (layerOk && close1.ok()) ? "true" : "false", packedOk ? "true" : "false",
+                    residualOk ? "true" : "false", coversOk ? "true" : "false", touched,
                     res.execution.tensorBackend.c_str());
         return ok ? 0 : 1;
     } catch (const std::exception& e) {

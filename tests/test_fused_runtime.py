@@ -5,7 +5,12 @@ layer, compiled against the reference's headers and driven through the
 reference's own CudaTensorBackend by oracle/_ref/fused_runtime_check, which
 compares it with the reference's CPU classes: ids and expert groups bit for
 bit, scores to the CPU expf's last place, outputs within the INT8 layer
-tolerance (tests/tolerance.py)."""
+tolerance (tests/tolerance.py).  Without shared experts it also builds the
+runtime from a packed ExpertStore written by the reference's own
+ExpertStore::create (FusedMoERuntime::fromPackedStore: same output bit for
+bit), runs the transformer block's MoE stage with the residual fused
+(executeWithResidual: residual + output in one FP32 rounding, and its BF16
+copy rounded to nearest even) and checks the all-resident budget rule."""
 import json
 import os
 import subprocess
@@ -33,3 +38,6 @@ def test_fused_runtime_matches_reference_cpu_path(cuda, cfg_name, T, seed):
     assert p.returncode == 0, (p.stdout + p.stderr)[-3000:]
     r = json.loads(p.stdout.strip().splitlines()[-1])
     assert r["ok"] and r["ids_equal"] and r["groups_equal"] and r["execute_layer_ok"], r
+    # all-resident mode from a packed ExpertStore, the fused residual stage
+    # and the budget rule (configurations without shared experts)
+    assert r["packed_store_ok"] and r["residual_ok"] and r["covers_ok"], r
