@@ -69,6 +69,10 @@ def parse():
     p.add_argument("--placement", default="balanced", choices=["balanced", "contiguous"],
                    help="expert placement under expert parallelism: balanced from a calibration batch's "
                         "routing counts (EPLB-style static placement), or contiguous expert ids")
+    p.add_argument("--no-e2e", action="store_true",
+                   help="skip the host-buffer (e2e) measurements (e.g. for a kernel launch list)")
+    p.add_argument("--no-decode", action="store_true",
+                   help="skip the decode-size stage splits added to a prefill line")
     p.add_argument("--eager", action="store_true",
                    help="time eager hmoe_moe_forward calls instead of CUDA-graph replays")
     return p.parse_args()
@@ -509,81 +513,83 @@ def main():
     # e2e: host buffers in and out, both copies inside the timed region
     # (single GPU: hmoe_moe_forward_host; expert parallelism: pinned copies
     # around hmoe_ep_moe_forward on the same stream)
-    xh = torch.from_numpy(x_np).pin_memory()
-    yh = torch.empty_like(xh).pin_memory()
+    e2e = e2e_serial = None
+    if not args.no_e2e:
+        xh = torch.from_numpy(x_np).pin_memory()
+        yh = torch.empty_like(xh).pin_memory()
 
-    def forward_host():
+        def forward_host():
+            if comm is None:
+                layer.forward_host(xh, yh)
+            else:
+                x.copy_(xh, non_blocking=True)
+                layer.forward(x, y, max_tokens=T)
+                yh.copy_(y, non_blocking=True)
+
+        for _ in range(max(1, args.warmup // 2)):
+            forward_host()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e2e_ms = []
+        for _ in range(args.steps):
+            flush.zero_()
+            e0.record(stream)
+            forward_host()
+            e1.record(stream)
+            e1.synchronize()
+            e2e_ms.append(e0.elapsed_time(e1))
+        em = statistics.mean(e2e_ms)
+        if dist is not None:
+            t = torch.tensor([em], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            em = float(t.item())
+        e2e_serial = {"value": world * T / (em * 1e-3), "unit": UNIT, "h2d_bytes_per_step": int(x_np.nbytes),
+                      "d2h_bytes_per_step": int(x_np.nbytes),
+                      "timing": "one call at a time: 256 MiB L2 flush, then H2D copy, layer, D2H copy; CUDA events"}
+        e2e = e2e_serial
         if comm is None:
-            layer.forward_host(xh, yh)
-        else:
-            x.copy_(xh, non_blocking=True)
-            layer.forward(x, y, max_tokens=T)
-            yh.copy_(y, non_blocking=True)
+            # A caller with a stream of batches keeps several calls in flight:
+            # one stream, one workspace and one pair of page-locked buffers per
+            # call in flight.  Each step still copies its own tokens in and its
+            # output back; a call runs copy-in, layer, copy-out in order on its
+            # stream, so with three in flight one call's layer overlaps the
+            # others' copies in both directions.  The K steps are timed as a
+            # whole (events on the first stream, the others joined into it).
+            inflight = 3
+            xhs, yhs = [xh], [yh]
+            for i in range(1, inflight):
+                xhs.append(torch.from_numpy(H.make_tokens(cfg, T, seed=args.seed + i)).pin_memory())
+                yhs.append(torch.empty_like(xh).pin_memory())
+            pstreams = [torch.cuda.Stream(device=dev) for _ in range(inflight)]
+            pws = [torch.empty(layer.workspace_bytes(T, host_io=True), dtype=torch.uint8, device=dev)
+                   for _ in range(inflight)]
 
-    for _ in range(max(1, args.warmup // 2)):
-        forward_host()
-    barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e2e_ms = []
-    for _ in range(args.steps):
-        flush.zero_()
-        e0.record(stream)
-        forward_host()
-        e1.record(stream)
-        e1.synchronize()
-        e2e_ms.append(e0.elapsed_time(e1))
-    em = statistics.mean(e2e_ms)
-    if dist is not None:
-        t = torch.tensor([em], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        em = float(t.item())
-    e2e_serial = {"value": world * T / (em * 1e-3), "unit": UNIT, "h2d_bytes_per_step": int(x_np.nbytes),
-                  "d2h_bytes_per_step": int(x_np.nbytes),
-                  "timing": "one call at a time: 256 MiB L2 flush, then H2D copy, layer, D2H copy; CUDA events"}
-    e2e = e2e_serial
-    if comm is None:
-        # A caller with a stream of batches keeps several calls in flight:
-        # one stream, one workspace and one pair of page-locked buffers per
-        # call in flight.  Each step still copies its own tokens in and its
-        # output back; a call runs copy-in, layer, copy-out in order on its
-        # stream, so with three in flight one call's layer overlaps the
-        # others' copies in both directions.  The K steps are timed as a
-        # whole (events on the first stream, the others joined into it).
-        inflight = 3
-        xhs, yhs = [xh], [yh]
-        for i in range(1, inflight):
-            xhs.append(torch.from_numpy(H.make_tokens(cfg, T, seed=args.seed + i)).pin_memory())
-            yhs.append(torch.empty_like(xh).pin_memory())
-        pstreams = [torch.cuda.Stream(device=dev) for _ in range(inflight)]
-        pws = [torch.empty(layer.workspace_bytes(T, host_io=True), dtype=torch.uint8, device=dev)
-               for _ in range(inflight)]
+            def pipelined(n):
+                for i in range(n):
+                    j = i % inflight
+                    layer.forward_host(xhs[j], yhs[j], stream=pstreams[j], workspace=pws[j])
 
-        def pipelined(n):
-            for i in range(n):
-                j = i % inflight
-                layer.forward_host(xhs[j], yhs[j], stream=pstreams[j], workspace=pws[j])
-
-        pipelined(max(inflight, args.warmup))
-        torch.cuda.synchronize()
-        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        p0.record(pstreams[0])
-        for ps in pstreams[1:]:
-            ps.wait_event(p0)
-        pipelined(args.steps)
-        for ps in pstreams[1:]:
-            join = torch.cuda.Event()
-            join.record(ps)
-            pstreams[0].wait_event(join)
-        p1.record(pstreams[0])
-        p1.synchronize()
-        pm = p0.elapsed_time(p1) / args.steps
-        e2e = {"value": T / (pm * 1e-3), "unit": UNIT, "h2d_bytes_per_step": int(x_np.nbytes),
-               "d2h_bytes_per_step": int(x_np.nbytes), "ms_per_step": pm,
-               "timing": (f"{args.steps} hmoe_moe_forward_host calls, {inflight} in flight on {inflight} streams "
-                          f"with {inflight} workspaces (each call: H2D copy of its tokens, layer, D2H copy of "
-                          "its output); total time over the calls; inputs larger than L2 (INT8 expert arena), "
-                          "no flush")}
-        del pws
+            pipelined(max(inflight, args.warmup))
+            torch.cuda.synchronize()
+            p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            p0.record(pstreams[0])
+            for ps in pstreams[1:]:
+                ps.wait_event(p0)
+            pipelined(args.steps)
+            for ps in pstreams[1:]:
+                join = torch.cuda.Event()
+                join.record(ps)
+                pstreams[0].wait_event(join)
+            p1.record(pstreams[0])
+            p1.synchronize()
+            pm = p0.elapsed_time(p1) / args.steps
+            e2e = {"value": T / (pm * 1e-3), "unit": UNIT, "h2d_bytes_per_step": int(x_np.nbytes),
+                   "d2h_bytes_per_step": int(x_np.nbytes), "ms_per_step": pm,
+                   "timing": (f"{args.steps} hmoe_moe_forward_host calls, {inflight} in flight on {inflight} streams "
+                              f"with {inflight} workspaces (each call: H2D copy of its tokens, layer, D2H copy of "
+                              "its output); total time over the calls; inputs larger than L2 (INT8 expert arena), "
+                              "no flush")}
+            del pws
 
     status = layer.read_status()
     if rank != 0:
@@ -628,7 +634,7 @@ def main():
                          f"(oracle/_ref), {dt:.1f} s, expert groups over {threads} threads"}
 
     decode = None
-    if world == 1 and T > 16:
+    if world == 1 and T > 16 and not args.no_decode:
         decode = [decode_split(layer, cfg, t, args.seed, dev, flush, ev, peaks) for t in (1, 16)]
 
     ref_cuda = None
