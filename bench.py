@@ -312,41 +312,55 @@ def decode_split(layer, cfg, T, seed, dev, flush, events, peaks, steps=20):
     torch.cuda.synchronize()
     U = int((np.diff(off.cpu().numpy()) > 0).sum()) + cfg.shared_experts
     arr = (ctypes.c_void_p * 6)(*[e.cuda_event for e in events])
-    H.check("stage events", H.lib().hmoe_set_stage_events(arr, 6))
-    try:
-        for _ in range(3):
-            layer.forward(x, y)
-        side = torch.cuda.Stream()
-        side.wait_stream(torch.cuda.current_stream())
-        with torch.cuda.stream(side):
-            layer.forward(x, y)
-        torch.cuda.current_stream().wait_stream(side)
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            layer.forward(x, y)
-        torch.cuda.synchronize()
-        st = {s_: [] for s_ in STAGES}
-        tot = []
-        for _ in range(steps):
-            flush.zero_()
-            graph.replay()
-            events[5].synchronize()
-            tot.append(events[0].elapsed_time(events[5]))
-            for i, s_ in enumerate(STAGES):
-                st[s_].append(events[i].elapsed_time(events[i + 1]))
-        del graph
-    finally:
-        H.check("stage events", H.lib().hmoe_set_stage_events(None, 0))
-    ms = statistics.median(tot)
-    med = {k: statistics.median(v) for k, v in st.items()}
+
+    def replay(variant):
+        H.set_variant(variant)
+        H.check("stage events", H.lib().hmoe_set_stage_events(arr, 6))
+        try:
+            for _ in range(3):
+                layer.forward(x, y)
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                layer.forward(x, y)
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                layer.forward(x, y)
+            torch.cuda.synchronize()
+            st = {s_: [] for s_ in STAGES}
+            tot = []
+            for _ in range(steps):
+                flush.zero_()
+                graph.replay()
+                events[5].synchronize()
+                tot.append(events[0].elapsed_time(events[5]))
+                for i, s_ in enumerate(STAGES):
+                    st[s_].append(events[i].elapsed_time(events[i + 1]))
+            del graph
+        finally:
+            H.check("stage events", H.lib().hmoe_set_stage_events(None, 0))
+            H.set_variant(0)
+        return statistics.median(tot), {k: statistics.median(v) for k, v in st.items()}
+
+    # The automatic choice (the single-kernel decode layer up to 8 tokens),
+    # then, for its stage split, the multi-kernel GEMV path on the same batch.
+    ms, med = replay(0)
+    single = T <= 8
+    multi_ms, multi = replay(1) if single else (ms, med)
     alg = algorithmic(cfg, T, U)
     roof_ms = 1e3 * max(alg["layer"]["bytes"] / (peaks["hbm_gbs"] * 1e9),
                         alg["layer"]["flops"] / (peaks["bf16_tflops"] * 1e12))
     expert_bytes = alg["gate_up"]["bytes"] + alg["down"]["bytes"]
-    expert_ms = med["gate_up"] + med["down"]
+    # single kernel: expert bytes over the whole layer's time (a lower bound
+    # of the expert stream's rate); otherwise over the expert stages' time
+    expert_ms = ms if single else med["gate_up"] + med["down"]
     return {"tokens": T, "ms_per_step": ms, "value": T / (ms * 1e-3), "unit": UNIT,
-            "stages_ms": med, "unique_experts": U, "layer_roofline_ms": roof_ms,
+            "path": "single-kernel decode layer" if single else "multi-kernel layer",
+            "stages_ms": None if single else med,
+            "multi_kernel": {"ms_per_step": multi_ms, "stages_ms": multi} if single else None,
+            "unique_experts": U, "layer_roofline_ms": roof_ms,
             "layer_roofline_frac": roof_ms / ms,
             "expert_hbm_gbs": expert_bytes / (expert_ms * 1e-3) / 1e9,
             "expert_hbm_frac": expert_bytes / (expert_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
@@ -603,9 +617,13 @@ def main():
     avg = {s: statistics.mean(v) for s, v in stage_ms.items()}
     top = max(STAGES, key=lambda s: avg[s])
     a = alg[top]
+    dt_s = avg[top] * 1e-3
+    if world == 1 and T <= 8:
+        # one kernel runs the whole layer (decode_layer_kernel): its bytes
+        # are the layer's, its time the step's
+        top, a, dt_s = "decode_layer", alg["layer"], ms * 1e-3
     ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
     tensor = a["flops"] > 0 and a["flops"] / max(a["bytes"], 1) > ridge
-    dt_s = avg[top] * 1e-3
     if tensor:
         roof = {"bound": "tensor", "achieved": a["flops"] / dt_s / 1e12, "peak": peaks["bf16_tflops"],
                 "unit": "TFLOP/s"}
@@ -635,7 +653,7 @@ def main():
 
     decode = None
     if world == 1 and T > 16 and not args.no_decode:
-        decode = [decode_split(layer, cfg, t, args.seed, dev, flush, ev, peaks) for t in (1, 16)]
+        decode = [decode_split(layer, cfg, t, args.seed, dev, flush, ev, peaks) for t in (1, 8, 16)]
 
     ref_cuda = None
     ref_cuda_decode = None

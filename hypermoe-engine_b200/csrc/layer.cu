@@ -33,6 +33,8 @@
 namespace hmoe {
 
 int g_variant = 0;
+constexpr int kDecodeLayerAutoTokens = 1; // single-kernel decode layer chosen automatically up to here
+extern int g_route_variant; // router.cu
 cudaEvent_t g_stage_events[6];
 int g_stage_count = 0;
 
@@ -63,6 +65,8 @@ Workspace plan_workspace(const hmoe_layer_desc& d, size_t T) {
     w.block_counts = take(((T + kGroupBlock - 1) / kGroupBlock) * E * 4);
     w.route_acc_bytes = route_decode_scratch_bytes(T, static_cast<int>(d.hidden), static_cast<int>(E));
     w.route_acc = take(w.route_acc_bytes); // decode router partials (zeroed)
+    w.dl_ctl_bytes = decode_layer_ctl_bytes(d, T);
+    w.dl_ctl = take(w.dl_ctl_bytes); // decode layer barriers and counters (zeroed)
     w.zero_bytes = off;
     w.offsets = take((E + S + 1) * 4);
     w.ids = take(T * k * 4);
@@ -77,6 +81,8 @@ Workspace plan_workspace(const hmoe_layer_desc& d, size_t T) {
     w.tile_count = take(16);
     w.tile_cap = tile_capacity_for(static_cast<long>(R), static_cast<int>(E + S));
     w.tiles = take(static_cast<size_t>(w.tile_cap) * 16);
+    w.dl_data_bytes = decode_layer_data_bytes(d, T);
+    w.dl_data = take(w.dl_data_bytes);
     w.total = off;
     return w;
 }
@@ -216,7 +222,7 @@ using namespace hmoe;
 extern "C" {
 
 hmoe_status hmoe_set_variant(int32_t variant) {
-    if (variant < 0 || variant > 2) return HMOE_INVALID_ARGUMENT;
+    if (variant < 0 || variant > 3) return HMOE_INVALID_ARGUMENT;
     if (variant == 2 && !gemm_available()) return HMOE_UNSUPPORTED;
     g_variant = variant;
     return HMOE_OK;
@@ -295,6 +301,25 @@ hmoe_status forward_layer(const hmoe_layer_desc* desc, const float* x, const flo
     const int E = static_cast<int>(desc->experts), S = static_cast<int>(desc->shared_experts);
     const int slots = static_cast<int>(desc->top_k) + S;
     stage(0, s);
+    // Decode-sized batches: the whole layer in one kernel (the GEMV
+    // variant's arithmetic), unless a variant or a router kernel is forced.
+    // Automatic up to kDecodeLayerAutoTokens, where it is measured faster.
+    const bool dl_forced = g_variant == 3;
+    if (dl_forced || (g_variant == 0 && (g_route_variant == 0 || g_route_variant == 3) &&
+                      tokens <= static_cast<size_t>(kDecodeLayerAutoTokens) && decode_layer_shape_ok(*desc, tokens))) {
+        cudaError_t err = cudaMemsetAsync(ws, 0, w.zero_bytes, s);
+        if (err != cudaSuccess) {
+            set_last_error("hmoe workspace reset", err);
+            return HMOE_CUDA_ERROR;
+        }
+        const hmoe_status r = launch_decode_layer(*desc, x, residual, y, y16, tokens, ws, w, s);
+        if (r == HMOE_OK || dl_forced || r != HMOE_UNSUPPORTED) {
+            for (int i = 1; i < 6; ++i) stage(i, s);
+            if (dl_forced && r == HMOE_UNSUPPORTED)
+                set_last_error_text("hmoe: the decode layer kernel does not take this shape or batch");
+            return r;
+        }
+    }
     hmoe_status r = enqueue_route(*desc, x, tokens, ws, w, true, s);
     if (r != HMOE_OK) return r;
     const ExpertRun run = local_run(*desc, tokens, ws, w);

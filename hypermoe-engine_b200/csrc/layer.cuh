@@ -17,6 +17,7 @@ constexpr int kGroupBlock = 256;
 struct Workspace {
     size_t status, counts, block_counts, route_acc, route_acc_bytes, zero_bytes, offsets, ids, scores, perm_token, perm_weight, inv;
     size_t xperm, xscale, hmid, yrows, tiles, tile_count;
+    size_t dl_ctl, dl_ctl_bytes, dl_data, dl_data_bytes; // decode layer kernel (0 bytes when it does not apply)
     int tile_cap;
     size_t total;
 };
@@ -168,6 +169,15 @@ hmoe_status run_experts(const ExpertRun& r, bool gemv, bool stages, cudaStream_t
 // GEMV or tensor-core GEMM for `rows` permuted rows of an [H, I] expert.
 bool use_gemv(long rows, int H, int I);
 
+// The single-kernel decode layer (decode_layer.cu): whether the shape and
+// batch qualify, its zeroed control bytes and its scratch bytes (0 when the
+// shape does not qualify), and the launch (HMOE_UNSUPPORTED when this device
+// cannot hold it; the caller then runs the multi-kernel layer).
+bool decode_layer_shape_ok(const hmoe_layer_desc& d, size_t T);
+size_t decode_layer_ctl_bytes(const hmoe_layer_desc& d, size_t T);
+size_t decode_layer_data_bytes(const hmoe_layer_desc& d, size_t T);
+hmoe_status launch_decode_layer(const hmoe_layer_desc& d, const float* x, const float* residual, float* y,
+                                __nv_bfloat16* y16, size_t T, char* ws, const Workspace& w, cudaStream_t stream);
 // Records stage event i (0..5) when stage events are registered.  Under
 // stream capture the record becomes an external event node, so the caller
 // can still synchronise on and time the event after each graph launch.

@@ -247,9 +247,13 @@ hmoe_status hmoe_moe_forward_noalloc(const hmoe_layer_desc *desc,
 hmoe_status hmoe_noalloc_read_status(int32_t *status, int32_t *near_ties,
                                      int32_t *sequential_logits, void *stream);
 
-/* Forces the expert-MLP variant for measurement: 0 = automatic (GEMV for
- * experts with few tokens, tensor-core GEMM otherwise), 1 = GEMV only,
- * 2 = tensor-core GEMM only.  Process-wide. */
+/* Forces the expert-MLP variant for measurement: 0 = automatic (the
+ * single-kernel decode layer for batches of at most 8 tokens whose shape it
+ * takes, GEMV for experts with few tokens, tensor-core GEMM otherwise),
+ * 1 = multi-kernel GEMV only, 2 = tensor-core GEMM only, 3 = the decode
+ * layer only (HMOE_UNSUPPORTED for a batch or shape it does not take).  The
+ * decode layer gives the multi-kernel GEMV variant's result bit for bit.
+ * Process-wide. */
 hmoe_status hmoe_set_variant(int32_t variant);
 
 /* Forces the router kernel for measurement: 0 = automatic (the tiled kernel
