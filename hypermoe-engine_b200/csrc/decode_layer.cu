@@ -9,20 +9,27 @@
 // three grid barriers (bounded waits, with a shared abort word):
 //
 //   A  router partial sums over (128 hidden rows x 32 experts) items, FP64,
-//      stored per row chunk; the token scales of the FP16 token rows (as the
-//      permutation computes them)
-//   B  every CTA, redundantly and identically: the row chunks added in
-//      order, the decode router's certification, settling and selection,
+//      added into zeroed sums with atomics (the order varies, but every
+//      logit is a sum of exact products with a bounded chain of roundings,
+//      which the certificate covers); the token scales of the FP16 token
+//      rows (as the permutation computes them)
+//   B  every CTA, redundantly and identically: the decode router's
+//      certification, settling and selection,
 //      and the grouping by (expert, token), all in shared memory (no
 //      barrier, no global round trip); then L2 prefetches of this CTA's
 //      down-projection boxes
-//   C  gate/up: (segment, 128 columns, K rank) items; INT8 boxes stream
-//      through one TMA ring of up to ~190 KB per CTA, and each item stores
-//      its rank's partial sums (no atomics)
-//   D  down: (segment, K rank, group of 256-column blocks) items; the item
-//      first forms its SwiGLU rows from the gate/up rank partials (ranks
-//      added in order), then streams its down boxes through the same ring,
-//      which kept issuing them ahead while C finished; stores rank partials
+//   C  gate/up: (row, projection, K rank) items.  A rank's rows of one
+//      projection are contiguous in the packed layout, so an item streams
+//      whole-row chunks of up to 32 KB with 1D bulk copies through one ring
+//      of ~190 KB per CTA (TMA tensor boxes are row-rate bound on this path:
+//      a 256-byte row per box row reaches about half the per-SM rate of a
+//      32 KB bulk copy), and stores its rank's partial sums (no atomics).  A
+//      row is one (expert, token): an expert with several tokens is streamed
+//      once per token, mostly from L2
+//   D  down: (row, K rank, column part) items; the item first forms its
+//      SwiGLU values from the gate/up rank partials (ranks added in order),
+//      then streams its chunks through the same ring, which kept issuing
+//      them ahead while C finished; stores rank partials
 //   E  combine: per token and column, each routed row's down ranks added
 //      in order, weighted and rounded to BF16, the rows added in ascending
 //      expert id from zero (plus the residual)
@@ -52,9 +59,10 @@ constexpr int kDlMaxTokens = 8;  // tokens per call
 constexpr int kDlMaxRows = 64;   // T x (k + S)
 constexpr int kDlMaxSlots = 16;  // k + S
 constexpr int kDlMaxStages = 8;  // ring stages at most
-constexpr int kDlStage = 32768;  // bytes per ring stage: a gate box and an up box, or one down box.
-                                 // Boxes are 256 bytes wide and 32-128 rows deep: TMA moves
-                                 // narrower or shallower boxes at a fraction of the HBM rate
+constexpr int kDlStage = 32768;  // bytes per ring stage: whole rows of one projection
+constexpr int kDlPartCols = 1024; // columns an item accumulates
+constexpr int kDlCw = kDlThreads / 32 - 1; // consumer warps in phases C, D, E; the last warp issues the copies
+constexpr int kDlCt = 32 * kDlCw;
 constexpr int kDlDynLimit = 232448 - 5120;  // dynamic shared memory (the static arrays take the rest)
 constexpr int kDlPrefetchBytes = 256 * 1024; // down bytes per CTA prefetched into L2
 constexpr uint64_t kDlWaitNs = 2000000000ull;
@@ -74,13 +82,15 @@ struct DlArgs {
     __nv_bfloat16* y16;
     const hmoe_expert_quant* quant;
     int slots, I;
-    int KS, kc, bk2;   // gate/up: K ranks, rows per rank (multiple of 32), rows per box
-    int KSd, kcd, bk3; // down: the same
+    int KS, kc;        // gate/up: K ranks, rows per rank (multiple of 32)
+    int KSd, kcd;      // down: the same
+    const int8_t* arena; // expert blobs: gate [H][I] | up [H][I] | down [I][H] at the offsets
+    uint64_t stride, gate_off, up_off, down_off;
     int nstage;        // ring stages
     DlCtl* ctl;
-    double* rpart;     // [H/128][T][E] router partial sums
-    double* wpart;     // [H/128][E] squared router-column norms
-    double* xpart;     // [H/128][T] squared token norms
+    double* racc;      // [T][E] router sums (zeroed)
+    double* rwn;       // [E] squared router-column norms (zeroed)
+    double* rxn;       // [T] squared token norms (zeroed)
     float* tscale;     // [2][T] s_t, 1/s_t
     float* pgu;        // [KS][R][2I] gate/up rank partials (gate | up)
     float* pdn;        // [KSd][R][H] down rank partials
@@ -91,23 +101,20 @@ struct DlArgs {
 // use yet); C, D and E keep their scratch below `ring`.
 struct DlSmem {
     int a_xs, a_red, a_wred, a_end;
-    int b_racc, b_wn2, b_xn2, b_logit, b_evs, b_wn, b_xn, b_bias, b_fb, b_stage, b_grp, b_end;
-    int c_xs, c_red, d_hs, d_red, e_v;
+    int b_logit, b_evs, b_wn, b_xn, b_bias, b_fb, b_stage, b_grp, b_q, b_end;
+    int c_xs, red, d_hs, e_v;
     int ring, bars, total;
 };
 
 __host__ __device__ inline int dl_al(int v) { return (v + 127) & ~127; }
 
-__host__ __device__ inline DlSmem dl_smem(int T, int maxt, int H, int E, int kc, int kcd, int R, int S) {
+__host__ __device__ inline DlSmem dl_smem(int T, int H, int E, int kc, int kcd, int R, int S) {
     DlSmem m{};
     m.a_xs = 0;
     m.a_red = dl_al(m.a_xs + T * kDecRows * 4);
     m.a_wred = dl_al(m.a_red + 8 * T * 32 * 8);
     m.a_end = dl_al(m.a_wred + 8 * 32 * 8);
-    m.b_racc = 0;
-    m.b_wn2 = dl_al(m.b_racc + T * E * 8);
-    m.b_xn2 = dl_al(m.b_wn2 + E * 8);
-    m.b_logit = dl_al(m.b_xn2 + T * 8);
+    m.b_logit = 0;
     m.b_evs = dl_al(m.b_logit + T * E * 4);
     m.b_wn = dl_al(m.b_evs + 8 * kMaxExperts * 4);
     m.b_xn = dl_al(m.b_wn + E * 8);
@@ -115,23 +122,20 @@ __host__ __device__ inline DlSmem dl_smem(int T, int maxt, int H, int E, int kc,
     m.b_fb = dl_al(m.b_bias + E * 4);
     m.b_stage = dl_al(m.b_fb + (1 + kRouteFallbacks) * 4);
     m.b_grp = dl_al(m.b_stage + kDecSlots * staged_logit_doubles(H) * 8);
-    m.b_end = dl_al(m.b_grp + 3 * R * 4);
-    // C: token rows of this rank, row-group partials; D: SwiGLU rows of the
-    // item, row-group partials; E: the slot values of one 32-column unit
+    m.b_q = dl_al(m.b_grp + 3 * R * 4);
+    m.b_end = dl_al(m.b_q + (E + kDlMaxSlots) * 6 * 4);
+    // C: token rows of this rank; D: the item's SwiGLU values; C and D: the
+    // row classes' partial sums of one item; E: the slot values of one
+    // 32-column unit
     m.c_xs = 0;
-    m.c_red = dl_al(m.c_xs + T * kc * 4);
-    const int c_end = dl_al(m.c_red + maxt * 2 * 256 * 4);
-    m.d_hs = 0;
-    m.d_red = dl_al(m.d_hs + maxt * kcd * 4);
-    const int d_end = dl_al(m.d_red + maxt * 256 * 4);
-    m.e_v = 0;
-    const int e_end = dl_al(m.e_v + kDlMaxSlots * 32 * 4);
-    int r = c_end > d_end ? c_end : d_end;
-    r = r > e_end ? r : e_end;
+    m.d_hs = dl_al(m.c_xs + T * kc * 4);
+    m.red = dl_al(m.d_hs + kcd * 4);
+    m.e_v = dl_al(m.red + kDlPartCols * 4);
+    int r = dl_al(m.e_v + kDlMaxSlots * 32 * 4);
     r = r > m.a_end ? r : m.a_end;
     m.ring = dl_al(r);
     m.bars = dl_al(m.ring + S * kDlStage);
-    m.total = m.bars + S * 8 + 128; // room to align the base
+    m.total = m.bars + 2 * S * 8 + 128; // full and empty barriers; room to align the base
     return m;
 }
 
@@ -167,10 +171,35 @@ __device__ bool dl_grid_sync(const DlArgs& d, int i, int& abort_s) {
     return !abort_s;
 }
 
-// Ring wait (every thread waits; a timeout or the abort word marks the call
-// failed).  The caller combines the threads' results with __syncthreads_or,
-// so every thread takes the same branch.  Threads poll the barrier in shared
-// memory; the abort word and the clock, which live in global memory, are
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kDlCt) : "memory"); }
+
+// dl_grid_sync for the consumer warps only (phases C to E, while the
+// producer warp may still be issuing copies).
+__device__ bool dl_grid_sync_consumers(const DlArgs& d, int i, int& abort_s) {
+    consumers_sync();
+    if (threadIdx.x == 0 && !abort_s) {
+        __threadfence();
+        atomicAdd(&d.ctl->bar[i], 1u);
+        const uint64_t t0 = sm100::global_timer_ns();
+        for (;;) {
+            if (ld_acquire(reinterpret_cast<const int*>(&d.ctl->bar[i])) >= static_cast<int>(gridDim.x)) break;
+            if (ld_acquire(&d.ctl->abort)) break;
+            if (sm100::global_timer_ns() - t0 > kDlWaitNs) {
+                device_fail(d.ra.st, HMOE_TIMEOUT);
+                atomicExch(&d.ctl->abort, 1);
+                break;
+            }
+            __nanosleep(100);
+        }
+        if (ld_acquire(&d.ctl->abort)) abort_s = 1;
+        __threadfence();
+    }
+    consumers_sync();
+    return !abort_s;
+}
+
+// Ring wait: false after a timeout (recorded) or once the abort word is set.
+// Threads poll the barrier in shared memory; the abort word and the clock, which live in global memory, are
 // read only every 64 polls, so a grid of waiting threads does not flood one
 // L2 line.
 __device__ __forceinline__ bool dl_wait(const DlArgs& d, uint64_t* bar, uint32_t parity) {
@@ -189,21 +218,17 @@ __device__ __forceinline__ bool dl_wait(const DlArgs& d, uint64_t* bar, uint32_t
     }
 }
 
-// L2 prefetch of one tensor box (no shared memory, no completion to wait for).
-__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap* map, int x, int y, int z) {
-    asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(map), "r"(x),
-                 "r"(y), "r"(z)
-                 : "memory");
+// L2 prefetch of a contiguous range (no shared memory, no completion to wait for).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 } // namespace
 
 namespace {
 
-template <int C, int MAXT>
-__global__ void __launch_bounds__(kDlThreads, 1)
-    decode_layer_kernel(const __grid_constant__ CUtensorMap tmg, const __grid_constant__ CUtensorMap tmu,
-                        const __grid_constant__ CUtensorMap tmd, DlArgs d) {
+template <int C>
+__global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __grid_constant__ DlArgs d) {
     extern __shared__ __align__(128) unsigned char dsm[];
     __shared__ int abort_s, nseg_s;
     __shared__ int4 seg_s[kDlMaxRows];     // segment: (expert, first row, rows, 0)
@@ -213,6 +238,7 @@ __global__ void __launch_bounds__(kDlThreads, 1)
     __shared__ float rw_s[kDlMaxRows];     // row: routing weight (1 for shared experts)
     __shared__ float rsc_s[kDlMaxRows];    // row: down scale of its expert
     __shared__ int trow_s[kDlMaxRows];     // [T][slots] the token's rows, ascending
+    __shared__ int rseg_s[kDlMaxRows];     // row: its segment
     __shared__ uint32_t ids_s[kDlMaxRows]; // [T][k] selected experts
     __shared__ float scores_s[kDlMaxRows]; // [T][k] their scores
     __shared__ float tsc_s[2 * kDlMaxTokens];
@@ -223,17 +249,17 @@ __global__ void __launch_bounds__(kDlThreads, 1)
     const int G = static_cast<int>(gridDim.x), b = static_cast<int>(blockIdx.x);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int S = d.nstage;
-    const DlSmem L = dl_smem(T, MAXT, H, E, d.kc, d.kcd, R, S);
+    const DlSmem L = dl_smem(T, H, E, d.kc, d.kcd, R, S);
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(dsm) + 127) & ~uintptr_t(127));
     uint8_t* ring = base + L.ring;
     uint64_t* full = reinterpret_cast<uint64_t*>(base + L.bars);
     if (tid == 0) {
         abort_s = 0;
-        for (int s = 0; s < S; ++s) sm100::mbar_init(&full[s], 1);
+        for (int s = 0; s < S; ++s) {
+            sm100::mbar_init(&full[s], 1);          // the producer's expect_tx (or plain) arrival
+            sm100::mbar_init(&full[S + s], kDlCw);  // empty: one arrival per consumer warp
+        }
         sm100::fence_mbarrier_init();
-        sm100::prefetch_tmap(&tmg);
-        sm100::prefetch_tmap(&tmu);
-        sm100::prefetch_tmap(&tmd);
     }
     __syncthreads();
 
@@ -278,12 +304,12 @@ __global__ void __launch_bounds__(kDlThreads, 1)
                 const int t = idx / 32, l = idx % 32;
                 double s = 0.0;
                 for (int w = 0; w < 8; ++w) s += red0[(w * T + t) * 32 + l];
-                if (e0 + l < E) d.rpart[(static_cast<size_t>(rc) * T + t) * E + e0 + l] = s;
+                if (e0 + l < E) atomicAdd(d.racc + static_cast<size_t>(t) * E + e0 + l, s);
             }
             if (tid < 32 && e0 + tid < E) {
                 double s = 0.0;
                 for (int w = 0; w < 8; ++w) s += wred0[w * 32 + tid];
-                d.wpart[static_cast<size_t>(rc) * E + e0 + tid] = s;
+                atomicAdd(d.rwn + e0 + tid, s);
             }
             if (ec == 0 && tid < T) {
                 double s = 0.0;
@@ -291,7 +317,7 @@ __global__ void __launch_bounds__(kDlThreads, 1)
                     const double v = static_cast<double>(xs0[tid * kDecRows + i]);
                     s = fma(v, v, s);
                 }
-                d.xpart[static_cast<size_t>(rc) * T + tid] = s;
+                atomicAdd(d.rxn + tid, s);
             }
         }
         // token scales, exactly as the permutation (rows.cuh permute_token)
@@ -323,45 +349,17 @@ __global__ void __launch_bounds__(kDlThreads, 1)
 
     // ------------------------- B: selection and grouping, in every CTA
     if (ok) {
-        double* racc = reinterpret_cast<double*>(base + L.b_racc); // [T][E]
-        double* wn2 = reinterpret_cast<double*>(base + L.b_wn2);   // [E]
-        double* xn2 = reinterpret_cast<double*>(base + L.b_xn2);   // [T]
-        // the row chunks in order (two logits per thread at a time, eight
-        // chunk loads each in flight)
-        for (int i0 = tid; i0 < T * E; i0 += 2 * kDlThreads) {
-            const int i1 = i0 + kDlThreads;
-            const int t0 = i0 / E, e0 = i0 % E, t1 = i1 / E, e1 = i1 % E;
-            const bool has1 = i1 < T * E;
-            double s0 = 0.0, s1 = 0.0;
-            for (int c0 = 0; c0 < nRC; c0 += 8) {
-                double v0[8], v1[8];
-#pragma unroll
-                for (int u = 0; u < 8; ++u) {
-                    const bool in = c0 + u < nRC;
-                    v0[u] = in ? __ldcg(d.rpart + (static_cast<size_t>(c0 + u) * T + t0) * E + e0) : 0.0;
-                    v1[u] = in && has1 ? __ldcg(d.rpart + (static_cast<size_t>(c0 + u) * T + t1) * E + e1) : 0.0;
-                }
-#pragma unroll
-                for (int u = 0; u < 8; ++u)
-                    if (c0 + u < nRC) {
-                        s0 += v0[u];
-                        s1 += v1[u];
-                    }
-            }
-            racc[i0] = s0;
-            if (has1) racc[i1] = s1;
-        }
-        for (int e = tid; e < E; e += kDlThreads) {
-            double s = 0.0;
-            for (int c = 0; c < nRC; ++c) s += __ldcg(d.wpart + static_cast<size_t>(c) * E + e);
-            wn2[e] = s;
-        }
-        if (tid < T) {
-            double s = 0.0;
-            for (int c = 0; c < nRC; ++c) s += __ldcg(d.xpart + static_cast<size_t>(c) * T + tid);
-            xn2[tid] = s;
-        }
         if (tid < 2 * T) tsc_s[tid] = __ldcg(d.tscale + tid);
+        // every expert's dequantisation constants, while the selection runs
+        float* qall = reinterpret_cast<float*>(base + L.b_q); // [E + S][scale x3, offset x3]
+        for (int e = tid; e < E + slots - k; e += kDlThreads) {
+            const hmoe_expert_quant q = d.quant[e];
+#pragma unroll
+            for (int p = 0; p < 3; ++p) {
+                qall[e * 6 + p] = q.scale[p];
+                qall[e * 6 + 3 + p] = 8388608.0f + 128.0f + static_cast<float>(q.zero_point[p]);
+            }
+        }
         __syncthreads();
         // Certify, settle and select.  Every CTA reaches the same result; only
         // CTA 0 counts near-ties and sequential sums and reports failures.
@@ -374,8 +372,10 @@ __global__ void __launch_bounds__(kDlThreads, 1)
                                reinterpret_cast<float*>(base + L.b_bias), reinterpret_cast<int*>(base + L.b_fb),
                                reinterpret_cast<int*>(base + L.b_fb) + 1,
                                reinterpret_cast<double*>(base + L.b_stage)};
-        decode_finish<C>(
-            ra, [&](int idx) { return racc[idx]; }, [&](int t) { return xn2[t]; }, [&](int e) { return wn2[e]; }, m);
+        decode_certify(
+            ra, [&](int idx) { return __ldcg(d.racc + idx); }, [&](int t) { return __ldcg(d.rxn + t); },
+            [&](int e) { return __ldcg(d.rwn + e); }, m);
+        decode_select_block(ra, m);
         __syncthreads();
         // Rows in (expert, token) order, shared experts E.. after the routed
         // ones, as the grouping kernel orders them.
@@ -413,13 +413,15 @@ __global__ void __launch_bounds__(kDlThreads, 1)
                 while (r + len < R && ex_s[r + len] == ex_s[r]) ++len;
                 const int e = ex_s[r];
                 seg_s[u] = make_int4(e, r, len, 0);
-                const hmoe_expert_quant& q = d.quant[e];
 #pragma unroll
                 for (int p = 0; p < 3; ++p) {
-                    qs_s[u][p] = q.scale[p];
-                    qz_s[u][p] = 8388608.0f + 128.0f + static_cast<float>(q.zero_point[p]);
+                    qs_s[u][p] = qall[e * 6 + p];
+                    qz_s[u][p] = qall[e * 6 + 3 + p];
                 }
-                for (int rr = r; rr < r + len; ++rr) rsc_s[rr] = q.scale[2];
+                for (int rr = r; rr < r + len; ++rr) {
+                    rsc_s[rr] = qall[e * 6 + 2];
+                    rseg_s[rr] = u;
+                }
             }
         }
         if (tid == 0) {
@@ -439,83 +441,189 @@ __global__ void __launch_bounds__(kDlThreads, 1)
     __syncthreads();
 
     // ------------------------------------------- work of phases C and D
-    // Phase C items: (segment, 256-column block, K rank), rank r2 = b mod KS
-    // fixed per CTA, blocks q2, q2 + nq2, ...; phase D items: (segment, K
-    // rank, group of CGW 256-column blocks), b, b + G, ...
-    const int nseg = nseg_s;
-    const int KS = d.KS, kc = d.kc, bk2 = d.bk2, nb2 = kc / bk2, nCB = (I + 255) / 256;
+    // C items: (row, projection, column part) for this CTA's K rank
+    // r2 = b mod KS, pairs q2, q2 + nq2, ...; D items: (row, K rank, column
+    // part), b, b + G, ...  Every item streams the whole rows of its rank's
+    // slab in chunks of rc rows (a multiple of 4, so a row's class mod 4 is
+    // its index mod 4 within any chunk) and accumulates the columns of its
+    // part.  The last warp issues the chunks into the ring (waiting for the
+    // consumers to free each stage); the other warps consume them.
+    const int KS = d.KS, kc = d.kc, KSd = d.KSd, kcd = d.kcd;
+    const int PC = (I + kDlPartCols - 1) / kDlPartCols, WC = ((I + PC - 1) / PC + 15) / 16 * 16;
+    const int PD = (H + kDlPartCols - 1) / kDlPartCols, WD = ((H + PD - 1) / PD + 15) / 16 * 16;
+    const int rc2 = min(kc, kDlStage / I / 4 * 4), nb2 = (kc + rc2 - 1) / rc2;
+    const int rc3 = min(kcd, kDlStage / H / 4 * 4), nb3 = (kcd + rc3 - 1) / rc3;
     const int r2 = b % KS, q2 = b / KS, nq2 = (G - r2 + KS - 1) / KS;
     const int kb2 = r2 * kc; // at or past H for a rank with no rows (its partials stay zero)
-    const int pairs2 = nseg * nCB;
-    const int n2 = q2 < pairs2 ? (pairs2 - q2 + nq2 - 1) / nq2 : 0;
+    const int pairs2 = R * 2 * PC;
+    const int n2 = ok && q2 < pairs2 ? (pairs2 - q2 + nq2 - 1) / nq2 : 0;
     const int tot2 = n2 * nb2;
-    const int KSd = d.KSd, kcd = d.kcd, bk3 = d.bk3, nb3 = kcd / bk3, nCBd = H / 256;
-    const int CGW = nCBd % 4 == 0 ? 4 : (nCBd % 3 == 0 ? 3 : (nCBd % 2 == 0 ? 2 : 1));
-    const int nCG = nCBd / CGW, nbi3 = CGW * nb3;
-    const int items3 = nseg * KSd * nCG;
-    const int n3 = b < items3 ? (items3 - b + G - 1) / G : 0;
-    const int tot = tot2 + n3 * nbi3;
-    // Down box m of this CTA (m < n3 * nbi3): tensor coordinates.
-    auto down_box = [&](int m, int& x, int& y, int& z) {
-        const int i3 = m / nbi3, w = m % nbi3;
+    const int items3 = R * KSd * PD;
+    const int n3 = ok && b < items3 ? (items3 - b + G - 1) / G : 0;
+    const int tot = tot2 + n3 * nb3;
+    // C item i: row, projection (0 gate, 1 up), part
+    auto c_item = [&](int i, int& row, int& pj, int& part) {
+        const int j = q2 + i * nq2;
+        part = j % PC;
+        pj = (j / PC) & 1;
+        row = j / (2 * PC);
+    };
+    // D item i3: row, rank, part
+    auto d_item = [&](int i3, int& row, int& r3, int& part) {
         const int idx3 = b + i3 * G;
-        const int cg = idx3 % nCG, r3 = (idx3 / nCG) % KSd, u = idx3 / (nCG * KSd);
-        x = (cg * CGW + w / nb3) * 256;
-        y = r3 * kcd + (w % nb3) * bk3;
-        z = seg_s[u].x;
+        part = idx3 % PD;
+        r3 = (idx3 / PD) % KSd;
+        row = idx3 / (PD * KSd);
     };
-    // Box n of the ring sequence (phase C's boxes, then phase D's), issued
-    // into stage n mod S.  A box wholly past K is not copied; its barrier
-    // completes with a plain arrival.  Columns past N read as zeros.
-    auto issue = [&](int n) {
-        const int s = n % S;
-        uint8_t* dst = ring + s * kDlStage;
-        if (n < tot2) {
-            const int i = n / nb2, bx = n % nb2;
-            const int j = q2 + i * nq2;
-            const int e = seg_s[j / nCB].x, c0 = (j % nCB) * 256, kk = kb2 + bx * bk2;
-            if (kk < H) {
-                sm100::mbar_arrive_expect_tx(&full[s], 2 * 256 * bk2);
-                sm100::tma_load_3d(dst, &tmg, c0, kk, e, &full[s]);
-                sm100::tma_load_3d(dst + kDlStage / 2, &tmu, c0, kk, e, &full[s]);
-            } else {
-                sm100::mbar_arrive(&full[s]);
+    uint64_t* empty = full + S;
+
+    if (warp == kDlCw) {
+        // ------------------------------------------------------ producer
+        if (lane == 0 && ok) {
+            // L2 prefetches of this CTA's first down slabs: the down
+            // weights cross HBM while gate/up streams
+            const int np = min(n3, kDlPrefetchBytes / max(1, kcd * H));
+            for (int i3 = 0; i3 < np; ++i3) {
+                int row, r3, part;
+                d_item(i3, row, r3, part);
+                const int rows = min(kcd, I - r3 * kcd);
+                if (rows > 0 && part == 0)
+                    bulk_prefetch_l2(d.arena + static_cast<size_t>(seg_s[rseg_s[row]].x) * d.stride + d.down_off +
+                                         static_cast<size_t>(r3) * kcd * H,
+                                     static_cast<uint32_t>(rows * H));
             }
-        } else {
-            int x, y, z;
-            down_box(n - tot2, x, y, z);
-            if (y < I) {
-                sm100::mbar_arrive_expect_tx(&full[s], 256 * bk3);
-                sm100::tma_load_3d(dst, &tmd, x, y, z, &full[s]);
-            } else {
-                sm100::mbar_arrive(&full[s]);
+            int issued = 0;
+            for (int n = 0; n < tot; ++n) {
+                const int s = n % S;
+                // the consumers have freed the stage (chunk n - S)
+                if (n >= S && !dl_wait(d, &empty[s], ((n / S) - 1) & 1)) break;
+                const int8_t* src;
+                int rows, N;
+                if (n < tot2) {
+                    int row, pj, part;
+                    c_item(n / nb2, row, pj, part);
+                    const int ch = n % nb2, r0 = kb2 + ch * rc2;
+                    rows = min(min(rc2, kc - ch * rc2), H - r0);
+                    N = I;
+                    src = d.arena + static_cast<size_t>(seg_s[rseg_s[row]].x) * d.stride +
+                          (pj ? d.up_off : d.gate_off) + static_cast<size_t>(r0) * I;
+                } else {
+                    int row, r3, part;
+                    const int m = n - tot2;
+                    d_item(m / nb3, row, r3, part);
+                    const int ch = m % nb3, r0 = r3 * kcd + ch * rc3;
+                    rows = min(min(rc3, kcd - ch * rc3), I - r0);
+                    N = H;
+                    src = d.arena + static_cast<size_t>(seg_s[rseg_s[row]].x) * d.stride + d.down_off +
+                          static_cast<size_t>(r0) * H;
+                }
+                // a chunk wholly past K is not copied: its barrier completes
+                // with a plain arrival
+                if (rows > 0) {
+                    sm100::mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(rows * N));
+                    sm100::bulk_load(ring + s * kDlStage, src, static_cast<uint32_t>(rows * N), &full[s]);
+                } else {
+                    sm100::mbar_arrive(&full[s]);
+                }
+                issued = n + 1;
             }
+            // every copy lands before the warp exits (the earlier ones were
+            // consumed, which the stage waits above saw)
+            for (int n = max(0, issued - S); n < issued; ++n)
+                sm100::mbar_wait_for(&full[n % S], (n / S) & 1, kDlWaitNs);
         }
-    };
-    int issued = ok ? min(S, tot) : 0; // uniform over the CTA
-    int cons = 0;                      // boxes thread 0 has seen complete
-    if (warp == 0 && ok) {
-        // the ring's first S boxes, then L2 prefetches of the first down
-        // boxes, so the down weights cross HBM while gate/up streams
-        for (int n = lane; n < issued; n += 32) issue(n);
-        const int np = min(n3 * nbi3, kDlPrefetchBytes / (256 * bk3));
-        for (int m = lane; m < np; m += 32) {
-            int x, y, z;
-            down_box(m, x, y, z);
-            if (y < I) tma_prefetch_l2_3d(&tmd, x, y, z);
-        }
+        return; // the producer warp takes no part in the rest
     }
-    bool dead = !ok; // uniform over the CTA
-    // thread (column quad cq of the 256-column block, row class g): rows
-    // g, g + 4, ... of each box, in order, as the GEMV's row groups
-    const int cq = tid & 63, g = tid >> 6;
+
+    // ------------------------------------------------------ consumers
+    __shared__ int cdead_s; // a consumer's wait failed
+    if (tid == 0) cdead_s = !ok;
+    consumers_sync();
+    float* red = reinterpret_cast<float*>(base + L.red); // [part columns] row classes added in order
+    // Accumulates chunk n (rows x N bytes in stage n mod S; columns
+    // [c0, c0 + w) of the part) times v[0..rows) into acc, then frees the
+    // stage.  Unit u = thread + kDlCt * k (k < 2) is (16-column group
+    // u mod JG, row class u / JG): rows g, g + 4, ... of the chunk, in
+    // order, as the GEMV's row groups.  Packed FP32 pairs (FADD2 / FFMA2) do
+    // the dequantisation and the products, each lane rounding as fmaf.
+    auto consume = [&](int n, int N, int nr, int c0, int w, float zoff, const float* v, float2 (&acc)[2][8]) {
+        const int s = n % S;
+        const bool got = dl_wait(d, &full[s], (n / S) & 1);
+        if (got) {
+            const uint8_t* chunk = ring + s * kDlStage + c0;
+            const int JG = w / 16;
+            const float2 noff = make_float2(-zoff, -zoff);
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const int u = tid + kDlCt * k;
+                if (u < 4 * JG) {
+                    const int j = u % JG, g = u / JG;
+#pragma unroll 2
+                    for (int rr = g; rr < nr; rr += 4) {
+                        const float xv = v[rr];
+                        const float2 x2 = make_float2(xv, xv);
+                        const uint4 q4 = *reinterpret_cast<const uint4*>(chunk + rr * N + 16 * j);
+                        const uint32_t qw[4] = {q4.x, q4.y, q4.z, q4.w};
+#pragma unroll
+                        for (int h = 0; h < 4; ++h) {
+                            const uint32_t q = qw[h] ^ 0x80808080u;
+                            float2 lo = make_float2(__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7540)),
+                                                    __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7541)));
+                            float2 hi = make_float2(__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7542)),
+                                                    __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7543)));
+                            lo = __fadd2_rn(lo, noff);
+                            hi = __fadd2_rn(hi, noff);
+                            acc[k][2 * h] = __ffma2_rn(x2, lo, acc[k][2 * h]);
+                            acc[k][2 * h + 1] = __ffma2_rn(x2, hi, acc[k][2 * h + 1]);
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) sm100::mbar_arrive(&empty[s]);
+        } else {
+            cdead_s = 1; // the stage is not freed: the producer stops at the abort word
+        }
+        return got;
+    };
+    // The row classes' sums added in order (class 0 stores, 1..3 add in
+    // turn) into red[0..w).
+    auto fold = [&](const float2 (&acc)[2][8], int w) {
+        const int JG = w / 16;
+        for (int gg = 0; gg < 4; ++gg) {
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+                const int u = tid + kDlCt * k;
+                if (u < 4 * JG && u / JG == gg) {
+                    float2* r = reinterpret_cast<float2*>(red + 16 * (u % JG));
+#pragma unroll
+                    for (int h = 0; h < 8; ++h) {
+                        if (gg == 0) {
+                            r[h] = acc[k][h];
+                        } else {
+                            float2 o = r[h];
+                            o.x += acc[k][h].x;
+                            o.y += acc[k][h].y;
+                            r[h] = o;
+                        }
+                    }
+                }
+            }
+            consumers_sync();
+        }
+    };
+    auto zero = [](float2 (&acc)[2][8]) {
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+#pragma unroll
+            for (int h = 0; h < 8; ++h) acc[k][h] = make_float2(0.0f, 0.0f);
+    };
 
     // ------------------------------------------------------- C: gate/up
     {
-        float* xs2 = reinterpret_cast<float*>(base + L.c_xs);  // [T][kc] token rows of this rank
-        float* red2 = reinterpret_cast<float*>(base + L.c_red); // [MAXT][2][256] row classes added in order
-        if (ok && n2 > 0) {
-            for (int i = tid; i < T * kc; i += kDlThreads) {
+        float* xs2 = reinterpret_cast<float*>(base + L.c_xs); // [T][kc] token rows of this rank
+        if (n2 > 0) {
+            for (int i = tid; i < T * kc; i += kDlCt) {
                 const int t = i / kc, kk = i % kc;
                 float v = 0.0f;
                 if (kb2 + kk < H)
@@ -524,107 +632,41 @@ __global__ void __launch_bounds__(kDlThreads, 1)
                 xs2[i] = v;
             }
         }
-        __syncthreads();
-        for (int i = 0; i < n2 && !dead; ++i) {
-            const int j = q2 + i * nq2, u = j / nCB, cb = j % nCB;
-            const int4 sg = seg_s[u];
-            const int first = sg.y, tu = min(sg.z, MAXT);
-            const float zg = qz_s[u][0], zu = qz_s[u][1];
-            int xoff[MAXT];
-#pragma unroll
-            for (int tt = 0; tt < MAXT; ++tt) xoff[tt] = tt < tu ? rtok_s[first + tt] * kc : 0;
-            float acc[MAXT][2][4];
-#pragma unroll
-            for (int tt = 0; tt < MAXT; ++tt)
-#pragma unroll
-                for (int c = 0; c < 4; ++c) acc[tt][0][c] = acc[tt][1][c] = 0.0f;
-            for (int bx = 0; bx < nb2; ++bx) {
-                const int n = i * nb2 + bx, s = n % S;
-                const bool got = dl_wait(d, &full[s], (n / S) & 1);
-                const int nr = got ? min(bk2, H - (kb2 + bx * bk2)) : 0;
-                const uint8_t* bg = ring + s * kDlStage;
-                const uint8_t* bu = bg + kDlStage / 2;
-#pragma unroll 2
-                for (int rr = g; rr < bk2; rr += 4) {
-                    if (rr < nr) {
-                        float wg[4], wu[4];
-                        dequant4_fast(*reinterpret_cast<const uint32_t*>(bg + rr * 256 + 4 * cq), zg, wg);
-                        dequant4_fast(*reinterpret_cast<const uint32_t*>(bu + rr * 256 + 4 * cq), zu, wu);
-                        const float* xr = xs2 + bx * bk2 + rr;
-#pragma unroll
-                        for (int tt = 0; tt < MAXT; ++tt) {
-                            if (tt < tu) {
-                                const float xv = xr[xoff[tt]];
-#pragma unroll
-                                for (int c = 0; c < 4; ++c) {
-                                    acc[tt][0][c] = fmaf(xv, wg[c], acc[tt][0][c]);
-                                    acc[tt][1][c] = fmaf(xv, wu[c], acc[tt][1][c]);
-                                }
-                            }
-                        }
-                    }
-                }
-                cons += got;
-                dead = __syncthreads_or(!got) != 0; // stage s is free
-                if (dead) break;
-                if (n + S < tot) {
-                    if (tid == 0) issue(n + S);
-                    issued = n + S + 1;
-                }
-            }
-            if (dead) break;
-            // row classes added in order: class 0 stores, 1..3 add in turn
-            for (int gg = 0; gg < 4; ++gg) {
-                if (g == gg) {
-#pragma unroll
-                    for (int tt = 0; tt < MAXT; ++tt)
-                        if (tt < tu)
-#pragma unroll
-                            for (int pj = 0; pj < 2; ++pj) {
-                                float4* r = reinterpret_cast<float4*>(red2 + (tt * 2 + pj) * 256 + 4 * cq);
-                                const float4 v = make_float4(acc[tt][pj][0], acc[tt][pj][1], acc[tt][pj][2],
-                                                             acc[tt][pj][3]);
-                                if (gg == 0) {
-                                    *r = v;
-                                } else {
-                                    float4 o = *r;
-                                    o.x += v.x;
-                                    o.y += v.y;
-                                    o.z += v.z;
-                                    o.w += v.w;
-                                    *r = o;
-                                }
-                            }
-                }
-                __syncthreads();
-            }
-            for (int idx = tid; idx < tu * 512; idx += kDlThreads) {
-                const int tt = idx / 512, pj = (idx / 256) & 1, c = cb * 256 + idx % 256;
-                if (c < I)
-                    d.pgu[(static_cast<size_t>(r2) * R + first + tt) * (2 * I) + pj * I + c] = red2[idx];
-            }
-            __syncthreads();
+        consumers_sync();
+        for (int i = 0; i < n2; ++i) {
+            int row, pj, part;
+            c_item(i, row, pj, part);
+            const int u = rseg_s[row];
+            const int c0 = part * WC, w = min(WC, I - c0);
+            const float zoff = qz_s[u][pj];
+            const float* xrow = xs2 + rtok_s[row] * kc;
+            float2 acc[2][8];
+            zero(acc);
+            for (int ch = 0; ch < nb2; ++ch)
+                consume(i * nb2 + ch, I, min(min(rc2, kc - ch * rc2), H - (kb2 + ch * rc2)), c0, w, zoff,
+                        xrow + ch * rc2, acc);
+            fold(acc, w);
+            if (cdead_s) break; // uniform: read after a consumer barrier
+            for (int c = tid; c < w; c += kDlCt)
+                d.pgu[(static_cast<size_t>(r2) * R + row) * (2 * I) + pj * I + c0 + c] = red[c];
+            consumers_sync();
         }
     }
-    ok = dl_grid_sync(d, 1, abort_s) && !dead;
+    ok = dl_grid_sync_consumers(d, 1, abort_s) && !cdead_s;
 
     // ---------------------------------------------------------- D: down
     {
-        float* hs = reinterpret_cast<float*>(base + L.d_hs);    // [MAXT][kcd] SwiGLU rows of the item
-        float* red3 = reinterpret_cast<float*>(base + L.d_red); // [MAXT][256] row classes added in order
-        for (int i3 = 0; ok && !dead && i3 < n3; ++i3) {
-            const int idx3 = b + i3 * G;
-            const int cg = idx3 % nCG, r3 = (idx3 / nCG) % KSd, u = idx3 / (nCG * KSd);
-            const int4 sg = seg_s[u];
-            const int first = sg.y, tu = min(sg.z, MAXT);
+        float* hs = reinterpret_cast<float*>(base + L.d_hs); // [kcd] SwiGLU values of the item
+        for (int i3 = 0; ok && i3 < n3; ++i3) {
+            int row, r3, part;
+            d_item(i3, row, r3, part);
+            const int u = rseg_s[row];
             const int kb3 = r3 * kcd;
-            // SwiGLU rows [kb3, kb3 + kcd) of the segment: the gate/up ranks
+            // SwiGLU values [kb3, kb3 + kcd) of the row: the gate/up ranks
             // added in order, as the GEMV's gate/up epilogue does
-            for (int x = tid; x < tu * kcd; x += kDlThreads) {
-                const int tt = x / kcd, kk = x % kcd;
+            for (int kk = tid; kk < kcd; kk += kDlCt) {
                 float v = 0.0f;
                 if (kb3 + kk < I) {
-                    const size_t row = static_cast<size_t>(first + tt);
                     float v0[8], v1[8];
 #pragma unroll
                     for (int r = 0; r < 8; ++r) {
@@ -643,76 +685,24 @@ __global__ void __launch_bounds__(kDlThreads, 1)
                     const float uu = qs_s[u][1] * s1;
                     v = silu(gg) * uu;
                 }
-                hs[tt * kcd + kk] = v;
+                hs[kk] = v;
             }
-            __syncthreads();
+            consumers_sync();
+            const int c0 = part * WD, w = min(WD, H - c0);
             const float zoff = qz_s[u][2];
-            for (int cbl = 0; cbl < CGW && !dead; ++cbl) {
-                const int cb = cg * CGW + cbl;
-                float acc[MAXT][4];
-#pragma unroll
-                for (int tt = 0; tt < MAXT; ++tt)
-#pragma unroll
-                    for (int c = 0; c < 4; ++c) acc[tt][c] = 0.0f;
-                for (int bx = 0; bx < nb3; ++bx) {
-                    const int n = tot2 + i3 * nbi3 + cbl * nb3 + bx, s = n % S;
-                    const bool got = dl_wait(d, &full[s], (n / S) & 1);
-                    const int nr = got ? min(bk3, I - (kb3 + bx * bk3)) : 0;
-                    const uint8_t* box = ring + s * kDlStage;
-#pragma unroll 2
-                    for (int rr = g; rr < bk3; rr += 4) {
-                        if (rr < nr) {
-                            float w[4];
-                            dequant4_fast(*reinterpret_cast<const uint32_t*>(box + rr * 256 + 4 * cq), zoff, w);
-                            const float* hr = hs + bx * bk3 + rr;
-#pragma unroll
-                            for (int tt = 0; tt < MAXT; ++tt) {
-                                if (tt < tu) {
-                                    const float xv = hr[tt * kcd];
-#pragma unroll
-                                    for (int c = 0; c < 4; ++c) acc[tt][c] = fmaf(xv, w[c], acc[tt][c]);
-                                }
-                            }
-                        }
-                    }
-                    cons += got;
-                    dead = __syncthreads_or(!got) != 0;
-                    if (dead) break;
-                    if (n + S < tot) {
-                        if (tid == 0) issue(n + S);
-                        issued = n + S + 1;
-                    }
-                }
-                if (dead) break;
-                for (int gg = 0; gg < 4; ++gg) {
-                    if (g == gg) {
-#pragma unroll
-                        for (int tt = 0; tt < MAXT; ++tt)
-                            if (tt < tu) {
-                                float4* r = reinterpret_cast<float4*>(red3 + tt * 256 + 4 * cq);
-                                const float4 v = make_float4(acc[tt][0], acc[tt][1], acc[tt][2], acc[tt][3]);
-                                if (gg == 0) {
-                                    *r = v;
-                                } else {
-                                    float4 o = *r;
-                                    o.x += v.x;
-                                    o.y += v.y;
-                                    o.z += v.z;
-                                    o.w += v.w;
-                                    *r = o;
-                                }
-                            }
-                    }
-                    __syncthreads();
-                }
-                for (int idx = tid; idx < tu * 256; idx += kDlThreads)
-                    d.pdn[(static_cast<size_t>(r3) * R + first + idx / 256) * H + cb * 256 + idx % 256] = red3[idx];
-                __syncthreads();
-            }
-            __syncthreads(); // hs is rewritten by the next item
+            float2 acc[2][8];
+            zero(acc);
+            for (int ch = 0; ch < nb3; ++ch)
+                consume(tot2 + i3 * nb3 + ch, H, min(min(rc3, kcd - ch * rc3), I - (kb3 + ch * rc3)), c0, w, zoff,
+                        hs + ch * rc3, acc);
+            fold(acc, w);
+            if (cdead_s) break;
+            for (int c = tid; c < w; c += kDlCt)
+                d.pdn[(static_cast<size_t>(r3) * R + row) * H + c0 + c] = red[c];
+            consumers_sync(); // red and hs are rewritten by the next item
         }
     }
-    ok = dl_grid_sync(d, 2, abort_s) && !dead;
+    ok = dl_grid_sync_consumers(d, 2, abort_s) && ok && !cdead_s;
 
     // -------------------------------------------------------- E: combine
     if (ok) {
@@ -720,9 +710,10 @@ __global__ void __launch_bounds__(kDlThreads, 1)
         const int units = T * (H / 32);
         for (int un = b; un < units; un += G) {
             const int t = un / (H / 32), c = (un % (H / 32)) * 32 + lane;
-            // warp w: the BF16 output rows of slots w, w + 8 (as the down
-            // projection rounds them), each the down ranks added in order
-            for (int sl = warp; sl < slots; sl += kDlThreads / 32) {
+            // warp w: the BF16 output rows of slots w, w + kDlCw, ... (as
+            // the down projection rounds them), each the down ranks added in
+            // order
+            for (int sl = warp; sl < slots; sl += kDlCw) {
                 const int r = trow_s[t * slots + sl];
                 float v[8];
 #pragma unroll
@@ -734,7 +725,7 @@ __global__ void __launch_bounds__(kDlThreads, 1)
                     if (q < KSd) s0 += v[q];
                 vb[sl * 32 + lane] = __bfloat162float(__float2bfloat16_rn(rw_s[r] * (rsc_s[r] * s0)));
             }
-            __syncthreads();
+            consumers_sync();
             if (warp == 0) { // rows in ascending expert id, from zero
                 float acc = 0.0f;
                 for (int sl = 0; sl < slots; ++sl) acc = __fadd_rn(acc, vb[sl * 32 + lane]);
@@ -743,13 +734,9 @@ __global__ void __launch_bounds__(kDlThreads, 1)
                 d.y[o] = acc;
                 if (d.y16) d.y16[o] = __float2bfloat16_rn(acc);
             }
-            __syncthreads();
+            consumers_sync();
         }
     }
-
-    // Every issued box is waited for (bounded) before the CTA exits.
-    if (tid == 0)
-        for (int n = cons; n < issued; ++n) sm100::mbar_wait_for(&full[n % S], (n / S) & 1, kDlWaitNs);
 }
 
 } // namespace
@@ -771,22 +758,13 @@ int dl_rows_per_rank(int K, int ks) {
     return (kc + 31) / 32 * 32;
 }
 
-// Rows per TMA box for a rank of kc rows (a multiple of 32): kc split into
-// the fewest equal boxes of at most `most` rows (each a multiple of 4, so a
-// row's class mod 4 is the same within the box and within the rank).
-int dl_box_rows(int kc, int most) {
-    int n = (kc + most - 1) / most;
-    while (kc % n || (kc / n) % 4) ++n;
-    return kc / n;
-}
-
 struct DlLayout {
-    size_t rpart, wpart, xpart, tscale, pgu, pdn, total;
+    size_t tscale, pgu, pdn, total;
 };
 
 DlLayout dl_layout(const hmoe_layer_desc& d, size_t T) {
-    const size_t H = d.hidden, I = d.intermediate, E = d.experts, slots = d.top_k + d.shared_experts;
-    const size_t R = T * slots, nRC = H / kDecRows;
+    const size_t H = d.hidden, I = d.intermediate, slots = d.top_k + d.shared_experts;
+    const size_t R = T * slots;
     const size_t KS = dl_split(static_cast<int>(H)), KSd = dl_split(static_cast<int>(I));
     DlLayout l{};
     size_t off = 0;
@@ -795,9 +773,6 @@ DlLayout dl_layout(const hmoe_layer_desc& d, size_t T) {
         off = align_up(off + bytes, 256);
         return at;
     };
-    l.rpart = take(nRC * T * E * 8);
-    l.wpart = take(nRC * E * 8);
-    l.xpart = take(nRC * T * 8);
     l.tscale = take(2 * T * 4);
     l.pgu = take(KS * R * 2 * I * 4);
     l.pdn = take(KSd * R * H * 4);
@@ -805,27 +780,25 @@ DlLayout dl_layout(const hmoe_layer_desc& d, size_t T) {
     return l;
 }
 
-template <int C, int MAXT>
+template <int C>
 const void* dl_kernel() {
-    return reinterpret_cast<const void*>(decode_layer_kernel<C, MAXT>);
+    return reinterpret_cast<const void*>(decode_layer_kernel<C>);
 }
 
-const void* dl_pick(int E, int T) {
+const void* dl_pick(int E) {
     const int c = (E + 31) / 32;
-    const bool one = T == 1;
-    if (c <= 1) return one ? dl_kernel<1, 1>() : dl_kernel<1, 8>();
-    if (c <= 2) return one ? dl_kernel<2, 1>() : dl_kernel<2, 8>();
-    if (c <= 4) return one ? dl_kernel<4, 1>() : dl_kernel<4, 8>();
-    return one ? dl_kernel<8, 1>() : dl_kernel<8, 8>();
+    if (c <= 1) return dl_kernel<1>();
+    if (c <= 2) return dl_kernel<2>();
+    if (c <= 4) return dl_kernel<4>();
+    return dl_kernel<8>();
 }
 
 // Ring stages for a shape, 0 when the phases' scratch leaves too little.
 int dl_stages(int T, int H, int E, int kc, int kcd, int R) {
-    const int maxt = T == 1 ? 1 : kDlMaxTokens;
-    const DlSmem L0 = dl_smem(T, maxt, H, E, kc, kcd, R, 0);
+    const DlSmem L0 = dl_smem(T, H, E, kc, kcd, R, 0);
     int S = std::min(kDlMaxStages, (kDlDynLimit - L0.total) / (kDlStage + 8));
     while (S > 0) {
-        const DlSmem L = dl_smem(T, maxt, H, E, kc, kcd, R, S);
+        const DlSmem L = dl_smem(T, H, E, kc, kcd, R, S);
         if (L.total <= kDlDynLimit && L.b_end <= L.bars) break; // phase B stays clear of the barriers
         --S;
     }
@@ -838,7 +811,7 @@ bool decode_layer_shape_ok(const hmoe_layer_desc& d, size_t T) {
     const size_t slots = d.top_k + d.shared_experts;
     if (!(T >= 1 && T <= static_cast<size_t>(kDlMaxTokens) && slots <= static_cast<size_t>(kDlMaxSlots) &&
           T * slots <= static_cast<size_t>(kDlMaxRows) && d.hidden % 256 == 0 && d.intermediate % 128 == 0 &&
-          d.intermediate >= 256 &&
+          d.intermediate >= 256 && reinterpret_cast<uintptr_t>(d.arena) % 16 == 0 &&
           d.experts <= static_cast<uint32_t>(kMaxExperts) && d.ep_size == 1))
         return false;
     const int H = static_cast<int>(d.hidden), I = static_cast<int>(d.intermediate);
@@ -846,8 +819,11 @@ bool decode_layer_shape_ok(const hmoe_layer_desc& d, size_t T) {
     return dl_stages(static_cast<int>(T), H, static_cast<int>(d.experts), kc, kcd, static_cast<int>(T * slots)) > 0;
 }
 
+// Zeroed per call: the control words, then the router sums [T][E], the
+// column norms [E] and the token norms [T] (FP64).
 size_t decode_layer_ctl_bytes(const hmoe_layer_desc& d, size_t T) {
-    return decode_layer_shape_ok(d, T) ? sizeof(DlCtl) : 0;
+    if (!decode_layer_shape_ok(d, T)) return 0;
+    return sizeof(DlCtl) + align_up(T * d.experts * 8, 256) + align_up(d.experts * 8, 256) + align_up(T * 8, 256);
 }
 
 size_t decode_layer_data_bytes(const hmoe_layer_desc& d, size_t T) {
@@ -874,31 +850,26 @@ hmoe_status launch_decode_layer(const hmoe_layer_desc& desc, const float* x, con
     d.I = I;
     d.KS = dl_split(H);
     d.kc = dl_rows_per_rank(H, d.KS);
-    d.bk2 = dl_box_rows(d.kc, 64);
     d.KSd = dl_split(I);
     d.kcd = dl_rows_per_rank(I, d.KSd);
-    d.bk3 = dl_box_rows(d.kcd, 128);
+    d.arena = desc.arena;
+    d.stride = desc.expert_stride;
+    d.gate_off = desc.gate_offset;
+    d.up_off = desc.up_offset;
+    d.down_off = desc.down_offset;
     d.nstage = dl_stages(T, H, E, d.kc, d.kcd, R);
-    const int maxt = T == 1 ? 1 : kDlMaxTokens;
-    const DlSmem L = dl_smem(T, maxt, H, E, d.kc, d.kcd, R, d.nstage);
+    const DlSmem L = dl_smem(T, H, E, d.kc, d.kcd, R, d.nstage);
     char* base = ws + w.dl_data;
     const DlLayout l = dl_layout(desc, tokens);
     d.ctl = reinterpret_cast<DlCtl*>(ws + w.dl_ctl);
-    d.rpart = reinterpret_cast<double*>(base + l.rpart);
-    d.wpart = reinterpret_cast<double*>(base + l.wpart);
-    d.xpart = reinterpret_cast<double*>(base + l.xpart);
+    char* z = ws + w.dl_ctl + sizeof(DlCtl);
+    d.racc = reinterpret_cast<double*>(z);
+    d.rwn = reinterpret_cast<double*>(z + align_up(tokens * desc.experts * 8, 256));
+    d.rxn = reinterpret_cast<double*>(z + align_up(tokens * desc.experts * 8, 256) + align_up(desc.experts * 8, 256));
     d.tscale = reinterpret_cast<float*>(base + l.tscale);
     d.pgu = reinterpret_cast<float*>(base + l.pgu);
     d.pdn = reinterpret_cast<float*>(base + l.pdn);
-    const int experts = E + S;
-    CUtensorMap mg, mu, md;
-    if (!map_weights_box(&mg, desc.arena + desc.gate_offset, I, H, experts, desc.expert_stride, 256, d.bk2) ||
-        !map_weights_box(&mu, desc.arena + desc.up_offset, I, H, experts, desc.expert_stride, 256, d.bk2) ||
-        !map_weights_box(&md, desc.arena + desc.down_offset, H, I, experts, desc.expert_stride, 256, d.bk3)) {
-        set_last_error_text("hmoe: cuTensorMapEncodeTiled failed (decode layer)");
-        return HMOE_CUDA_ERROR;
-    }
-    const void* fn = dl_pick(E, T);
+    const void* fn = dl_pick(E);
     cudaError_t err = set_smem_limit(fn, L.total);
     if (err != cudaSuccess) {
         set_last_error("hmoe decode layer shared memory", err);
@@ -917,7 +888,7 @@ hmoe_status launch_decode_layer(const hmoe_layer_desc& desc, const float* x, con
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    void* args[] = {&mg, &mu, &md, &d};
+    void* args[] = {&d};
     err = cudaLaunchKernelExC(&cfg, fn, args);
     if (err != cudaSuccess) {
         set_last_error("hmoe decode layer launch", err);

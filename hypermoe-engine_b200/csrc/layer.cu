@@ -33,7 +33,7 @@
 namespace hmoe {
 
 int g_variant = 0;
-constexpr int kDecodeLayerAutoTokens = 1; // single-kernel decode layer chosen automatically up to here
+constexpr int kDecodeLayerAutoTokens = 2; // single-kernel decode layer chosen automatically up to here (faster at T <= 2)
 extern int g_route_variant; // router.cu
 cudaEvent_t g_stage_events[6];
 int g_stage_count = 0;

@@ -393,9 +393,9 @@ struct DecodeTailSmem {
 // does not matter), against the squared norms xn2(t) and wn2(e); settle the
 // queued ones; select every token (one warp per token).  Writes a.ids,
 // a.scores and the counts RouteArgs names.
-template <int C, class Acc, class Xn, class Wn>
-__device__ void decode_finish(const RouteArgs& a, const Acc& acc, const Xn& xn2, const Wn& wn2,
-                              const DecodeTailSmem& m) {
+template <class Acc, class Xn, class Wn>
+__device__ void decode_certify(const RouteArgs& a, const Acc& acc, const Xn& xn2, const Wn& wn2,
+                               const DecodeTailSmem& m) {
     const int T = a.T, H = a.H, E = a.E;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) *m.fb_count = 0;
@@ -435,6 +435,16 @@ __device__ void decode_finish(const RouteArgs& a, const Acc& acc, const Xn& xn2,
         }
     }
     __syncthreads();
+}
+
+// The decode routers' finish: certify (above), then select every token, one
+// warp per token (select_token).
+template <int C, class Acc, class Xn, class Wn>
+__device__ void decode_finish(const RouteArgs& a, const Acc& acc, const Xn& xn2, const Wn& wn2,
+                              const DecodeTailSmem& m) {
+    decode_certify(a, acc, xn2, wn2, m);
+    const int T = a.T, E = a.E;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int t = warp; t < T; t += blockDim.x >> 5) {
         float lv[C];
 #pragma unroll
@@ -445,6 +455,130 @@ __device__ void decode_finish(const RouteArgs& a, const Acc& acc, const Xn& xn2,
         select_token<C>(lv, E, a.k, a.softmax, a.renorm, m.evs + warp * kMaxExperts,
                         a.ids + static_cast<size_t>(t) * a.k, a.scores + static_cast<size_t>(t) * a.k, a.counts,
                         token_block_counts(a, t), a.st, false, nullptr);
+    }
+}
+
+// select_token's result for every token of m.logit ([T][E], exact logits),
+// computed by the whole CTA at once: the exponentials and divisions spread
+// over all threads, and each candidate's rank in the order (probability
+// descending, id ascending) counted directly instead of k + 1 sequential
+// argmax rounds.  The ranks are those rounds' outcome: the order is total
+// (ids differ), a NaN probability is keyed lowest as there, and -0.0 and
+// +0.0 compare equal as there.  The maximum, the denominator (a tree sum
+// exactly when every term is at least 2^-22, else the sequential sum in
+// expert order), the probabilities float(e / den), the renormalising sum in
+// rank order, the near-tie test between adjacent ranks and the non-finite
+// handling are select_token's, operation for operation.  Uses m.evs as
+// [T][E] and m.stage as scratch (after decode_certify); T <= 8, k <= 32.
+__device__ inline void decode_select_block(const RouteArgs& a, const DecodeTailSmem& m) {
+    const int T = a.T, E = a.E, k = a.k;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nth = blockDim.x, nw = nth >> 5;
+    const int nk = k < E ? k + 1 : k; // ranks the selection looks at
+    constexpr int kRk = 33;           // per-token stride of the rank tables
+    const float* lg = m.logit;
+    float* pv = m.evs;                // [T][E] exponentials, then probabilities
+    double* den_s = m.stage;          // [T]
+    float* mx_s = reinterpret_cast<float*>(den_s + T);
+    int* ok_s = reinterpret_cast<int*>(mx_s + T);
+    int* sel_e = ok_s + T;            // [T][kRk] expert of each rank
+    float* sel_p = reinterpret_cast<float*>(sel_e + T * kRk);
+    float* sel_l = sel_p + T * kRk;   // its logit
+    for (int t = warp; t < T; t += nw) {
+        float mm = -FLT_MAX * 2.0f;
+        for (int j = lane; j < E; j += 32) mm = fmaxf(mm, lg[t * E + j]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mm = fmaxf(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+        if (lane == 0) {
+            mx_s[t] = mm;
+            ok_s[t] = 1;
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < T * E; i += nth) {
+        const float x = lg[i];
+        pv[i] = a.softmax ? static_cast<float>(exp(static_cast<double>(x - mx_s[i / E]))) : x;
+    }
+    __syncthreads();
+    if (a.softmax) {
+        for (int t = warp; t < T; t += nw) {
+            double den = 0.0;
+            bool small = false;
+            for (int j = lane; j < E; j += 32) {
+                const float e = pv[t * E + j];
+                den += static_cast<double>(e);
+                small |= e < 0x1.0p-22f;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+            if (__any_sync(0xffffffffu, small)) {
+                den = 0.0;
+                if (lane == 0)
+                    for (int j = 0; j < E; ++j) den += static_cast<double>(pv[t * E + j]);
+                den = __shfl_sync(0xffffffffu, den, 0);
+            }
+            if (lane == 0) {
+                den_s[t] = den;
+                if (!(isfinite(den) && den > 0.0)) ok_s[t] = 0;
+            }
+        }
+        __syncthreads();
+        for (int i = tid; i < T * E; i += nth)
+            pv[i] = static_cast<float>(static_cast<double>(pv[i]) / den_s[i / E]);
+        __syncthreads();
+    }
+    for (int i = tid; i < T * E; i += nth) {
+        const float p = pv[i];
+        if (p != p) { // ranks lowest; the token is flagged
+            pv[i] = -FLT_MAX * 2.0f;
+            ok_s[i / E] = 0;
+        }
+    }
+    __syncthreads();
+    for (int i = tid; i < T * E; i += nth) {
+        const int t = i / E, e = i % E;
+        const float p = pv[i];
+        const float* row = pv + t * E;
+        int r = 0;
+        for (int j = 0; j < E; ++j) {
+            const float q = row[j];
+            r += (q > p) || (q == p && j < e);
+        }
+        if (r < nk) {
+            sel_e[t * kRk + r] = e;
+            sel_p[t * kRk + r] = p;
+            sel_l[t * kRk + r] = lg[i];
+        }
+    }
+    __syncthreads();
+    for (int t = warp; t < T; t += nw) {
+        bool ok = ok_s[t] != 0;
+        bool tie = false;
+        if (a.softmax && lane >= 1 && lane < nk && sel_l[t * kRk + lane] != sel_l[t * kRk + lane - 1]) {
+            const int dd = abs(__float_as_int(sel_p[t * kRk + lane - 1]) - __float_as_int(sel_p[t * kRk + lane]));
+            tie = dd <= 2;
+        }
+        tie = __any_sync(0xffffffffu, tie);
+        double rsum = 0.0; // rank order
+        if (lane == 0)
+            for (int r = 0; r < k; ++r) rsum += static_cast<double>(sel_p[t * kRk + r]);
+        rsum = __shfl_sync(0xffffffffu, rsum, 0);
+        if (a.renorm && !(isfinite(rsum) && rsum != 0.0)) ok = false;
+        if (lane < k) {
+            const float mine = sel_p[t * kRk + lane];
+            const int id = sel_e[t * kRk + lane];
+            float sc = mine;
+            if (a.renorm && ok) sc = static_cast<float>(static_cast<double>(mine) / rsum);
+            if (!ok && lane == 0) sc = __int_as_float(0x7fc00000);
+            a.ids[static_cast<size_t>(t) * k + lane] = static_cast<uint32_t>(id);
+            a.scores[static_cast<size_t>(t) * k + lane] = sc;
+            if (a.counts) atomicAdd(a.counts + id, 1);
+            int32_t* bc = token_block_counts(a, t);
+            if (bc) atomicAdd(bc + id, 1);
+        }
+        if (lane == 0) {
+            if (!ok) device_fail(a.st, HMOE_NON_FINITE_ROUTER);
+            if (tie && a.st) atomicAdd(&a.st->near_ties, 1);
+        }
     }
 }
 

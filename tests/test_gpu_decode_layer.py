@@ -135,3 +135,39 @@ def test_forced_decode_layer_rejects_larger_batches(cuda):
     finally:
         H.set_variant(0)
     assert rc == 7  # HMOE_UNSUPPORTED
+
+
+@pytest.mark.parametrize("cfg_name,T", [("c3", 1), ("c3", 6), ("c1", 8)])
+def test_decode_layer_exact_ties_break_by_expert_id(cuda, cfg_name, T):
+    """Router columns duplicated (and, for C3, the bias made equal) give
+    experts with identical logits for every token; both selections order
+    them by ascending id (CpuRouterBackend.cpp:57-62), so the CTA-wide ranking
+    of the decode layer and the warp rounds of the routers agree bit for
+    bit, and exact ties are not counted as near-ties."""
+    import dataclasses
+    cfg = H.CONFIGS[cfg_name]
+    base = host_layer(cfg_name, 21)
+    w = base.router_w.copy()
+    w[:, 1] = w[:, 0]
+    w[:, 3] = w[:, 0]
+    w[:, 6] = w[:, 2]
+    bias = None
+    if base.router_bias is not None:
+        bias = base.router_bias.copy()
+        bias[1] = bias[3] = bias[0]
+        bias[6] = bias[2]
+        # make the tied experts win often
+        bias[0] = bias[2] = float(bias.max()) + 1.0
+        bias[1] = bias[3] = bias[0]
+        bias[6] = bias[2]
+    hl = dataclasses.replace(base, router_w=w, router_bias=bias)
+    x_np = H.make_tokens(cfg, T, seed=31)
+    dl = H.DeviceLayer(hl, cuda)
+    x = t(x_np, cuda)
+    ref = forward_with(dl, x, GEMV)
+    assert dl.read_status()[:2] == (0, 0)
+    y = forward_with(dl, x, DECODE)
+    assert dl.read_status()[:2] == (0, 0)
+    np.testing.assert_array_equal(y, ref)
+    out_p, *_ = O.moe_layer_port(hl, x_np)
+    assert_layer_close(y, out_p)
