@@ -344,26 +344,27 @@ def decode_split(layer, cfg, T, seed, dev, flush, events, peaks, steps=20):
             H.set_variant(0)
         return statistics.median(tot), {k: statistics.median(v) for k, v in st.items()}
 
-    # The automatic choice (the single-kernel decode layer up to 8 tokens),
-    # then, for its stage split, the multi-kernel GEMV path on the same batch.
+    # The automatic choice (what a caller gets), the single-kernel decode
+    # layer forced (it takes up to 8 tokens) and the multi-kernel GEMV path
+    # with its stage split.
     ms, med = replay(0)
-    single = T <= 8
-    multi_ms, multi = replay(1) if single else (ms, med)
+    single_ms, _ = replay(3) if T <= 8 else (None, None)
+    multi_ms, multi = replay(1)
     alg = algorithmic(cfg, T, U)
     roof_ms = 1e3 * max(alg["layer"]["bytes"] / (peaks["hbm_gbs"] * 1e9),
                         alg["layer"]["flops"] / (peaks["bf16_tflops"] * 1e12))
     expert_bytes = alg["gate_up"]["bytes"] + alg["down"]["bytes"]
-    # single kernel: expert bytes over the whole layer's time (a lower bound
-    # of the expert stream's rate); otherwise over the expert stages' time
-    expert_ms = ms if single else med["gate_up"] + med["down"]
+    # expert bytes over the expert stages of the multi-kernel path, and over
+    # the whole single-kernel layer (a lower bound of its expert stream rate)
+    multi_expert_ms = multi["gate_up"] + multi["down"]
     return {"tokens": T, "ms_per_step": ms, "value": T / (ms * 1e-3), "unit": UNIT,
-            "path": "single-kernel decode layer" if single else "multi-kernel layer",
-            "stages_ms": None if single else med,
-            "multi_kernel": {"ms_per_step": multi_ms, "stages_ms": multi} if single else None,
+            "single_kernel_ms": single_ms, "multi_kernel_ms": multi_ms, "multi_kernel_stages_ms": multi,
             "unique_experts": U, "layer_roofline_ms": roof_ms,
             "layer_roofline_frac": roof_ms / ms,
-            "expert_hbm_gbs": expert_bytes / (expert_ms * 1e-3) / 1e9,
-            "expert_hbm_frac": expert_bytes / (expert_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+            "expert_hbm_gbs": expert_bytes / (multi_expert_ms * 1e-3) / 1e9,
+            "expert_hbm_frac": expert_bytes / (multi_expert_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+            "single_kernel_layer_hbm_frac": (alg["layer"]["bytes"] / (single_ms * 1e-3) / 1e9 / peaks["hbm_gbs"]
+                                             if single_ms else None),
             "timing": "cuda-graph replay, median of %d steps, 256 MiB L2 flush before each" % steps}
 
 
@@ -618,9 +619,9 @@ def main():
     top = max(STAGES, key=lambda s: avg[s])
     a = alg[top]
     dt_s = avg[top] * 1e-3
-    if world == 1 and T <= 8:
-        # one kernel runs the whole layer (decode_layer_kernel): its bytes
-        # are the layer's, its time the step's
+    if world == 1 and launches == args.steps:
+        # one launch per step: the single-kernel decode layer runs the whole
+        # layer, so its bytes are the layer's and its time the step's
         top, a, dt_s = "decode_layer", alg["layer"], ms * 1e-3
     ridge = peaks["bf16_tflops"] * 1e12 / (peaks["hbm_gbs"] * 1e9)
     tensor = a["flops"] > 0 and a["flops"] / max(a["bytes"], 1) > ridge

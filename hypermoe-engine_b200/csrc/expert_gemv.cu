@@ -126,13 +126,14 @@ __global__ void __launch_bounds__(kVThreads, 2)
             xs[t * kc + kk] = v;
         }
         __syncthreads();
-        float acc[TOK][NP][4];
+        // column pairs in packed FP32 (FADD2 / FFMA2): each lane rounds as
+        // the scalar subtraction and fmaf would
+        float2 acc[TOK][NP][2];
 #pragma unroll
         for (int t = 0; t < TOK; ++t)
 #pragma unroll
-            for (int p = 0; p < NP; ++p)
-#pragma unroll
-                for (int c = 0; c < 4; ++c) acc[t][p][c] = 0.0f;
+            for (int p = 0; p < NP; ++p) acc[t][p][0] = acc[t][p][1] = make_float2(0.0f, 0.0f);
+        const float2 noff0 = make_float2(-zoff0, -zoff0), noff1 = make_float2(-zoff1, -zoff1);
         for (int b = 0; b < nbox; ++b) {
             const int s = (it + b) % kVStages;
             // Boxes that were issued are always waited for (bounded), so no
@@ -146,20 +147,29 @@ __global__ void __launch_bounds__(kVThreads, 2)
 #pragma unroll 2
             for (int rr = kr; rr < kVRows; rr += kVGroups) {
                 if (rr < nr) {
-                    float w[NP][4];
+                    float2 w[NP][2];
 #pragma unroll
                     for (int p = 0; p < NP; ++p) {
-                        const uint32_t q = *reinterpret_cast<const uint32_t*>(box + (p * kVRows + rr) * kVCols + 4 * cq);
-                        dequant4_fast(q, p ? zoff1 : zoff0, w[p]);
+                        const uint32_t q =
+                            *reinterpret_cast<const uint32_t*>(box + (p * kVRows + rr) * kVCols + 4 * cq) ^ 0x80808080u;
+                        // float(2^23 + (q + 128)) - (2^23 + 128 + zp) = q - zp, exact
+                        const float2 lo = make_float2(__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7540)),
+                                                      __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7541)));
+                        const float2 hi = make_float2(__uint_as_float(__byte_perm(q, 0x4B000000u, 0x7542)),
+                                                      __uint_as_float(__byte_perm(q, 0x4B000000u, 0x7543)));
+                        w[p][0] = __fadd2_rn(lo, p ? noff1 : noff0);
+                        w[p][1] = __fadd2_rn(hi, p ? noff1 : noff0);
                     }
                     const float* xr = xs + b * kVRows + rr;
 #pragma unroll
                     for (int t = 0; t < TOK; ++t) {
                         const float xv = xr[t * kc];
+                        const float2 x2 = make_float2(xv, xv);
 #pragma unroll
-                        for (int p = 0; p < NP; ++p)
-#pragma unroll
-                            for (int c = 0; c < 4; ++c) acc[t][p][c] = fmaf(xv, w[p][c], acc[t][p][c]);
+                        for (int p = 0; p < NP; ++p) {
+                            acc[t][p][0] = __ffma2_rn(x2, w[p][0], acc[t][p][0]);
+                            acc[t][p][1] = __ffma2_rn(x2, w[p][1], acc[t][p][1]);
+                        }
                     }
                 }
             }
@@ -177,7 +187,7 @@ __global__ void __launch_bounds__(kVThreads, 2)
 #pragma unroll
             for (int p = 0; p < NP; ++p)
                 *reinterpret_cast<float4*>(red + ((kr * TOK + t) * NP + p) * kVCols + 4 * cq) =
-                    make_float4(acc[t][p][0], acc[t][p][1], acc[t][p][2], acc[t][p][3]);
+                    make_float4(acc[t][p][0].x, acc[t][p][0].y, acc[t][p][1].x, acc[t][p][1].y);
         __syncthreads();
         for (int i = tid; i < TOK * NP * kVCols; i += kVThreads) {
             float v = red[i];
