@@ -64,7 +64,7 @@ constexpr int kDlPartCols = 1024; // columns an item accumulates
 constexpr int kDlCw = kDlThreads / 32 - 1; // consumer warps in phases C, D, E; the last warp issues the copies
 constexpr int kDlCt = 32 * kDlCw;
 constexpr int kDlDynLimit = 232448 - 5120;  // dynamic shared memory (the static arrays take the rest)
-constexpr int kDlPrefetchBytes = 256 * 1024; // down bytes per CTA prefetched into L2
+constexpr int kDlPrefetchBytes = 768 * 1024; // weight bytes per CTA prefetched into L2 (148 x 768 KB < L2)
 constexpr uint64_t kDlWaitNs = 2000000000ull;
 
 // Zeroed control words of one call.
@@ -218,6 +218,45 @@ __device__ __forceinline__ bool dl_wait(const DlArgs& d, uint64_t* bar, uint32_t
     }
 }
 
+// The k experts a token's router sums rank highest (logit descending, id
+// ascending), by one warp, without certification or softmax: the exact
+// selection orders by the same key (the softmax is monotone) and differs
+// only where the certificate settles a logit across a float boundary.  Used
+// only to prefetch weights; NaN sums rank lowest.
+template <int C>
+__device__ void guess_topk(const double* sums, const float* bias, int E, int k, uint32_t* out) {
+    const int lane = threadIdx.x & 31;
+    uint32_t key[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        const int j = lane + 32 * c;
+        float v = -FLT_MAX * 2.0f;
+        if (j < E) {
+            v = static_cast<float>(__ldcg(sums + j) + (bias ? static_cast<double>(bias[j]) : 0.0));
+            if (v != v) v = -FLT_MAX * 2.0f;
+        }
+        uint32_t u = __float_as_uint(v + 0.0f);
+        key[c] = j < E ? ((u & 0x80000000u) ? ~u : (u | 0x80000000u)) : 0u;
+    }
+    unsigned taken = 0;
+    for (int r = 0; r < k; ++r) {
+        uint32_t bk = 0, bi = 0xffffffffu;
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+            const uint32_t j = lane + 32 * c;
+            if (j < static_cast<uint32_t>(E) && !((taken >> c) & 1u) && (key[c] > bk || (key[c] == bk && j < bi))) {
+                bk = key[c];
+                bi = j;
+            }
+        }
+        const uint32_t kmax = __reduce_max_sync(0xffffffffu, bk);
+        const uint32_t imin = __reduce_min_sync(0xffffffffu, bk == kmax ? bi : 0xffffffffu);
+        if (imin == 0xffffffffu) break;
+        if (static_cast<int>(imin & 31u) == lane) taken |= 1u << (imin >> 5);
+        if (lane == 0) out[r] = imin;
+    }
+}
+
 // L2 prefetch of a contiguous range (no shared memory, no completion to wait for).
 __device__ __forceinline__ void bulk_prefetch_l2(const void* p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
@@ -347,6 +386,90 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
     }
     bool ok = dl_grid_sync(d, 0, abort_s);
 
+    // ------------------------------------------- work of phases C and D
+    // C items: (row, projection, column part) for this CTA's K rank
+    // r2 = b mod KS, pairs q2, q2 + nq2, ...; D items: (row, K rank, column
+    // part), b, b + G, ...  Every item streams the whole rows of its rank's
+    // slab in chunks of rc rows (a multiple of 4, so a row's class mod 4 is
+    // its index mod 4 within any chunk) and accumulates the columns of its
+    // part.  The last warp issues the chunks into the ring (waiting for the
+    // consumers to free each stage); the other warps consume them.
+    const int KS = d.KS, kc = d.kc, KSd = d.KSd, kcd = d.kcd;
+    const int PC = (I + kDlPartCols - 1) / kDlPartCols, WC = ((I + PC - 1) / PC + 15) / 16 * 16;
+    const int PD = (H + kDlPartCols - 1) / kDlPartCols, WD = ((H + PD - 1) / PD + 15) / 16 * 16;
+    const int rc2 = min(kc, kDlStage / I / 4 * 4), nb2 = (kc + rc2 - 1) / rc2;
+    const int rc3 = min(kcd, kDlStage / H / 4 * 4), nb3 = (kcd + rc3 - 1) / rc3;
+    const int r2 = b % KS, q2 = b / KS, nq2 = (G - r2 + KS - 1) / KS;
+    const int kb2 = r2 * kc; // at or past H for a rank with no rows (its partials stay zero)
+    const int pairs2 = R * 2 * PC;
+    const int n2 = ok && q2 < pairs2 ? (pairs2 - q2 + nq2 - 1) / nq2 : 0;
+    const int tot2 = n2 * nb2;
+    const int items3 = R * KSd * PD;
+    const int n3 = ok && b < items3 ? (items3 - b + G - 1) / G : 0;
+    const int tot = tot2 + n3 * nb3;
+    // C item i: row, projection (0 gate, 1 up), part
+    auto c_item = [&](int i, int& row, int& pj, int& part) {
+        const int j = q2 + i * nq2;
+        part = j % PC;
+        pj = (j / PC) & 1;
+        row = j / (2 * PC);
+    };
+    // D item i3: row, rank, part
+    auto d_item = [&](int i3, int& row, int& r3, int& part) {
+        const int idx3 = b + i3 * G;
+        part = idx3 % PD;
+        r3 = (idx3 / PD) % KSd;
+        row = idx3 / (PD * KSd);
+    };
+
+    // ------------- speculative L2 prefetch of this CTA's weight slabs
+    // The experts the router sums already rank highest are, but for a
+    // logit the certificate moves across a float boundary, the ones the
+    // exact selection below picks.  Grouping them the same way gives the
+    // rows, hence this CTA's items; their slabs start crossing HBM into L2
+    // now and the exact selection's 10-20 us overlap that transfer.
+    __shared__ int gex_s[kDlMaxRows]; // row -> guessed expert
+    if (ok) {
+        uint32_t* gid = ids_s; // overwritten by the exact selection below
+        for (int t = warp; t < T; t += kDlThreads / 32)
+            guess_topk<C>(d.racc + static_cast<size_t>(t) * E, a.bias, E, k, gid + t * k);
+        __syncthreads();
+        for (int i = tid; i < R; i += kDlThreads) {
+            const int t = i / slots, j = i % slots;
+            const int e = j < k ? static_cast<int>(gid[t * k + j]) : E + (j - k);
+            rtok_s[i] = e * T + t; // sort key, scratch until the exact grouping
+        }
+        __syncthreads();
+        for (int i = tid; i < R; i += kDlThreads) {
+            const int ki = rtok_s[i];
+            int rnk = 0;
+            for (int i2 = 0; i2 < R; ++i2) rnk += rtok_s[i2] < ki;
+            gex_s[rnk] = ki / T;
+        }
+        __syncthreads();
+        if (warp == 0) {
+            int budget = kDlPrefetchBytes;
+            for (int i = lane; i < n2; i += 32) { // gate/up slabs of this CTA's rank
+                int row, pj, part;
+                c_item(i, row, pj, part);
+                const int rows = min(kc, H - kb2);
+                if (part == 0 && rows > 0 && (budget -= rows * I * 32) >= 0)
+                    bulk_prefetch_l2(d.arena + static_cast<size_t>(gex_s[row]) * d.stride +
+                                         (pj ? d.up_off : d.gate_off) + static_cast<size_t>(kb2) * I,
+                                     static_cast<uint32_t>(rows * I));
+            }
+            for (int i3 = lane; i3 < n3; i3 += 32) { // down slabs of this CTA's items
+                int row, r3, part;
+                d_item(i3, row, r3, part);
+                const int rows = min(kcd, I - r3 * kcd);
+                if (part == 0 && rows > 0 && (budget -= rows * H * 32) >= 0)
+                    bulk_prefetch_l2(d.arena + static_cast<size_t>(gex_s[row]) * d.stride + d.down_off +
+                                         static_cast<size_t>(r3) * kcd * H,
+                                     static_cast<uint32_t>(rows * H));
+            }
+        }
+    }
+
     // ------------------------- B: selection and grouping, in every CTA
     if (ok) {
         if (tid < 2 * T) tsc_s[tid] = __ldcg(d.tscale + tid);
@@ -440,58 +563,11 @@ __global__ void __launch_bounds__(kDlThreads, 1) decode_layer_kernel(const __gri
     sm100::fence_proxy_async_smem(); // phase B's writes precede the ring's TMA copies
     __syncthreads();
 
-    // ------------------------------------------- work of phases C and D
-    // C items: (row, projection, column part) for this CTA's K rank
-    // r2 = b mod KS, pairs q2, q2 + nq2, ...; D items: (row, K rank, column
-    // part), b, b + G, ...  Every item streams the whole rows of its rank's
-    // slab in chunks of rc rows (a multiple of 4, so a row's class mod 4 is
-    // its index mod 4 within any chunk) and accumulates the columns of its
-    // part.  The last warp issues the chunks into the ring (waiting for the
-    // consumers to free each stage); the other warps consume them.
-    const int KS = d.KS, kc = d.kc, KSd = d.KSd, kcd = d.kcd;
-    const int PC = (I + kDlPartCols - 1) / kDlPartCols, WC = ((I + PC - 1) / PC + 15) / 16 * 16;
-    const int PD = (H + kDlPartCols - 1) / kDlPartCols, WD = ((H + PD - 1) / PD + 15) / 16 * 16;
-    const int rc2 = min(kc, kDlStage / I / 4 * 4), nb2 = (kc + rc2 - 1) / rc2;
-    const int rc3 = min(kcd, kDlStage / H / 4 * 4), nb3 = (kcd + rc3 - 1) / rc3;
-    const int r2 = b % KS, q2 = b / KS, nq2 = (G - r2 + KS - 1) / KS;
-    const int kb2 = r2 * kc; // at or past H for a rank with no rows (its partials stay zero)
-    const int pairs2 = R * 2 * PC;
-    const int n2 = ok && q2 < pairs2 ? (pairs2 - q2 + nq2 - 1) / nq2 : 0;
-    const int tot2 = n2 * nb2;
-    const int items3 = R * KSd * PD;
-    const int n3 = ok && b < items3 ? (items3 - b + G - 1) / G : 0;
-    const int tot = tot2 + n3 * nb3;
-    // C item i: row, projection (0 gate, 1 up), part
-    auto c_item = [&](int i, int& row, int& pj, int& part) {
-        const int j = q2 + i * nq2;
-        part = j % PC;
-        pj = (j / PC) & 1;
-        row = j / (2 * PC);
-    };
-    // D item i3: row, rank, part
-    auto d_item = [&](int i3, int& row, int& r3, int& part) {
-        const int idx3 = b + i3 * G;
-        part = idx3 % PD;
-        r3 = (idx3 / PD) % KSd;
-        row = idx3 / (PD * KSd);
-    };
     uint64_t* empty = full + S;
 
     if (warp == kDlCw) {
         // ------------------------------------------------------ producer
         if (lane == 0 && ok) {
-            // L2 prefetches of this CTA's first down slabs: the down
-            // weights cross HBM while gate/up streams
-            const int np = min(n3, kDlPrefetchBytes / max(1, kcd * H));
-            for (int i3 = 0; i3 < np; ++i3) {
-                int row, r3, part;
-                d_item(i3, row, r3, part);
-                const int rows = min(kcd, I - r3 * kcd);
-                if (rows > 0 && part == 0)
-                    bulk_prefetch_l2(d.arena + static_cast<size_t>(seg_s[rseg_s[row]].x) * d.stride + d.down_off +
-                                         static_cast<size_t>(r3) * kcd * H,
-                                     static_cast<uint32_t>(rows * H));
-            }
             int issued = 0;
             for (int n = 0; n < tot; ++n) {
                 const int s = n % S;
