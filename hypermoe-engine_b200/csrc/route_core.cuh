@@ -260,9 +260,22 @@ __device__ inline void stage_products(const RouteArgs& a, int tok, int e, double
     const int lane = threadIdx.x & 31;
     const int H = a.H, E = a.E, seg = H / 32;
     const float* xr = a.x + static_cast<size_t>(tok) * H;
-#pragma unroll 8
-    for (int i = lane; i < H; i += 32)
-        buf[i + i / seg] = static_cast<double>(xr[i]) * static_cast<double>(a.w[static_cast<size_t>(i) * E + e]);
+    // 16 rows per lane in flight at a time: the router column is strided
+    // (one 4-byte load per row), so the latency, not the bytes, sets the time
+    for (int i0 = lane; i0 < H; i0 += 32 * 16) {
+        float xv[16], wv[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int i = i0 + 32 * j;
+            xv[j] = i < H ? __ldg(xr + i) : 0.0f;
+            wv[j] = i < H ? __ldg(a.w + static_cast<size_t>(i) * E + e) : 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+            const int i = i0 + 32 * j;
+            if (i < H) buf[i + i / seg] = static_cast<double>(xv[j]) * static_cast<double>(wv[j]);
+        }
+    }
     __syncwarp();
 }
 

@@ -77,3 +77,35 @@ def test_noalloc_rejects_oversized_batch(cuda):
                                           torch.cuda.current_stream().cuda_stream)
     assert rc == 6  # HMOE_WORKSPACE_TOO_SMALL
     assert b"16 MiB" in H.lib().hmoe_last_error()
+
+
+def test_two_devices_in_one_process():
+    """Per-device state (shared-memory limits of every kernel, the static
+    no-allocation scratch, the SM count) is kept per device: one process
+    runs the tensor-core GEMM path, the single-kernel decode layer and the
+    no-allocation entry point on device 0, then on device 1, with the same
+    results bit for bit."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    cfg = H.CONFIGS["c3"]
+    hl = H.make_host_layer(cfg, seed=13)
+    results = []
+    for ordinal in (0, 1):
+        dev = torch.device("cuda", ordinal)
+        with torch.cuda.device(dev):
+            dl = H.DeviceLayer(hl, dev)
+            res = []
+            for T in (300, 1, 4):  # GEMM, decode layer, GEMV
+                x = torch.from_numpy(H.make_tokens(cfg, T, seed=13 + T)).to(dev)
+                res.append(dl.forward(x).cpu().numpy())
+                y = torch.full((T, cfg.hidden), float("nan"), device=dev)
+                H.check("hmoe_moe_forward_noalloc", H.lib().hmoe_moe_forward_noalloc(
+                    ctypes.byref(dl.desc), x.data_ptr(), y.data_ptr(), T, torch.cuda.current_stream(dev).cuda_stream))
+                torch.cuda.synchronize(dev)
+                assert np.array_equal(y.cpu().numpy(), res[-1])
+                assert noalloc_status()[0] == 0
+                assert dl.read_status()[0] == 0
+            results.append(res)
+    for a, b in zip(results[0], results[1]):
+        assert np.array_equal(a, b)
