@@ -96,7 +96,7 @@ def test_two_devices_in_one_process():
         with torch.cuda.device(dev):
             dl = H.DeviceLayer(hl, dev)
             res = []
-            for T in (300, 1, 4):  # GEMM, decode layer, GEMV
+            for T in (150, 1, 4):  # GEMM, decode layer, GEMV (all within the 16 MiB scratch)
                 x = torch.from_numpy(H.make_tokens(cfg, T, seed=13 + T)).to(dev)
                 res.append(dl.forward(x).cpu().numpy())
                 y = torch.full((T, cfg.hidden), float("nan"), device=dev)
