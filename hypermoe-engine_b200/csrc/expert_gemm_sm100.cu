@@ -535,57 +535,82 @@ __global__ void __launch_bounds__(kThreadsGemm, 1)
 // largest first (ties by segment order), all tiles of a segment together,
 // so the persistent CTAs start with the longest work items.  One CTA, one
 // thread per segment.
-__global__ void __launch_bounds__(kMaxSegments) tile_list_kernel(SegSpec sp, int4* tiles, int32_t* tile_count,
-                                                                 int capacity) {
-    using Scan = cub::BlockScan<int, kMaxSegments>;
+// The tile list by one CTA of NT threads (kMaxSegments / NT segments per
+// thread, blocked): each segment of r rows is cut into ceil(r / kTileRows)
+// near-equal tiles (expert, first row, rows, segment group), and the tiles
+// are ordered longest first (ties by segment index).
+template <int NT>
+__device__ void build_tile_list(const SegSpec& sp, int4* tiles, int32_t* tile_count, int capacity) {
+    constexpr int IPT = kMaxSegments / NT;
+    using Scan = cub::BlockScan<int, NT>;
     __shared__ typename Scan::TempStorage scan_s;
     __shared__ int2 kn_s[kMaxSegments]; // (longest tile, tiles) of each segment
-    const int i = threadIdx.x;
-    const bool valid = i < sp.nseg;
-    int r0 = 0, cnt = 0;
-    if (valid) {
-        if (sp.offsets) {
-            r0 = sp.offsets[i];
-            cnt = sp.offsets[i + 1] - r0;
-        } else {
-            cnt = sp.counts[(i / sp.eps) * sp.count_stride + i % sp.eps];
+    __shared__ int total_s;
+    const int tid = threadIdx.x;
+    int r0[IPT], cnt[IPT];
+#pragma unroll
+    for (int q = 0; q < IPT; ++q) {
+        const int i = tid * IPT + q;
+        r0[q] = 0;
+        cnt[q] = 0;
+        if (i < sp.nseg) {
+            if (sp.offsets) {
+                r0[q] = sp.offsets[i];
+                cnt[q] = sp.offsets[i + 1] - r0[q];
+            } else {
+                cnt[q] = sp.counts[(i / sp.eps) * sp.count_stride + i % sp.eps];
+            }
         }
     }
     if (!sp.offsets) {
         Scan(scan_s).ExclusiveSum(cnt, r0);
-        r0 += sp.row_base;
+#pragma unroll
+        for (int q = 0; q < IPT; ++q) r0[q] += sp.row_base;
         __syncthreads();
     }
-    const int ntile = cnt > 0 ? (cnt + kTileRows - 1) / kTileRows : 0;
-    const int base = ntile > 0 ? cnt / ntile : 0, extra = ntile > 0 ? cnt % ntile : 0;
-    const int key = ntile > 0 ? base + (extra > 0) : 0; // longest tile of the segment
-    kn_s[i] = make_int2(key, ntile);
-    int total = 0;
-    Scan(scan_s).ExclusiveSum(ntile, total); // only the last thread's sum is used below
-    __shared__ int total_s;
-    if (i == kMaxSegments - 1) total_s = total + ntile;
+    int ntile[IPT], base[IPT], extra[IPT], key[IPT];
+#pragma unroll
+    for (int q = 0; q < IPT; ++q) {
+        ntile[q] = cnt[q] > 0 ? (cnt[q] + kTileRows - 1) / kTileRows : 0;
+        base[q] = ntile[q] > 0 ? cnt[q] / ntile[q] : 0;
+        extra[q] = ntile[q] > 0 ? cnt[q] % ntile[q] : 0;
+        key[q] = ntile[q] > 0 ? base[q] + (extra[q] > 0) : 0; // longest tile of the segment
+        kn_s[tid * IPT + q] = make_int2(key[q], ntile[q]);
+    }
+    int excl[IPT], total = 0;
+    Scan(scan_s).ExclusiveSum(ntile, excl, total);
+    if (tid == 0) total_s = total;
     __syncthreads();
-    if (i == 0) *tile_count = min(capacity, total_s);
-    if (!valid || ntile == 0) return;
-    const int group = i / sp.eps;
-    // tiles of segments ordered before this one: longer tiles, or equal
-    // tiles and a lower segment index (independent partial sums so that the
-    // shared-memory loads pipeline)
-    int pos4[4] = {0, 0, 0, 0};
+    if (tid == 0) *tile_count = min(capacity, total_s);
     const int nseg = sp.nseg;
+#pragma unroll
+    for (int q = 0; q < IPT; ++q) {
+        const int i = tid * IPT + q;
+        if (i >= nseg || ntile[q] == 0) continue;
+        const int group = i / sp.eps;
+        // tiles of segments ordered before this one: longer tiles, or equal
+        // tiles and a lower segment index (independent partial sums so that
+        // the shared-memory loads pipeline)
+        int pos4[4] = {0, 0, 0, 0};
 #pragma unroll 4
-    for (int j = 0; j < nseg; ++j) {
-        const int2 kj = kn_s[j];
-        pos4[j & 3] += (kj.x > key || (kj.x == key && j < i)) ? kj.y : 0;
+        for (int j = 0; j < nseg; ++j) {
+            const int2 kj = kn_s[j];
+            pos4[j & 3] += (kj.x > key[q] || (kj.x == key[q] && j < i)) ? kj.y : 0;
+        }
+        const int pos = pos4[0] + pos4[1] + pos4[2] + pos4[3];
+        const int e = sp.expert_base + i % sp.eps;
+        int row = r0[q];
+        for (int f = 0; f < ntile[q]; ++f) {
+            const int rows = base[q] + (f < extra[q]);
+            if (pos + f < capacity) tiles[pos + f] = make_int4(e, row, rows, group);
+            row += rows;
+        }
     }
-    const int pos = pos4[0] + pos4[1] + pos4[2] + pos4[3];
-    const int e = sp.expert_base + i % sp.eps;
-    int row = r0;
-    for (int f = 0; f < ntile; ++f) {
-        const int rows = base + (f < extra);
-        if (pos + f < capacity) tiles[pos + f] = make_int4(e, row, rows, group);
-        row += rows;
-    }
+}
+
+__global__ void __launch_bounds__(kMaxSegments) tile_list_kernel(SegSpec sp, int4* tiles, int32_t* tile_count,
+                                                                 int capacity) {
+    build_tile_list<kMaxSegments>(sp, tiles, tile_count, capacity);
 }
 
 // Token-major permutation (permute_token) into this GPU's rows.
@@ -598,10 +623,18 @@ struct LocalRows {
     }
 };
 
+// One CTA per token; with a segment spec, CTA 0 (scheduled first, so it
+// overlaps the permutation) builds the tile list, which needs only the
+// group offsets, saving its own launch.
 __global__ void __launch_bounds__(256) permute_kernel(const float* __restrict__ x, const int32_t* __restrict__ inv,
-                                                      int slots, int H, __half* __restrict__ xrows,
-                                                      float* __restrict__ xscale) {
-    permute_token(x, inv, slots, H, blockIdx.x, LocalRows{xrows, xscale, H});
+                                                      int first_token_block, int slots, int H,
+                                                      __half* __restrict__ xrows, float* __restrict__ xscale,
+                                                      SegSpec seg, int4* tiles, int32_t* tile_count, int capacity) {
+    if (static_cast<int>(blockIdx.x) < first_token_block) {
+        build_tile_list<256>(seg, tiles, tile_count, capacity);
+        return;
+    }
+    permute_token(x, inv, slots, H, blockIdx.x - first_token_block, LocalRows{xrows, xscale, H});
 }
 
 // ---------------------------------------------------------------- host
@@ -734,9 +767,15 @@ hmoe_status launch_tile_list(const SegSpec& spec, int4* tiles, int32_t* tile_cou
 }
 
 hmoe_status launch_permute(const float* x, const int32_t* inv, int tokens, int slots, int H, __half* xrows,
-                           float* xscale, cudaStream_t s) {
+                           float* xscale, cudaStream_t s, const SegSpec* seg, int4* tiles, int32_t* tile_count,
+                           int capacity) {
     if (tokens <= 0) return HMOE_OK;
-    permute_kernel<<<static_cast<unsigned>(tokens), 256, 0, s>>>(x, inv, slots, H, xrows, xscale);
+    const bool with_tiles = seg != nullptr;
+    if (with_tiles && (seg->nseg <= 0 || seg->nseg > kMaxSegments || seg->eps <= 0 || capacity <= 0))
+        return HMOE_INVALID_ARGUMENT;
+    const int first = with_tiles ? 1 : 0;
+    permute_kernel<<<static_cast<unsigned>(tokens + first), 256, 0, s>>>(
+        x, inv, first, slots, H, xrows, xscale, with_tiles ? *seg : SegSpec{}, tiles, tile_count, capacity);
     return check_launch("hmoe permute");
 }
 

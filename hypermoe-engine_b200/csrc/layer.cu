@@ -12,8 +12,8 @@
 //   memset(status, counts)                          (one cudaMemsetAsync)
 //   route_kernel     logits, softmax, top-k, renorm, expert histogram
 //   group_kernel     offsets, permutation, inverse map
-//   permute_kernel   each token row once -> FP16 copies (power-of-two scaled)
-//   tile_list_kernel (expert, first row, rows) tiles, longest first
+//   permute_kernel   each token row once -> FP16 copies (power-of-two scaled);
+//                    one more CTA builds the (expert, first row, rows) tiles
 //   gate/up          tcgen05 GEMM (or the weight-streaming GEMV for
 //                    decode-sized batches), SwiGLU in the epilogue
 //   down             same variant, routing weight in the epilogue, BF16 rows
@@ -320,11 +320,15 @@ hmoe_status forward_layer(const hmoe_layer_desc* desc, const float* x, const flo
             return r;
         }
     }
-    hmoe_status r = enqueue_route(*desc, x, tokens, ws, w, true, s);
+    hmoe_status r = enqueue_route(*desc, x, tokens, ws, w, false, s);
     if (r != HMOE_OK) return r;
     const ExpertRun run = local_run(*desc, tokens, ws, w);
+    // the permutation's launch also builds the tile list (one more CTA)
     const SegSpec seg{reinterpret_cast<int32_t*>(ws + w.offsets), nullptr, 0, E + S, E + S, 0, 0};
-    r = launch_tile_list(seg, const_cast<int4*>(run.tiles), const_cast<int32_t*>(run.tile_count), run.tile_cap, s);
+    r = launch_permute(x, reinterpret_cast<int32_t*>(ws + w.inv), static_cast<int>(tokens), slots,
+                       static_cast<int>(desc->hidden), reinterpret_cast<__half*>(ws + w.xperm),
+                       reinterpret_cast<float*>(ws + w.xscale), s, &seg, const_cast<int4*>(run.tiles),
+                       const_cast<int32_t*>(run.tile_count), run.tile_cap);
     if (r != HMOE_OK) return r;
     stage(2, s);
     r = run_experts(run, use_gemv(static_cast<long>(tokens) * slots, run.H, run.I), true, s);

@@ -131,8 +131,11 @@ hmoe_status launch_tile_list(const SegSpec& spec, int4* tiles, int32_t* tile_cou
                              cudaStream_t stream);
 // xrows[inv[t, s]] = FP16(x[t] * s_t), xscale[inv[t, s]] = 1 / s_t for
 // every token t and slot s (s_t: power of two, max |x[t]| s_t in [2^14, 2^15)).
+// With `seg`, the same launch also builds the tile list of `seg` (as
+// launch_tile_list does).
 hmoe_status launch_permute(const float* x, const int32_t* inv, int tokens, int slots, int H, __half* xrows,
-                           float* xscale, cudaStream_t stream);
+                           float* xscale, cudaStream_t stream, const SegSpec* seg = nullptr, int4* tiles = nullptr,
+                           int32_t* tile_count = nullptr, int capacity = 0);
 
 // Upper bound of the tiles of `rows` rows spread over `segments` segments.
 int tile_capacity_for(long rows, int segments);
