@@ -10,6 +10,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <climits>
+
 namespace hmoe {
 
 // Destination of one permuted row: its FP16 elements, its 1/scale and (for
@@ -76,23 +78,31 @@ __device__ __forceinline__ void combine_token(const int32_t* __restrict__ inv, c
                                               const Src& src, const float* residual = nullptr,
                                               __nv_bfloat16* __restrict__ out16 = nullptr) {
     __shared__ const __nv_bfloat16* rows_s[kMaxSlots];
-    if (threadIdx.x == 0) {
-        int keys[kMaxSlots];
-        int rr[kMaxSlots];
-        int n = 0;
-        for (int s = 0; s < slots; ++s) {
-            const int r = inv[static_cast<size_t>(t) * slots + s];
-            const int key = ids ? (s < k ? static_cast<int>(ids[static_cast<size_t>(t) * k + s]) : E + (s - k)) : r;
-            int j = n++;
-            while (j > 0 && keys[j - 1] > key) {
-                keys[j] = keys[j - 1];
-                rr[j] = rr[j - 1];
-                --j;
+    __shared__ int keys_s[kMaxSlots];
+    if (threadIdx.x < 32) { // warp 0: every slot's key at once, then its rank among the keys
+        const int lane = threadIdx.x;
+        int key[3], row[3];
+#pragma unroll
+        for (int q = 0; q < 3; ++q) {
+            const int s = lane + 32 * q;
+            key[q] = INT_MAX;
+            row[q] = 0;
+            if (s < slots) {
+                row[q] = inv[static_cast<size_t>(t) * slots + s];
+                key[q] = ids ? (s < k ? static_cast<int>(ids[static_cast<size_t>(t) * k + s]) : E + (s - k)) : row[q];
+                keys_s[s] = key[q];
             }
-            keys[j] = key;
-            rr[j] = r;
         }
-        for (int s = 0; s < slots; ++s) rows_s[s] = src(rr[s]);
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < 3; ++q) {
+            const int s = lane + 32 * q;
+            if (s < slots) {
+                int rank = 0; // keys are distinct: a token's rows, or its experts
+                for (int j = 0; j < slots; ++j) rank += keys_s[j] < key[q];
+                rows_s[rank] = src(row[q]);
+            }
+        }
     }
     __syncthreads();
     const int H8 = H / 8;
