@@ -58,7 +58,8 @@ def parse():
     p.add_argument("--config", default="c3")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--impl", default="hmoe", choices=["hmoe", "reference"])
-    p.add_argument("--variant", type=int, default=0, help="0 auto, 1 GEMV only, 2 GEMM only")
+    p.add_argument("--variant", type=int, default=0,
+                   help="0 auto, 1 GEMV only, 2 GEMM only, 3 single-kernel decode layer (T <= 8)")
     p.add_argument("--route-variant", type=int, default=0, help="0 auto, 1 cluster router, 2 tiled router")
     p.add_argument("--ep-path", default="peer", choices=["peer", "nccl"],
                    help="expert parallelism: peer-memory stores (registered workspace) or NCCL send/recv")
@@ -73,6 +74,8 @@ def parse():
                    help="skip the host-buffer (e2e) measurements (e.g. for a kernel launch list)")
     p.add_argument("--no-decode", action="store_true",
                    help="skip the decode-size stage splits added to a prefill line")
+    p.add_argument("--decode-tokens", default="1,8,16",
+                   help="comma-separated decode batch sizes for the stage splits of a prefill line")
     p.add_argument("--eager", action="store_true",
                    help="time eager hmoe_moe_forward calls instead of CUDA-graph replays")
     return p.parse_args()
@@ -345,11 +348,12 @@ def decode_split(layer, cfg, T, seed, dev, flush, events, peaks, steps=20):
         return statistics.median(tot), {k: statistics.median(v) for k, v in st.items()}
 
     # The automatic choice (what a caller gets), the single-kernel decode
-    # layer forced (it takes up to 8 tokens) and the multi-kernel GEMV path
-    # with its stage split.
+    # layer forced (it takes up to 8 tokens), the multi-kernel GEMV path
+    # with its stage split and the multi-kernel tensor-core GEMM path.
     ms, med = replay(0)
     single_ms, _ = replay(3) if T <= 8 else (None, None)
     multi_ms, multi = replay(1)
+    gemm_ms, gemm = replay(2)
     alg = algorithmic(cfg, T, U)
     roof_ms = 1e3 * max(alg["layer"]["bytes"] / (peaks["hbm_gbs"] * 1e9),
                         alg["layer"]["flops"] / (peaks["bf16_tflops"] * 1e12))
@@ -359,6 +363,7 @@ def decode_split(layer, cfg, T, seed, dev, flush, events, peaks, steps=20):
     multi_expert_ms = multi["gate_up"] + multi["down"]
     return {"tokens": T, "ms_per_step": ms, "value": T / (ms * 1e-3), "unit": UNIT,
             "single_kernel_ms": single_ms, "multi_kernel_ms": multi_ms, "multi_kernel_stages_ms": multi,
+            "gemm_ms": gemm_ms, "gemm_stages_ms": gemm,
             "unique_experts": U, "layer_roofline_ms": roof_ms,
             "layer_roofline_frac": roof_ms / ms,
             "expert_hbm_gbs": expert_bytes / (multi_expert_ms * 1e-3) / 1e9,
@@ -654,7 +659,8 @@ def main():
 
     decode = None
     if world == 1 and T > 16 and not args.no_decode:
-        decode = [decode_split(layer, cfg, t, args.seed, dev, flush, ev, peaks) for t in (1, 8, 16)]
+        decode = [decode_split(layer, cfg, t, args.seed, dev, flush, ev, peaks)
+                  for t in (int(v) for v in args.decode_tokens.split(","))]
 
     ref_cuda = None
     ref_cuda_decode = None

@@ -66,11 +66,7 @@ namespace {
 
 constexpr int kTileT = 256;   // tokens per work item (pair MMA N <= 256)
 static_assert(kTileT == kTileRows, "GEMM work items are whole tiles");
-constexpr int kHalfT = 128;   // token rows per CTA (B box height)
 constexpr int kBK = 128;      // K per stage: 8 MMAs (K = 16 each) per barrier round trip
-constexpr int kWStages = 3;   // INT8 staging ring
-constexpr int kAStages = 2;   // A ring (dequantised weights)
-constexpr int kBStages = 3;   // B ring (token rows): one more stage hides the L2 latency of a 32 KB tile
 constexpr int kDequantWarps = 8;
 constexpr int kEpiWarps = 8;                // two groups of 4 (one per column half)
 constexpr int kThreadsGemm = 32 * (3 + kDequantWarps + kEpiWarps);
@@ -79,8 +75,6 @@ constexpr uint32_t kTmemCols = 512;         // 2 accumulator buffers x 256 colum
 
 constexpr int kAAtom = 128 * kBK;           // one 64-row MN atom: 128 B x kBK k rows (16 KB)
 constexpr int kABytes = 2 * kAAtom;         // 32 KB: 128 A rows (two 64-row atoms)
-constexpr int kBBox = kHalfT * 64 * 2;      // 16 KB: one TMA box, 128 token rows x 64 k
-constexpr int kBBytes = 2 * kBBox;          // 32 KB: 128 token rows x 128 k
 constexpr int kSBytes = 64 * kBK;           // 8 KB: one [128 k][64 n] INT8 box
 // Epilogue scratch per column-half group, 8 KB: the gate/up exchange (2 x 64
 // x 16 FP32), whose outputs are stored straight from registers (a warp's 32
@@ -89,13 +83,30 @@ constexpr int kSBytes = 64 * kBK;           // 8 KB: one [128 k][64 n] INT8 box
 constexpr int kXchBytes = 2 * 64 * 16 * 4;  // 8 KB
 constexpr int kXBytes = 2 * kXchBytes;
 
-constexpr int kSOff = 0;
-constexpr int kAOff = kSOff + kWStages * 2 * kSBytes;
-constexpr int kBOff = kAOff + kAStages * kABytes;
-constexpr int kXOff = kBOff + kBStages * kBBytes;
-constexpr int kBarOff = kXOff + kXBytes;
-constexpr int kSmem = kBarOff + 512 + 1024 /*alignment slack*/;
-static_assert(kSmem <= 232448, "shared memory budget");
+// Shared-memory plan of a kernel whose CTAs hold HT token rows (the token
+// box height).  HT = 128 takes tiles of up to 256 rows.  HT = 32 takes tiles
+// of up to 64 rows (decode-sized batches): its token stages are a quarter of
+// the size, and the room they free deepens all three rings.  A narrow
+// tile's MMAs take little time, so each ring's round trip (an INT8 stage:
+// HBM latency; a token stage: L2 latency; an A stage: dequantise, arrive,
+// MMA, commit) over its depth sets the pace.
+template <int HT>
+struct GemmCfg {
+    static constexpr int kWStages = HT == 128 ? 3 : 4;   // INT8 staging ring
+    static constexpr int kAStages = HT == 128 ? 2 : 3;   // A ring (dequantised weights)
+    static constexpr int kBStages = HT == 128 ? 3 : 6;   // B ring (token rows): one more stage hides the L2 latency
+    static constexpr int kBBox = HT * 64 * 2;            // one TMA box: HT token rows x 64 k
+    static constexpr int kBBytes = 2 * kBBox;            // HT token rows x 128 k
+    static constexpr int kSOff = 0;
+    static constexpr int kAOff = kSOff + kWStages * 2 * kSBytes;
+    static constexpr int kBOff = kAOff + kAStages * kABytes;
+    static constexpr int kXOff = kBOff + kBStages * kBBytes;
+    static constexpr int kBarOff = kXOff + kXBytes;
+    static constexpr int kSmem = kBarOff + 512 + 1024 /*alignment slack*/;
+    static_assert(HT == 128 || HT == 32, "token box heights");
+    static_assert(kSmem <= 232448, "shared memory budget");
+};
+constexpr int kNarrowRows = 64; // largest tile of the HT = 32 kernel (two CTAs x 32 rows)
 
 struct GemmArgs {
     const int4* tiles;          // (expert, first row, rows, 0), longest first
@@ -184,10 +195,14 @@ __device__ __forceinline__ void epi_barrier(int group) {
 
 __device__ __forceinline__ float silu_fast(float g) { return __fdividef(g, 1.0f + __expf(-g)); }
 
-template <bool GATE_UP>
+template <bool GATE_UP, int HT>
 __global__ void __launch_bounds__(kThreadsGemm, 1)
     expert_gemm_kernel(const __grid_constant__ CUtensorMap tm_w0, const __grid_constant__ CUtensorMap tm_w1,
                        const __grid_constant__ CUtensorMap tm_b, GemmArgs a) {
+    using G = GemmCfg<HT>;
+    constexpr int kWStages = G::kWStages, kAStages = G::kAStages, kBStages = G::kBStages;
+    constexpr int kBBox = G::kBBox, kBBytes = G::kBBytes;
+    constexpr int kSOff = G::kSOff, kAOff = G::kAOff, kBOff = G::kBOff, kXOff = G::kXOff, kBarOff = G::kBarOff;
     const int n_items = *a.tile_count * a.nblocks;
     const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
     if (pair >= n_items) return; // both CTAs of the pair, before any barrier/TMEM use
@@ -637,6 +652,69 @@ __global__ void __launch_bounds__(256) permute_kernel(const float* __restrict__ 
     permute_token(x, inv, slots, H, blockIdx.x - first_token_block, LocalRows{xrows, xscale, H});
 }
 
+// The grouping of a batch of at most kGroupBlock tokens, the permutation and
+// the tile list in one launch.  Every CTA scans the group sizes into the
+// group offsets (routed experts in id order, then the shared experts).
+// CTA 0 stores the offsets and builds the tile list from them.  CTA 1 + t
+// places token t's rows where group_kernel's stable counting sort puts them
+// -- the group offset plus the number of earlier tokens routed to that
+// expert (CpuRouterBackend.cpp:78-90 appends tokens in order) -- writes the
+// permutation and the inverse map, and permutes the token.
+__global__ void __launch_bounds__(256) group_permute_kernel(const float* __restrict__ x, int H,
+                                                            __half* __restrict__ xrows, float* __restrict__ xscale,
+                                                            SmallGroup g, SegSpec seg, int4* tiles,
+                                                            int32_t* tile_count, int capacity) {
+    using Scan = cub::BlockScan<int, 256>;
+    __shared__ typename Scan::TempStorage scan_s;
+    __shared__ int off_s[2 * 256 + 1];
+    __shared__ int e_s[kMaxSlots], cnt_s[kMaxSlots];
+    const int tid = threadIdx.x, nb = g.E + g.S, k = g.k;
+    int v[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+        const int b = 2 * tid + q;
+        v[q] = b < nb ? (b < g.E ? g.counts[b] : g.T) : 0;
+    }
+    int total = 0;
+    Scan(scan_s).ExclusiveSum(v, v, total);
+#pragma unroll
+    for (int q = 0; q < 2; ++q)
+        if (2 * tid + q < nb) off_s[2 * tid + q] = v[q];
+    if (tid == 0) off_s[nb] = total;
+    __syncthreads();
+    if (blockIdx.x == 0) {
+        for (int b = tid; b <= nb; b += blockDim.x) g.offsets[b] = off_s[b];
+        __syncthreads(); // the tile list reads the offsets back
+        build_tile_list<256>(seg, tiles, tile_count, capacity);
+        return;
+    }
+    const int t = static_cast<int>(blockIdx.x) - 1, slots = k + g.S;
+    if (tid < k) {
+        e_s[tid] = static_cast<int>(g.ids[static_cast<size_t>(t) * k + tid]);
+        cnt_s[tid] = 0;
+    }
+    __syncthreads();
+    // earlier tokens routed to each of this token's experts (a token's k
+    // experts are distinct, so each earlier token counts once per expert)
+    for (int tp = tid; tp < t; tp += blockDim.x) {
+        const uint32_t* r = g.ids + static_cast<size_t>(tp) * k;
+        for (int jj = 0; jj < k; ++jj) {
+            const int ep = static_cast<int>(r[jj]);
+            for (int j = 0; j < k; ++j)
+                if (ep == e_s[j]) atomicAdd(&cnt_s[j], 1);
+        }
+    }
+    __syncthreads();
+    if (tid < slots) {
+        const int row = tid < k ? off_s[e_s[tid]] + cnt_s[tid] : off_s[g.E + (tid - k)] + t;
+        g.perm_token[row] = static_cast<uint32_t>(t);
+        g.perm_weight[row] = tid < k ? g.scores[static_cast<size_t>(t) * k + tid] : 1.0f;
+        g.inv[static_cast<size_t>(t) * slots + tid] = row;
+    }
+    __syncthreads(); // permute_token reads the inverse map back
+    permute_token(x, g.inv, slots, H, t, LocalRows{xrows, xscale, H});
+}
+
 // ---------------------------------------------------------------- host
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -659,11 +737,11 @@ bool map_weights(CUtensorMap* m, const int8_t* base, int N, int K, int experts, 
     return map_weights_box(m, base, N, K, experts, stride, 64, kBK);
 }
 
-// 16-bit rows [rows, K] (K contiguous), 128-byte swizzle, box 64 x 128 rows.
-bool map_rows(CUtensorMap* m, const void* base, int K, int rows, bool f16) {
+// 16-bit rows [rows, K] (K contiguous), 128-byte swizzle, box 64 x box_rows.
+bool map_rows(CUtensorMap* m, const void* base, int K, int rows, bool f16, int box_rows) {
     const cuuint64_t dims[2] = {static_cast<cuuint64_t>(K), static_cast<cuuint64_t>(rows)};
     const cuuint64_t strides[1] = {static_cast<cuuint64_t>(K) * 2};
-    const cuuint32_t box[2] = {64, kHalfT}; // 128 bytes: the swizzle span
+    const cuuint32_t box[2] = {64, static_cast<cuuint32_t>(box_rows)}; // 128 bytes: the swizzle span
     const cuuint32_t es[2] = {1, 1};
     return encode_fn()(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
                        const_cast<void*>(base), dims, strides, box, es,
@@ -673,10 +751,11 @@ bool map_rows(CUtensorMap* m, const void* base, int K, int rows, bool f16) {
 
 int sm_count() { return current_sm_count(); }
 
-template <bool GATE_UP>
+template <bool GATE_UP, int HT>
 hmoe_status launch_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUtensorMap& b, const GemmArgs& args,
                         int item_capacity, cudaStream_t s) {
-    const cudaError_t aerr = set_smem_limit(reinterpret_cast<const void*>(expert_gemm_kernel<GATE_UP>), kSmem);
+    constexpr int kSmem = GemmCfg<HT>::kSmem;
+    const cudaError_t aerr = set_smem_limit(reinterpret_cast<const void*>(expert_gemm_kernel<GATE_UP, HT>), kSmem);
     if (aerr != cudaSuccess) {
         set_last_error("hmoe expert GEMM shared-memory limit", aerr);
         return HMOE_CUDA_ERROR;
@@ -694,7 +773,7 @@ hmoe_status launch_gemm(const CUtensorMap& w0, const CUtensorMap& w1, const CUte
     attrs[0].val.clusterDim.z = 1;
     cfg.attrs = attrs;
     cfg.numAttrs = 1;
-    const cudaError_t err = cudaLaunchKernelEx(&cfg, expert_gemm_kernel<GATE_UP>, w0, w1, b, args);
+    const cudaError_t err = cudaLaunchKernelEx(&cfg, expert_gemm_kernel<GATE_UP, HT>, w0, w1, b, args);
     if (err != cudaSuccess) {
         set_last_error(GATE_UP ? "hmoe expert GEMM gate/up launch" : "hmoe expert GEMM down launch", err);
         return HMOE_CUDA_ERROR;
@@ -779,35 +858,57 @@ hmoe_status launch_permute(const float* x, const int32_t* inv, int tokens, int s
     return check_launch("hmoe permute");
 }
 
+hmoe_status launch_group_permute(const SmallGroup& g, const float* x, int H, __half* xrows, float* xscale,
+                                 const SegSpec& seg, int4* tiles, int32_t* tile_count, int capacity,
+                                 cudaStream_t s) {
+    if (g.T <= 0) return HMOE_OK;
+    if (g.T > kGroupBlock || g.E + g.S > 2 * 256 || g.k + g.S > kMaxSlots || seg.nseg <= 0 ||
+        seg.nseg > kMaxSegments || seg.eps <= 0 || capacity <= 0)
+        return HMOE_INVALID_ARGUMENT;
+    group_permute_kernel<<<static_cast<unsigned>(g.T + 1), 256, 0, s>>>(x, H, xrows, xscale, g, seg, tiles,
+                                                                         tile_count, capacity);
+    return check_launch("hmoe group and permute");
+}
+
 // Full tiles are at most rows / kTileRows; each segment with rows adds at
 // most one partial tile, and at most `rows` segments have rows.
 int tile_capacity_for(long rows, int segments) {
     return static_cast<int>(rows / kTileRows + std::min<long>(segments, rows) + 1);
 }
 
+extern int g_variant; // layer.cu: 4 forces the wide-tile kernel
+
+// Every tile of the run fits the narrow kernel: no expert holds more than
+// kNarrowRows rows.
+bool narrow_run(const ExpertRun& r) { return g_variant != 4 && r.max_group >= 0 && r.max_group <= kNarrowRows; }
+
 hmoe_status gemm_gate_up(const ExpertRun& r, cudaStream_t s) {
+    const bool narrow = narrow_run(r);
     CUtensorMap mg, mu, mb;
     if (!map_weights(&mg, r.arena + r.gate_offset, r.I, r.H, r.experts, r.stride) ||
         !map_weights(&mu, r.arena + r.up_offset, r.I, r.H, r.experts, r.stride) ||
-        !map_rows(&mb, r.xrows, r.H, r.rows_cap, true)) {
+        !map_rows(&mb, r.xrows, r.H, r.rows_cap, true, narrow ? 32 : 128)) {
         set_last_error_text("hmoe: cuTensorMapEncodeTiled failed (gate/up)");
         return HMOE_CUDA_ERROR;
     }
     const int nb = (r.I + 127) / 128; // 128 features (64 per CTA) per pair
     GemmArgs a{r.tiles, r.tile_count, nb, r.quant, nullptr, r.xscale, r.hmid16, r.H, r.I, r.st, PushRows{}};
-    return launch_gemm<true>(mg, mu, mb, a, r.tile_cap * nb, s);
+    return narrow ? launch_gemm<true, 32>(mg, mu, mb, a, r.tile_cap * nb, s)
+                  : launch_gemm<true, 128>(mg, mu, mb, a, r.tile_cap * nb, s);
 }
 
 hmoe_status gemm_down(const ExpertRun& r, cudaStream_t s) {
+    const bool narrow = narrow_run(r);
     CUtensorMap md, mb;
     if (!map_weights(&md, r.arena + r.down_offset, r.H, r.I, r.experts, r.stride) ||
-        !map_rows(&mb, r.hmid16, r.I, r.rows_cap, false)) {
+        !map_rows(&mb, r.hmid16, r.I, r.rows_cap, false, narrow ? 32 : 128)) {
         set_last_error_text("hmoe: cuTensorMapEncodeTiled failed (down)");
         return HMOE_CUDA_ERROR;
     }
     const int nb = (r.H + 255) / 256; // 256 features (128 per CTA) per pair
     GemmArgs a{r.tiles, r.tile_count, nb, r.quant, r.weight, nullptr, r.yrows, r.I, r.H, r.st, r.push};
-    return launch_gemm<false>(md, md, mb, a, r.tile_cap * nb, s);
+    return narrow ? launch_gemm<false, 32>(md, md, mb, a, r.tile_cap * nb, s)
+                  : launch_gemm<false, 128>(md, md, mb, a, r.tile_cap * nb, s);
 }
 
 } // namespace hmoe

@@ -139,7 +139,8 @@ hmoe_status launch_combine(const __nv_bfloat16* yrows, const int32_t* inv, const
 
 // Router, histogram, grouping and the BF16 row permutation of one batch.
 hmoe_status enqueue_route(const hmoe_layer_desc& d, const float* x, size_t T, char* ws, const Workspace& w,
-                          bool permute, cudaStream_t s, const int32_t* expert_of_slot, int32_t* slot_counts) {
+                          bool permute, cudaStream_t s, const int32_t* expert_of_slot, int32_t* slot_counts,
+                          bool group) {
     cudaError_t err = cudaMemsetAsync(ws, 0, w.zero_bytes, s);
     if (err != cudaSuccess) {
         set_last_error("hmoe workspace reset", err);
@@ -156,6 +157,7 @@ hmoe_status enqueue_route(const hmoe_layer_desc& d, const float* x, size_t T, ch
                                  w.route_acc_bytes ? reinterpret_cast<double*>(ws + w.route_acc) : nullptr, st, s);
     if (r != HMOE_OK) return r;
     stage(1, s);
+    if (!group) return HMOE_OK;
     r = launch_group(reinterpret_cast<uint32_t*>(ws + w.ids), reinterpret_cast<float*>(ws + w.scores),
                      reinterpret_cast<int32_t*>(ws + w.counts), reinterpret_cast<int32_t*>(ws + w.block_counts),
                      static_cast<int>(T), static_cast<int>(d.top_k),
@@ -180,12 +182,12 @@ hmoe_status run_experts(const ExpertRun& r, bool gemv, bool stages, cudaStream_t
 }
 
 // The GEMV streams each touched expert's weights once per 4 rows; the
-// tensor-core GEMM wins as soon as experts hold more than a few rows.  The
-// choice is made per launch from the number of permuted rows, which the host
-// knows without reading the routing.
+// tensor-core GEMM wins as soon as a launch holds more than one token's rows.
+// The choice is made per launch from the number of permuted rows, which the
+// host knows without reading the routing.
 bool use_gemv(long rows, int H, int I) {
     if (g_variant == 1 || !gemm_available() || !gemm_shape_ok(H, I)) return true;
-    if (g_variant == 2) return false;
+    if (g_variant == 2 || g_variant == 4) return false;
     return rows <= kGemvMaxAssignments;
 }
 
@@ -222,8 +224,8 @@ using namespace hmoe;
 extern "C" {
 
 hmoe_status hmoe_set_variant(int32_t variant) {
-    if (variant < 0 || variant > 3) return HMOE_INVALID_ARGUMENT;
-    if (variant == 2 && !gemm_available()) return HMOE_UNSUPPORTED;
+    if (variant < 0 || variant > 4) return HMOE_INVALID_ARGUMENT;
+    if ((variant == 2 || variant == 4) && !gemm_available()) return HMOE_UNSUPPORTED;
     g_variant = variant;
     return HMOE_OK;
 }
@@ -320,15 +322,29 @@ hmoe_status forward_layer(const hmoe_layer_desc* desc, const float* x, const flo
             return r;
         }
     }
-    hmoe_status r = enqueue_route(*desc, x, tokens, ws, w, false, s);
+    // Batches of one group block: the grouping joins the permutation's
+    // launch (one launch less on the decode-sized path).
+    const bool small = tokens <= static_cast<size_t>(kGroupBlock) && E + S <= 2 * kGroupBlock;
+    hmoe_status r = enqueue_route(*desc, x, tokens, ws, w, false, s, nullptr, nullptr, !small);
     if (r != HMOE_OK) return r;
     const ExpertRun run = local_run(*desc, tokens, ws, w);
     // the permutation's launch also builds the tile list (one more CTA)
     const SegSpec seg{reinterpret_cast<int32_t*>(ws + w.offsets), nullptr, 0, E + S, E + S, 0, 0};
-    r = launch_permute(x, reinterpret_cast<int32_t*>(ws + w.inv), static_cast<int>(tokens), slots,
-                       static_cast<int>(desc->hidden), reinterpret_cast<__half*>(ws + w.xperm),
-                       reinterpret_cast<float*>(ws + w.xscale), s, &seg, const_cast<int4*>(run.tiles),
-                       const_cast<int32_t*>(run.tile_count), run.tile_cap);
+    if (small) {
+        const SmallGroup g{reinterpret_cast<const uint32_t*>(ws + w.ids), reinterpret_cast<const float*>(ws + w.scores),
+                           reinterpret_cast<const int32_t*>(ws + w.counts), static_cast<int>(tokens),
+                           static_cast<int>(desc->top_k), E, S, reinterpret_cast<int32_t*>(ws + w.offsets),
+                           reinterpret_cast<uint32_t*>(ws + w.perm_token), reinterpret_cast<float*>(ws + w.perm_weight),
+                           reinterpret_cast<int32_t*>(ws + w.inv)};
+        r = launch_group_permute(g, x, static_cast<int>(desc->hidden), reinterpret_cast<__half*>(ws + w.xperm),
+                                 reinterpret_cast<float*>(ws + w.xscale), seg, const_cast<int4*>(run.tiles),
+                                 const_cast<int32_t*>(run.tile_count), run.tile_cap, s);
+    } else {
+        r = launch_permute(x, reinterpret_cast<int32_t*>(ws + w.inv), static_cast<int>(tokens), slots,
+                           static_cast<int>(desc->hidden), reinterpret_cast<__half*>(ws + w.xperm),
+                           reinterpret_cast<float*>(ws + w.xscale), s, &seg, const_cast<int4*>(run.tiles),
+                           const_cast<int32_t*>(run.tile_count), run.tile_cap);
+    }
     if (r != HMOE_OK) return r;
     stage(2, s);
     r = run_experts(run, use_gemv(static_cast<long>(tokens) * slots, run.H, run.I), true, s);

@@ -25,8 +25,11 @@ struct Workspace {
 Workspace plan_workspace(const hmoe_layer_desc& d, size_t T);
 
 // Batches with at most this many (token, expert) assignments use the
-// weight-streaming GEMV for every expert; larger ones the tcgen05 GEMM.
-constexpr int kGemvMaxAssignments = 64;
+// weight-streaming GEMV for every expert; larger ones the tcgen05 GEMM.  On
+// the Qwen3-30B-A3B layer (top-8) the GEMM is as fast as the GEMV at one
+// token (95 us per layer call) and faster from two tokens on (106 against
+// 123 us at T=2, 124 against 172 us at T=8).
+constexpr int kGemvMaxAssignments = 8;
 
 // Upper bound of a token's rows (top_k routed + shared experts).
 constexpr int kMaxSlots = 96;
@@ -137,6 +140,25 @@ hmoe_status launch_permute(const float* x, const int32_t* inv, int tokens, int s
                            float* xscale, cudaStream_t stream, const SegSpec* seg = nullptr, int4* tiles = nullptr,
                            int32_t* tile_count = nullptr, int capacity = 0);
 
+// The grouping of a batch of at most kGroupBlock tokens fused with its
+// permutation and tile list (one launch instead of the grouping's and the
+// permutation's): the same offsets, permutation, inverse map, token rows
+// and tiles as launch_group followed by launch_permute with `seg`, for a
+// layer without an expert placement.  ids/scores/counts are the router's.
+struct SmallGroup {
+    const uint32_t* ids;   // [T, k]
+    const float* scores;   // [T, k]
+    const int32_t* counts; // [E] routed rows per expert
+    int T, k, E, S;
+    int32_t* offsets;      // [E+S+1]
+    uint32_t* perm_token;  // [T*(k+S)]
+    float* perm_weight;    // [T*(k+S)]
+    int32_t* inv;          // [T*(k+S)]
+};
+hmoe_status launch_group_permute(const SmallGroup& g, const float* x, int H, __half* xrows, float* xscale,
+                                 const SegSpec& seg, int4* tiles, int32_t* tile_count, int capacity,
+                                 cudaStream_t stream);
+
 // Upper bound of the tiles of `rows` rows spread over `segments` segments.
 int tile_capacity_for(long rows, int segments);
 
@@ -163,9 +185,10 @@ hmoe_status launch_combine(const __nv_bfloat16* yrows, const int32_t* inv, const
 
 // Layer driver pieces shared by the single-GPU and expert-parallel paths.
 hmoe_status validate_layer(const hmoe_layer_desc* d);
+// With group = false only the router runs (the caller groups the rows).
 hmoe_status enqueue_route(const hmoe_layer_desc& d, const float* x, size_t T, char* ws, const Workspace& w,
                           bool permute, cudaStream_t s, const int32_t* expert_of_slot = nullptr,
-                          int32_t* slot_counts = nullptr);
+                          int32_t* slot_counts = nullptr, bool group = true);
 ExpertRun local_run(const hmoe_layer_desc& d, size_t T, char* ws, const Workspace& w);
 // gate/up then down of every tile of `r`; `stages` records stage events 3, 4.
 hmoe_status run_experts(const ExpertRun& r, bool gemv, bool stages, cudaStream_t s);

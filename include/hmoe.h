@@ -248,12 +248,14 @@ hmoe_status hmoe_noalloc_read_status(int32_t *status, int32_t *near_ties,
                                      int32_t *sequential_logits, void *stream);
 
 /* Forces the expert-MLP variant for measurement: 0 = automatic (the
- * single-kernel decode layer for batches of at most 8 tokens whose shape it
- * takes, GEMV for experts with few tokens, tensor-core GEMM otherwise),
- * 1 = multi-kernel GEMV only, 2 = tensor-core GEMM only, 3 = the decode
- * layer only (HMOE_UNSUPPORTED for a batch or shape it does not take).  The
- * decode layer gives the multi-kernel GEMV variant's result bit for bit.
- * Process-wide. */
+ * single-kernel decode layer for batches of at most 2 tokens whose shape it
+ * takes, GEMV for launches of at most 8 permuted rows, tensor-core GEMM
+ * otherwise, with its narrow-tile kernel when no expert can hold more than
+ * 64 rows), 1 = multi-kernel GEMV only, 2 = tensor-core GEMM only, 3 = the
+ * decode layer only (HMOE_UNSUPPORTED for a batch or shape it does not
+ * take), 4 = tensor-core GEMM with its wide-tile kernel only.  The decode
+ * layer gives the multi-kernel GEMV variant's result bit for bit, and the
+ * two GEMM kernels give the same bits.  Process-wide. */
 hmoe_status hmoe_set_variant(int32_t variant);
 
 /* Forces the router kernel for measurement: 0 = automatic (the tiled kernel

@@ -1,6 +1,6 @@
 """The single-kernel decode layer (hypermoe-engine_b200/csrc/decode_layer.cu)
-through the C ABI.  For batches of at most 8 tokens hmoe_moe_forward runs the
-whole layer as one cooperative kernel; its arithmetic, every summation order
+through the C ABI.  For batches of at most 2 tokens (8 when forced)
+hmoe_moe_forward runs the whole layer as one cooperative kernel; its arithmetic, every summation order
 included, is the multi-kernel GEMV variant's, so the two agree bit for bit,
 and both match the reference-pinned port within the layer tolerance
 (tests/tolerance.py).  Routing is the decode router's, certified against the
@@ -19,6 +19,7 @@ pytestmark = pytest.mark.gpu
 
 DECODE = 3  # hmoe_set_variant: the decode layer only
 GEMV = 1    # the multi-kernel GEMV variant
+GEMM = 2    # the multi-kernel tensor-core GEMM variant
 
 
 def t(a, dev):
@@ -56,8 +57,11 @@ def test_decode_layer_equals_gemv_variant(cuda, cfg_name, T):
     st, ties, _ = dl.read_status()
     assert st == 0 and ties == 0
     np.testing.assert_array_equal(y, ref)
-    # the automatic choice (the decode layer or the multi-kernel GEMV) agrees
-    np.testing.assert_array_equal(host(dl.forward(x)), ref)
+    # the automatic choice: the decode layer up to 2 tokens, then the GEMV up
+    # to 8 permuted rows, then the tensor-core GEMM
+    rows = T * (cfg.top_k + cfg.shared_experts)
+    auto = ref if T <= 2 or rows <= 8 else forward_with(dl, x, GEMM)
+    np.testing.assert_array_equal(host(dl.forward(x)), auto)
     # and the port (the reference's CPU path restated, pinned bit for bit)
     out_p, *_ = O.moe_layer_port(hl, x_np)
     assert_layer_close(y, out_p)

@@ -27,6 +27,7 @@ pytestmark = pytest.mark.gpu
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 PATHS = [os.path.join(ROOT, "hypermoe-engine_b200"), os.path.join(ROOT, "oracle"), os.path.join(ROOT, "tests")]
+GEMV_MAX_ROWS = 8  # kGemvMaxAssignments (csrc/layer.cuh): larger launches take the GEMM
 
 
 def _single_gpu(hl, x, dev, variant):
@@ -51,7 +52,14 @@ def test_ep_one_rank_equals_forward(cuda, cfg_name, T, variant, placed, peer):
     cfg = H.CONFIGS[cfg_name]
     hl = H.make_host_layer(cfg, seed=3)
     x = H.make_tokens(cfg, T, seed=3)
-    ref = _single_gpu(hl, x, cuda, variant)
+    ref_variant = variant
+    if variant == 0:
+        # the automatic choice: the EP path decides by its row capacity
+        # (peer path) or by the rows it received (NCCL path), the one-GPU
+        # layer by its batch; compare against the variant the EP path takes
+        rows = (T + 7) * cfg.top_k if peer else T * cfg.top_k
+        ref_variant = 1 if rows <= GEMV_MAX_ROWS else 2
+    ref = _single_gpu(hl, x, cuda, ref_variant)
     comm = H.EpComm(H.ep_unique_id(), 0, 1, timeout_ms=30000)
     try:
         H.set_variant(variant)

@@ -334,6 +334,30 @@ def test_layer_configs_gemm_and_gemv_agree_with_port(cuda, cfg, T):
         assert_layer_close(y, out_p)
 
 
+@pytest.mark.parametrize("cfg,T", [("c3", 1), ("c3", 7), ("c3", 64), ("c2", 40), ("c1", 64)])
+def test_gemm_narrow_and_wide_kernels_equal(cuda, cfg, T):
+    """The GEMM's narrow-tile kernel (32 token rows per CTA, deeper rings),
+    which serves batches whose experts hold at most 64 rows, gives the wide kernel's output bit for bit: both issue
+    the same MMAs on the same operands.  Variant 2 takes the narrow kernel
+    at these sizes, variant 4 forces the wide one."""
+    c = H.CONFIGS[cfg]
+    hl = H.make_host_layer(c, seed=12)
+    x = H.make_tokens(c, T, seed=12)
+    out_p, *_ = O.moe_layer_port(hl, x)
+    dl = H.DeviceLayer(hl, cuda)
+    dx = t(x, cuda)
+    ys = []
+    for v in (2, 4):
+        H.set_variant(v)
+        try:
+            ys.append(host(dl.forward(dx)))
+        finally:
+            H.set_variant(0)
+        assert dl.read_status()[0] == 0
+    np.testing.assert_array_equal(ys[0].view(np.uint32), ys[1].view(np.uint32))
+    assert_layer_close(ys[0], out_p)
+
+
 @pytest.mark.parametrize("T", [1, 300])
 def test_forward_host_equals_forward(cuda, T):
     """hmoe_moe_forward_host (page-locked host buffers in and out, copies on
