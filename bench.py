@@ -54,8 +54,14 @@ def parse():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--tokens", type=int, default=4096)
-    p.add_argument("--config", default="c3")
+    p.add_argument("--tokens", type=int, default=None,
+                   help="tokens per GPU (default 4096; c4: the 2048-token prefill)")
+    p.add_argument("--config", default="c3",
+                   help="c1/c2/c3/c5: one MoE layer; c4: the 48-layer Qwen3-30B-A3B stack of c3 layers")
+    p.add_argument("--layers", type=int, default=48, help="c4: layers in the stack")
+    p.add_argument("--decode-batch", type=int, default=64, help="c4: decode batch over all GPUs")
+    p.add_argument("--stack-cpu-tokens", type=int, default=8,
+                   help="c4: tokens the reference CPU path runs through the whole stack")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--impl", default="hmoe", choices=["hmoe", "reference"])
     p.add_argument("--variant", type=int, default=0,
@@ -373,11 +379,265 @@ def decode_split(layer, cfg, T, seed, dev, flush, events, peaks, steps=20):
             "timing": "cuda-graph replay, median of %d steps, 256 MiB L2 flush before each" % steps}
 
 
+STACK_METRIC = "MoE-stack tokens/s (Qwen3-30B-A3B, {layers} INT8 MoE layers)"
+
+
+def reference_stack_sample(cfg, layers, seed, n, threads, repeats=1):
+    """The reference's CPU path (oracle/_ref: its RMSNorm and MoE layer
+    classes) through a stack of `layers` blocks, x += layer(rms_norm(x) * g)
+    in FP32 as TransformerBlock::execute does with an identity attention, on
+    `n` tokens.  Layers are generated from (seed, layer) one at a time
+    (untimed); each block is run `repeats` times on the same input, so
+    repeat r's stack time is the sum over blocks of the r-th run.  Returns
+    the per-repeat seconds."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import hmoe_api as H
+    import oracle as O
+    if not O.ref_available():
+        O.build(reference=False)
+    x = H.make_tokens(cfg, n, seed=seed)
+    spent = [0.0] * repeats
+    for l in range(layers):
+        rl = O.RefLayer(H.make_host_layer(cfg, seed=seed, layer=l))
+        g = H.make_norm_weight(cfg, seed, l)
+        for r in range(repeats):
+            t0 = time.perf_counter()
+            y = rl.forward(O.rms_norm_ref(x, g, 1e-6), threads=threads)
+            spent[r] += time.perf_counter() - t0
+        x = (x + y).astype(np.float32)
+        del rl
+    return spent
+
+
+def stack_main(args, world, rank, local):
+    """the Qwen3-30B-A3B stack of 48 c3 MoE layers,
+    weights per layer from (seed, layer), every layer resident (no tiering).
+    Each block is hmoe_rms_norm then hmoe_moe_forward_residual in place
+    (x += layer(rms_norm(x) * g), TransformerBlock::execute with an identity
+    attention); over torchrun ranks hmoe_ep_moe_forward_residual with the routed experts
+    split contiguously (16 per GPU at 8 ranks), one communicator and one
+    registered workspace for the whole stack.  A step is a prefill of
+    `--tokens` tokens per GPU through every layer (`value`, whole job); the
+    `decode` object is a step of the `--decode-batch` batch (over all GPUs)
+    through every layer."""
+    import numpy as np
+    import hmoe_api as H
+    cfg = H.CONFIGS["c3"]
+    L, T = args.layers, args.tokens
+    Td = max(1, args.decode_batch // world)
+    config = {"workload": f"c4: qwen3-30b-a3b {L}-layer moe stack (c3 layers)", "layers": L,
+              "hidden": cfg.hidden, "experts": cfg.experts, "top_k": cfg.top_k, "intermediate": cfg.intermediate,
+              "prefill_tokens_per_gpu": T, "decode_batch": Td * world, "decode_tokens_per_gpu": Td,
+              "routing": "zipf1.1 (bias per layer from seed+layer)", "weights": "int8 per-projection affine",
+              "seed": args.seed, "parallelism": (f"ep{world}" if world > 1 else "single"),
+              "ep_path": (args.ep_path if world > 1 else None),
+              "placement": ("contiguous" if world > 1 else None),
+              "l2": "inputs larger than L2 (the stack's INT8 experts), no flush"}
+    threads = os.cpu_count() or 1
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        if not os.path.exists(O.SYNTH_PATH):
+            O.build(reference=False)
+        H.use_synth_library(O.SYNTH_PATH)
+        n = args.stack_cpu_tokens
+        times = reference_stack_sample(cfg, L, args.seed, n, threads, repeats=max(1, args.steps))
+        value = n / statistics.mean(times)
+        print(json.dumps({
+            "metric": STACK_METRIC.format(layers=L), "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": len(times), "warmup": 0, "ms_per_step": 1e3 * statistics.mean(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights quantised to INT8)",
+            "config": config,
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference",
+                             "sample": f"{n} tokens through all {L} layers per step, each layer run once per "
+                                       f"step on the same input (layer generation untimed)"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+
+    import torch
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = comm = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+        uid = [H.ep_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(uid, src=0)
+        comm = H.EpComm(uid[0], rank, world, timeout_ms=120000)
+    H.set_variant(args.variant)
+    H.set_route_variant(args.route_variant)
+
+    # the reference CPU stack runs on a few tokens while the layers upload
+    cpu = None
+    cpu_on = world == 1 and not args.no_cpu_baseline
+    spent = [0.0]
+    if cpu_on:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        if not O.ref_available():
+            O.build(reference=False)
+    x_cpu = [H.make_tokens(cfg, args.stack_cpu_tokens, seed=args.seed)]
+
+    def hosts():
+        # each layer is generated once and used by both the device upload
+        # and, on one GPU, the CPU sample
+        for l in range(L):
+            host = H.make_host_layer(cfg, seed=args.seed, layer=l)
+            if cpu_on:
+                rl = O.RefLayer(host)
+                g = H.make_norm_weight(cfg, args.seed, l)
+                t0 = time.perf_counter()
+                y = rl.forward(O.rms_norm_ref(x_cpu[0], g, 1e-6), threads=threads)
+                spent[0] += time.perf_counter() - t0
+                x_cpu[0] = (x_cpu[0] + y).astype(np.float32)
+                del rl
+            yield host
+
+    stack = H.MoEStack(cfg, L, seed=args.seed, device=dev, comm=comm, peer=args.ep_path == "peer", hosts=hosts())
+    if cpu_on:
+        n = args.stack_cpu_tokens
+        cpu = {"value": n / spent[0], "unit": UNIT, "cores": threads, "kind": "reference",
+               "sample": f"{n} tokens through all {L} blocks (RMSNorm + MoE layer) of the reference CPU path "
+                         f"(oracle/_ref), "
+                         f"{spent[0]:.1f} s in the layers, expert groups over {threads} threads"}
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream()
+
+    def phase(Tn, seed_off, with_e2e):
+        x0 = torch.from_numpy(H.make_tokens(cfg, Tn, seed=args.seed + seed_off + 7919 * rank)).to(dev)
+        x = torch.empty_like(x0)
+
+        def fwd():
+            stack.forward(x, max_tokens=Tn)
+
+        for _ in range(args.warmup):  # also sizes (and registers) the shared workspace
+            x.copy_(x0)
+            fwd()
+        barrier()
+        graph = None
+        per = None
+        if comm is None and not args.eager:
+            side = torch.cuda.Stream()
+            side.wait_stream(stream)
+            with torch.cuda.stream(side):
+                x.copy_(x0)
+                fwd()
+            stream.wait_stream(side)
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            c1 = H.lib().hmoe_launch_count()
+            with torch.cuda.graph(graph):
+                fwd()
+            per = H.lib().hmoe_launch_count() - c1
+            torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        launches0 = H.lib().hmoe_launch_count()
+        times = []
+        barrier()
+        for _ in range(args.steps):
+            x.copy_(x0)
+            e0.record(stream)
+            if graph is not None:
+                graph.replay()
+            else:
+                fwd()
+            e1.record(stream)
+            e1.synchronize()
+            times.append(e0.elapsed_time(e1))
+        barrier()
+        launches = per * args.steps if graph is not None else H.lib().hmoe_launch_count() - launches0
+        ms = statistics.mean(times)
+        e2e = None
+        if with_e2e:
+            xh = x0.cpu().pin_memory()
+            yh = torch.empty_like(xh).pin_memory()
+            et = []
+            for i in range(args.steps + 1):
+                barrier()
+                e0.record(stream)
+                x.copy_(xh, non_blocking=True)
+                if graph is not None:
+                    graph.replay()
+                else:
+                    fwd()
+                yh.copy_(x, non_blocking=True)
+                e1.record(stream)
+                e1.synchronize()
+                if i:
+                    et.append(e0.elapsed_time(e1))
+            em = statistics.mean(et)
+            if dist is not None:
+                t = torch.tensor([em], device=dev)
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+                em = float(t.item())
+            e2e = {"value": world * Tn / (em * 1e-3), "unit": UNIT, "h2d_bytes_per_step": int(xh.numel() * 4),
+                   "d2h_bytes_per_step": int(yh.numel() * 4), "ms_per_step": em,
+                   "timing": "H2D copy of the step's tokens from page-locked memory, the stack, D2H copy of "
+                             "its output; CUDA events on the launch stream"}
+        if dist is not None:
+            t = torch.tensor([ms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        del graph
+        return ms, launches, e2e
+
+    props = torch.cuda.get_device_properties(dev)
+    pci = None
+    if hasattr(props, "pci_bus_id"):
+        pci = f"{getattr(props, 'pci_domain_id', 0):08X}:{props.pci_bus_id:02X}:{getattr(props, 'pci_device_id', 0):02X}.0"
+    clocks = Clocks(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local])
+                    if os.environ.get("CUDA_VISIBLE_DEVICES") else local, pci)
+    clocks.start()
+    ms, launches, e2e = phase(T, 0, True)
+    clk = clocks.stop()
+    dms, dlaunches, _ = phase(Td, 31, False)
+    status = stack.read_status()
+    if rank == 0:
+        peaks = load_peaks()
+        # tensor-bound: router logits plus the routed rows' expert MLPs,
+        # per GPU per layer (rows averaged over the ranks)
+        flops = L * (2 * T * cfg.hidden * cfg.experts + 6 * T * cfg.top_k * cfg.hidden * cfg.intermediate)
+        ach = flops / (ms * 1e-3) / 1e12
+        roof = {"bound": "tensor", "achieved": ach, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": ach / peaks["bf16_tflops"], "kernel": "whole stack (all kernels of every layer)",
+                "peak_source": peaks["source"] + " burst", "traffic": None}
+        print(json.dumps({
+            "metric": STACK_METRIC.format(layers=L), "value": world * T / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "fp16+bf16",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights quantised to INT8)",
+            "config": config, "e2e": e2e, "gpu_launches": launches,
+            "timing": ("cuda-graph replay of the stack (hmoe_rms_norm + hmoe_moe_forward_residual per layer)"
+                       if comm is None else "eager hmoe_rms_norm + hmoe_ep_moe_forward_residual per layer"),
+            "roofline": roof, "cpu_baseline": cpu, "clocks": clk,
+            "decode": {"tokens_per_step": Td * world, "ms_per_step": dms,
+                       "value": Td * world / (dms * 1e-3), "unit": UNIT, "gpu_launches": dlaunches},
+            "device_status": {"status": status[0], "near_ties": status[1], "sequential_logits": status[2]}}))
+    if dist is not None:
+        dist.barrier()
+        comm.close()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.config == "c4":
+        args.tokens = args.tokens or 2048
+        stack_main(args, world, rank, local)
+        return
+    args.tokens = args.tokens or 4096
     import numpy as np
     import hmoe_api as H
 

@@ -513,8 +513,9 @@ __global__ void ep_signal_kernel(PeerCtx c, int kind) {
 // Peer-memory forward (workspace == comm->reg_ws); the steps of
 // hmoe_ep_moe_forward with the count exchange, dispatch and return done by
 // the kernels above.
-hmoe_status ep_forward_peer(const hmoe_layer_desc* desc, hmoe_ep_comm* comm, const float* x, float* y,
-                            size_t tokens, size_t max_tokens, char* ws, const EpWorkspace& w, cudaStream_t s) {
+hmoe_status ep_forward_peer(const hmoe_layer_desc* desc, hmoe_ep_comm* comm, const float* x,
+                            const float* residual, float* y, __nv_bfloat16* y16, size_t tokens,
+                            size_t max_tokens, char* ws, const EpWorkspace& w, cudaStream_t s) {
     const int E = static_cast<int>(desc->experts), S = static_cast<int>(desc->shared_experts);
     const int k = static_cast<int>(desc->top_k), P = comm->size;
     const size_t H = desc->hidden;
@@ -612,7 +613,7 @@ hmoe_status ep_forward_peer(const hmoe_layer_desc* desc, hmoe_ep_comm* comm, con
     r = launch_combine(reinterpret_cast<const __nv_bfloat16*>(wsl + w.local.yrows),
                        reinterpret_cast<const int32_t*>(wsl + w.local.inv),
                        placed ? reinterpret_cast<const uint32_t*>(wsl + w.local.ids) : nullptr, placed ? k : 0, E,
-                       static_cast<int>(tokens), slots, static_cast<int>(H), y, s);
+                       static_cast<int>(tokens), slots, static_cast<int>(H), y, s, residual, y16);
 
     stage(5, s);
     return r;
@@ -1025,9 +1026,11 @@ hmoe_status hmoe_ep_workspace_size(const hmoe_layer_desc* desc, size_t max_token
     return HMOE_OK;
 }
 
-hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm, const float* x, float* y,
-                                size_t tokens, size_t max_tokens, void* workspace, size_t workspace_bytes,
-                                void* stream) {
+// Both expert-parallel entry points; residual and y16 as in
+// hmoe_moe_forward_residual (both may be null).
+static hmoe_status ep_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm, const float* x,
+                              const float* residual, float* y, __nv_bfloat16* y16, size_t tokens,
+                              size_t max_tokens, void* workspace, size_t workspace_bytes, void* stream) {
     const hmoe_status v = validate_ep(desc);
     if (v != HMOE_OK) return v;
     if (!comm || comm->broken || !comm->comm) return HMOE_INVALID_ARGUMENT;
@@ -1041,8 +1044,8 @@ hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm,
     const EpWorkspace w = plan_ep(*desc, max_tokens);
     if (workspace_bytes < w.total) return HMOE_WORKSPACE_TOO_SMALL;
     if (comm->reg_ws && workspace == comm->reg_ws)
-        return ep_forward_peer(desc, comm, x, y, tokens, max_tokens, static_cast<char*>(workspace), w,
-                               as_stream(stream));
+        return ep_forward_peer(desc, comm, x, residual, y, y16, tokens, max_tokens, static_cast<char*>(workspace),
+                               w, as_stream(stream));
     comm->last_peer = false;
     const NcclApi& N = nccl();
     char* ws = static_cast<char*>(workspace);
@@ -1172,9 +1175,23 @@ hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm,
     // 6. combine in ascending expert id
     r = launch_combine(yrows, reinterpret_cast<int32_t*>(wsl + w.local.inv),
                        placed ? reinterpret_cast<uint32_t*>(wsl + w.local.ids) : nullptr, k, E,
-                       static_cast<int>(tokens), slots, static_cast<int>(H), y, s);
+                       static_cast<int>(tokens), slots, static_cast<int>(H), y, s, residual, y16);
     stage(5, s);
     return r;
+}
+
+hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm, const float* x, float* y,
+                                size_t tokens, size_t max_tokens, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+    return ep_forward(desc, comm, x, nullptr, y, nullptr, tokens, max_tokens, workspace, workspace_bytes, stream);
+}
+
+hmoe_status hmoe_ep_moe_forward_residual(const hmoe_layer_desc* desc, hmoe_ep_comm* comm, const float* x,
+                                         const float* residual, float* y, uint16_t* y_bf16, size_t tokens,
+                                         size_t max_tokens, void* workspace, size_t workspace_bytes,
+                                         void* stream) {
+    return ep_forward(desc, comm, x, residual, y, reinterpret_cast<__nv_bfloat16*>(y_bf16), tokens, max_tokens,
+                      workspace, workspace_bytes, stream);
 }
 
 } // extern "C"

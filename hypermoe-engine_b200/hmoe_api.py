@@ -43,7 +43,7 @@ EXPORTS = [
     "hmoe_moe_forward_noalloc", "hmoe_selftest_bounded_wait", "hmoe_ep_set_placement",
     "hmoe_ep_balanced_placement", "hmoe_set_route_variant", "hmoe_ep_register_workspace",
     "hmoe_ep_selftest_flag_wait", "hmoe_ep_read_status", "hmoe_noalloc_read_status",
-    "hmoe_moe_forward_residual", "hmoe_ep_peer_plan",
+    "hmoe_moe_forward_residual", "hmoe_ep_peer_plan", "hmoe_ep_moe_forward_residual", "hmoe_rms_norm",
 ]
 EP_MAX_RANKS = 64
 EP_UNIQUE_ID_BYTES = 128
@@ -135,6 +135,8 @@ def lib() -> ctypes.CDLL:
             "hmoe_ep_comm_destroy": [vp],
             "hmoe_ep_workspace_size": [ctypes.POINTER(LayerDesc), sz, ctypes.POINTER(sz)],
             "hmoe_ep_moe_forward": [ctypes.POINTER(LayerDesc), vp, vp, vp, sz, sz, vp, sz, vp],
+            "hmoe_ep_moe_forward_residual": [ctypes.POINTER(LayerDesc), vp, vp, vp, vp, vp, sz, sz, vp, sz, vp],
+            "hmoe_rms_norm": [vp, vp, vp, sz, sz, f32, vp],
             "hmoe_ep_last_plan": [vp, ctypes.POINTER(EpPlan)],
             "hmoe_ep_register_workspace": [vp, vp, sz],
             "hmoe_ep_selftest_flag_wait": [vp, ctypes.c_uint64, ctypes.POINTER(i32)],
@@ -565,3 +567,127 @@ class EpLayer(DeviceLayer):
             ctypes.byref(self.desc), self.comm.handle, x.data_ptr() if T else None, y.data_ptr() if T else None,
             T, max_tokens, ws.data_ptr(), ws.numel(), _stream(stream)))
         return y
+
+    def forward_residual(self, x, residual=None, y=None, y_bf16=None, stream=None,
+                         max_tokens: Optional[int] = None):
+        """Collective: y = residual + layer(x) over the communicator's ranks
+        (hmoe_ep_moe_forward_residual); residual and y may alias x."""
+        import torch
+        T = x.shape[0]
+        max_tokens = max_tokens or max(T, 1)
+        if y is None:
+            y = torch.empty((T, self.cfg.hidden), dtype=torch.float32, device=x.device)
+        ws = self.ep_workspace(max_tokens)
+        check("hmoe_ep_moe_forward_residual", lib().hmoe_ep_moe_forward_residual(
+            ctypes.byref(self.desc), self.comm.handle, x.data_ptr() if T else None,
+            _ptr(residual) if T else None, y.data_ptr() if T else None, _ptr(y_bf16) if T else None,
+            T, max_tokens, ws.data_ptr(), ws.numel(), _stream(stream)))
+        return y
+
+
+# ------------------------------------------------------------ layer stacks
+
+def make_norm_weight(cfg: LayerConfig, seed: int = 0, layer: int = 0) -> np.ndarray:
+    """Seeded RMSNorm weight [H] of layer `layer`'s block: 1 + N(0, 0.1^2)."""
+    return (1.0 + synth_normal(seed, (1 << 60) + layer, 0.1, (cfg.hidden,))).astype(np.float32)
+
+
+def rms_norm(x, weight, out=None, eps: float = 1e-6, stream=None):
+    """hmoe_rms_norm over device tensors [T, H] FP32 (out may be x)."""
+    import torch
+    if out is None:
+        out = torch.empty_like(x)
+    T, Hd = x.shape
+    check("hmoe_rms_norm", lib().hmoe_rms_norm(x.data_ptr() if T else None, weight.data_ptr(),
+                                               out.data_ptr() if T else None, T, Hd, eps, _stream(stream)))
+    return out
+
+
+class MoEStack:
+    """A stack of transformer blocks whose attention is the identity (as in
+    MoELayer::execute), i.e. per block the post-attention RMSNorm, the MoE
+    layer and its residual add (TransformerBlock::execute,
+    src/transformer/runtime/TransformerBlock.cpp:90-104):
+        x_{l+1} = x_l + layer_l(rms_norm(x_l) * g_l),  l = 0 .. n_layers-1,
+    the add in one FP32 rounding, in place in the caller's buffer.  The norm
+    is what keeps a deep stack finite: SwiGLU's output grows with the square
+    of its input, so without it the residual stream overflows within a few
+    dozen layers.
+
+    Layer l's weights are generated from (seed, l) by make_host_layer and its
+    norm weight by make_norm_weight, so the stack is BASELINE's 48-layer
+    Qwen3-30B-A3B configuration when built from CONFIGS["c3"] with
+    n_layers=48.  Every layer stays resident on the device (no tiering).  All
+    layers share one workspace, since they run one after another on one
+    stream.  With `comm` the layers are expert-parallel over its ranks
+    (EpLayer), sharing the communicator, its expert placement and one
+    registered workspace."""
+
+    def __init__(self, cfg: LayerConfig, n_layers: int, seed: int = 0, device="cuda", comm=None,
+                 slot_of_expert=None, peer: bool = True, hosts=None, eps: float = 1e-6):
+        """hosts: an iterable of the layers' HostLayers (a list the caller
+        keeps to compare against, or a generator); by default each layer is
+        generated from (seed, layer), uploaded and dropped, so host memory
+        holds one layer at a time.  eps: RMSNorm's epsilon (its default,
+        src/transformer/norm/RMSNorm.hpp:18)."""
+        import torch
+        self.cfg = cfg
+        self.comm = comm
+        self.eps = eps
+        self.layers = []
+        self.norm_host = [make_norm_weight(cfg, seed, l) for l in range(n_layers)]
+        self.norm_w = [torch.from_numpy(g).to(device) for g in self.norm_host]
+        it = iter(hosts) if hosts is not None else (make_host_layer(cfg, seed=seed, layer=l)
+                                                    for l in range(n_layers))
+        for _ in range(n_layers):
+            host = next(it)
+            if comm is None:
+                layer = DeviceLayer(host, device)
+            else:
+                layer = EpLayer(host, comm, device, slot_of_expert=slot_of_expert, peer=peer)
+                layer.full_host = None
+            layer.host = None
+            self.layers.append(layer)
+            del host
+        self._ws = None
+        self._xn = None
+
+    def _share_workspace(self, T: int, max_tokens: Optional[int]):
+        import torch
+        first = self.layers[0]
+        if self.comm is None:
+            need = first.workspace_bytes(T)
+            if self._ws is None or self._ws.numel() < need:
+                self._ws = torch.empty(need, dtype=torch.uint8, device=first.arena.device)
+        else:
+            # the first layer sizes and registers it (collective); the others
+            # reuse it, so every layer call takes the same transfer path
+            self._ws = first.ep_workspace(max_tokens or max(T, 1))
+            for layer in self.layers[1:]:
+                layer.peer = first.peer
+        for layer in self.layers:
+            layer._ws = self._ws
+
+    def forward(self, x, stream=None, max_tokens: Optional[int] = None, trace=None):
+        """x [T, H] FP32 on the device, updated in place and returned.
+        trace: a list that receives, per layer, host copies of the layer's
+        residual input and of its normalised input (tests only: it
+        synchronises)."""
+        import torch
+        T = x.shape[0]
+        self._share_workspace(T, max_tokens)
+        if self._xn is None or self._xn.shape[0] < T:
+            self._xn = torch.empty((max(T, 1), self.cfg.hidden), dtype=torch.float32, device=x.device)
+        xn = self._xn[:T]
+        for l, layer in enumerate(self.layers):
+            rms_norm(x, self.norm_w[l], out=xn, eps=self.eps, stream=stream)
+            if trace is not None:
+                trace.append((x.cpu().numpy().copy(), xn.cpu().numpy().copy()))
+            if self.comm is None:
+                layer.forward_residual(xn, residual=x, y=x, stream=stream)
+            else:
+                layer.forward_residual(xn, residual=x, y=x, stream=stream, max_tokens=max_tokens)
+        return x
+
+    def read_status(self, stream=None):
+        return self.layers[0].read_status(stream)

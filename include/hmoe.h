@@ -223,6 +223,21 @@ hmoe_status hmoe_moe_forward_residual(const hmoe_layer_desc *desc,
                                       size_t tokens, void *workspace,
                                       size_t workspace_bytes, void *stream);
 
+/* RMSNorm of `tokens` rows of `hidden` FP32 values (replaces the CUDA
+ * branch of RMSNorm::execute, src/transformer/norm/RMSNorm.cpp:53-58, with
+ * the CPU branch's arithmetic, :64-77):
+ *   output[t][i] = float(double(input[t][i]) * inv_t * double(weight[i])),
+ *   inv_t = 1 / sqrt(sum_i double(input[t][i])^2 / hidden + epsilon),
+ * the sum taken in double (as a tree, where the reference sums
+ * sequentially).  This is the normalisation a transformer block applies
+ * before its MoE layer (TransformerBlock.cpp:90-92); a stack of MoE layers
+ * calls it before every layer.  output may alias input.  epsilon > 0 and
+ * finite (RMSNorm's constructor check); tokens == 0 is a no-op.  Enqueues
+ * on `stream`; no host synchronisation, no allocation. */
+hmoe_status hmoe_rms_norm(const float *input, const float *weight,
+                          float *output, size_t tokens, size_t hidden,
+                          float epsilon, void *stream);
+
 /* hmoe_moe_forward with no caller workspace: scratch is a file-scope
  * device array of 16 MiB per device inside libhmoe.so, so the call allocates
  * nothing.  No counterpart in the reference (whose layer path allocates
@@ -440,6 +455,21 @@ hmoe_status hmoe_ep_moe_forward(const hmoe_layer_desc *desc,
                                 size_t tokens, size_t max_tokens,
                                 void *workspace, size_t workspace_bytes,
                                 void *stream);
+
+/* Collective: hmoe_ep_moe_forward with the residual add and the BF16 copy
+ * of hmoe_moe_forward_residual fused into this rank's combine
+ * (MoELayer::execute, src/transformer/MoELayer.cpp:19-48, plus the residual
+ * add of TransformerBlock::forward, TransformerBlock.cpp:101-104, for a
+ * layer whose experts are spread over ranks).  residual may be NULL and may
+ * alias x or y; y may alias x; y_bf16 may be NULL.  A stack of layers calls
+ * it once per layer with the same communicator and workspace. */
+hmoe_status hmoe_ep_moe_forward_residual(const hmoe_layer_desc *desc,
+                                         hmoe_ep_comm *comm, const float *x,
+                                         const float *residual, float *y,
+                                         uint16_t *y_bf16, size_t tokens,
+                                         size_t max_tokens, void *workspace,
+                                         size_t workspace_bytes,
+                                         void *stream);
 
 /* Failure-detection self-test (no counterpart in the reference): launches
  * one kernel that waits on an mbarrier nothing arrives on, using the same

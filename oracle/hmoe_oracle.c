@@ -167,6 +167,21 @@ void hmo_int8_matmul(const float *left, const int8_t *q, float *out,
 /* Activation.cpp:44 */
 float hmo_silu(float v) { return v / (1.0f + expf(-v)); }
 
+/* RMSNorm::execute, CPU branch (src/transformer/norm/RMSNorm.cpp:64-77):
+ * squares summed sequentially in double, inverse RMS in double, one rounding
+ * to float per output. */
+void hmo_rms_norm(const float *x, const float *w, float *out, size_t T, size_t H, float eps) {
+    for (size_t t = 0; t < T; ++t) {
+        double ss = 0.0;
+        for (size_t i = 0; i < H; ++i) {
+            const float v = x[t * H + i];
+            ss += (double)v * v;
+        }
+        const double inv = 1.0 / sqrt(ss / (double)H + eps);
+        for (size_t i = 0; i < H; ++i) out[t * H + i] = (float)(x[t * H + i] * inv * w[i]);
+    }
+}
+
 /* down(SiLU(x*Wg) (.) (x*Wu)), ExpertExecutor.cpp:118-131 with the CPU
  * backend: two INT8 GEMMs, elementwise SiLU, elementwise multiply
  * (CpuTensorBackend.cpp:207-220), INT8 GEMM. */

@@ -72,6 +72,8 @@ def port() -> ctypes.CDLL:
         L.hmo_quantize_int8.argtypes = [vp, sz, vp, vp, vp, vp]
         L.hmo_silu.argtypes = [f32]
         L.hmo_silu.restype = f32
+        L.hmo_rms_norm.argtypes = [vp, vp, vp, sz, sz, f32]
+        L.hmo_rms_norm.restype = None
         _port = L
     return _port
 
@@ -87,6 +89,7 @@ def ref() -> ctypes.CDLL:
         L.hmr_int8_matmul.argtypes = [vp, vp, vp, sz, sz, sz, f32, i32]
         L.hmr_expert_mlp.argtypes = [vp, sz, sz, sz, vp, vp, vp, vp, vp, vp]
         L.hmr_quantize_int8.argtypes = [vp, sz, vp, vp, vp, vp]
+        L.hmr_rms_norm.argtypes = [vp, vp, vp, sz, sz, f32]
         L.hmr_layer_create.argtypes = [sz, sz, sz, sz, ctypes.c_int, ctypes.c_int, vp, vp, sz, vp, sz,
                                        sz, sz, sz, vp, vp]
         L.hmr_layer_create.restype = vp
@@ -194,6 +197,26 @@ def moe_layer_port(host_layer, x, threads=None):
     if st != 0:
         raise OracleError(f"moe layer failed with status {st}")
     return out, ids, sc, off
+
+
+def rms_norm_port(x, w, eps):
+    """RMSNorm through the C port (RMSNorm.cpp:64-77): [T, H] FP32."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.empty_like(x)
+    port().hmo_rms_norm(_p(x), _p(w), _p(out), x.shape[0], x.shape[1], float(eps))
+    return out
+
+
+def rms_norm_ref(x, w, eps):
+    """RMSNorm through the reference's own RMSNorm class on its CPU backend."""
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.empty_like(x)
+    st = ref().hmr_rms_norm(_p(x), _p(w), _p(out), x.shape[0], x.shape[1], float(eps))
+    if st != 0:
+        raise OracleError(f"hmr_rms_norm failed with status {st}")
+    return out
 
 
 class RefLayer:

@@ -23,6 +23,7 @@
 #include "router/RouterConfig.hpp"
 #include "tensor/backend/CpuTensorBackend.hpp"
 #include "tensor/quantization/Quantization.hpp"
+#include "transformer/norm/RMSNorm.hpp"
 
 #include <algorithm>
 #include <atomic>
@@ -174,6 +175,23 @@ int hmr_expert_mlp(const float* x, std::size_t rows, std::size_t H,
             in, {g, u, d, QP{scale[0], zp[0]}, QP{scale[1], zp[1]}, QP{scale[2], zp[2]}},
             out);
         std::memcpy(y, out.data(), rows * H * 4);
+        return kOk;
+    } catch (const std::invalid_argument&) {
+        return kInvalid;
+    } catch (const std::exception&) {
+        return kFailed;
+    }
+}
+
+// RMSNorm::execute on the CPU backend (src/transformer/norm/RMSNorm.cpp:35-77).
+int hmr_rms_norm(const float* x, const float* w, float* out, std::size_t T, std::size_t H, float eps) {
+    try {
+        auto cpu = std::make_shared<tensor::CpuTensorBackend>();
+        auto in = hostTensor(*cpu, {T, H}, DType::FP32, x, T * H * 4);
+        auto g = hostTensor(*cpu, {H}, DType::FP32, w, H * 4);
+        transformer::norm::RMSNorm norm(cpu, H, eps);
+        auto o = norm.execute(in.view(), g.view());
+        std::memcpy(out, o.data(), T * H * 4);
         return kOk;
     } catch (const std::invalid_argument&) {
         return kInvalid;

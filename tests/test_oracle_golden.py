@@ -130,6 +130,40 @@ def test_port_matches_reference_on_random_layers(port, seed):
     np.testing.assert_array_equal(out_p, out_r)
 
 
+@pytest.mark.skipif(not O.ref_available(), reason="reference sources not built here")
+@pytest.mark.parametrize("T,Hd,eps", [(9, 2048, 1e-6), (4, 7, 1e-5), (2, 4096, 1e-6)])
+def test_rms_norm_port_matches_reference(port, T, Hd, eps):
+    """The port's RMSNorm equals the reference's own RMSNorm class on its CPU
+    backend (src/transformer/norm/RMSNorm.cpp:64-77) bit for bit."""
+    rng = np.random.default_rng(Hd)
+    x = (rng.standard_normal((T, Hd)) * rng.uniform(1e-3, 1e3, size=(T, 1))).astype(np.float32)
+    g = (1.0 + 0.1 * rng.standard_normal(Hd)).astype(np.float32)
+    np.testing.assert_array_equal(O.rms_norm_port(x, g, eps), O.rms_norm_ref(x, g, eps))
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="reference sources not built here")
+def test_stack_port_matches_reference(port):
+    """A stack of blocks with per-layer weights from (seed, layer): the
+    post-attention RMSNorm, the MoE layer and the residual add of
+    TransformerBlock::execute with an identity attention
+    (src/transformer/runtime/TransformerBlock.cpp:90-104).  The port and the
+    reference's own classes agree bit for bit through every block, routing
+    included, and the residual stream stays finite."""
+    cfg = H.LayerConfig(128, 192, 16, 4, True, True, 0, 1.1)
+    xp = H.make_tokens(cfg, 19, seed=8)
+    xr = xp.copy()
+    for l in range(6):
+        hl = H.make_host_layer(cfg, seed=8, layer=l)
+        g = H.make_norm_weight(cfg, 8, l)
+        out_p, ids_p, _, _ = O.moe_layer_port(hl, O.rms_norm_port(xp, g, 1e-6))
+        out_r, ids_r, _, _ = O.RefLayer(hl).forward(O.rms_norm_ref(xr, g, 1e-6), threads=2, want_routing=True)
+        np.testing.assert_array_equal(ids_p, ids_r)
+        xp = (xp + out_p).astype(np.float32)
+        xr = (xr + out_r).astype(np.float32)
+        np.testing.assert_array_equal(xp, xr)
+    assert np.isfinite(xp).all()
+
+
 def test_router_rejects_non_finite(port):
     x = np.ones((2, 4), np.float32)
     w = np.ones((4, 3), np.float32)
