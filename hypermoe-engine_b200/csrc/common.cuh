@@ -49,6 +49,12 @@ inline hmoe_status check_launch(const char* what) {
 
 inline cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
 
+// Whether p (null allowed) is a multiple of `a` bytes.  Token rows, the
+// workspace, the router matrix and the expert arena are read and written
+// with 16-byte vector accesses and bulk/tensor copies, which fault on
+// misaligned addresses, so the entry points check them on the host.
+inline bool aligned(const void* p, size_t a) { return reinterpret_cast<uintptr_t>(p) % a == 0; }
+
 constexpr unsigned kThreads = 256;
 
 inline unsigned blocks_for(size_t n, unsigned per = kThreads) {

@@ -1038,6 +1038,9 @@ static hmoe_status ep_forward(const hmoe_layer_desc* desc, hmoe_ep_comm* comm, c
     if (tokens > max_tokens || max_tokens == 0 || max_tokens > static_cast<size_t>(INT_MAX) / 128 ||
         !workspace || (tokens > 0 && (!x || !y)))
         return HMOE_INVALID_ARGUMENT;
+    if (!aligned(workspace, 16) ||
+        (tokens > 0 && (!aligned(x, 16) || !aligned(y, 16) || !aligned(residual, 16) || !aligned(y16, 16))))
+        return HMOE_INVALID_ARGUMENT;
     if (!ep_rows_fit(*desc, max_tokens)) return HMOE_UNSUPPORTED;
     int dev = -1;
     if (cudaGetDevice(&dev) != cudaSuccess || dev != comm->device) return HMOE_INVALID_ARGUMENT;

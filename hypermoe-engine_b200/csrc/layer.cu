@@ -96,6 +96,9 @@ hmoe_status validate_layer(const hmoe_layer_desc* d) {
     if (d->hidden % 64 || d->intermediate % 64) return HMOE_UNSUPPORTED;
     if (d->expert_stride % 16 || d->gate_offset % 16 || d->up_offset % 16 || d->down_offset % 16)
         return HMOE_INVALID_ARGUMENT;
+    if (!aligned(d->router_weight, 16) || !aligned(d->arena, 16) || !aligned(d->quant, 4) ||
+        !aligned(d->router_bias, 4))
+        return HMOE_INVALID_ARGUMENT;
     if (d->experts > 256 || d->top_k > 32 || d->shared_experts > 64 ||
         d->top_k + d->shared_experts > static_cast<uint32_t>(kMaxSlots))
         return HMOE_UNSUPPORTED;
@@ -259,6 +262,7 @@ hmoe_status hmoe_route(const hmoe_layer_desc* desc, const float* x, size_t token
     if (v != HMOE_OK) return v;
     if (tokens == 0) return HMOE_OK;
     if (!x || !workspace || tokens > static_cast<size_t>(INT_MAX) / 128) return HMOE_INVALID_ARGUMENT;
+    if (!aligned(x, 16) || !aligned(workspace, 16)) return HMOE_INVALID_ARGUMENT;
     const Workspace w = plan_workspace(*desc, tokens);
     if (workspace_bytes < w.total) return HMOE_WORKSPACE_TOO_SMALL;
     char* ws = static_cast<char*>(workspace);
@@ -296,6 +300,9 @@ hmoe_status forward_layer(const hmoe_layer_desc* desc, const float* x, const flo
     if (v != HMOE_OK) return v;
     if (tokens == 0) return HMOE_OK;
     if (!x || !y || !workspace || tokens > static_cast<size_t>(INT_MAX) / 128) return HMOE_INVALID_ARGUMENT;
+    if (!aligned(x, 16) || !aligned(y, 16) || !aligned(residual, 16) || !aligned(y16, 16) ||
+        !aligned(workspace, 16))
+        return HMOE_INVALID_ARGUMENT;
     const Workspace w = plan_workspace(*desc, tokens);
     if (workspace_bytes < w.total) return HMOE_WORKSPACE_TOO_SMALL;
     char* ws = static_cast<char*>(workspace);
@@ -378,6 +385,7 @@ hmoe_status hmoe_moe_forward_host(const hmoe_layer_desc* desc, const float* x_ho
     if (tokens == 0) return HMOE_OK;
     if (!x_host || !y_host || !workspace || tokens > static_cast<size_t>(INT_MAX) / 128)
         return HMOE_INVALID_ARGUMENT;
+    if (!aligned(workspace, 16)) return HMOE_INVALID_ARGUMENT;
     const Workspace w = plan_workspace(*desc, tokens);
     const size_t io = align_up(tokens * desc->hidden * sizeof(float), 256);
     if (workspace_bytes < w.total + 2 * io) return HMOE_WORKSPACE_TOO_SMALL;

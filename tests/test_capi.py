@@ -83,6 +83,21 @@ def test_invalid_layer_descriptors_rejected_on_host():
     d.hidden = cfg.hidden
     d.expert_stride = cfg.expert_stride + 8  # TMA needs 16-byte strides
     assert H.lib().hmoe_workspace_size(ctypes.byref(d), 4, ctypes.byref(n)) == 1
+    d.expert_stride = cfg.expert_stride
+    # bulk/tensor copies and 16-byte vector accesses fault on misaligned
+    # addresses: the layer's buffers are checked before anything is enqueued
+    for field, bad in (("router_weight", 256 + 4), ("arena", 256 + 8), ("quant", 256 + 2), ("router_bias", 258)):
+        setattr(d, field, bad)
+        assert H.lib().hmoe_workspace_size(ctypes.byref(d), 4, ctypes.byref(n)) == 1, field
+        setattr(d, field, 256 if field != "router_bias" else None)
+    assert H.lib().hmoe_workspace_size(ctypes.byref(d), 4, ctypes.byref(n)) == 0
+    L = H.lib()
+    for x, y, ws in ((4096 + 4, 8192, 1 << 20), (4096, 8192 + 8, 1 << 20), (4096, 8192, (1 << 20) + 4)):
+        assert L.hmoe_moe_forward(ctypes.byref(d), x, y, 4, ws, 1 << 40, None) == 1
+    assert L.hmoe_moe_forward_residual(ctypes.byref(d), 4096, 4096 + 12, 8192, None, 4, 1 << 20, 1 << 40, None) == 1
+    assert L.hmoe_moe_forward_residual(ctypes.byref(d), 4096, None, 8192, 8192 + 2, 4, 1 << 20, 1 << 40, None) == 1
+    assert L.hmoe_route(ctypes.byref(d), 4096 + 4, 4, None, None, None, None, None, 1 << 20, 1 << 40, None) == 1
+    assert L.hmoe_moe_forward_host(ctypes.byref(d), 4096, 8192, 4, (1 << 20) + 8, 1 << 40, None) == 1
 
 
 def test_synth_is_deterministic_across_thread_counts():
