@@ -62,6 +62,8 @@ def parse():
     p.add_argument("--decode-batch", type=int, default=64, help="c4: decode batch over all GPUs")
     p.add_argument("--stack-cpu-tokens", type=int, default=8,
                    help="c4: tokens the reference CPU path runs through the whole stack")
+    p.add_argument("--no-stack", action="store_true",
+                   help="single GPU: skip the c4 stack measurement added to the c3 line")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--impl", default="hmoe", choices=["hmoe", "reference"])
     p.add_argument("--variant", type=int, default=0,
@@ -272,6 +274,25 @@ def reference_arm(args, cfg, config, rank):
                           "sample": f"{n1} tokens in {dt1:.1f} s on one thread (the reference's own loop)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
+
+
+def stack_subprocess(seed, steps, warmup, timeout=420):
+    """BASELINE configs[3] measured in a process of its own (bench.py --config
+    c4: the 48-block stack, prefill and decode), so that the c3 line's own
+    figures never depend on it; returns its JSON line or why it is missing."""
+    cmd = [sys.executable, os.path.abspath(__file__), "--config", "c4", "--steps", str(steps),
+           "--warmup", str(warmup), "--seed", str(seed)]
+    env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
+    try:
+        p = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"the c4 stack run did not finish within {timeout} s"}
+    lines = [ln for ln in p.stdout.strip().splitlines() if ln.startswith("{")]
+    if p.returncode != 0 or not lines:
+        return {"unavailable": f"bench.py --config c4 exited {p.returncode}: {p.stderr.strip()[-300:]}"}
+    out = json.loads(lines[-1])
+    out["command"] = " ".join(["python", "bench.py"] + cmd[2:])
+    return out
 
 
 def reference_cuda(cfg, T, seed, steps, warmup, gpu_index, pci, timeout=600):
@@ -930,6 +951,10 @@ def main():
         if T > 1:
             ref_cuda_decode = reference_cuda(cfg, 1, args.seed, 20, 3, gpu_index, pci)
 
+    stack = None
+    if world == 1 and args.config == "c3" and not args.no_stack:
+        stack = stack_subprocess(args.seed, steps=5, warmup=3)
+
     # tensor-core GEMM present (hmoe_set_variant(2) is refused without it)?
     has_gemm = H.lib().hmoe_set_variant(2) == 0
     H.lib().hmoe_set_variant(args.variant)
@@ -951,6 +976,7 @@ def main():
         "decode": decode,
         "reference_cuda": ref_cuda,
         "reference_cuda_decode_t1": ref_cuda_decode,
+        "stack_c4": stack,
     }
     print(json.dumps(line))
     if dist is not None:
