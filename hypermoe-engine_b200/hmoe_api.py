@@ -597,6 +597,11 @@ def rms_norm(x, weight, out=None, eps: float = 1e-6, stream=None):
     import torch
     if out is None:
         out = torch.empty_like(x)
+    for name, t in (("x", x), ("weight", weight), ("out", out)):
+        if t.dtype != torch.float32 or not t.is_contiguous() or t.device != x.device:
+            raise ValueError(f"rms_norm: {name} must be a contiguous FP32 tensor on {x.device}")
+    if x.dim() != 2 or out.shape != x.shape or weight.shape != (x.shape[1],):
+        raise ValueError("rms_norm: x and out are [T, H], weight is [H]")
     T, Hd = x.shape
     check("hmoe_rms_norm", lib().hmoe_rms_norm(x.data_ptr() if T else None, weight.data_ptr(),
                                                out.data_ptr() if T else None, T, Hd, eps, _stream(stream)))
@@ -674,6 +679,8 @@ class MoEStack:
         residual input and of its normalised input (tests only: it
         synchronises)."""
         import torch
+        if x.dtype != torch.float32 or not x.is_contiguous() or x.dim() != 2 or x.shape[1] != self.cfg.hidden:
+            raise ValueError(f"MoEStack.forward: x must be a contiguous FP32 [T, {self.cfg.hidden}] tensor")
         T = x.shape[0]
         self._share_workspace(T, max_tokens)
         if self._xn is None or self._xn.shape[0] < T:
