@@ -167,6 +167,13 @@ void hmo_int8_matmul(const float *left, const int8_t *q, float *out,
 /* Activation.cpp:44 */
 float hmo_silu(float v) { return v / (1.0f + expf(-v)); }
 
+/* The host libm's expf over an array (the exponential of the reference's
+ * softmax, CpuRouterBackend.cpp:54), for tests that look for inputs it
+ * rounds differently from the correctly rounded exponential. */
+void hmo_expf_array(const float *x, float *out, size_t n) {
+    for (size_t i = 0; i < n; ++i) out[i] = expf(x[i]);
+}
+
 /* RMSNorm::execute, CPU branch (src/transformer/norm/RMSNorm.cpp:64-77):
  * squares summed sequentially in double, inverse RMS in double, one rounding
  * to float per output. */

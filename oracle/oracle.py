@@ -73,6 +73,8 @@ def port() -> ctypes.CDLL:
         L.hmo_silu.argtypes = [f32]
         L.hmo_silu.restype = f32
         L.hmo_rms_norm.argtypes = [vp, vp, vp, sz, sz, f32]
+        L.hmo_expf_array.argtypes = [vp, vp, sz]
+        L.hmo_expf_array.restype = None
         L.hmo_rms_norm.restype = None
         _port = L
     return _port
@@ -197,6 +199,14 @@ def moe_layer_port(host_layer, x, threads=None):
     if st != 0:
         raise OracleError(f"moe layer failed with status {st}")
     return out, ids, sc, off
+
+
+def expf_host(x):
+    """The host libm's expf of every element (float32 in, float32 out)."""
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    port().hmo_expf_array(_p(x), _p(out), x.size)
+    return out
 
 
 def rms_norm_port(x, w, eps):
