@@ -87,9 +87,11 @@ __global__ void activation_kernel(int type, const float* __restrict__ in,
 constexpr int kMmCols = 128;
 constexpr int kMmRows = 4;
 
+// ldl: row stride of `left` (K, or the full K when this launch is one pass
+// of a longer K); accumulate: add to `out` instead of overwriting it.
 __global__ void __launch_bounds__(kMmCols) int8_matmul_kernel(
     const float* __restrict__ left, const int8_t* __restrict__ right,
-    float* __restrict__ out, int rows, int K, int N, float scale, int zp, int KS) {
+    float* __restrict__ out, int rows, int K, int N, float scale, int zp, int KS, int ldl, int accumulate) {
     extern __shared__ __align__(16) float msm[];
     cg::cluster_group cluster = cg::this_cluster();
     const int rank = static_cast<int>(cluster.block_rank());
@@ -102,7 +104,7 @@ __global__ void __launch_bounds__(kMmCols) int8_matmul_kernel(
     float* part = msm + kMmRows * KP;    // [kMmRows][kMmCols]
     for (int i = threadIdx.x; i < kMmRows * kc; i += blockDim.x) {
         const int r = i / kc, kk = i % kc;
-        xs[r * KP + kk] = r < nr ? left[static_cast<size_t>(r0 + r) * K + kb + kk] : 0.0f;
+        xs[r * KP + kk] = r < nr ? left[static_cast<size_t>(r0 + r) * ldl + kb + kk] : 0.0f;
     }
     __syncthreads();
     float acc[kMmRows] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -126,7 +128,8 @@ __global__ void __launch_bounds__(kMmCols) int8_matmul_kernel(
         if (r >= nr || c >= N) continue;
         float s = 0.0f;
         for (int q = 0; q < KS; ++q) s += cluster.map_shared_rank(part, q)[r * kMmCols + cl];
-        out[static_cast<size_t>(r0 + r) * N + c] = scale * s;
+        const size_t o = static_cast<size_t>(r0 + r) * N + c;
+        out[o] = accumulate ? out[o] + scale * s : scale * s;
     }
     cluster.sync();
 }
@@ -140,38 +143,54 @@ hmoe_status launch_int8_matmul(const float* left, const int8_t* right, float* ou
         return HMOE_INVALID_ARGUMENT; // validateParameters, Quantization.cpp:24-40
     if (rows > INT_MAX || K > INT_MAX || N > INT_MAX) return HMOE_UNSUPPORTED;
     const size_t col_blocks = (N + kMmCols - 1) / kMmCols;
-    const size_t row_blocks = (rows + kMmRows - 1) / kMmRows;
-    if (row_blocks > 65535) return HMOE_UNSUPPORTED;
+    if (col_blocks > 65535) return HMOE_UNSUPPORTED;
+    // Rows beyond one grid's z extent go in further launches.
+    constexpr size_t kRowsPerLaunch = static_cast<size_t>(65535) * kMmRows;
+    const size_t row_blocks_all = (rows + kMmRows - 1) / kMmRows;
+    const size_t row_blocks = std::min<size_t>(row_blocks_all, 65535);
     int KS = 1;
     while (KS < 8 && col_blocks * row_blocks * KS < 296 && K / (KS * 2) >= 64) KS *= 2;
-    const int KP = static_cast<int>((K + KS - 1) / KS);
-    const size_t smem = static_cast<size_t>(kMmRows * KP + kMmRows * kMmCols) * sizeof(float);
-    if (smem > 200 * 1024) {
-        // Very long K: keep the x tile within shared memory by splitting more.
-        return HMOE_UNSUPPORTED;
+    // The CTA's x rows ([kMmRows][K / KS] FP32) live in shared memory: a long
+    // K is split over more cluster ranks, and beyond 8 ranks into passes
+    // whose partial products are added into `out` (each pass's sum is
+    // deterministic; the passes add in K order).
+    constexpr size_t kSmemCap = 200 * 1024;
+    constexpr size_t kMaxKP = kSmemCap / sizeof(float) / kMmRows - kMmCols; // K per rank
+    while (KS < 8 && (K + KS - 1) / KS > kMaxKP) KS *= 2;
+    const size_t k_pass = static_cast<size_t>(KS) * kMaxKP;
+    for (size_t r0 = 0; r0 < rows; r0 += kRowsPerLaunch) {
+        const size_t nrows = std::min(kRowsPerLaunch, rows - r0);
+        for (size_t k0 = 0; k0 < K; k0 += k_pass) {
+            const size_t kc = std::min(k_pass, K - k0);
+            const int KP = static_cast<int>((kc + KS - 1) / KS);
+            const size_t smem = static_cast<size_t>(kMmRows * KP + kMmRows * kMmCols) * sizeof(float);
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(static_cast<unsigned>(KS), static_cast<unsigned>(col_blocks),
+                               static_cast<unsigned>((nrows + kMmRows - 1) / kMmRows));
+            cfg.blockDim = dim3(kMmCols);
+            cfg.dynamicSmemBytes = smem;
+            cfg.stream = stream;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = static_cast<unsigned>(KS);
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            cudaError_t err = set_smem_limit(reinterpret_cast<const void*>(int8_matmul_kernel), static_cast<int>(smem));
+            if (err == cudaSuccess)
+                err = cudaLaunchKernelEx(&cfg, int8_matmul_kernel, left + r0 * K + k0, right + k0 * N, out + r0 * N,
+                                         static_cast<int>(nrows), static_cast<int>(kc), static_cast<int>(N), scale,
+                                         static_cast<int>(zp), KS, static_cast<int>(K), k0 > 0 ? 1 : 0);
+            if (err != cudaSuccess) {
+                set_last_error("CUDA INT8 weight matmul kernel", err);
+                return HMOE_CUDA_ERROR;
+            }
+            const hmoe_status st = check_launch("CUDA INT8 weight matmul kernel");
+            if (st != HMOE_OK) return st;
+        }
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(static_cast<unsigned>(KS), static_cast<unsigned>(col_blocks), static_cast<unsigned>(row_blocks));
-    cfg.blockDim = dim3(kMmCols);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(KS);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cudaError_t err = set_smem_limit(reinterpret_cast<const void*>(int8_matmul_kernel), static_cast<int>(smem));
-    if (err == cudaSuccess)
-        err = cudaLaunchKernelEx(&cfg, int8_matmul_kernel, left, right, out,
-                                               static_cast<int>(rows), static_cast<int>(K),
-                                               static_cast<int>(N), scale, static_cast<int>(zp), KS);
-    if (err != cudaSuccess) {
-        set_last_error("CUDA INT8 weight matmul kernel", err);
-        return HMOE_CUDA_ERROR;
-    }
-    return check_launch("CUDA INT8 weight matmul kernel");
+    return HMOE_OK;
 }
 
 // ------------------------------------------------------- gather / scatter

@@ -57,6 +57,32 @@ def test_int8_matmul_phase23_shapes(cuda, golden):
         assert_op_close(host(out2), g[f"out_{r}_{k}_{n}"])
 
 
+@pytest.mark.parametrize("rows,K,N", [(3, 120_000, 65), (2000, 20_000, 300), (300_000, 64, 8)])
+def test_int8_matmul_long_k_and_many_rows(cuda, rows, K, N):
+    """The per-op INT8 matmul takes any K and any row count, as the
+    reference's launcher does (CudaKernels.cu:30-107): a K whose x rows do not
+    fit one CTA's shared memory is split over more cluster ranks and then
+    into passes that add into the output; rows beyond one grid go in further
+    launches.  Against a double-precision product, within a bound on FP32
+    accumulation error over K terms (4 sigma of sqrt(K) roundings)."""
+    import torch
+    rng = np.random.default_rng(rows + K)
+    x = rng.standard_normal((rows, K)).astype(np.float32)
+    q = rng.integers(-127, 128, size=(K, N), dtype=np.int8)
+    scale, zp = np.float32(0.003), -3
+    w = (q.astype(np.float64) - zp) * np.float64(scale)
+    ref = x.astype(np.float64) @ w
+    bound = 4.0 * np.sqrt(K) * 2.0 ** -24 * (np.abs(x).astype(np.float64) @ np.abs(w)) + 1e-6
+    dx, dq = t(x, cuda), t(q, cuda)  # kept alive until the kernel has run
+    out = torch.empty((rows, N), dtype=torch.float32, device=cuda)
+    L = H.lib()
+    H.check("mm", L.hmoe_int8_weight_matmul(dx.data_ptr(), dq.data_ptr(), out.data_ptr(),
+                                            rows, K, N, float(scale), zp, stream()))
+    got = host(out).astype(np.float64)
+    assert (np.abs(got - ref) <= bound).all(), float((np.abs(got - ref) / bound).max())
+    assert np.linalg.norm(got - ref) <= 1e-4 * np.linalg.norm(ref)
+
+
 def test_int8_mlp_through_per_op_dropins(cuda, golden):
     import torch
     g = golden("int8_mlp_phase23.npz")
