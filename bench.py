@@ -754,6 +754,13 @@ def main():
         # every local expert counted as touched (an upper bound on the bytes)
         alg = algorithmic(cfg, T, int(plan.local_experts) + cfg.shared_experts, rows_in)
         alg["rows_received"] = int(plan.recv_total)
+        # bytes this rank moves over NVLink per call: its dispatched rows (FP16
+        # row + scale + routing weight) out and the outputs of the rows it
+        # computed for other ranks (BF16) back out; the mirror image in
+        row_out, row_ret = 2 * cfg.hidden + 8, 2 * cfg.hidden
+        peers = [q for q in range(world) if q != rank]
+        nv_out = sum(int(plan.send_rows[q]) * row_out + int(plan.recv_rows[q]) * row_ret for q in peers)
+        nv_in = sum(int(plan.recv_rows[q]) * row_out + int(plan.send_rows[q]) * row_ret for q in peers)
 
     # Single GPU: one layer call, stage events included, captured once into a
     # CUDA graph (hmoe_moe_forward allocates nothing and never synchronises,
@@ -805,10 +812,22 @@ def main():
         launches = per_forward * args.steps  # kernels inside each replayed graph
     H.check("stage events", H.lib().hmoe_set_stage_events(None, 0))
     ms = statistics.mean(step_ms)
+    nvlink = None
     if dist is not None:
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
+        nv = torch.tensor([float(nv_out), float(nv_in)], dtype=torch.float64, device=dev)
+        nv_max = nv.clone()
+        dist.all_reduce(nv_max, op=dist.ReduceOp.MAX)
+        dist.all_reduce(nv, op=dist.ReduceOp.SUM)
+        nvlink = {"bytes_out_per_rank_max": int(nv_max[0].item()), "bytes_in_per_rank_max": int(nv_max[1].item()),
+                  "bytes_total": int(nv[0].item()),
+                  "gbs_out_per_rank_max": nv_max[0].item() / (ms * 1e-3) / 1e9,
+                  "gbs_in_per_rank_max": nv_max[1].item() / (ms * 1e-3) / 1e9,
+                  "note": "per layer call: dispatched rows (FP16 + scale + weight) and returned outputs (BF16) "
+                          "between different ranks, over the step time; link reference 770 GB/s per direction "
+                          "(measured peer copy)"}
     value = world * T / (ms * 1e-3)
 
     # e2e: host buffers in and out, both copies inside the timed region
@@ -972,6 +991,7 @@ def main():
         "stages_ms": avg, "layer_roofline_ms": layer_roof_ms,
         "layer_roofline_frac": layer_roof_ms / ms, "unique_experts": alg["unique_experts"],
         "rows_received_rank0": alg.get("rows_received"),
+        "nvlink": nvlink,
         "device_status": {"status": status[0], "near_ties": status[1], "sequential_logits": status[2]},
         "decode": decode,
         "reference_cuda": ref_cuda,
