@@ -228,6 +228,18 @@ def cpu_reference_sample(cfg, host_layer, x_all, seconds, threads):
         n = min(x_all.shape[0], max(n + 1, int(n * min(8.0, 1.2 * seconds / max(dt, 1e-3)))))
 
 
+def cpu_model() -> Optional[str]:
+    """The host CPU's model name (/proc/cpuinfo), or None."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
 def reference_arm(args, cfg, config, rank):
     """The reference's own CPU implementation of the layer (oracle/_ref: its
     CpuRouterBackend, CpuTensorBackend INT8 GEMMs and ExpertMlpExecutor
@@ -269,7 +281,8 @@ def reference_arm(args, cfg, config, rank):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights quantised to INT8)",
         "config": config,
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "reference", "sample": sample,
+                         "cpu_model": cpu_model()},
         "single_thread": {"value": rate1, "unit": UNIT, "cores": 1,
                           "sample": f"{n1} tokens in {dt1:.1f} s on one thread (the reference's own loop)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -955,7 +968,12 @@ def main():
         rate, n, dt = cpu_reference_sample(cfg, host_layer, x_np, args.cpu_seconds, threads)
         cpu = {"value": rate, "unit": UNIT, "cores": threads, "kind": "reference",
                "sample": f"{n} tokens of this workload through the reference CPU path "
-                         f"(oracle/_ref), {dt:.1f} s, expert groups over {threads} threads"}
+                         f"(oracle/_ref), {dt:.1f} s, expert groups over {threads} threads",
+               "cpu_model": cpu_model()}
+        # the reference's own loop is single-threaded (CpuTensorBackend.cpp:173-186)
+        rate1, n1, dt1 = cpu_reference_sample(cfg, host_layer, x_np, min(args.cpu_seconds, 5.0), 1)
+        cpu["single_thread"] = {"value": rate1, "unit": UNIT, "cores": 1,
+                                "sample": f"{n1} tokens in {dt1:.1f} s on one thread"}
 
     decode = None
     if world == 1 and T > 16 and not args.no_decode:
