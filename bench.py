@@ -45,6 +45,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "hypermoe-engine_b200"))
 
 METRIC = "MoE-layer tokens/s (Qwen3-30B-A3B shape, INT8 experts)"
+WORKLOADS = {"c1": "c1: small cpu-runnable moe layer", "c2": "c2: qwen1.5-moe-a2.7b moe layer (4 shared experts)",
+             "c3": "c3: qwen3-30b-a3b moe layer", "c5": "c5: qwen3-235b-a22b moe layer"}
+SHAPES = {"c1": "H256 E8 k2 I512", "c2": "Qwen1.5-MoE-A2.7B shape", "c3": "Qwen3-30B-A3B shape",
+          "c5": "Qwen3-235B-A22B shape"}
 UNIT = "tokens/s"
 STAGES = ["route", "group", "gate_up", "down", "combine"]
 
@@ -63,7 +67,7 @@ def parse():
     p.add_argument("--stack-cpu-tokens", type=int, default=8,
                    help="c4: tokens the reference CPU path runs through the whole stack")
     p.add_argument("--no-stack", action="store_true",
-                   help="single GPU: skip the c4 stack measurement added to the c3 line")
+                   help="single GPU: skip the c4 stack and the c2/c5 layer measurements added to the c3 line")
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--impl", default="hmoe", choices=["hmoe", "reference"])
     p.add_argument("--variant", type=int, default=0,
@@ -87,6 +91,11 @@ def parse():
     p.add_argument("--eager", action="store_true",
                    help="time eager hmoe_moe_forward calls instead of CUDA-graph replays")
     return p.parse_args()
+
+
+def metric_for(config: str) -> str:
+    """BASELINE's metric for the c3 workload; the same wording for the others."""
+    return METRIC if config == "c3" else f"MoE-layer tokens/s ({SHAPES.get(config, config)}, INT8 experts)"
 
 
 def load_peaks():
@@ -276,7 +285,7 @@ def reference_arm(args, cfg, config, rank):
               f"CpuTensorBackend INT8 GEMMs; aggregate over {threads} host threads, one expert group per "
               f"thread at a time)")
     print(json.dumps({
-        "metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+        "metric": metric_for(args.config), "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * statistics.mean(times),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights quantised to INT8)",
@@ -289,23 +298,41 @@ def reference_arm(args, cfg, config, rank):
     }))
 
 
-def stack_subprocess(seed, steps, warmup, timeout=420):
-    """BASELINE configs[3] measured in a process of its own (bench.py --config
-    c4: the 48-block stack, prefill and decode), so that the c3 line's own
-    figures never depend on it; returns its JSON line or why it is missing."""
-    cmd = [sys.executable, os.path.abspath(__file__), "--config", "c4", "--steps", str(steps),
-           "--warmup", str(warmup), "--seed", str(seed)]
+def config_subprocess(extra, timeout):
+    """Another BASELINE configuration measured by this script in a process of
+    its own, so that the c3 line's own figures never depend on it; returns
+    that run's JSON line or why it is missing."""
+    cmd = [sys.executable, os.path.abspath(__file__)] + extra
     env = {k: v for k, v in os.environ.items() if k not in ("RANK", "WORLD_SIZE", "LOCAL_RANK")}
     try:
         p = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
     except subprocess.TimeoutExpired:
-        return {"unavailable": f"the c4 stack run did not finish within {timeout} s"}
+        return {"unavailable": f"`bench.py {' '.join(extra)}` did not finish within {timeout} s"}
     lines = [ln for ln in p.stdout.strip().splitlines() if ln.startswith("{")]
     if p.returncode != 0 or not lines:
-        return {"unavailable": f"bench.py --config c4 exited {p.returncode}: {p.stderr.strip()[-300:]}"}
+        return {"unavailable": f"`bench.py {' '.join(extra)}` exited {p.returncode}: {p.stderr.strip()[-300:]}"}
     out = json.loads(lines[-1])
-    out["command"] = " ".join(["python", "bench.py"] + cmd[2:])
+    out["command"] = " ".join(["python", "bench.py"] + extra)
     return out
+
+
+def stack_subprocess(seed, steps, warmup, timeout=420):
+    """the 48-block stack (prefill and decode)."""
+    return config_subprocess(["--config", "c4", "--steps", str(steps), "--warmup", str(warmup),
+                              "--seed", str(seed)], timeout)
+
+
+def layer_subprocesses(seed, steps, warmup, timeout=300):
+    """BASELINE configs[1] and [4] as single layers: C2 (Qwen1.5-MoE-A2.7B,
+    shared experts) at its 512-token prefill and 1-token decode, and C5
+    (Qwen3-235B-A22B) at 8192 tokens with 1- and 128-token decode batches.
+    Device timing and stage splits only (no e2e, CPU or reference runs)."""
+    common = ["--steps", str(steps), "--warmup", str(warmup), "--seed", str(seed), "--no-cpu-baseline",
+              "--no-reference-cuda", "--no-e2e", "--no-stack"]
+    return {"c2_t512": config_subprocess(["--config", "c2", "--tokens", "512", "--decode-tokens", "1"] + common,
+                                         timeout),
+            "c5_t8192": config_subprocess(["--config", "c5", "--tokens", "8192", "--decode-tokens", "1,128"] + common,
+                                          timeout)}
 
 
 def reference_cuda(cfg, T, seed, steps, warmup, gpu_index, pci, timeout=600):
@@ -390,24 +417,36 @@ def decode_split(layer, cfg, T, seed, dev, flush, events, peaks, steps=20):
     # The automatic choice (what a caller gets), the single-kernel decode
     # layer forced (it takes up to 8 tokens), the multi-kernel GEMV path
     # with its stage split and the multi-kernel tensor-core GEMM path.
+    refused = {}
+
+    def forced(variant, name):
+        # a forced variant the shape or batch does not fit is reported, not fatal
+        try:
+            return replay(variant)
+        except H.HmoeError as exc:
+            refused[name] = str(exc)
+            return None, None
+
     ms, med = replay(0)
-    single_ms, _ = replay(3) if T <= 8 else (None, None)
-    multi_ms, multi = replay(1)
-    gemm_ms, gemm = replay(2)
+    single_ms, _ = forced(3, "single_kernel") if T <= 8 else (None, None)
+    multi_ms, multi = forced(1, "multi_kernel_gemv")
+    gemm_ms, gemm = forced(2, "gemm")
     alg = algorithmic(cfg, T, U)
     roof_ms = 1e3 * max(alg["layer"]["bytes"] / (peaks["hbm_gbs"] * 1e9),
                         alg["layer"]["flops"] / (peaks["bf16_tflops"] * 1e12))
     expert_bytes = alg["gate_up"]["bytes"] + alg["down"]["bytes"]
     # expert bytes over the expert stages of the multi-kernel path, and over
     # the whole single-kernel layer (a lower bound of its expert stream rate)
-    multi_expert_ms = multi["gate_up"] + multi["down"]
+    multi_expert_ms = multi["gate_up"] + multi["down"] if multi else None
     return {"tokens": T, "ms_per_step": ms, "value": T / (ms * 1e-3), "unit": UNIT,
             "single_kernel_ms": single_ms, "multi_kernel_ms": multi_ms, "multi_kernel_stages_ms": multi,
-            "gemm_ms": gemm_ms, "gemm_stages_ms": gemm,
+            "gemm_ms": gemm_ms, "gemm_stages_ms": gemm, "stages_ms": med,
+            "variants_refused": refused or None,
             "unique_experts": U, "layer_roofline_ms": roof_ms,
             "layer_roofline_frac": roof_ms / ms,
-            "expert_hbm_gbs": expert_bytes / (multi_expert_ms * 1e-3) / 1e9,
-            "expert_hbm_frac": expert_bytes / (multi_expert_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+            "expert_hbm_gbs": expert_bytes / (multi_expert_ms * 1e-3) / 1e9 if multi_expert_ms else None,
+            "expert_hbm_frac": (expert_bytes / (multi_expert_ms * 1e-3) / 1e9 / peaks["hbm_gbs"]
+                                if multi_expert_ms else None),
             "single_kernel_layer_hbm_frac": (alg["layer"]["bytes"] / (single_ms * 1e-3) / 1e9 / peaks["hbm_gbs"]
                                              if single_ms else None),
             "timing": "cuda-graph replay, median of %d steps, 256 MiB L2 flush before each" % steps}
@@ -677,7 +716,7 @@ def main():
 
     cfg = H.CONFIGS[args.config]
     T = args.tokens
-    config = {"workload": f"{args.config}: qwen3-30b-a3b moe layer" if args.config == "c3" else args.config,
+    config = {"workload": WORKLOADS.get(args.config, args.config),
               "hidden": cfg.hidden, "experts": cfg.experts, "top_k": cfg.top_k,
               "intermediate": cfg.intermediate, "shared_experts": cfg.shared_experts,
               "tokens_per_gpu": T, "routing": "zipf1.1" if cfg.zipf_alpha else "uniform",
@@ -988,16 +1027,18 @@ def main():
         if T > 1:
             ref_cuda_decode = reference_cuda(cfg, 1, args.seed, 20, 3, gpu_index, pci)
 
-    stack = None
+    stack = others = None
     if world == 1 and args.config == "c3" and not args.no_stack:
         stack = stack_subprocess(args.seed, steps=5, warmup=3)
+        others = layer_subprocesses(args.seed, steps=10, warmup=3)
 
     # tensor-core GEMM present (hmoe_set_variant(2) is refused without it)?
     has_gemm = H.lib().hmoe_set_variant(2) == 0
     H.lib().hmoe_set_variant(args.variant)
     used_gemm = has_gemm and args.variant != 1 and T * (cfg.top_k + cfg.shared_experts) > 64
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "metric": metric_for(args.config),
+        "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp32" if not used_gemm else "fp16+bf16",
         "data": "synthetic (seeded N(0,1) activations, N(0,0.02^2) weights quantised to INT8)",
@@ -1015,6 +1056,7 @@ def main():
         "reference_cuda": ref_cuda,
         "reference_cuda_decode_t1": ref_cuda_decode,
         "stack_c4": stack,
+        "other_configs": others,
     }
     print(json.dumps(line))
     if dist is not None:
