@@ -132,7 +132,12 @@ typedef struct {
  * row-major [in,out] (INPUT_OUTPUT), at gate_offset/up_offset/down_offset
  * inside the blob.  ExpertWeightMap::createViews (ExpertWeightMap.cpp:
  * 65-108) slices exactly these views.  expert_stride and the offsets must
- * be multiples of 16 bytes and H, I multiples of 64.
+ * be multiples of 16 bytes and H, I multiples of 64.  The arena and the
+ * router matrix must start on a 16-byte boundary, the quantisation records
+ * and the bias on a 4-byte one (cudaMalloc and the reference's memory pool
+ * give 256): tensor and bulk copies read them, and a misaligned address
+ * would fault, so every layer entry point refuses it with
+ * HMOE_INVALID_ARGUMENT.
  *
  * Routed experts are ids [0, experts); `shared_experts` always-on experts
  * follow them in the arena (ids experts..experts+shared-1), see every token
@@ -190,7 +195,9 @@ hmoe_status hmoe_route(const hmoe_layer_desc *desc, const float *x,
                        size_t workspace_bytes, void *stream);
 
 /* One MoE layer forward: y[T,H] FP32 = sum over the token's experts, in
- * ascending expert id, of routing_weight * expert_mlp(x).  x [T,H] FP32. */
+ * ascending expert id, of routing_weight * expert_mlp(x).  x [T,H] FP32.
+ * x, y and the workspace start on 16-byte boundaries (HMOE_INVALID_ARGUMENT
+ * otherwise), as do residual and y_bf16 in the entry points that take them. */
 hmoe_status hmoe_moe_forward(const hmoe_layer_desc *desc, const float *x,
                              float *y, size_t tokens, void *workspace,
                              size_t workspace_bytes, void *stream);
