@@ -308,6 +308,18 @@ def make_tokens(cfg: LayerConfig, T: int, seed: int = 0, threads: int = 0) -> np
     return synth_normal(seed, 1, 1.0, (T, cfg.hidden), threads)
 
 
+def _check_rows(name, t, T, width, dtype, device=None):
+    """The C ABI reads raw pointers: refuse a tensor whose dtype, shape,
+    layout or device the kernels would misread (None passes)."""
+    if t is None:
+        return
+    if (t.dtype != dtype or not t.is_contiguous() or t.dim() != 2 or tuple(t.shape) != (T, width)
+            or (device is not None and t.device != device)):
+        where = f" on {device}" if device is not None else ""
+        raise ValueError(f"{name} must be a contiguous {dtype} tensor of shape [{T}, {width}]{where}; "
+                         f"got {t.dtype} {tuple(t.shape)} on {t.device}")
+
+
 class DeviceLayer:
     """A HostLayer resident on the current CUDA device, plus its descriptor."""
 
@@ -334,6 +346,14 @@ class DeviceLayer:
         self.desc = d
         self._ws = None
 
+    def _check_io(self, T, x=None, y=None, residual=None, y_bf16=None):
+        import torch
+        dev, Hd = self.arena.device, self.cfg.hidden
+        _check_rows("x", x, T, Hd, torch.float32, dev)
+        _check_rows("y", y, T, Hd, torch.float32, dev)
+        _check_rows("residual", residual, T, Hd, torch.float32, dev)
+        _check_rows("y_bf16", y_bf16, T, Hd, torch.bfloat16, dev)
+
     def workspace_bytes(self, T: int, host_io: bool = False) -> int:
         n = ctypes.c_size_t()
         check("hmoe_workspace_size", lib().hmoe_workspace_size(
@@ -354,6 +374,7 @@ class DeviceLayer:
         T = x.shape[0]
         if y is None:
             y = torch.empty((T, self.cfg.hidden), dtype=torch.float32, device=x.device)
+        self._check_io(T, x=x, y=y)
         ws = self.workspace(T)
         check("hmoe_moe_forward", lib().hmoe_moe_forward(
             ctypes.byref(self.desc), x.data_ptr(), y.data_ptr(), T, ws.data_ptr(), ws.numel(), _stream(stream)))
@@ -366,6 +387,7 @@ class DeviceLayer:
         T = x.shape[0]
         if y is None:
             y = torch.empty((T, self.cfg.hidden), dtype=torch.float32, device=x.device)
+        self._check_io(T, x=x, y=y, residual=residual, y_bf16=y_bf16)
         ws = self.workspace(T)
         check("hmoe_moe_forward_residual", lib().hmoe_moe_forward_residual(
             ctypes.byref(self.desc), x.data_ptr(), _ptr(residual), y.data_ptr(), _ptr(y_bf16), T,
@@ -377,7 +399,10 @@ class DeviceLayer:
         (a device uint8 tensor of at least workspace_bytes(T, host_io=True))
         replaces the layer's own, so that calls on different streams can be
         in flight together."""
+        import torch
         T = x_host.shape[0]
+        for name, t in (("x_host", x_host), ("y_host", y_host)):
+            _check_rows(name, t, T, self.cfg.hidden, torch.float32, torch.device("cpu"))
         ws = workspace if workspace is not None else self.workspace(T, host_io=True)
         check("hmoe_moe_forward_host", lib().hmoe_moe_forward_host(
             ctypes.byref(self.desc), x_host.data_ptr(), y_host.data_ptr(), T, ws.data_ptr(), ws.numel(),
@@ -387,6 +412,7 @@ class DeviceLayer:
     def route(self, x, stream=None):
         import torch
         T, k, E = x.shape[0], self.cfg.top_k, self.cfg.experts
+        self._check_io(T, x=x)
         dev = x.device
         ids = torch.empty((T, k), dtype=torch.int32, device=dev)
         scores = torch.empty((T, k), dtype=torch.float32, device=dev)
@@ -562,6 +588,7 @@ class EpLayer(DeviceLayer):
         max_tokens = max_tokens or max(T, 1)
         if y is None:
             y = torch.empty((T, self.cfg.hidden), dtype=torch.float32, device=x.device)
+        self._check_io(T, x=x, y=y)
         ws = self.ep_workspace(max_tokens)
         check("hmoe_ep_moe_forward", lib().hmoe_ep_moe_forward(
             ctypes.byref(self.desc), self.comm.handle, x.data_ptr() if T else None, y.data_ptr() if T else None,
@@ -577,6 +604,7 @@ class EpLayer(DeviceLayer):
         max_tokens = max_tokens or max(T, 1)
         if y is None:
             y = torch.empty((T, self.cfg.hidden), dtype=torch.float32, device=x.device)
+        self._check_io(T, x=x, y=y, residual=residual, y_bf16=y_bf16)
         ws = self.ep_workspace(max_tokens)
         check("hmoe_ep_moe_forward_residual", lib().hmoe_ep_moe_forward_residual(
             ctypes.byref(self.desc), self.comm.handle, x.data_ptr() if T else None,

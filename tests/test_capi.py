@@ -9,6 +9,7 @@ import numpy as np
 import pytest
 
 import hmoe_api as H
+from conftest import host_layer
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
@@ -125,3 +126,29 @@ def test_arena_layout_matches_packer():
             q = hl.arena[e * cfg.expert_stride + p * cfg.proj_bytes:][:cfg.proj_bytes]
             assert np.abs(q).max() == 127  # symmetric per-projection scale
             assert hl.zps[e, p] == 0 and hl.scales[e, p] > 0
+
+
+def test_layer_binding_refuses_tensors_the_kernels_would_misread():
+    """The ctypes layer methods hand raw pointers to the C ABI, so they
+    refuse a token or output tensor of the wrong dtype, shape, layout or
+    device before anything is enqueued (checked here without a GPU: every
+    call below is refused on the host)."""
+    import torch
+    cfg = H.CONFIGS["c1"]
+    dl = H.DeviceLayer(host_layer("c1", 0), "cpu")
+    good = torch.zeros((4, cfg.hidden), dtype=torch.float32)
+    bad_inputs = [good.double(), good.t().contiguous().t(), torch.zeros((4, cfg.hidden + 1)),
+                  torch.zeros((4, cfg.hidden), dtype=torch.float32).view(2, 2 * cfg.hidden)]
+    for x in bad_inputs:
+        with pytest.raises(ValueError):
+            dl.forward(x)
+        with pytest.raises(ValueError):
+            dl.route(x)
+    with pytest.raises(ValueError):
+        dl.forward(good, y=torch.zeros((3, cfg.hidden)))
+    with pytest.raises(ValueError):
+        dl.forward_residual(good, residual=good.half())
+    with pytest.raises(ValueError):
+        dl.forward_residual(good, y_bf16=torch.zeros((4, cfg.hidden), dtype=torch.float16))
+    with pytest.raises(ValueError):
+        dl.forward_host(good.double(), good)
